@@ -1,0 +1,216 @@
+/*
+ * tfv.h — C ABI of the batched warpgroup schedule verifier for NVIDIA B200 (sm_100a).
+ *
+ * The library replaces, for whole batches of candidate schedules, the CPU verifier of
+ * TileFoundry: `_verify_warpgroup_schedule(problem, schedule)`
+ * (src/tilefoundry/schedule/warpgroup/verify.py:203-322) and its public wrapper
+ * `verify_warpgroup_schedule(program, hardware, schedule)` (verify.py:325-331).
+ * For every candidate it returns the id of the first violated check class (0 = the
+ * schedule verifies; the numbering follows the reference's check order, see
+ * TFV_CLASS_* below), the makespan (max completion over all timed rows, api.py:29-33)
+ * and the initiation interval (start(2, first op) - start(1, first op) when the loop
+ * has >= 3 iterations, verify.py:261-262; otherwise 0).
+ *
+ * Conventions
+ *   - Every function returns TFV_OK (0) or a negative TFV_ERR_* status; no C++
+ *     exception crosses the boundary. tfv_last_error() copies the calling thread's
+ *     last error message.
+ *   - Operations are identified by their index in the problem's id-sorted operation
+ *     list (Python str ordering of the ids, model.py:308).
+ *   - All times are int32 and must lie in [0, 2^30); candidates outside that domain
+ *     get TFV_CLASS_OUT_OF_RANGE instead of a verdict.
+ *   - Device entry points take DEVICE pointers owned by the caller and are ordered on
+ *     the given CUDA stream (NULL = the legacy default stream); they return once the
+ *     work is enqueued. The library owns only the tfv_problem handle (per device).
+ *   - A problem handle is immutable after creation and may be used from several host
+ *     threads at once.
+ */
+#ifndef TFV_H_
+#define TFV_H_
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+#define TFV_ABI_VERSION 1
+
+/* ---- status codes ---------------------------------------------------------------- */
+#define TFV_OK 0
+#define TFV_ERR_INVALID_ARGUMENT (-1)
+#define TFV_ERR_CUDA (-2)
+#define TFV_ERR_UNSUPPORTED (-3)
+#define TFV_ERR_RANGE (-4)
+#define TFV_ERR_DEVICE_TIMEOUT (-5)
+
+/* ---- verdict classes (reference check order, verify.py:203-322) -------------------- */
+#define TFV_CLASS_PASS 0
+#define TFV_CLASS_SCHEDULE_MALFORMED 1        /* record constructors, model.py:431-507 */
+#define TFV_CLASS_LANE_COUNT 2                /* verify.py:211-212 */
+#define TFV_CLASS_LANE_REPEAT 3               /* verify.py:216-217 (unreachable after 1) */
+#define TFV_CLASS_LANE_COVERAGE 4             /* verify.py:223-226 */
+#define TFV_CLASS_OWNERSHIP 5                 /* verify.py:227-236 */
+#define TFV_CLASS_DUP_TIMES 6                 /* verify.py:244-245 (unreachable after 1) */
+#define TFV_CLASS_TIME_COVERAGE 7             /* verify.py:246-252 */
+#define TFV_CLASS_ISSUE_DURATION 8            /* verify.py:256-257 */
+#define TFV_CLASS_COMPLETION_LATENCY 9        /* verify.py:258-259 */
+#define TFV_CLASS_II_NONPOSITIVE 10           /* verify.py:262-264 */
+#define TFV_CLASS_II_MISMATCH 11              /* verify.py:265-276 */
+#define TFV_CLASS_LANE_ORDER 12               /* verify.py:278-282 */
+#define TFV_CLASS_SYNC_UNKNOWN_OP 13          /* verify.py:285-286 */
+#define TFV_CLASS_SYNC_NO_INSTANCE 14         /* verify.py:287-289 */
+#define TFV_CLASS_SYNC_INEQUALITY 15          /* verify.py:290-292 */
+#define TFV_CLASS_REGISTER_CROSSES_LANES 16   /* verify.py:296-304 */
+#define TFV_CLASS_RELATION_TIMING 17          /* verify.py:311-312 */
+#define TFV_CLASS_RELATION_NO_PATH 18         /* verify.py:313-314 */
+#define TFV_CLASS_CARRIED_SHARED_LIFETIME 19  /* verify.py:315-318 */
+#define TFV_CLASS_RESOURCE_CAPACITY 20        /* verify.py:183-200, 320 */
+#define TFV_CLASS_CYCLE 21                    /* verify.py:321-322 (unreachable after 12,15,17,19) */
+#define TFV_CLASS_OUT_OF_RANGE (-1)           /* a time is outside [0, 2^30): no verdict */
+#define TFV_CLASS_BAD_PACKING (-2)            /* lane positions are not a permutation per lane */
+
+/* ---- frame flags ------------------------------------------------------------------ */
+#define TFV_FRAME_MALFORMED 1       /* lanes/sync violate the record constructors -> class 1 */
+#define TFV_FRAME_UNKNOWN_LANE_OP 2 /* a lane names an operation the problem lacks -> class 4 */
+
+/* per-candidate row flags of a rows batch (what the dense [I][N] layout cannot hold) */
+#define TFV_ROWS_MALFORMED 1  /* a row violates the TimedOperation/WarpgroupSchedule constructors -> class 1 */
+#define TFV_ROWS_COVERAGE 2   /* rows are missing or name unknown instances -> class 7 */
+
+/* lane_pos encoding: (lane << 12) | position; lane TFV_LANE_ABSENT = not in any lane. */
+#define TFV_LANE_SHIFT 12
+#define TFV_POS_MASK 0x0FFF
+#define TFV_LANE_ABSENT 15
+#define TFV_MAX_LANES 15
+#define TFV_MAX_OPS 4095
+#define TFV_TIME_LIMIT (1 << 30)
+
+typedef struct tfv_problem tfv_problem;
+
+/* The integer closure of one WarpgroupProblem (model.py:377), host pointers.
+ * Replaces the per-call tables the reference derives inside the verifier:
+ *   operations        problem.loop.ops (model.py:248)
+ *   relations         _required_completion_relations (verify.py:55-71), sorted
+ *   carried edges     _carried_shared_lifetime_edges (verify.py:74-86), (user, def) pairs
+ *   register groups   owner+users of each register value (verify.py:296-304)
+ *   resources         problem.resources sorted by id; per-op resource_windows (verify.py:183-200) */
+typedef struct tfv_problem_desc {
+    int32_t n_ops;        /* N, 1..TFV_MAX_OPS */
+    int32_t iterations;   /* I >= 1 */
+    int32_t warp_groups;  /* L, 1..TFV_MAX_LANES */
+    const int32_t* issue_duration;     /* [N] > 0 */
+    const int32_t* completion_latency; /* [N] >= issue_duration */
+    const int32_t* warp_group;         /* [N] declared lane, or -1 when undeclared */
+    int32_t n_relations;
+    const int32_t* relation_after;     /* [R] op index */
+    const int32_t* relation_before;    /* [R] op index */
+    const int32_t* relation_distance;  /* [R] 0 or 1 */
+    int32_t n_carried;
+    const int32_t* carried_user;       /* [C] */
+    const int32_t* carried_def;        /* [C] */
+    int32_t n_register_groups;
+    const int32_t* register_group_offsets; /* [G + 1] */
+    const int32_t* register_group_ops;     /* [offsets[G]] */
+    int32_t n_resources;
+    const int32_t* resource_capacity;  /* [Q] > 0, resources in id order */
+    const int32_t* window_offsets;     /* [N + 1] CSR over operations */
+    const int32_t* window_resource;    /* [offsets[N]] resource index */
+    const int32_t* window_amount;      /* [offsets[N]] > 0 */
+    const int32_t* window_duration;    /* [offsets[N]] in (0, completion_latency] */
+} tfv_problem_desc;
+
+/* Schedule skeletons ("frames"): the lane programs plus the sync edge set of one or
+ * more candidates — everything of a WarpgroupSchedule (model.py:481) except its times.
+ * Device pointers. Sync sets are shared between frames; each set's edges are in the
+ * sorted order of SynchronizationEdge (model.py:506). */
+typedef struct tfv_frames {
+    int32_t n_frames;
+    const uint16_t* lane_pos;   /* [n_frames][N] (lane << 12) | position */
+    const int32_t* lane_count;  /* [n_frames] number of lanes the schedule lists */
+    const int32_t* flags;       /* [n_frames] TFV_FRAME_* */
+    const int32_t* sync_set;    /* [n_frames] index into the sync sets */
+    int32_t n_sync_sets;
+    const int32_t* sync_offsets; /* [n_sync_sets + 1] */
+    const int32_t* sync_edges;   /* [sync_offsets[n_sync_sets]][3]: after, before, distance;
+                                    an op index of -1 names an operation the problem lacks */
+} tfv_frames;
+
+/* Compact periodic candidates (solve.py:206-231): iteration 0 starts at
+ * prologue[op], iteration i >= 1 at offset[op] + i * ii; issue end and completion add
+ * the operation's issue duration and completion latency. Per-candidate times are int16
+ * deltas against a shared base. Device pointers; op-major ("flat SoA") layout. */
+typedef struct tfv_periodic_batch {
+    int64_t n_candidates;
+    int64_t op_stride;              /* elements between consecutive ops' rows, >= n_candidates */
+    const int32_t* base_prologue;   /* [N] */
+    const int32_t* base_offset;     /* [N] */
+    const int16_t* prologue_delta;  /* [N][op_stride] */
+    const int16_t* offset_delta;    /* [N][op_stride] */
+    const int32_t* ii;              /* [n_candidates] */
+    const int32_t* frame;           /* [n_candidates] index into the frames */
+} tfv_periodic_batch;
+
+/* Explicit timing rows (the `times` of WarpgroupSchedule, serialization.py:706-722),
+ * candidate-major [n][I][N]. Device pointers. */
+typedef struct tfv_rows_batch {
+    int64_t n_candidates;
+    const int32_t* start;       /* [n][I][N] */
+    const int32_t* issue_end;   /* [n][I][N] */
+    const int32_t* completion;  /* [n][I][N] */
+    const int32_t* frame;       /* [n] */
+    const int32_t* row_flags;   /* [n] TFV_ROWS_* or NULL; missing rows are stored as
+                                   (start 0, issue_end 1, completion 1) */
+} tfv_rows_batch;
+
+/* Per-candidate results, device (or, for the *_host entry, host) pointers. */
+typedef struct tfv_results {
+    int32_t* verdict;    /* [n] TFV_CLASS_* */
+    int32_t* makespan;   /* [n] max completion, saturated to int32 */
+    int32_t* ii;         /* [n] */
+} tfv_results;
+
+/* Library identity. */
+int tfv_abi_version(void);
+int tfv_last_error(char* buffer, size_t size);
+
+/* Create/destroy the device-resident problem tables on `device`
+ * (the closure `build_warpgroup_problem`, build.py:169-220, hands to the verifier). */
+int tfv_problem_create(const tfv_problem_desc* desc, int device, tfv_problem** out);
+int tfv_problem_destroy(tfv_problem* problem);
+
+/* Bytes of device scratch ("frame table") that tfv_analyze_frames writes for n_frames. */
+int tfv_frame_table_bytes(const tfv_problem* problem, int32_t n_frames, size_t* bytes);
+
+/* Structural analysis of every frame: lane coverage and ownership
+ * (verify.py:209-236), lane successors (verify.py:99-112), register locality
+ * (verify.py:296-304) and lane/sync reachability of every required completion relation
+ * (verify.py:122-160, 306-314). Writes the frame table. */
+int tfv_analyze_frames(const tfv_problem* problem, const tfv_frames* frames,
+                       void* frame_table, size_t frame_table_bytes, void* stream);
+
+/* Verify compact periodic candidates against analysed frames
+ * (verify.py:203-322 for every candidate of the batch). */
+int tfv_verify_periodic(const tfv_problem* problem, const tfv_frames* frames,
+                        const void* frame_table, const tfv_periodic_batch* batch,
+                        const tfv_results* results, void* stream);
+
+/* Verify explicit timing rows against analysed frames (general schedules). */
+int tfv_verify_rows(const tfv_problem* problem, const tfv_frames* frames,
+                    const void* frame_table, const tfv_rows_batch* batch,
+                    const tfv_results* results, void* stream);
+
+/* End-to-end entry with HOST buffers: copies frames and candidates to the problem's
+ * device in chunks (pinned host memory gives full PCIe bandwidth), analyses the frames,
+ * verifies every candidate with copies overlapped with compute, and writes host results.
+ * Synchronous. All pointers in `frames`, `batch` (op_stride counts host elements) and
+ * `results` are host pointers. */
+int tfv_verify_periodic_host(const tfv_problem* problem, const tfv_frames* frames,
+                             const tfv_periodic_batch* batch, const tfv_results* results);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* TFV_H_ */

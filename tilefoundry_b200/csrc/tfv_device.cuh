@@ -1,0 +1,140 @@
+// Device-side tables and kernel entry points of the batched schedule verifier.
+//
+// One tfv_problem owns a single device allocation holding every per-problem table
+// (DevProblem below). Kernels receive DevProblem by value: it is a bundle of device
+// pointers and counts, all immutable after tfv_problem_create.
+#pragma once
+
+#include <cstddef>
+#include <cstdint>
+
+#include <cuda_runtime.h>
+
+#include "tfv.h"
+
+namespace tfv {
+
+// Successor encoding in the frame table: the op index of the next operation on the
+// same lane in the same iteration, or kWrap | first-op-of-lane for the last operation
+// of a lane (the wrap edge (i, last) -> (i + 1, first), verify.py:105-111).
+constexpr int kWrap = 0x4000;
+constexpr int kSuccMask = 0x0FFF;
+constexpr uint16_t kInfPos = 0xFFFF;
+
+// Frame-table flag bits.
+constexpr int kFrameRegisterCross = 1;  // some register value spans lanes (class 16)
+
+struct DevProblem {
+    int n_ops;
+    int iterations;
+    int warp_groups;
+    int n_relations;
+    int n_carried;
+    int n_register_groups;
+    int n_resources;
+    int n_windows;
+    // [N] per operation
+    const int* issue;       // issue_duration
+    const int* latency;     // completion_latency
+    const int* warp_group;  // declared lane or -1
+    // [R] relations packed as after | before << 12 | distance << 24 (distance 0/1)
+    const int* relation;
+    // [C] carried-lifetime edges packed as user | def << 16
+    const int* carried;
+    // register groups CSR
+    const int* reg_offsets;  // [G + 1]
+    const int* reg_ops;
+    // resources: capacity [Q]; windows grouped by resource: res_offsets [Q + 1],
+    // res_win packed op | (window index) — amount and duration arrays parallel.
+    const int* capacity;
+    const int* res_offsets;
+    const int* res_win_op;
+    const int* res_win_amount;
+    const int* res_win_duration;
+};
+
+struct DevFrames {
+    int n_frames;
+    const uint16_t* lane_pos;
+    const int* lane_count;
+    const int* flags;
+    const int* sync_set;
+    int n_sync_sets;
+    const int* sync_offsets;
+    const int* sync_edges;  // [E][3]
+};
+
+// Frame table (device scratch written by the analysis kernel). Layout inside one
+// buffer, for F frames and N operations:
+//   int32  frame_class[F]       0 or the first structural verdict (1, 2, 4, 5, -2)
+//   int32  frame_flags[F]       kFrameRegisterCross
+//   int32  first_unreached[F]   first relation (sorted order, with instances) whose
+//                               completion -> start path is absent, or -1
+//   int16  succ[F][N]           lane successor (see kWrap)
+struct FrameTable {
+    int* frame_class;
+    int* frame_flags;
+    int* first_unreached;
+    int16_t* succ;
+};
+
+inline size_t frame_table_bytes(int n_frames, int n_ops) {
+    size_t head = 3 * sizeof(int) * static_cast<size_t>(n_frames);
+    head = (head + 15) & ~static_cast<size_t>(15);
+    return head + sizeof(int16_t) * static_cast<size_t>(n_frames) * n_ops + 16;
+}
+
+inline FrameTable frame_table_view(void* base, int n_frames) {
+    FrameTable t;
+    char* p = static_cast<char*>(base);
+    t.frame_class = reinterpret_cast<int*>(p);
+    t.frame_flags = t.frame_class + n_frames;
+    t.first_unreached = t.frame_flags + n_frames;
+    size_t head = 3 * sizeof(int) * static_cast<size_t>(n_frames);
+    head = (head + 15) & ~static_cast<size_t>(15);
+    t.succ = reinterpret_cast<int16_t*>(p + head);
+    return t;
+}
+
+struct DevPeriodic {
+    long long n;
+    long long stride;
+    const int* base_prologue;
+    const int* base_offset;
+    const int16_t* prologue_delta;
+    const int16_t* offset_delta;
+    const int* ii;
+    const int* frame;
+};
+
+struct DevRows {
+    long long n;
+    const int* start;
+    const int* issue_end;
+    const int* completion;
+    const int* frame;
+    const int* row_flags;  // may be null
+};
+
+struct DevResults {
+    int* verdict;
+    int* makespan;
+    int* ii;
+};
+
+// Launchers (tfv_kernels.cu). Each returns the cudaError_t of its launch.
+cudaError_t launch_analyze_frames(const DevProblem& p, const DevFrames& f, FrameTable t,
+                                  int sm_count, cudaStream_t stream);
+cudaError_t launch_verify_periodic(const DevProblem& p, const DevFrames& f, FrameTable t,
+                                   const DevPeriodic& b, DevResults r, int sm_count,
+                                   cudaStream_t stream);
+cudaError_t launch_verify_rows(const DevProblem& p, const DevFrames& f, FrameTable t,
+                               const DevRows& b, DevResults r, int sm_count,
+                               cudaStream_t stream);
+
+// Shared-memory footprint checks used by the host before launching.
+size_t analyze_smem_bytes(int n_ops, int lanes);
+int periodic_tile(int n_ops);
+size_t periodic_smem_bytes(const DevProblem& p, int tile);
+
+}  // namespace tfv

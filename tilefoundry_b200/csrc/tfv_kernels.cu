@@ -1,0 +1,678 @@
+// Kernels of the batched warpgroup schedule verifier (sm_100a).
+//
+// The reference verifier (src/tilefoundry/schedule/warpgroup/verify.py:203-322) checks
+// one schedule at a time and spends ~95% of its time rebuilding the unrolled event graph
+// and running a DFS per required relation (verify.py:144-160). The GPU path splits the
+// work by what it depends on:
+//
+//   analyze_frames_kernel   one warp per frame (lanes + sync set, no times): structural
+//                           verdicts (lane count/coverage/ownership, register locality),
+//                           lane successors, and the reachability of every required
+//                           relation, computed once per frame instead of once per
+//                           candidate and relation.
+//   verify_periodic_kernel  one thread per compact periodic candidate: every
+//                           time-dependent check, reading the frame table.
+//   verify_rows_kernel      one warp per candidate with explicit timing rows.
+//
+// Two facts make the per-candidate work small and exact:
+//   (1) Reachability in the event graph depends only on lanes, sync edges and which
+//       operations have issue_duration == completion_latency (verify.py:134-140), and,
+//       because every event edge goes from iteration i to i or i + 1, a query
+//       completion(i, a) -> start(i + d, b) has the same answer for every i.
+//   (2) Once lane order (class 12) and sync inequalities (class 15) hold, every event
+//       edge is non-decreasing in time, so an existing path implies the relation's
+//       timing inequality at every instance. The first failing relation is therefore
+//       the first relation whose path is absent; its class is 17 if its timing fails at
+//       instance 0 (checked first, verify.py:311) and 18 otherwise.
+#include <climits>
+#include <cstdint>
+
+#include "tfv_device.cuh"
+
+namespace tfv {
+
+namespace {
+
+constexpr unsigned kFull = 0xFFFFFFFFu;
+
+__host__ __device__ inline size_t align16(size_t x) { return (x + 15) & ~static_cast<size_t>(15); }
+
+__device__ __forceinline__ int lane_of(uint16_t v) { return v >> TFV_LANE_SHIFT; }
+__device__ __forceinline__ int pos_of(uint16_t v) { return v & TFV_POS_MASK; }
+
+__device__ __forceinline__ int floor_div(int u, int d) {  // d > 0
+    return u >= 0 ? u / d : -((-u + d - 1) / d);
+}
+
+}  // namespace
+
+// ---------------------------------------------------------------------------------------
+// Frame analysis
+// ---------------------------------------------------------------------------------------
+
+size_t analyze_smem_bytes(int n, int lanes) {
+    size_t b = 0;
+    b += align16(sizeof(uint16_t) * n);          // lane_pos
+    b += align16(sizeof(int16_t) * n);           // slot: op at (lane, position)
+    b += align16(sizeof(int16_t) * n);           // succ
+    b += align16(sizeof(int) * n) * 2;           // adjacency [lo, hi) into the sync set
+    b += align16(sizeof(uint16_t) * n * lanes) * 2;  // M0, M1
+    b += sizeof(int) * 32;                       // per-lane counts and starts
+    return b;
+}
+
+// M0[y][l]: smallest position on lane l whose start, in the same iteration, is reachable
+//           from start(y) (suffixes of a lane are closed under reachability, because
+//           start -> issue_end -> next start follows the lane, verify.py:132-137).
+// M1[y][l]: the same for lane l in the next iteration.
+__global__ void __launch_bounds__(32) analyze_frames_kernel(DevProblem p, DevFrames fr, FrameTable ft) {
+    extern __shared__ __align__(16) unsigned char smem[];
+    const int N = p.n_ops;
+    const int L = p.warp_groups;
+    const int I = p.iterations;
+    const int lane = threadIdx.x;
+
+    unsigned char* cur = smem;
+    uint16_t* lp = reinterpret_cast<uint16_t*>(cur);
+    cur += align16(sizeof(uint16_t) * N);
+    int16_t* slot = reinterpret_cast<int16_t*>(cur);
+    cur += align16(sizeof(int16_t) * N);
+    int16_t* succ = reinterpret_cast<int16_t*>(cur);
+    cur += align16(sizeof(int16_t) * N);
+    int* adj_lo = reinterpret_cast<int*>(cur);
+    cur += align16(sizeof(int) * N);
+    int* adj_hi = reinterpret_cast<int*>(cur);
+    cur += align16(sizeof(int) * N);
+    uint16_t* M0 = reinterpret_cast<uint16_t*>(cur);
+    cur += align16(sizeof(uint16_t) * N * L);
+    uint16_t* M1 = reinterpret_cast<uint16_t*>(cur);
+    cur += align16(sizeof(uint16_t) * N * L);
+    int* cnt = reinterpret_cast<int*>(cur);
+    int* first = cnt + 16;
+
+    const int* E = fr.sync_edges;
+    const int total_edges = fr.sync_offsets[fr.n_sync_sets];
+
+    for (int f = blockIdx.x; f < fr.n_frames; f += gridDim.x) {
+        if (lane < 16) cnt[lane] = 0;
+        __syncwarp();
+        for (int a = lane; a < N; a += 32) {
+            const uint16_t v = fr.lane_pos[static_cast<size_t>(f) * N + a];
+            lp[a] = v;
+            if (lane_of(v) != TFV_LANE_ABSENT) atomicAdd(&cnt[lane_of(v)], 1);
+        }
+        __syncwarp();
+        if (lane == 0) {
+            int s = 0;
+            for (int l = 0; l < 16; ++l) {
+                first[l] = s;
+                s += cnt[l];
+            }
+        }
+        __syncwarp();
+        const int lane_count = fr.lane_count[f];
+        const int flags = fr.flags[f];
+
+        // Lane programs: positions must be a permutation of 0..count-1 on every lane.
+        bool bad = false, absent = false;
+        for (int a = lane; a < N; a += 32) {
+            const uint16_t v = lp[a];
+            const int l = lane_of(v), q = pos_of(v);
+            if (l == TFV_LANE_ABSENT) {
+                absent = true;
+            } else if (l >= lane_count || q >= cnt[l]) {
+                bad = true;
+            } else {
+                slot[first[l] + q] = static_cast<int16_t>(a);
+            }
+        }
+        __syncwarp();
+        bool owner_bad = false;
+        for (int a = lane; a < N; a += 32) {
+            const uint16_t v = lp[a];
+            const int l = lane_of(v), q = pos_of(v);
+            if (l == TFV_LANE_ABSENT || l >= lane_count || q >= cnt[l]) continue;
+            if (slot[first[l] + q] != a) bad = true;
+            const int w = p.warp_group[a];
+            if (w >= 0 && w != l) owner_bad = true;  // verify.py:227-236
+        }
+        // Sync set of the frame: indices inside the problem, distances non-negative.
+        const int set = fr.sync_set[f];
+        int e0 = 0, e1 = 0;
+        if (set < 0 || set >= fr.n_sync_sets) {
+            bad = true;
+        } else {
+            e0 = fr.sync_offsets[set];
+            e1 = fr.sync_offsets[set + 1];
+            if (e0 < 0 || e1 < e0 || e1 > total_edges) {
+                bad = true;
+                e0 = e1 = 0;
+            }
+        }
+        bool unusable_for_paths = false;  // the set fails with class 13/14 before 17/18
+        for (int k = e0 + lane; k < e1; k += 32) {
+            const int a = E[3 * k], b = E[3 * k + 1], d = E[3 * k + 2];
+            if (a < -1 || b < -1 || a >= N || b >= N || d < 0) bad = true;
+            if (a < 0 || b < 0 || d >= I) unusable_for_paths = true;
+        }
+        bad = __any_sync(kFull, bad);
+        absent = __any_sync(kFull, absent);
+        owner_bad = __any_sync(kFull, owner_bad);
+        unusable_for_paths = __any_sync(kFull, unusable_for_paths);
+
+        int cls = 0;
+        if (bad) cls = TFV_CLASS_BAD_PACKING;
+        else if (flags & TFV_FRAME_MALFORMED) cls = TFV_CLASS_SCHEDULE_MALFORMED;
+        else if (lane_count != L) cls = TFV_CLASS_LANE_COUNT;
+        else if ((flags & TFV_FRAME_UNKNOWN_LANE_OP) || absent) cls = TFV_CLASS_LANE_COVERAGE;
+        else if (owner_bad) cls = TFV_CLASS_OWNERSHIP;
+
+        // Lane successors (verify.py:99-112).
+        for (int a = lane; a < N; a += 32) {
+            int s = -1;
+            if (!bad) {
+                const uint16_t v = lp[a];
+                const int l = lane_of(v), q = pos_of(v);
+                if (l != TFV_LANE_ABSENT) {
+                    s = (q + 1 < cnt[l]) ? slot[first[l] + q + 1] : (kWrap | slot[first[l]]);
+                }
+            }
+            succ[a] = static_cast<int16_t>(s);
+            ft.succ[static_cast<size_t>(f) * N + a] = static_cast<int16_t>(s);
+        }
+        __syncwarp();
+
+        // Register locality (verify.py:296-304).
+        int out_flags = 0;
+        if (cls == 0) {
+            bool cross = false;
+            for (int g = lane; g < p.n_register_groups; g += 32) {
+                const int o0 = p.reg_offsets[g], o1 = p.reg_offsets[g + 1];
+                const int l0 = lane_of(lp[p.reg_ops[o0]]);
+                for (int k = o0 + 1; k < o1; ++k) cross |= lane_of(lp[p.reg_ops[k]]) != l0;
+            }
+            if (__any_sync(kFull, cross)) out_flags |= kFrameRegisterCross;
+        }
+
+        // Reachability of every required relation (verify.py:122-160, 306-314).
+        int first_unreached = -1;
+        if (cls == 0 && !unusable_for_paths) {
+            for (int a = lane; a < N; a += 32) {
+                adj_lo[a] = e0;
+                adj_hi[a] = e0;
+            }
+            __syncwarp();
+            // Edges are sorted by (after, before, distance): each op's out-edges are one run.
+            for (int k = e0 + lane; k < e1; k += 32) {
+                const int a = E[3 * k];
+                if (k == e0 || E[3 * (k - 1)] != a) adj_lo[a] = k;
+                if (k == e1 - 1 || E[3 * (k + 1)] != a) adj_hi[a] = k + 1;
+            }
+            for (int idx = lane; idx < N * L; idx += 32) {
+                const int a = idx / L, l = idx - a * L;
+                M0[idx] = (lane_of(lp[a]) == l) ? static_cast<uint16_t>(pos_of(lp[a])) : kInfPos;
+            }
+            __syncwarp();
+            // Closure within one iteration: lane successor and distance-0 sync targets.
+            for (int round = 0; round <= N + 1; ++round) {
+                bool changed = false;
+                for (int a = lane; a < N; a += 32) {
+                    const int s = succ[a];
+                    const bool same = !(s & kWrap);
+                    const int lo = adj_lo[a], hi = adj_hi[a];
+                    for (int l = 0; l < L; ++l) {
+                        uint16_t m = M0[a * L + l];
+                        if (same) m = min(m, M0[s * L + l]);
+                        for (int k = lo; k < hi; ++k)
+                            if (E[3 * k + 2] == 0) m = min(m, M0[E[3 * k + 1] * L + l]);
+                        if (m < M0[a * L + l]) {
+                            M0[a * L + l] = m;
+                            changed = true;
+                        }
+                    }
+                }
+                __syncwarp();
+                if (!__any_sync(kFull, changed)) break;
+            }
+            // Next-iteration reach: entered through a wrap edge or a distance-1 sync edge.
+            for (int a = lane; a < N; a += 32) {
+                const int s = succ[a];
+                const int lo = adj_lo[a], hi = adj_hi[a];
+                for (int l = 0; l < L; ++l) {
+                    uint16_t m = kInfPos;
+                    if (s & kWrap) m = min(m, M0[(s & kSuccMask) * L + l]);
+                    for (int k = lo; k < hi; ++k)
+                        if (E[3 * k + 2] == 1) m = min(m, M0[E[3 * k + 1] * L + l]);
+                    M1[a * L + l] = m;
+                }
+            }
+            __syncwarp();
+            for (int round = 0; round <= N + 1; ++round) {
+                bool changed = false;
+                for (int a = lane; a < N; a += 32) {
+                    const int s = succ[a];
+                    const bool same = !(s & kWrap);
+                    const int lo = adj_lo[a], hi = adj_hi[a];
+                    for (int l = 0; l < L; ++l) {
+                        uint16_t m = M1[a * L + l];
+                        if (same) m = min(m, M1[s * L + l]);
+                        for (int k = lo; k < hi; ++k)
+                            if (E[3 * k + 2] == 0) m = min(m, M1[E[3 * k + 1] * L + l]);
+                        if (m < M1[a * L + l]) {
+                            M1[a * L + l] = m;
+                            changed = true;
+                        }
+                    }
+                }
+                __syncwarp();
+                if (!__any_sync(kFull, changed)) break;
+            }
+            // Queries from completion(a): its sync targets always; its lane successor only
+            // through the completion -> issue_end edge of issue_duration == latency ops.
+            for (int r0 = 0; r0 < p.n_relations; r0 += 32) {
+                const int r = r0 + lane;
+                bool unreached = false;
+                if (r < p.n_relations) {
+                    const int packed = p.relation[r];
+                    const int a = packed & 0xFFF, b = (packed >> 12) & 0xFFF, d = packed >> 24;
+                    if (d < I) {
+                        const int lb = lane_of(lp[b]), qb = pos_of(lp[b]);
+                        int best = kInfPos;
+                        for (int k = adj_lo[a]; k < adj_hi[a]; ++k) {
+                            const int t = E[3 * k + 1], dd = E[3 * k + 2];
+                            if (dd == 0) best = min(best, static_cast<int>(d == 0 ? M0[t * L + lb] : M1[t * L + lb]));
+                            else if (dd == 1 && d == 1) best = min(best, static_cast<int>(M0[t * L + lb]));
+                        }
+                        if (p.issue[a] == p.latency[a]) {
+                            const int s = succ[a];
+                            if (!(s & kWrap)) best = min(best, static_cast<int>(d == 0 ? M0[s * L + lb] : M1[s * L + lb]));
+                            else if (d == 1) best = min(best, static_cast<int>(M0[(s & kSuccMask) * L + lb]));
+                        }
+                        unreached = qb < best;
+                    }
+                }
+                const unsigned m = __ballot_sync(kFull, unreached);
+                if (m) {
+                    first_unreached = r0 + __ffs(m) - 1;
+                    break;
+                }
+            }
+        }
+        if (lane == 0) {
+            ft.frame_class[f] = cls;
+            ft.frame_flags[f] = out_flags;
+            ft.first_unreached[f] = first_unreached;
+        }
+        __syncwarp();
+    }
+}
+
+cudaError_t launch_analyze_frames(const DevProblem& p, const DevFrames& f, FrameTable t, int sm_count,
+                                  cudaStream_t stream) {
+    if (f.n_frames <= 0) return cudaSuccess;
+    const size_t smem = analyze_smem_bytes(p.n_ops, p.warp_groups);
+    if (smem > 48 * 1024) {
+        cudaError_t e = cudaFuncSetAttribute(analyze_frames_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                             static_cast<int>(smem));
+        if (e != cudaSuccess) return e;
+    }
+    const int grid = min(f.n_frames, sm_count * 32);
+    analyze_frames_kernel<<<grid, 32, smem, stream>>>(p, f, t);
+    return cudaGetLastError();
+}
+
+// ---------------------------------------------------------------------------------------
+// Periodic candidates: one thread per candidate
+// ---------------------------------------------------------------------------------------
+
+int periodic_tile(int n) {
+    for (int t = 256; t >= 32; t >>= 1)
+        if (static_cast<size_t>(8) * n * t + 16 * static_cast<size_t>(n) <= 96 * 1024) return t;
+    if (static_cast<size_t>(8) * n * 32 + 16 * static_cast<size_t>(n) <= 200 * 1024) return 32;
+    return 0;
+}
+
+size_t periodic_smem_bytes(const DevProblem& p, int tile) {
+    return static_cast<size_t>(4) * p.n_ops * sizeof(int) + static_cast<size_t>(2) * p.n_ops * tile * sizeof(int);
+}
+
+namespace {
+
+// Demand of resource window w at time t, counting every iteration's copy
+// (verify.py:183-200 nets +amount at start and -amount at start + duration).
+__device__ __forceinline__ int window_cover(int t, int p0, int o, int dur, int ii, int I) {
+    int count = (p0 <= t && t < p0 + dur) ? 1 : 0;
+    if (I == 2) {
+        const int s = o + ii;
+        count += (s <= t && t < s + dur) ? 1 : 0;
+    } else if (I >= 3) {
+        const int u = t - o;
+        const int hi = min(floor_div(u, ii), I - 1);
+        const int lo = max(floor_div(u - dur, ii) + 1, 1);
+        count += max(0, hi - lo + 1);
+    }
+    return count;
+}
+
+__device__ int periodic_resources(const DevProblem& p, const int* P, const int* O, int T, int ii, int I) {
+    for (int q = 0; q < p.n_resources; ++q) {
+        const int w0 = p.res_offsets[q], w1 = p.res_offsets[q + 1];
+        const int cap = p.capacity[q];
+        for (int v = w0; v < w1; ++v) {
+            const int x = p.res_win_op[v];
+            for (int j = 0; j < I; ++j) {
+                const int t = (j == 0) ? P[x * T] : O[x * T] + j * ii;
+                int demand = 0;
+                for (int w = w0; w < w1; ++w) {
+                    const int y = p.res_win_op[w];
+                    demand += p.res_win_amount[w] * window_cover(t, P[y * T], O[y * T], p.res_win_duration[w], ii, I);
+                }
+                if (demand > cap) return TFV_CLASS_RESOURCE_CAPACITY;
+            }
+        }
+    }
+    return 0;
+}
+
+// Checks 10..20 of one periodic candidate whose times are in range and whose frame is
+// structurally valid. P/O point at the candidate's column (stride T) in shared memory.
+__device__ int periodic_checks(const DevProblem& p, const DevFrames& fr, const FrameTable& ft, int f,
+                               const int* P, const int* O, int T, const int* issue, const int* lat, int ii) {
+    const int N = p.n_ops;
+    const int I = p.iterations;
+    if (I >= 3 && ii <= 0) return TFV_CLASS_II_NONPOSITIVE;  // verify.py:262-264
+
+    // Lane order (verify.py:278-282): iteration 0 uses prologue starts, iterations >= 1
+    // the periodic offsets, so each lane edge reduces to at most two inequalities.
+    const int16_t* succ = ft.succ + static_cast<size_t>(f) * N;
+    bool lane_bad = false;
+    for (int a = 0; a < N; ++a) {
+        const int s = succ[a];
+        const int pa = P[a * T] + issue[a];
+        const int oa = O[a * T] + issue[a];
+        if (!(s & kWrap)) {
+            lane_bad |= pa > P[s * T];
+            lane_bad |= (I >= 2) & (oa > O[s * T]);
+        } else {
+            const int next = O[(s & kSuccMask) * T] + ii;
+            lane_bad |= (I >= 2) & (pa > next);
+            lane_bad |= (I >= 3) & (oa > next);
+        }
+    }
+    if (lane_bad) return TFV_CLASS_LANE_ORDER;
+
+    // Sync edges in sorted order (verify.py:284-292).
+    const int set = fr.sync_set[f];
+    const int e0 = fr.sync_offsets[set], e1 = fr.sync_offsets[set + 1];
+    for (int k = e0; k < e1; ++k) {
+        const int a = fr.sync_edges[3 * k], b = fr.sync_edges[3 * k + 1], d = fr.sync_edges[3 * k + 2];
+        if (a < 0 || b < 0) return TFV_CLASS_SYNC_UNKNOWN_OP;
+        if (d >= I) return TFV_CLASS_SYNC_NO_INSTANCE;
+        const int ready0 = P[a * T] + lat[a];
+        const int shift = d * ii;
+        const int target0 = (d == 0) ? P[b * T] : O[b * T] + shift;
+        if (ready0 > target0) return TFV_CLASS_SYNC_INEQUALITY;
+        if (I - d >= 2 && O[a * T] + lat[a] > O[b * T] + shift) return TFV_CLASS_SYNC_INEQUALITY;
+    }
+
+    if (ft.frame_flags[f] & kFrameRegisterCross) return TFV_CLASS_REGISTER_CROSSES_LANES;
+
+    const int r = ft.first_unreached[f];
+    if (r >= 0) {
+        const int packed = p.relation[r];
+        const int a = packed & 0xFFF, b = (packed >> 12) & 0xFFF, d = packed >> 24;
+        const int target = (d == 0) ? P[b * T] : O[b * T] + ii;
+        return (P[a * T] + lat[a] > target) ? TFV_CLASS_RELATION_TIMING : TFV_CLASS_RELATION_NO_PATH;
+    }
+
+    if (I >= 2) {  // verify.py:315-318, iterations 1..I-1 share the periodic offsets
+        for (int k = 0; k < p.n_carried; ++k) {
+            const int packed = p.carried[k];
+            const int u = packed & 0xFFFF, df = packed >> 16;
+            if (O[u * T] + lat[u] > O[df * T]) return TFV_CLASS_CARRIED_SHARED_LIFETIME;
+        }
+    }
+    if (p.n_resources > 0) return periodic_resources(p, P, O, T, ii, I);
+    return TFV_CLASS_PASS;
+}
+
+}  // namespace
+
+__global__ void verify_periodic_kernel(DevProblem p, DevFrames fr, FrameTable ft, DevPeriodic b, DevResults out) {
+    extern __shared__ __align__(16) int psm[];
+    const int N = p.n_ops;
+    const int I = p.iterations;
+    const int T = blockDim.x;
+    const int t = threadIdx.x;
+    int* issue_s = psm;
+    int* lat_s = psm + N;
+    int* bp_s = psm + 2 * N;
+    int* bo_s = psm + 3 * N;
+    int* Ps = psm + 4 * N;
+    int* Os = Ps + static_cast<size_t>(N) * T;
+    for (int a = t; a < N; a += T) {
+        issue_s[a] = p.issue[a];
+        lat_s[a] = p.latency[a];
+        bp_s[a] = b.base_prologue[a];
+        bo_s[a] = b.base_offset[a];
+    }
+    __syncthreads();
+
+    for (long long c0 = static_cast<long long>(blockIdx.x) * T; c0 < b.n; c0 += static_cast<long long>(gridDim.x) * T) {
+        const long long c = c0 + t;
+        if (c >= b.n) continue;
+        int* P = Ps + t;
+        int* O = Os + t;
+        const int f = b.frame[c];
+        const int ii = b.ii[c];
+        int min_p = INT_MAX, max_pl = INT_MIN, min_o = INT_MAX, max_ol = INT_MIN;
+        for (int a = 0; a < N; ++a) {
+            const int pv = bp_s[a] + b.prologue_delta[a * b.stride + c];
+            const int ov = bo_s[a] + b.offset_delta[a * b.stride + c];
+            P[a * T] = pv;
+            O[a * T] = ov;
+            min_p = min(min_p, pv);
+            max_pl = max(max_pl, pv + lat_s[a]);
+            min_o = min(min_o, ov);
+            max_ol = max(max_ol, ov + lat_s[a]);
+        }
+        // Starts of iterations >= 1 are offset + i * ii: extremes at i = 1 and i = I - 1.
+        long long makespan = max_pl;
+        bool negative = min_p < 0;
+        bool out_of_range = false;
+        if (I >= 2) {
+            const long long k1 = ii, kl = static_cast<long long>(I - 1) * ii;
+            const long long lo = k1 < kl ? k1 : kl, hi = k1 < kl ? kl : k1;
+            negative |= static_cast<long long>(min_o) + lo < 0;
+            const long long body = static_cast<long long>(max_ol) + hi;
+            makespan = makespan > body ? makespan : body;
+            out_of_range |= hi >= TFV_TIME_LIMIT || lo <= -static_cast<long long>(TFV_TIME_LIMIT);
+        }
+        out_of_range |= makespan >= TFV_TIME_LIMIT;
+
+        int cls;
+        const bool frame_ok = static_cast<unsigned>(f) < static_cast<unsigned>(fr.n_frames);
+        const int fclass = frame_ok ? ft.frame_class[f] : TFV_CLASS_BAD_PACKING;
+        if (fclass == TFV_CLASS_BAD_PACKING) cls = TFV_CLASS_BAD_PACKING;
+        else if (fclass == TFV_CLASS_SCHEDULE_MALFORMED || negative) cls = TFV_CLASS_SCHEDULE_MALFORMED;
+        else if (out_of_range) cls = TFV_CLASS_OUT_OF_RANGE;
+        else if (fclass != 0) cls = fclass;
+        else cls = periodic_checks(p, fr, ft, f, P, O, T, issue_s, lat_s, ii);
+
+        out.verdict[c] = cls;
+        out.makespan[c] = makespan > INT_MAX ? INT_MAX : (makespan < INT_MIN ? INT_MIN : static_cast<int>(makespan));
+        out.ii[c] = I >= 3 ? ii : 0;
+    }
+}
+
+cudaError_t launch_verify_periodic(const DevProblem& p, const DevFrames& f, FrameTable t, const DevPeriodic& b,
+                                   DevResults r, int sm_count, cudaStream_t stream) {
+    if (b.n <= 0) return cudaSuccess;
+    const int tile = periodic_tile(p.n_ops);
+    if (tile == 0) return cudaErrorInvalidValue;
+    const size_t smem = periodic_smem_bytes(p, tile);
+    if (smem > 48 * 1024) {
+        cudaError_t e = cudaFuncSetAttribute(verify_periodic_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                             static_cast<int>(smem));
+        if (e != cudaSuccess) return e;
+    }
+    int per_sm = 0;
+    cudaError_t e = cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, verify_periodic_kernel, tile, smem);
+    if (e != cudaSuccess) return e;
+    if (per_sm < 1) per_sm = 1;
+    const long long tiles = (b.n + tile - 1) / tile;
+    const long long grid = tiles < static_cast<long long>(sm_count) * per_sm ? tiles : static_cast<long long>(sm_count) * per_sm;
+    verify_periodic_kernel<<<static_cast<int>(grid), tile, smem, stream>>>(p, f, t, b, r);
+    return cudaGetLastError();
+}
+
+// ---------------------------------------------------------------------------------------
+// Explicit timing rows: one warp per candidate
+// ---------------------------------------------------------------------------------------
+
+namespace {
+
+__device__ __forceinline__ int warp_min(int v) { return __reduce_min_sync(kFull, v); }
+__device__ __forceinline__ int warp_max(int v) { return __reduce_max_sync(kFull, v); }
+
+}  // namespace
+
+__global__ void verify_rows_kernel(DevProblem p, DevFrames fr, FrameTable ft, DevRows b, DevResults out) {
+    const int N = p.n_ops;
+    const int I = p.iterations;
+    const int M = N * I;
+    const int lane = threadIdx.x & 31;
+    const long long warp = (static_cast<long long>(blockIdx.x) * blockDim.x + threadIdx.x) >> 5;
+    const long long warps = (static_cast<long long>(gridDim.x) * blockDim.x) >> 5;
+
+    for (long long c = warp; c < b.n; c += warps) {
+        const int* S = b.start + c * M;
+        const int* IE = b.issue_end + c * M;
+        const int* CP = b.completion + c * M;
+        const int f = b.frame[c];
+        const bool frame_ok = static_cast<unsigned>(f) < static_cast<unsigned>(fr.n_frames);
+        const int fclass = frame_ok ? ft.frame_class[f] : TFV_CLASS_BAD_PACKING;
+        const int rflags = b.row_flags ? b.row_flags[c] : 0;
+
+        // Constructor rules and the int32 domain; makespan over every row.
+        bool malformed = false, out_of_range = false;
+        int makespan = INT_MIN;
+        int first_dur = INT_MAX;  // 2 * row + (completion latency wrong ? 1 : 0)
+        for (int r = lane; r < M; r += 32) {
+            const int s = S[r], e = IE[r], cp = CP[r];
+            const int a = r % N;
+            malformed |= (s < 0) | (e <= s) | (cp < e);
+            out_of_range |= (s >= TFV_TIME_LIMIT) | (e >= TFV_TIME_LIMIT) | (cp >= TFV_TIME_LIMIT);
+            makespan = max(makespan, cp);
+            const unsigned du = static_cast<unsigned>(e) - static_cast<unsigned>(s);
+            const unsigned cu = static_cast<unsigned>(cp) - static_cast<unsigned>(s);
+            if (du != static_cast<unsigned>(p.issue[a])) first_dur = min(first_dur, 2 * r);
+            else if (cu != static_cast<unsigned>(p.latency[a])) first_dur = min(first_dur, 2 * r + 1);
+        }
+        malformed = __any_sync(kFull, malformed) || (rflags & TFV_ROWS_MALFORMED);
+        out_of_range = __any_sync(kFull, out_of_range);
+        makespan = warp_max(makespan);
+        first_dur = warp_min(first_dur);
+        const int ii = (I >= 3) ? S[2 * N] - S[N] : 0;  // operation 0 is the smallest id
+
+        int cls = 0;
+        if (fclass == TFV_CLASS_BAD_PACKING) cls = TFV_CLASS_BAD_PACKING;
+        else if (fclass == TFV_CLASS_SCHEDULE_MALFORMED || malformed) cls = TFV_CLASS_SCHEDULE_MALFORMED;
+        else if (out_of_range) cls = TFV_CLASS_OUT_OF_RANGE;
+        else if (fclass != 0) cls = fclass;
+        else if (rflags & TFV_ROWS_COVERAGE) cls = TFV_CLASS_TIME_COVERAGE;
+        else if (first_dur != INT_MAX) cls = (first_dur & 1) ? TFV_CLASS_COMPLETION_LATENCY : TFV_CLASS_ISSUE_DURATION;
+        else if (I >= 3 && ii <= 0) cls = TFV_CLASS_II_NONPOSITIVE;
+
+        if (cls == 0 && I >= 3) {  // verify.py:265-276
+            bool bad = false;
+            for (int r = N + lane; r < (I - 1) * N; r += 32) bad |= S[r + N] - S[r] != ii;
+            if (__any_sync(kFull, bad)) cls = TFV_CLASS_II_MISMATCH;
+        }
+        if (cls == 0) {  // verify.py:278-282
+            const int16_t* succ = ft.succ + static_cast<size_t>(f) * N;
+            bool bad = false;
+            for (int r = lane; r < M; r += 32) {
+                const int i = r / N, a = r - i * N;
+                const int s = succ[a];
+                if (!(s & kWrap)) bad |= IE[r] > S[i * N + s];
+                else if (i + 1 < I) bad |= IE[r] > S[(i + 1) * N + (s & kSuccMask)];
+            }
+            if (__any_sync(kFull, bad)) cls = TFV_CLASS_LANE_ORDER;
+        }
+        if (cls == 0) {  // verify.py:284-292, edges in sorted order
+            const int set = fr.sync_set[f];
+            const int e0 = fr.sync_offsets[set], e1 = fr.sync_offsets[set + 1];
+            for (int k = e0; k < e1 && cls == 0; ++k) {
+                const int a = fr.sync_edges[3 * k], bb = fr.sync_edges[3 * k + 1], d = fr.sync_edges[3 * k + 2];
+                if (a < 0 || bb < 0) {
+                    cls = TFV_CLASS_SYNC_UNKNOWN_OP;
+                } else if (d >= I) {
+                    cls = TFV_CLASS_SYNC_NO_INSTANCE;
+                } else {
+                    bool bad = false;
+                    for (int i = lane; i < I - d; i += 32) bad |= CP[i * N + a] > S[(i + d) * N + bb];
+                    if (__any_sync(kFull, bad)) cls = TFV_CLASS_SYNC_INEQUALITY;
+                }
+            }
+        }
+        if (cls == 0 && (ft.frame_flags[f] & kFrameRegisterCross)) cls = TFV_CLASS_REGISTER_CROSSES_LANES;
+        if (cls == 0 && ft.first_unreached[f] >= 0) {
+            const int packed = p.relation[ft.first_unreached[f]];
+            const int a = packed & 0xFFF, bb = (packed >> 12) & 0xFFF, d = packed >> 24;
+            cls = CP[a] > S[d * N + bb] ? TFV_CLASS_RELATION_TIMING : TFV_CLASS_RELATION_NO_PATH;
+        }
+        if (cls == 0 && p.n_carried > 0 && I >= 2) {  // verify.py:315-318
+            bool bad = false;
+            for (int idx = lane; idx < p.n_carried * (I - 1); idx += 32) {
+                const int k = idx / (I - 1), i = 1 + idx - k * (I - 1);
+                const int packed = p.carried[k];
+                const int u = packed & 0xFFFF, df = packed >> 16;
+                bad |= CP[i * N + u] > S[i * N + df];
+            }
+            if (__any_sync(kFull, bad)) cls = TFV_CLASS_CARRIED_SHARED_LIFETIME;
+        }
+        if (cls == 0 && p.n_resources > 0) {  // verify.py:183-200: demand at every window start
+            bool bad = false;
+            for (int q = 0; q < p.n_resources && !bad; ++q) {
+                const int w0 = p.res_offsets[q], w1 = p.res_offsets[q + 1];
+                const int cap = p.capacity[q];
+                const int points = (w1 - w0) * I;
+                for (int pt = lane; pt < points; pt += 32) {
+                    const int v = w0 + pt / I, j = pt % I;
+                    const int t = S[j * N + p.res_win_op[v]];
+                    int demand = 0;
+                    for (int w = w0; w < w1; ++w) {
+                        const int y = p.res_win_op[w], dur = p.res_win_duration[w];
+                        for (int i = 0; i < I; ++i) {
+                            const int s = S[i * N + y];
+                            demand += (s <= t && t < s + dur) ? p.res_win_amount[w] : 0;
+                        }
+                    }
+                    bad |= demand > cap;
+                }
+                bad = __any_sync(kFull, bad);
+            }
+            if (bad) cls = TFV_CLASS_RESOURCE_CAPACITY;
+        }
+        if (lane == 0) {
+            out.verdict[c] = cls;
+            out.makespan[c] = makespan;
+            out.ii[c] = ii;
+        }
+    }
+}
+
+cudaError_t launch_verify_rows(const DevProblem& p, const DevFrames& f, FrameTable t, const DevRows& b, DevResults r,
+                               int sm_count, cudaStream_t stream) {
+    if (b.n <= 0) return cudaSuccess;
+    const int block = 256;
+    const long long warps_needed = b.n;
+    const long long blocks = (warps_needed * 32 + block - 1) / block;
+    const long long cap = static_cast<long long>(sm_count) * 8;
+    const int grid = static_cast<int>(blocks < cap ? blocks : cap);
+    verify_rows_kernel<<<grid, block, 0, stream>>>(p, f, t, b, r);
+    return cudaGetLastError();
+}
+
+}  // namespace tfv

@@ -1,0 +1,445 @@
+#!/usr/bin/env python
+"""Benchmark: candidate schedules verified per second on 1..8 B200 GPUs.
+
+Workload (default ``mla``): seeded neighbourhood perturbations of the MLA decode
+example's verified witness schedule (51 operations, 16 iterations, 3 warpgroups, 48
+sync edges, 120 required relations), in the compact periodic form (int16 deltas of
+the prologue and body-offset starts plus an II and a frame index per candidate). A
+step verifies every candidate of one rank's batch: frame analysis plus one
+verification launch, and for N > 1 the gather of all verdicts to rank 0.
+
+Reported:
+  value     whole-job candidates/s with inputs resident in HBM (CUDA events, max over ranks)
+  e2e       candidates/s through the C ABI host-buffer entry (tfv_verify_periodic_host):
+            pinned host inputs copied in and host results copied out every step
+  roofline  the verification kernel's algorithmic bytes per launch / its mean CUDA-event
+            duration inside the timed region, against the measured HBM copy bandwidth
+  cpu_baseline  the oracle (a step-by-step restatement of the reference verifier) on
+            all host cores, on a bounded sample of the same batch
+
+``--impl reference`` times that oracle alone (rank 0; other ranks exit at once).
+"""
+
+from __future__ import annotations
+
+import argparse
+import json
+import os
+import statistics
+import sys
+import threading
+import time
+from pathlib import Path
+
+ROOT = Path(__file__).resolve().parent
+sys.path[:0] = [str(ROOT), str(ROOT / "tests")]
+
+METRIC = "candidate schedules verified/sec (bit-exact verdict+makespan) at 1/2/4/8 B200"
+UNIT = "candidates/s"
+FALLBACK_HBM_GBS = 6650.0
+
+
+def parse_args():
+    p = argparse.ArgumentParser(description=__doc__, formatter_class=argparse.RawDescriptionHelpFormatter)
+    p.add_argument("--gpus", type=int, default=1)
+    p.add_argument("--steps", type=int, default=20)
+    p.add_argument("--warmup", type=int, default=5)
+    p.add_argument("--impl", choices=["ours", "reference"], default="ours")
+    p.add_argument("--candidates", type=int, default=1 << 23, help="candidates per GPU")
+    p.add_argument("--seed", type=int, default=2026)
+    p.add_argument("--e2e-steps", type=int, default=None)
+    p.add_argument("--no-cpu-baseline", action="store_true")
+    p.add_argument("--cpu-sample", type=int, default=None, help="oracle sample size per step")
+    return p.parse_args()
+
+
+# --------------------------------------------------------------------------- workload
+
+
+def mla_workload(n: int, seed: int):
+    from golden_data import problem_text, raw_cases
+    from tilefoundry_b200 import pack_problem, problem_from_json
+    from tilefoundry_b200.workloads import mla_perturbations, shared_producers, witness_from_rows
+
+    problem = problem_from_json(problem_text("mla"))
+    packed = pack_problem(problem)
+    witness = witness_from_rows(packed, *raw_cases("mla")[0][0])
+    frames, batch, _kind = mla_perturbations(packed, witness, n, seed=seed, producers=shared_producers(problem))
+    return problem, packed, frames, batch
+
+
+def algorithmic_bytes_per_candidate(n_ops: int) -> int:
+    """Inputs: int16 prologue and offset deltas per op, int32 II and frame; outputs: 3 x int32."""
+    return 2 * 2 * n_ops + 4 + 4 + 12
+
+
+# --------------------------------------------------------------------------- oracle timing
+
+
+def _oracle_worker(args):
+    name, chunk = args
+    from golden_data import problem_text
+    from oracle import verify_port as port
+    from oracle.problem_doc import load_problem
+
+    problem = load_problem(problem_text(name))
+    return [port.classify(problem, *case)[0] for case in chunk]
+
+
+def oracle_sample(frames, batch, packed, start: int, count: int):
+    """Raw (lanes, sync, rows) candidates [start, start + count) of a periodic batch."""
+    import numpy as np
+
+    cases = []
+    n = batch.n
+    for j in range(count):
+        c = (start + j) % n
+        lanes, sync = frames.frames[int(batch.frame[c])]
+        p = batch.base_prologue.astype(np.int64) + batch.prologue_delta[:, c].astype(np.int64)
+        o = batch.base_offset.astype(np.int64) + batch.offset_delta[:, c].astype(np.int64)
+        ii = int(batch.ii[c])
+        rows = []
+        for i in range(packed.iterations):
+            for k, op in enumerate(packed.op_ids):
+                s = int(p[k]) if i == 0 else int(o[k]) + i * ii
+                rows.append((i, op, s, s + int(packed.issue[k]), s + int(packed.latency[k])))
+        cases.append(([list(l) for l in lanes], [tuple(e) for e in sync], rows))
+    return cases
+
+
+def time_oracle(pool, workers: int, frames, batch, packed, start: int, count: int) -> float:
+    cases = oracle_sample(frames, batch, packed, start, count)
+    chunks = [cases[k::workers] for k in range(workers)]
+    t0 = time.perf_counter()
+    list(pool.map(_oracle_worker, [("mla", chunk) for chunk in chunks if chunk]))
+    return time.perf_counter() - t0
+
+
+def make_pool():
+    import multiprocessing as mp
+    from concurrent.futures import ProcessPoolExecutor
+
+    workers = os.cpu_count() or 1
+    return ProcessPoolExecutor(max_workers=workers, mp_context=mp.get_context("spawn")), workers
+
+
+def run_reference(args) -> None:
+    rank = int(os.environ.get("RANK", "0"))
+    if rank != 0:
+        return
+    pool, workers = make_pool()
+    n = max(4096, args.steps * 64)
+    _problem, packed, frames, batch = mla_workload(n, args.seed)
+    sample = args.cpu_sample or max(16, 4 * workers)
+    with pool:
+        for w in range(args.warmup):
+            time_oracle(pool, workers, frames, batch, packed, w, min(workers, 8))
+        total, elapsed = 0, 0.0
+        for s in range(args.steps):
+            elapsed += time_oracle(pool, workers, frames, batch, packed, 1000 + s * sample, sample)
+            total += sample
+    value = total / elapsed
+    line = {
+        "impl": "reference",
+        "metric": METRIC,
+        "value": value,
+        "unit": UNIT,
+        "n_gpus": args.gpus,
+        "steps": args.steps,
+        "warmup": args.warmup,
+        "ms_per_step": 1000.0 * elapsed / args.steps,
+        "higher_is_better": True,
+        "scaling": "weak",
+        "vs_baseline": None,
+        "dtype": "int64",
+        "data": "synthetic: seeded MLA perturbations (same generator and seed as the GPU arm)",
+        "config": {"workload": "mla-decode-perturbations", "ops": 51, "iterations": 16, "warpgroups": 3},
+        "cpu_baseline": {
+            "value": value,
+            "unit": UNIT,
+            "cores": workers,
+            "kind": "port",
+            "sample": f"{sample} candidates per step, {args.steps} steps, oracle/verify_port.py in {workers} processes",
+        },
+        "e2e": {"value": value, "unit": UNIT, "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
+    }
+    print(json.dumps(line), flush=True)
+
+
+# --------------------------------------------------------------------------- clocks
+
+
+class ClockSampler:
+    """Polls NVML (read-only) for SM clock and clock-event reasons while running."""
+
+    REASONS = {
+        "gpu_idle": 0x1,
+        "applications_clocks_setting": 0x2,
+        "sw_power_cap": 0x4,
+        "hw_slowdown": 0x8,
+        "sync_boost": 0x10,
+        "sw_thermal_slowdown": 0x20,
+        "hw_thermal_slowdown": 0x40,
+        "hw_power_brake_slowdown": 0x80,
+        "display_clock_setting": 0x100,
+    }
+
+    def __init__(self, torch_device: int) -> None:
+        self.samples: list[tuple[int, int]] = []
+        self.max_mhz = None
+        self._stop = threading.Event()
+        self._thread = None
+        try:
+            import pynvml
+            import torch
+
+            pynvml.nvmlInit()
+            bus = torch.cuda.get_device_properties(torch_device).pci_bus_id.lower()
+            handle = None
+            for k in range(pynvml.nvmlDeviceGetCount()):
+                h = pynvml.nvmlDeviceGetHandleByIndex(k)
+                pci = pynvml.nvmlDeviceGetPciInfo(h).busId
+                pci = pci.decode() if isinstance(pci, bytes) else pci
+                if pci.lower().endswith(bus[-12:]) or bus.endswith(pci.lower()[-12:]):
+                    handle = h
+            self._nvml = pynvml
+            self._handle = handle
+            if handle is not None:
+                self.max_mhz = pynvml.nvmlDeviceGetMaxClockInfo(handle, pynvml.NVML_CLOCK_SM)
+        except Exception:
+            self._handle = None
+
+    def _run(self) -> None:
+        nv = self._nvml
+        while not self._stop.is_set():
+            try:
+                mhz = nv.nvmlDeviceGetClockInfo(self._handle, nv.NVML_CLOCK_SM)
+                reasons = nv.nvmlDeviceGetCurrentClocksEventReasons(self._handle)
+                self.samples.append((mhz, reasons))
+            except Exception:
+                pass
+            time.sleep(0.002)
+
+    def __enter__(self):
+        if self._handle is not None:
+            self._thread = threading.Thread(target=self._run, daemon=True)
+            self._thread.start()
+        return self
+
+    def __exit__(self, *exc):
+        self._stop.set()
+        if self._thread is not None:
+            self._thread.join()
+
+    def summary(self) -> dict:
+        if not self.samples:
+            return {"sm_mhz": None, "sm_max_mhz": self.max_mhz, "reasons": [], "samples": 0}
+        reasons = set()
+        for _, bits in self.samples:
+            for name, bit in self.REASONS.items():
+                if bits & bit and name != "gpu_idle":
+                    reasons.add(name)
+        return {
+            "sm_mhz": statistics.median(m for m, _ in self.samples),
+            "sm_max_mhz": self.max_mhz,
+            "reasons": sorted(reasons),
+            "samples": len(self.samples),
+        }
+
+
+# --------------------------------------------------------------------------- GPU arm
+
+
+def run_ours(args) -> None:
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    want_cpu = world == 1 and rank == 0 and not args.no_cpu_baseline
+    pool, workers = make_pool() if want_cpu else (None, 0)  # spawned before any CUDA call
+
+    import numpy as np
+    import torch
+
+    torch.cuda.set_device(local)
+    dev = torch.device("cuda", local)
+    dist = None
+    if world > 1:
+        import datetime
+
+        import torch.distributed as dist
+
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=300), device_id=dev)
+
+    from tilefoundry_b200 import WarpgroupVerifier
+    from tilefoundry_b200.verify import pinned_like
+    from tilefoundry_b200.shard import gather_results
+
+    n = args.candidates
+    _problem, packed, frames, batch = mla_workload(n, args.seed + rank)
+    verifier = WarpgroupVerifier(packed, device=local)
+    dframes = verifier.frames_to_device(frames)
+    tensors = {
+        key: torch.from_numpy(np.ascontiguousarray(getattr(batch, key))).to(dev)
+        for key in ("base_prologue", "base_offset", "prologue_delta", "offset_delta", "ii", "frame")
+    }
+    out = tuple(torch.empty(n, dtype=torch.int32, device=dev) for _ in range(3))
+    table = verifier.analyze(dframes)
+    stream = torch.cuda.current_stream(dev)
+
+    def barrier():
+        if dist is not None:
+            dist.barrier()
+
+    def step(events=None):
+        if events is not None:
+            events[0].record(stream)
+        verifier.analyze(dframes, table=table)
+        if events is not None:
+            events[1].record(stream)
+        verifier.verify_periodic_device(dframes, table, tensors, out=out)
+        if events is not None:
+            events[2].record(stream)
+        if dist is not None:
+            gather_results(out, n * world, dst=0)
+
+    for _ in range(args.warmup):
+        step()
+    torch.cuda.synchronize(dev)
+    barrier()
+    events = [[torch.cuda.Event(enable_timing=True) for _ in range(3)] for _ in range(args.steps)]
+    begin = torch.cuda.Event(enable_timing=True)
+    end = torch.cuda.Event(enable_timing=True)
+    with ClockSampler(local) as clocks:
+        torch.cuda.synchronize(dev)
+        barrier()
+        begin.record(stream)
+        for s in range(args.steps):
+            step(events[s])
+        end.record(stream)
+        torch.cuda.synchronize(dev)
+        barrier()
+    elapsed_ms = begin.elapsed_time(end)
+    analyze_ms = [e[0].elapsed_time(e[1]) for e in events]
+    verify_ms = [e[1].elapsed_time(e[2]) for e in events]
+    if dist is not None:
+        t = torch.tensor([elapsed_ms], device=dev)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        elapsed_ms = float(t.item())
+    value = n * world * args.steps / (elapsed_ms / 1e3)
+
+    # End to end through the C ABI host-buffer entry: pinned inputs in, host results out.
+    from tilefoundry_b200.batch import PeriodicBatch
+
+    hb = PeriodicBatch(*(pinned_like(getattr(batch, key)) for key in (
+        "base_prologue", "base_offset", "prologue_delta", "offset_delta", "ii", "frame")))
+    host_out = tuple(pinned_like(np.empty(n, dtype=np.int32)) for _ in range(3))
+    arrays = frames.arrays()
+    from tilefoundry_b200 import _lib
+
+    fstruct = _lib.Frames(len(frames), arrays["lane_pos"].ctypes.data, arrays["lane_count"].ctypes.data,
+                          arrays["flags"].ctypes.data, arrays["sync_set"].ctypes.data,
+                          len(arrays["sync_offsets"]) - 1, arrays["sync_offsets"].ctypes.data,
+                          arrays["sync_edges"].ctypes.data)
+    e2e_steps = args.e2e_steps or max(3, min(args.steps, 10))
+    for _ in range(min(args.warmup, 2)):
+        verifier.verify_periodic_host_arrays(fstruct, hb, host_out)
+    barrier()
+    t0 = time.perf_counter()
+    for _ in range(e2e_steps):
+        verifier.verify_periodic_host_arrays(fstruct, hb, host_out)
+    e2e_s = time.perf_counter() - t0
+    barrier()
+    if dist is not None:
+        t = torch.tensor([e2e_s], device=dev, dtype=torch.float64)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        e2e_s = float(t.item())
+    e2e_value = n * world * e2e_steps / e2e_s
+    assert np.array_equal(host_out[0], out[0].cpu().numpy()), "host-buffer and device entries disagree"
+    h2d = sum(int(np.asarray(v).nbytes) for v in arrays.values()) + sum(
+        int(getattr(batch, k).nbytes) for k in ("base_prologue", "base_offset", "prologue_delta", "offset_delta", "ii", "frame"))
+    d2h = 3 * 4 * n
+
+    if rank == 0:
+        per_launch = algorithmic_bytes_per_candidate(packed.n_ops) * n
+        mean_verify_s = statistics.mean(verify_ms) / 1e3
+        achieved = per_launch / mean_verify_s / 1e9
+        peak, peak_src = FALLBACK_HBM_GBS, "fallback"
+        peaks = ROOT / "MEASURED_PEAKS.json"
+        if peaks.exists():
+            peak, peak_src = float(json.loads(peaks.read_text())["hbm_gbs"]), "measured"
+        cpu = None
+        if want_cpu:
+            sample = args.cpu_sample or max(16, 4 * workers)
+            with pool:
+                time_oracle(pool, workers, frames, batch, packed, 0, min(workers, 8))
+                secs = time_oracle(pool, workers, frames, batch, packed, 7, sample)
+            cpu = {
+                "value": sample / secs,
+                "unit": UNIT,
+                "cores": workers,
+                "kind": "port",
+                "sample": f"{sample} candidates of this batch through oracle/verify_port.py in {workers} processes ({secs:.1f} s)",
+            }
+        verdicts = np.bincount(out[0].cpu().numpy() + 2, minlength=24)
+        line = {
+            "metric": METRIC,
+            "value": value,
+            "unit": UNIT,
+            "n_gpus": world,
+            "steps": args.steps,
+            "warmup": args.warmup,
+            "ms_per_step": elapsed_ms / args.steps,
+            "higher_is_better": True,
+            "scaling": "weak",
+            "vs_baseline": None,
+            "dtype": "int32",
+            "data": "synthetic: seeded perturbations of the MLA example's verified witness (per-rank seed)",
+            "config": {
+                "workload": "mla-decode-perturbations",
+                "candidates_per_gpu": n,
+                "ops": packed.n_ops,
+                "iterations": packed.iterations,
+                "warpgroups": packed.warp_groups,
+                "relations": int(packed.relations.shape[0]),
+                "frames": len(frames),
+                "format": "periodic: int16 prologue/offset deltas + int32 ii + int32 frame per candidate",
+                "bytes_per_candidate": algorithmic_bytes_per_candidate(packed.n_ops),
+                "l2": f"inputs {per_launch / 1e9:.2f} GB per GPU per step, larger than the 126 MB L2",
+                "parallelism": f"dp{world} (contiguous candidate shards, gather to rank 0)",
+                "valid_fraction": float(verdicts[2] / n),
+            },
+            "roofline": {
+                "bound": "hbm",
+                "achieved": achieved,
+                "peak": peak,
+                "unit": "GB/s",
+                "frac": achieved / peak,
+                "traffic": None,
+                "peak_source": peak_src,
+                "kernel": "tfv::verify_periodic_kernel",
+                "kernel_ms": statistics.mean(verify_ms),
+                "analyze_ms": statistics.mean(analyze_ms),
+            },
+            "cpu_baseline": cpu,
+            "e2e": {"value": e2e_value, "unit": UNIT, "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h,
+                    "steps": e2e_steps, "entry": "tfv_verify_periodic_host"},
+            "gpu_launches": 2 * args.steps,
+            "clocks": clocks.summary(),
+        }
+        print(json.dumps(line), flush=True)
+    verifier.close()
+    if dist is not None:
+        dist.barrier()
+        dist.destroy_process_group()
+
+
+def main() -> None:
+    args = parse_args()
+    if args.impl == "reference":
+        run_reference(args)
+    else:
+        run_ours(args)
+
+
+if __name__ == "__main__":
+    main()

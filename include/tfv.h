@@ -37,6 +37,12 @@ extern "C" {
 
 #define TFV_ABI_VERSION 1
 
+#if defined(__GNUC__)
+#define TFV_API __attribute__((visibility("default")))
+#else
+#define TFV_API
+#endif
+
 /* ---- status codes ---------------------------------------------------------------- */
 #define TFV_OK 0
 #define TFV_ERR_INVALID_ARGUMENT (-1)
@@ -172,32 +178,32 @@ typedef struct tfv_results {
 } tfv_results;
 
 /* Library identity. */
-int tfv_abi_version(void);
-int tfv_last_error(char* buffer, size_t size);
+TFV_API int tfv_abi_version(void);
+TFV_API int tfv_last_error(char* buffer, size_t size);
 
 /* Create/destroy the device-resident problem tables on `device`
  * (the closure `build_warpgroup_problem`, build.py:169-220, hands to the verifier). */
-int tfv_problem_create(const tfv_problem_desc* desc, int device, tfv_problem** out);
-int tfv_problem_destroy(tfv_problem* problem);
+TFV_API int tfv_problem_create(const tfv_problem_desc* desc, int device, tfv_problem** out);
+TFV_API int tfv_problem_destroy(tfv_problem* problem);
 
 /* Bytes of device scratch ("frame table") that tfv_analyze_frames writes for n_frames. */
-int tfv_frame_table_bytes(const tfv_problem* problem, int32_t n_frames, size_t* bytes);
+TFV_API int tfv_frame_table_bytes(const tfv_problem* problem, int32_t n_frames, size_t* bytes);
 
 /* Structural analysis of every frame: lane coverage and ownership
  * (verify.py:209-236), lane successors (verify.py:99-112), register locality
  * (verify.py:296-304) and lane/sync reachability of every required completion relation
  * (verify.py:122-160, 306-314). Writes the frame table. */
-int tfv_analyze_frames(const tfv_problem* problem, const tfv_frames* frames,
+TFV_API int tfv_analyze_frames(const tfv_problem* problem, const tfv_frames* frames,
                        void* frame_table, size_t frame_table_bytes, void* stream);
 
 /* Verify compact periodic candidates against analysed frames
  * (verify.py:203-322 for every candidate of the batch). */
-int tfv_verify_periodic(const tfv_problem* problem, const tfv_frames* frames,
+TFV_API int tfv_verify_periodic(const tfv_problem* problem, const tfv_frames* frames,
                         const void* frame_table, const tfv_periodic_batch* batch,
                         const tfv_results* results, void* stream);
 
 /* Verify explicit timing rows against analysed frames (general schedules). */
-int tfv_verify_rows(const tfv_problem* problem, const tfv_frames* frames,
+TFV_API int tfv_verify_rows(const tfv_problem* problem, const tfv_frames* frames,
                     const void* frame_table, const tfv_rows_batch* batch,
                     const tfv_results* results, void* stream);
 
@@ -206,7 +212,7 @@ int tfv_verify_rows(const tfv_problem* problem, const tfv_frames* frames,
  * verifies every candidate with copies overlapped with compute, and writes host results.
  * Synchronous. All pointers in `frames`, `batch` (op_stride counts host elements) and
  * `results` are host pointers. */
-int tfv_verify_periodic_host(const tfv_problem* problem, const tfv_frames* frames,
+TFV_API int tfv_verify_periodic_host(const tfv_problem* problem, const tfv_frames* frames,
                              const tfv_periodic_batch* batch, const tfv_results* results);
 
 #ifdef __cplusplus

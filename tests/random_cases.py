@@ -1,0 +1,97 @@
+"""Seeded random problems and raw schedules for parity tests (checked against the C oracle)."""
+
+from __future__ import annotations
+
+import numpy as np
+
+from tilefoundry_b200 import pack_problem
+from tilefoundry_b200.workloads import list_schedule_witness, random_dag_problem
+
+
+def random_problem(seed: int):
+    rng = np.random.default_rng(seed)
+    n = int(rng.integers(3, 100))
+    lanes = int(rng.integers(1, 9))
+    iterations = int(rng.choice([1, 2, 3, 4, 6, 9]))
+    problem = random_dag_problem(
+        n,
+        layers=max(2, n // int(rng.integers(3, 10))),
+        lanes=lanes,
+        n_resources=int(rng.integers(0, 4)),
+        iterations=iterations,
+        seed=seed,
+        latency=(4, 60),
+        capacity=(2, 12),
+        demand=(1, 4),
+        carried=0.15,
+        declared=float(rng.choice([1.0, 0.7, 0.0])),
+    )
+    packed = pack_problem(problem)
+    return problem, packed, list_schedule_witness(packed, seed=seed)
+
+
+def witness_rows(packed, witness, shift_body: np.ndarray | None = None):
+    rows = []
+    for i in range(packed.iterations):
+        for k, op in enumerate(packed.op_ids):
+            s = int(witness.prologue[k]) if i == 0 else int(witness.offset[k]) + i * witness.ii
+            if shift_body is not None and i > 0:
+                s += int(shift_body[i, k])
+            rows.append([i, op, s, s + int(packed.issue[k]), s + int(packed.latency[k])])
+    return rows
+
+
+def raw_mutations(packed, witness, count: int, seed: int):
+    """Raw ``(lanes, sync, rows)`` candidates around a valid witness (every verdict class)."""
+    rng = np.random.default_rng(seed)
+    out = []
+    ops = list(packed.op_ids)
+    for _ in range(count):
+        lanes = [list(l) for l in witness.lanes]
+        sync = [tuple(e) for e in witness.sync]
+        rows = witness_rows(packed, witness)
+        roll = rng.random()
+        if roll < 0.08 and len(ops) > 1:  # swap two neighbours on a lane
+            lane = max(lanes, key=len)
+            if len(lane) >= 2:
+                x = int(rng.integers(len(lane) - 1))
+                lane[x], lane[x + 1] = lane[x + 1], lane[x]
+        elif roll < 0.16 and sync:
+            sync.pop(int(rng.integers(len(sync))))
+        elif roll < 0.20:
+            op = ops[int(rng.integers(len(ops)))]
+            for lane in lanes:
+                if op in lane:
+                    lane.remove(op)
+            lanes[int(rng.integers(len(lanes)))].append(op)
+        elif roll < 0.23:
+            lanes.append([])
+        elif roll < 0.26:
+            lanes[int(rng.integers(len(lanes)))].append("ghost")
+        elif roll < 0.29:
+            sync.append(("ghost", ops[0], 0))
+        elif roll < 0.32:
+            sync.append((ops[0], ops[-1], packed.iterations + int(rng.integers(0, 3))))
+        roll = rng.random()
+        if roll < 0.25:
+            r = rows[int(rng.integers(len(rows)))]
+            delta = int(rng.integers(-3, 4))
+            r[2] += delta
+            r[3] += delta
+            r[4] += delta
+        elif roll < 0.32:
+            r = rows[int(rng.integers(len(rows)))]
+            r[3 + int(rng.integers(2))] += int(rng.choice([-1, 1]))
+        elif roll < 0.36:
+            rows.pop(int(rng.integers(len(rows))))
+        elif roll < 0.39:
+            rows[int(rng.integers(len(rows)))][2] = -1
+        elif roll < 0.55 and packed.iterations >= 2:  # tighten the body II
+            cut = int(rng.integers(1, max(2, witness.ii // 2)))
+            for r in rows:
+                if r[0] > 0:
+                    r[2] -= r[0] * cut
+                    r[3] -= r[0] * cut
+                    r[4] -= r[0] * cut
+        out.append((lanes, sync, [tuple(r) for r in rows]))
+    return out

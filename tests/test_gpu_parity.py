@@ -1,0 +1,196 @@
+"""GPU parity: every candidate's (verdict, makespan, II) from libtfv.so equals the oracle's.
+
+Three sources of truth, in decreasing strength:
+* the reference's own verdicts committed under tests/golden/ (make_golden.py),
+* the C oracle (pinned to those verdicts by test_oracle.py) on seeded batches of
+  every shape the kernels special-case (1, 2, >= 3 iterations; up to 8 lanes; over
+  64 operations; resources; loop-carried shared values),
+* size-independent properties on full-size batches.
+"""
+
+from __future__ import annotations
+
+import numpy as np
+import pytest
+
+from golden_data import PROBLEMS, periodic_cases, problem_text, raw_cases
+from oracle.fast import OracleProblem
+from oracle.problem_doc import load_problem
+from random_cases import random_problem, raw_mutations
+from tilefoundry_b200 import (
+    WarpgroupVerificationError,
+    WarpgroupVerifier,
+    _verify_warpgroup_schedule,
+    pack_problem,
+    problem_from_json,
+    problem_to_json,
+    verify_warpgroup_schedule,
+)
+from tilefoundry_b200.batch import PeriodicBatch
+from tilefoundry_b200.workloads import (
+    absolute_starts,
+    mla_perturbations,
+    neighbourhood,
+    shared_producers,
+    witness_from_rows,
+)
+
+pytestmark = pytest.mark.gpu
+
+
+def _torch():
+    import torch
+
+    assert torch.cuda.is_available(), "GPU tests need a CUDA device"
+    return torch
+
+
+@pytest.fixture(scope="module")
+def verifiers():
+    _torch()
+    cache = {}
+    yield cache
+    for v in cache.values():
+        v.close()
+
+
+def verifier_for(cache, name):
+    if name not in cache:
+        cache[name] = WarpgroupVerifier(problem_from_json(problem_text(name)))
+    return cache[name]
+
+
+@pytest.mark.parametrize("name", PROBLEMS)
+def test_rows_kernel_matches_reference_verdicts(verifiers, name):
+    verifier = verifier_for(verifiers, name)
+    cases, verdicts = raw_cases(name)
+    verdict, makespan, ii = verifier.verify_schedules(cases)
+    expected = np.array(verdicts, dtype=np.int64)
+    assert np.array_equal(verdict, expected[:, 0])
+    assert np.array_equal(makespan, expected[:, 1])
+    assert np.array_equal(ii, expected[:, 2])
+
+
+def _periodic_from_golden(verifier, data):
+    frames = verifier.new_frames()
+    ids = [frames.add(lanes, sync) for lanes, sync in data["frames"]]
+    batch = PeriodicBatch.from_starts(data["prologue"], data["offset"], data["ii"], np.array(ids)[data["frame"]])
+    return frames, batch
+
+
+@pytest.mark.parametrize("name", PROBLEMS)
+def test_periodic_host_entry_matches_reference_verdicts(verifiers, name):
+    verifier = verifier_for(verifiers, name)
+    data = periodic_cases(name)
+    frames, batch = _periodic_from_golden(verifier, data)
+    verdict, makespan, ii = verifier.verify_periodic(frames, batch)
+    assert np.array_equal(verdict, data["verdict"])
+    assert np.array_equal(makespan, data["makespan"])
+    assert np.array_equal(ii, data["iiv"])
+
+
+@pytest.mark.parametrize("name", ["mla", "tiny", "resource_c1_w2", "shared_init_i4"])
+def test_periodic_device_entry_matches_reference_verdicts(verifiers, name):
+    torch = _torch()
+    verifier = verifier_for(verifiers, name)
+    data = periodic_cases(name)
+    frames, batch = _periodic_from_golden(verifier, data)
+    dev = torch.device("cuda", verifier.device)
+    dframes = verifier.frames_to_device(frames)
+    table = verifier.analyze(dframes)
+    tensors = {
+        key: torch.from_numpy(getattr(batch, key)).to(dev)
+        for key in ("base_prologue", "base_offset", "prologue_delta", "offset_delta", "ii", "frame")
+    }
+    verdict, makespan, ii = (t.cpu().numpy() for t in verifier.verify_periodic_device(dframes, table, tensors))
+    assert np.array_equal(verdict, data["verdict"])
+    assert np.array_equal(makespan, data["makespan"])
+    assert np.array_equal(ii, data["iiv"])
+
+
+def test_mla_perturbation_batch_matches_oracle(verifiers):
+    problem = problem_from_json(problem_text("mla"))
+    verifier = verifier_for(verifiers, "mla")
+    witness = witness_from_rows(verifier.packed, *raw_cases("mla")[0][0])
+    frames, batch, _kind = mla_perturbations(verifier.packed, witness, 1 << 16, seed=5, producers=shared_producers(problem))
+    verdict, makespan, ii = verifier.verify_periodic(frames, batch)
+    oracle = OracleProblem(load_problem(problem_text("mla")))
+    p, o = absolute_starts(batch)
+    ov, om, oi = oracle.classify_periodic(p, o, batch.ii, frames.frames, batch.frame)
+    assert np.array_equal(verdict, ov)
+    assert np.array_equal(makespan, om)
+    assert np.array_equal(ii, oi)
+
+
+@pytest.mark.parametrize("seed", range(24))
+def test_random_problems_periodic_match_oracle(seed):
+    problem, packed, witness = random_problem(seed)
+    oracle = OracleProblem(load_problem(problem_to_json(problem)))
+    with WarpgroupVerifier(packed) as verifier:
+        frames, batch = neighbourhood(packed, witness, 3000, seed=seed, jitter=8)
+        verdict, makespan, ii = verifier.verify_periodic(frames, batch)
+    p, o = absolute_starts(batch)
+    ov, om, oi = oracle.classify_periodic(p, o, batch.ii, frames.frames, batch.frame)
+    assert np.array_equal(verdict, ov)
+    assert np.array_equal(makespan, om)
+    assert np.array_equal(ii, oi)
+
+
+@pytest.mark.parametrize("seed", range(24))
+def test_random_problems_rows_match_oracle(seed):
+    problem, packed, witness = random_problem(seed)
+    oracle = OracleProblem(load_problem(problem_to_json(problem)))
+    cases = raw_mutations(packed, witness, 300, seed)
+    with WarpgroupVerifier(packed) as verifier:
+        verdict, makespan, ii = verifier.verify_schedules(cases)
+    ov, om, oi = oracle.classify_raw(cases)
+    assert np.array_equal(verdict, ov)
+    assert np.array_equal(makespan, om)
+    assert np.array_equal(ii, oi)
+
+
+def test_domain_limits_and_packing_contract(verifiers):
+    verifier = verifier_for(verifiers, "tiny")
+    data = periodic_cases("tiny")
+    frames, batch = _periodic_from_golden(verifier, data)
+    huge = PeriodicBatch(batch.base_prologue, batch.base_offset, batch.prologue_delta[:, :2].copy(),
+                         batch.offset_delta[:, :2].copy(), np.array([1 << 29, 3], dtype=np.int32),
+                         np.array([0, len(frames) + 5], dtype=np.int32))
+    verdict, _, _ = verifier.verify_periodic(frames, huge)
+    assert verdict[0] == -1  # (I - 1) * II reaches 2^30: no verdict in the int32 domain
+    assert verdict[1] == -2  # frame index outside the frame table
+    empty = PeriodicBatch(batch.base_prologue, batch.base_offset, batch.prologue_delta[:, :0].copy(),
+                          batch.offset_delta[:, :0].copy(), np.zeros(0, np.int32), np.zeros(0, np.int32))
+    assert verifier.verify_periodic(frames, empty)[0].shape == (0,)
+
+
+def test_drop_in_raises_the_reference_errors():
+    """Mirrors test_verifier_requires_fixed_ownership_and_cross_lane_completion_sync (reference tests :272-288)."""
+    problem = problem_from_json(problem_text("tiny"))
+    packed = pack_problem(problem)
+    cases, verdicts = raw_cases("tiny")
+    lanes, sync, rows = next(c for c, v in zip(cases, verdicts) if v[0] == 0)
+    from tilefoundry_b200 import SCHEDULE_FORMAT, SynchronizationEdge, TimedOperation, WarpgroupLane, WarpgroupSchedule
+
+    def record(lanes, sync, rows):
+        return WarpgroupSchedule(SCHEDULE_FORMAT, tuple(WarpgroupLane(tuple(l)) for l in lanes),
+                                 tuple(SynchronizationEdge(*e) for e in sync), tuple(TimedOperation(*r) for r in rows))
+
+    _verify_warpgroup_schedule(problem, record(lanes, sync, rows))
+    required = ("load", "compute", 0)
+    assert required in [tuple(e) for e in sync]
+    with pytest.raises(WarpgroupVerificationError, match="no lane/sync path"):
+        _verify_warpgroup_schedule(problem, record(lanes, [e for e in sync if tuple(e) != required], rows))
+    moved = [list(l) for l in lanes]
+    moved[0] = []
+    moved[1] = ["load"] + [op for op in lanes[1]]
+    with pytest.raises(WarpgroupVerificationError, match="expected warp_group"):
+        _verify_warpgroup_schedule(problem, record(moved, sync, rows))
+    assert packed.n_ops == 4
+
+
+def test_mla_example_verifies_through_public_entry():
+    """Mirrors test_mla_example_is_one_complete_three_document_workflow (reference tests :478-488)."""
+    problem = problem_from_json(problem_text("mla"))
+    lanes, sync, rows = raw_cases("mla")[0][0]
+    verify_warpgroup_schedule("program", "hardware", (lanes, sync, rows), build=lambda program, hardware: problem)

@@ -1,0 +1,191 @@
+"""Host-side logic: codecs, problem packing, frame/row packing, workloads, sharding (CPU only)."""
+
+from __future__ import annotations
+
+import os
+
+import numpy as np
+import pytest
+
+from golden_data import PROBLEMS, problem_text, raw_cases
+from oracle.fast import OracleProblem
+from oracle.problem_doc import load_problem
+from tilefoundry_b200 import (
+    SCHEDULE_FORMAT,
+    SynchronizationEdge,
+    TimedOperation,
+    WarpgroupLane,
+    WarpgroupSchedule,
+    WarpgroupSerializationError,
+    WarpgroupValidationError,
+    pack_problem,
+    problem_from_json,
+    problem_to_json,
+    schedule_from_json,
+    schedule_to_json,
+)
+from tilefoundry_b200 import _lib
+from tilefoundry_b200.batch import FrameSet, PeriodicBatch, pack_rows
+from tilefoundry_b200.shard import shard_bounds
+from tilefoundry_b200.workloads import absolute_starts, mla_perturbations, shared_producers, witness_from_rows
+
+
+def mla():
+    problem = problem_from_json(problem_text("mla"))
+    cases, _ = raw_cases("mla")
+    return problem, pack_problem(problem), cases[0]
+
+
+@pytest.mark.parametrize("name", PROBLEMS)
+def test_problem_document_round_trip(name):
+    problem = problem_from_json(problem_text(name))
+    assert problem_from_json(problem_to_json(problem)) == problem
+
+
+@pytest.mark.parametrize("name", PROBLEMS)
+def test_packed_tables_match_oracle_derivation(name):
+    packed = pack_problem(problem_from_json(problem_text(name)))
+    oracle = OracleProblem(load_problem(problem_text(name)))
+    assert packed.op_ids == tuple(oracle.op_ids)
+    assert np.array_equal(packed.issue, oracle.issue)
+    assert np.array_equal(packed.latency, oracle.latency)
+    assert np.array_equal(packed.warp_group, oracle.wg)
+    assert np.array_equal(packed.relations, oracle.rel)
+    assert np.array_equal(packed.carried, oracle.car)
+    groups = lambda off, ops: sorted(tuple(ops[off[g]:off[g + 1]]) for g in range(len(off) - 1))  # noqa: E731
+    assert groups(packed.register_offsets, packed.register_ops) == groups(oracle.reg_off, oracle.reg_ops)
+    assert np.array_equal(packed.window_offsets, oracle.win_off)
+
+
+def test_schedule_document_round_trip_and_strictness():
+    _problem, _packed, (lanes, sync, rows) = mla()
+    schedule = WarpgroupSchedule(
+        SCHEDULE_FORMAT,
+        tuple(WarpgroupLane(tuple(lane)) for lane in lanes),
+        tuple(SynchronizationEdge(*edge) for edge in sync),
+        tuple(TimedOperation(*row) for row in rows),
+    )
+    text = schedule_to_json(schedule)
+    assert schedule_from_json(text) == schedule
+    with pytest.raises(WarpgroupSerializationError):
+        schedule_from_json(text.replace('"format"', '"fmt"'))
+    with pytest.raises(WarpgroupSerializationError):
+        schedule_from_json(text.replace(SCHEDULE_FORMAT, SCHEDULE_FORMAT + ".v2"))
+
+
+def test_schedule_constructor_rules_match_reference():
+    with pytest.raises(WarpgroupValidationError):
+        TimedOperation(0, "a", -1, 1, 2)
+    with pytest.raises(WarpgroupValidationError):
+        TimedOperation(0, "a", 3, 3, 4)
+    with pytest.raises(WarpgroupValidationError):
+        SynchronizationEdge("a", "a", 0)
+    with pytest.raises(WarpgroupValidationError):
+        WarpgroupLane(("a", "a"))
+    with pytest.raises(WarpgroupValidationError):
+        WarpgroupSchedule(SCHEDULE_FORMAT, (WarpgroupLane(("a",)), WarpgroupLane(("a",))), (), ())
+
+
+def test_frame_packing_flags_and_permutation():
+    _problem, packed, (lanes, sync, _rows) = mla()
+    frames = FrameSet(packed)
+    base = frames.add(lanes, sync)
+    assert frames.add(lanes, sync) == base
+    arrays = frames.arrays()
+    pos = arrays["lane_pos"][base]
+    for lane_index, lane in enumerate(lanes):
+        got = sorted((int(p) & 0xFFF, packed.op_ids[k]) for k, p in enumerate(pos) if int(p) >> 12 == lane_index)
+        assert [op for _, op in got] == lane
+    assert arrays["flags"][base] == 0
+    ghost = frames.add([lanes[0] + ["ghost"], lanes[1], lanes[2]], sync)
+    dup = frames.add([lanes[0] + [lanes[1][0]], lanes[1], lanes[2]], sync)
+    bad_sync = frames.add(lanes, list(sync) + [(lanes[0][0], lanes[0][0], 0)])
+    missing = frames.add([lanes[0][1:], lanes[1], lanes[2]], sync)
+    arrays = frames.arrays()
+    assert arrays["flags"][ghost] == _lib.TFV_FRAME_UNKNOWN_LANE_OP
+    assert arrays["flags"][dup] & _lib.TFV_FRAME_MALFORMED
+    assert arrays["flags"][bad_sync] & _lib.TFV_FRAME_MALFORMED
+    assert (arrays["lane_pos"][missing] >> 12 == 15).sum() == 1
+    assert arrays["sync_offsets"][-1] == arrays["sync_edges"].shape[0]
+
+
+def test_rows_packing_flags_coverage_and_overrides():
+    problem, packed, (lanes, sync, rows) = mla()
+    frames = FrameSet(packed)
+    missing = rows[:-1]
+    extra = list(rows) + [(99, packed.op_ids[0], 0, 1, 1000000)]
+    negative = [(r[0], r[1], -1, r[3], r[4]) if k == 3 else r for k, r in enumerate(rows)]
+    batch = pack_rows(packed, frames, [(lanes, sync, rows), (lanes, sync, missing), (lanes, sync, extra), (lanes, sync, negative)])
+    assert list(batch.row_flags) == [0, _lib.TFV_ROWS_COVERAGE, _lib.TFV_ROWS_COVERAGE, _lib.TFV_ROWS_MALFORMED]
+    assert batch.override_makespan[2] == 1000000
+    assert batch.start.shape == (4, packed.iterations, packed.n_ops)
+    assert batch.start[1].max() == batch.start[0].max()
+
+
+def test_periodic_batch_from_starts_round_trip_and_range():
+    rng = np.random.default_rng(3)
+    prologue = rng.integers(0, 50000, size=(7, 5))
+    offset = prologue + rng.integers(0, 100, size=(7, 5))
+    batch = PeriodicBatch.from_starts(prologue, offset, np.full(7, 10), np.zeros(7))
+    p, o = absolute_starts(batch)
+    assert np.array_equal(p, prologue) and np.array_equal(o, offset)
+    with pytest.raises(ValueError):
+        PeriodicBatch.from_starts(np.array([[0], [100000]]), np.array([[0], [0]]), [1, 1], [0, 0])
+
+
+def test_mla_workload_mix_is_about_half_invalid():
+    problem, packed, case = mla()
+    witness = witness_from_rows(packed, *case)
+    assert witness.ii == 3806
+    frames, batch, kind = mla_perturbations(packed, witness, 3000, seed=11, producers=shared_producers(problem))
+    oracle = OracleProblem(load_problem(problem_text("mla")))
+    p, o = absolute_starts(batch)
+    verdict, makespan, ii = oracle.classify_periodic(p, o, batch.ii, frames.frames, batch.frame)
+    assert 0.25 < (verdict == 0).mean() < 0.65
+    assert {0, 5, 12, 15, 18} <= set(np.unique(verdict).tolist())
+    assert (ii == batch.ii).all()
+
+
+def test_shard_bounds_cover_exactly():
+    for n in (0, 1, 7, 1000):
+        for world in (1, 2, 3, 8):
+            spans = [shard_bounds(n, r, world) for r in range(world)]
+            assert spans[0][0] == 0 and spans[-1][1] == n
+            assert all(a[1] == b[0] for a, b in zip(spans, spans[1:]))
+
+
+def _gather_worker(rank: int, world: int, port: int, queue) -> None:
+    import torch
+    import torch.distributed as dist
+
+    from tilefoundry_b200.shard import gather_results, shard_bounds
+
+    os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port))
+    dist.init_process_group("gloo", rank=rank, world_size=world)
+    n = 11
+    lo, hi = shard_bounds(n, rank, world)
+    values = torch.arange(lo, hi, dtype=torch.int32)
+    full = gather_results((values, values * 2, values * 3), n)
+    if rank == 0:
+        queue.put(full.tolist())
+    dist.destroy_process_group()
+
+
+def test_gather_results_two_gloo_ranks():
+    import multiprocessing as mp
+    import socket
+
+    with socket.socket() as sock:
+        sock.bind(("127.0.0.1", 0))
+        port = sock.getsockname()[1]
+    ctx = mp.get_context("spawn")
+    queue = ctx.Queue()
+    procs = [ctx.Process(target=_gather_worker, args=(r, 2, port, queue)) for r in range(2)]
+    for proc in procs:
+        proc.start()
+    full = queue.get(timeout=120)
+    for proc in procs:
+        proc.join(timeout=60)
+        assert proc.exitcode == 0
+    assert full[0] == list(range(11))
+    assert full[2] == [3 * v for v in range(11)]

@@ -1,0 +1,170 @@
+"""ctypes binding of ``libtfv.so`` (the C ABI declared in ``include/tfv.h``).
+
+The library is loaded from this package directory. There is no fallback: if it is
+missing or fails to load, every verifier entry point raises
+:class:`~tilefoundry_b200.errors.VerifierRuntimeError`.
+"""
+
+from __future__ import annotations
+
+import ctypes
+from pathlib import Path
+
+from .errors import VerifierRuntimeError
+
+LIBRARY = Path(__file__).resolve().parent / "libtfv.so"
+
+# Status codes and constants of include/tfv.h.
+TFV_OK = 0
+TFV_FRAME_MALFORMED = 1
+TFV_FRAME_UNKNOWN_LANE_OP = 2
+TFV_ROWS_MALFORMED = 1
+TFV_ROWS_COVERAGE = 2
+TFV_LANE_SHIFT = 12
+TFV_LANE_ABSENT = 15
+TFV_MAX_LANES = 15
+TFV_MAX_OPS = 4095
+TFV_TIME_LIMIT = 1 << 30
+CLASS_OUT_OF_RANGE = -1
+CLASS_BAD_PACKING = -2
+
+_p = ctypes.c_void_p
+
+
+class ProblemDesc(ctypes.Structure):
+    _fields_ = [
+        ("n_ops", ctypes.c_int32),
+        ("iterations", ctypes.c_int32),
+        ("warp_groups", ctypes.c_int32),
+        ("issue_duration", _p),
+        ("completion_latency", _p),
+        ("warp_group", _p),
+        ("n_relations", ctypes.c_int32),
+        ("relation_after", _p),
+        ("relation_before", _p),
+        ("relation_distance", _p),
+        ("n_carried", ctypes.c_int32),
+        ("carried_user", _p),
+        ("carried_def", _p),
+        ("n_register_groups", ctypes.c_int32),
+        ("register_group_offsets", _p),
+        ("register_group_ops", _p),
+        ("n_resources", ctypes.c_int32),
+        ("resource_capacity", _p),
+        ("window_offsets", _p),
+        ("window_resource", _p),
+        ("window_amount", _p),
+        ("window_duration", _p),
+    ]
+
+
+class Frames(ctypes.Structure):
+    _fields_ = [
+        ("n_frames", ctypes.c_int32),
+        ("lane_pos", _p),
+        ("lane_count", _p),
+        ("flags", _p),
+        ("sync_set", _p),
+        ("n_sync_sets", ctypes.c_int32),
+        ("sync_offsets", _p),
+        ("sync_edges", _p),
+    ]
+
+
+class PeriodicBatch(ctypes.Structure):
+    _fields_ = [
+        ("n_candidates", ctypes.c_int64),
+        ("op_stride", ctypes.c_int64),
+        ("base_prologue", _p),
+        ("base_offset", _p),
+        ("prologue_delta", _p),
+        ("offset_delta", _p),
+        ("ii", _p),
+        ("frame", _p),
+    ]
+
+
+class RowsBatch(ctypes.Structure):
+    _fields_ = [
+        ("n_candidates", ctypes.c_int64),
+        ("start", _p),
+        ("issue_end", _p),
+        ("completion", _p),
+        ("frame", _p),
+        ("row_flags", _p),
+    ]
+
+
+class Results(ctypes.Structure):
+    _fields_ = [("verdict", _p), ("makespan", _p), ("ii", _p)]
+
+
+EXPORTS = {
+    "tfv_abi_version": (ctypes.c_int, []),
+    "tfv_last_error": (ctypes.c_int, [ctypes.c_char_p, ctypes.c_size_t]),
+    "tfv_problem_create": (ctypes.c_int, [ctypes.POINTER(ProblemDesc), ctypes.c_int, ctypes.POINTER(_p)]),
+    "tfv_problem_destroy": (ctypes.c_int, [_p]),
+    "tfv_frame_table_bytes": (ctypes.c_int, [_p, ctypes.c_int32, ctypes.POINTER(ctypes.c_size_t)]),
+    "tfv_analyze_frames": (ctypes.c_int, [_p, ctypes.POINTER(Frames), _p, ctypes.c_size_t, _p]),
+    "tfv_verify_periodic": (
+        ctypes.c_int,
+        [_p, ctypes.POINTER(Frames), _p, ctypes.POINTER(PeriodicBatch), ctypes.POINTER(Results), _p],
+    ),
+    "tfv_verify_rows": (
+        ctypes.c_int,
+        [_p, ctypes.POINTER(Frames), _p, ctypes.POINTER(RowsBatch), ctypes.POINTER(Results), _p],
+    ),
+    "tfv_verify_periodic_host": (
+        ctypes.c_int,
+        [_p, ctypes.POINTER(Frames), ctypes.POINTER(PeriodicBatch), ctypes.POINTER(Results)],
+    ),
+}
+
+_lib: ctypes.CDLL | None = None
+
+
+def load() -> ctypes.CDLL:
+    """Load ``libtfv.so`` once and declare every exported signature."""
+    global _lib
+    if _lib is not None:
+        return _lib
+    if not LIBRARY.exists():
+        raise VerifierRuntimeError(
+            f"native verifier library missing: {LIBRARY} (build it with `python -m tilefoundry_b200._build`)"
+        )
+    try:
+        lib = ctypes.CDLL(str(LIBRARY))
+    except OSError as error:
+        raise VerifierRuntimeError(f"cannot load {LIBRARY}: {error}") from error
+    for name, (restype, argtypes) in EXPORTS.items():
+        fn = getattr(lib, name)
+        fn.restype = restype
+        fn.argtypes = argtypes
+    if lib.tfv_abi_version() != 1:
+        raise VerifierRuntimeError("libtfv.so ABI version mismatch")
+    _lib = lib
+    return lib
+
+
+def last_error() -> str:
+    buf = ctypes.create_string_buffer(1024)
+    load().tfv_last_error(buf, len(buf))
+    return buf.value.decode("utf-8", "replace")
+
+
+def check(status: int, what: str) -> None:
+    if status != TFV_OK:
+        raise VerifierRuntimeError(f"{what} failed with status {status}: {last_error()}")
+
+
+__all__ = [
+    "EXPORTS",
+    "Frames",
+    "PeriodicBatch",
+    "ProblemDesc",
+    "Results",
+    "RowsBatch",
+    "check",
+    "last_error",
+    "load",
+]

@@ -1,0 +1,389 @@
+"""GPU verification entry points, behind the reference's verifier interface.
+
+Drop-in functions (same names, arguments and error behaviour as
+``src/tilefoundry/schedule/warpgroup/verify.py``):
+
+* :func:`_verify_warpgroup_schedule` ``(problem, schedule)`` — verify.py:203. Raises
+  :class:`WarpgroupVerificationError` (a ``ValueError``) when the schedule fails; the
+  message carries the reference's wording for the failed check.
+* :func:`verify_warpgroup_schedule` ``(program, hardware, schedule)`` — verify.py:325.
+  Closes the program against the hardware with TileFoundry's own
+  ``build_warpgroup_problem`` (or the ``build`` callable given) and verifies.
+
+Batch additions (no reference counterpart):
+
+* :func:`verify_warpgroup_schedules` ``(problem, schedules)`` -> ``(verdict, makespan, ii)``.
+* :class:`WarpgroupVerifier` — a problem resident on one GPU, with host-buffer and
+  device-tensor entry points for compact periodic and explicit-row candidate batches.
+
+Every result comes from ``libtfv.so``; there is no CPU fallback. Verdict ids follow
+the reference's check order (``TFV_CLASS_*`` in include/tfv.h; 0 = verifies).
+"""
+
+from __future__ import annotations
+
+import ctypes
+from collections import OrderedDict
+from dataclasses import dataclass
+from typing import Any
+
+import numpy as np
+
+from . import _lib
+from .batch import FrameSet, PeriodicBatch, RowsBatch, pack_rows
+from .errors import (
+    VerifierRangeError,
+    VerifierRuntimeError,
+    WarpgroupValidationError,
+    WarpgroupVerificationError,
+)
+from .problem import PackedProblem, pack_problem, problem_desc
+
+CLASS_NAMES = {
+    -2: "BAD_PACKING",
+    -1: "OUT_OF_RANGE",
+    0: "PASS",
+    1: "SCHEDULE_MALFORMED",
+    2: "LANE_COUNT",
+    3: "LANE_REPEAT",
+    4: "LANE_COVERAGE",
+    5: "OWNERSHIP",
+    6: "DUP_TIMES",
+    7: "TIME_COVERAGE",
+    8: "ISSUE_DURATION",
+    9: "COMPLETION_LATENCY",
+    10: "II_NONPOSITIVE",
+    11: "II_MISMATCH",
+    12: "LANE_ORDER",
+    13: "SYNC_UNKNOWN_OP",
+    14: "SYNC_NO_INSTANCE",
+    15: "SYNC_INEQUALITY",
+    16: "REGISTER_CROSSES_LANES",
+    17: "RELATION_TIMING",
+    18: "RELATION_NO_PATH",
+    19: "CARRIED_SHARED_LIFETIME",
+    20: "RESOURCE_CAPACITY",
+    21: "CYCLE",
+}
+
+# The reference's wording for each failed check (verify.py:211-322).
+MESSAGES = {
+    2: "schedule lane count does not match warp_groups",
+    3: "schedule repeats an operation across lanes",
+    4: "schedule lane coverage differs from the problem operations",
+    5: "an operation is scheduled on a lane other than its expected warp_group",
+    6: "schedule contains duplicate timed instances",
+    7: "schedule time coverage differs from the problem instances",
+    8: "a timed operation has the wrong duration: issue duration",
+    9: "a timed operation has the wrong duration: completion latency",
+    10: "periodic initiation interval must be positive",
+    11: "periodic initiation interval differs between body iterations",
+    12: "a lane order edge is not respected",
+    13: "sync edge names an unknown operation",
+    14: "sync edge has no finite instance",
+    15: "a sync inequality is not respected",
+    16: "a register value crosses warpgroup lanes",
+    17: "a completion relation is not respected",
+    18: "a completion relation has no lane/sync path",
+    19: "a carried shared lifetime is not respected",
+    20: "a resource exceeds capacity",
+    21: "expanded lane, sync, and semantic graph contains a cycle",
+}
+
+
+def _torch():
+    import torch
+
+    if not torch.cuda.is_available():
+        raise VerifierRuntimeError("a CUDA device is required for the GPU verifier")
+    return torch
+
+
+@dataclass
+class DeviceFrames:
+    """Frames resident on one device (torch tensors) and their ``tfv_frames`` view."""
+
+    tensors: dict[str, Any]
+    struct: _lib.Frames
+    n_frames: int
+
+
+class WarpgroupVerifier:
+    """One closed problem resident on one GPU."""
+
+    def __init__(self, problem: object, device: int = 0) -> None:
+        self.packed: PackedProblem = problem if isinstance(problem, PackedProblem) else pack_problem(problem)
+        self.device = int(device)
+        self._lib = _lib.load()
+        desc = problem_desc(self.packed, _lib.ProblemDesc)
+        handle = ctypes.c_void_p()
+        _lib.check(self._lib.tfv_problem_create(ctypes.byref(desc), self.device, ctypes.byref(handle)), "tfv_problem_create")
+        self._handle = handle
+
+    # ------------------------------------------------------------------ lifetime
+    def close(self) -> None:
+        if getattr(self, "_handle", None) is not None and self._handle.value:
+            self._lib.tfv_problem_destroy(self._handle)
+            self._handle = None
+
+    def __del__(self) -> None:  # pragma: no cover - interpreter shutdown order varies
+        try:
+            self.close()
+        except Exception:
+            pass
+
+    def __enter__(self) -> "WarpgroupVerifier":
+        return self
+
+    def __exit__(self, *exc: object) -> None:
+        self.close()
+
+    def new_frames(self) -> FrameSet:
+        return FrameSet(self.packed)
+
+    # ------------------------------------------------------------------ device tensors
+    def frames_to_device(self, frames: FrameSet) -> DeviceFrames:
+        torch = _torch()
+        dev = torch.device("cuda", self.device)
+        arrays = frames.arrays()
+        tensors = {key: torch.from_numpy(np.ascontiguousarray(value)).to(dev) for key, value in arrays.items()}
+        lane_pos = tensors["lane_pos"]
+        struct = _lib.Frames(
+            len(frames),
+            lane_pos.data_ptr() if lane_pos.numel() else None,
+            tensors["lane_count"].data_ptr() if len(frames) else None,
+            tensors["flags"].data_ptr() if len(frames) else None,
+            tensors["sync_set"].data_ptr() if len(frames) else None,
+            len(arrays["sync_offsets"]) - 1,
+            tensors["sync_offsets"].data_ptr(),
+            tensors["sync_edges"].data_ptr(),
+        )
+        return DeviceFrames(tensors, struct, len(frames))
+
+    def frame_table_bytes(self, n_frames: int) -> int:
+        size = ctypes.c_size_t()
+        _lib.check(self._lib.tfv_frame_table_bytes(self._handle, n_frames, ctypes.byref(size)), "tfv_frame_table_bytes")
+        return int(size.value)
+
+    def _stream(self, stream: Any) -> int | None:
+        torch = _torch()
+        if stream is None:
+            stream = torch.cuda.current_stream(self.device)
+        return stream.cuda_stream
+
+    def analyze(self, frames: DeviceFrames, table: Any = None, stream: Any = None):
+        """Run the frame analysis; returns the frame-table tensor (device scratch)."""
+        torch = _torch()
+        nbytes = self.frame_table_bytes(frames.n_frames)
+        if table is None:
+            table = torch.empty(nbytes, dtype=torch.uint8, device=torch.device("cuda", self.device))
+        _lib.check(
+            self._lib.tfv_analyze_frames(self._handle, ctypes.byref(frames.struct), table.data_ptr(), nbytes, self._stream(stream)),
+            "tfv_analyze_frames",
+        )
+        return table
+
+    def _results(self, n: int, out: Any):
+        torch = _torch()
+        if out is None:
+            dev = torch.device("cuda", self.device)
+            out = tuple(torch.empty(n, dtype=torch.int32, device=dev) for _ in range(3))
+        verdict, makespan, ii = out
+        return out, _lib.Results(verdict.data_ptr(), makespan.data_ptr(), ii.data_ptr())
+
+    def verify_periodic_device(self, frames: DeviceFrames, table, batch: dict, out=None, stream: Any = None):
+        """Verify device-resident periodic candidates.
+
+        ``batch`` holds torch tensors on this device: ``base_prologue``/``base_offset``
+        [N] int32, ``prologue_delta``/``offset_delta`` [N, stride] int16 (op-major),
+        ``ii`` and ``frame`` [n] int32. Returns ``(verdict, makespan, ii)`` int32 tensors.
+        """
+        n = int(batch["ii"].shape[0])
+        struct = _lib.PeriodicBatch(
+            n,
+            int(batch["prologue_delta"].stride(0)),
+            batch["base_prologue"].data_ptr(),
+            batch["base_offset"].data_ptr(),
+            batch["prologue_delta"].data_ptr(),
+            batch["offset_delta"].data_ptr(),
+            batch["ii"].data_ptr(),
+            batch["frame"].data_ptr(),
+        )
+        out, results = self._results(n, out)
+        _lib.check(
+            self._lib.tfv_verify_periodic(
+                self._handle, ctypes.byref(frames.struct), table.data_ptr(), ctypes.byref(struct), ctypes.byref(results),
+                self._stream(stream),
+            ),
+            "tfv_verify_periodic",
+        )
+        return out
+
+    def verify_rows_device(self, frames: DeviceFrames, table, batch: dict, out=None, stream: Any = None):
+        """Verify device-resident explicit rows (``start``/``issue_end``/``completion`` [n, I, N])."""
+        n = int(batch["frame"].shape[0])
+        flags = batch.get("row_flags")
+        struct = _lib.RowsBatch(
+            n,
+            batch["start"].data_ptr(),
+            batch["issue_end"].data_ptr(),
+            batch["completion"].data_ptr(),
+            batch["frame"].data_ptr(),
+            flags.data_ptr() if flags is not None else None,
+        )
+        out, results = self._results(n, out)
+        _lib.check(
+            self._lib.tfv_verify_rows(
+                self._handle, ctypes.byref(frames.struct), table.data_ptr(), ctypes.byref(struct), ctypes.byref(results),
+                self._stream(stream),
+            ),
+            "tfv_verify_rows",
+        )
+        return out
+
+    # ------------------------------------------------------------------ host buffers
+    def verify_periodic(self, frames: FrameSet, batch: PeriodicBatch):
+        """Verify host-resident periodic candidates through the C ABI's host-buffer entry.
+
+        Frames, candidates and results stay in host memory; the library streams
+        them through the device (``tfv_verify_periodic_host``). Pinned host memory
+        (see :func:`pinned_like`) gives full PCIe bandwidth.
+        """
+        n = batch.n
+        arrays = frames.arrays()
+        fstruct = _lib.Frames(
+            len(frames),
+            arrays["lane_pos"].ctypes.data if len(frames) else None,
+            arrays["lane_count"].ctypes.data if len(frames) else None,
+            arrays["flags"].ctypes.data if len(frames) else None,
+            arrays["sync_set"].ctypes.data if len(frames) else None,
+            len(arrays["sync_offsets"]) - 1,
+            arrays["sync_offsets"].ctypes.data,
+            arrays["sync_edges"].ctypes.data,
+        )
+        verdict = np.empty(n, dtype=np.int32)
+        makespan = np.empty(n, dtype=np.int32)
+        ii = np.empty(n, dtype=np.int32)
+        return self.verify_periodic_host_arrays(fstruct, batch, (verdict, makespan, ii))
+
+    def verify_periodic_host_arrays(self, frames_struct: _lib.Frames, batch: PeriodicBatch, out):
+        """Host-buffer entry with caller-owned (e.g. pinned) result arrays."""
+        verdict, makespan, ii = out
+        stride = int(batch.prologue_delta.strides[0] // batch.prologue_delta.itemsize)
+        bstruct = _lib.PeriodicBatch(
+            batch.n, stride,
+            batch.base_prologue.ctypes.data, batch.base_offset.ctypes.data,
+            batch.prologue_delta.ctypes.data, batch.offset_delta.ctypes.data,
+            batch.ii.ctypes.data, batch.frame.ctypes.data,
+        )
+        results = _lib.Results(verdict.ctypes.data, makespan.ctypes.data, ii.ctypes.data)
+        _lib.check(
+            self._lib.tfv_verify_periodic_host(self._handle, ctypes.byref(frames_struct), ctypes.byref(bstruct), ctypes.byref(results)),
+            "tfv_verify_periodic_host",
+        )
+        return verdict, makespan, ii
+
+    def verify_schedules(self, schedules) -> tuple[np.ndarray, np.ndarray, np.ndarray]:
+        """Verify schedule records (or raw ``(lanes, sync, rows)`` triples) on the GPU."""
+        torch = _torch()
+        frames = self.new_frames()
+        rows: RowsBatch = pack_rows(self.packed, frames, list(schedules))
+        dframes = self.frames_to_device(frames)
+        dev = torch.device("cuda", self.device)
+        with torch.cuda.device(dev):
+            table = self.analyze(dframes)
+            batch = {
+                "start": torch.from_numpy(rows.start).to(dev),
+                "issue_end": torch.from_numpy(rows.issue_end).to(dev),
+                "completion": torch.from_numpy(rows.completion).to(dev),
+                "frame": torch.from_numpy(rows.frame).to(dev),
+                "row_flags": torch.from_numpy(rows.row_flags).to(dev),
+            }
+            verdict, makespan, ii = (t.cpu().numpy() for t in self.verify_rows_device(dframes, table, batch))
+        makespan = np.where(rows.override, rows.override_makespan, makespan)
+        ii = np.where(rows.override, rows.override_ii, ii)
+        return verdict, makespan, ii
+
+
+def pinned_like(array: np.ndarray) -> np.ndarray:
+    """A page-locked copy of ``array`` (numpy view of a pinned torch tensor)."""
+    import torch
+
+    tensor = torch.from_numpy(np.ascontiguousarray(array)).pin_memory()
+    view = tensor.numpy()
+    view._pinned_owner = tensor  # type: ignore[attr-defined]
+    return view
+
+
+_VERIFIERS: "OrderedDict[tuple, WarpgroupVerifier]" = OrderedDict()
+
+
+def _verifier_for(problem: object, device: int) -> WarpgroupVerifier:
+    try:
+        key = (problem, device)
+        hash(key)
+    except TypeError:
+        key = (id(problem), device)
+    found = _VERIFIERS.get(key)
+    if found is None:
+        found = WarpgroupVerifier(problem, device)
+        _VERIFIERS[key] = found
+        while len(_VERIFIERS) > 8:
+            _VERIFIERS.popitem(last=False)[1].close()
+    else:
+        _VERIFIERS.move_to_end(key)
+    return found
+
+
+def verify_warpgroup_schedules(problem: object, schedules, *, device: int = 0):
+    """Verify many schedules of one closed problem: ``(verdict, makespan, ii)`` int32 arrays."""
+    return _verifier_for(problem, device).verify_schedules(schedules)
+
+
+def raise_for_verdict(verdict: int) -> None:
+    """Raise the reference's exception for a failed verdict (no-op for 0)."""
+    if verdict == 0:
+        return
+    if verdict == 1:
+        raise WarpgroupValidationError("schedule records violate the scheduling contract")
+    if verdict == -1:
+        raise VerifierRangeError("schedule times lie outside the device domain [0, 2^30)")
+    if verdict == -2:
+        raise VerifierRuntimeError("packed schedule violates the device packing contract")
+    raise WarpgroupVerificationError(MESSAGES.get(verdict, f"verification failed (class {verdict})"))
+
+
+def _verify_warpgroup_schedule(problem: object, schedule: object, *, device: int = 0) -> None:
+    """Verify one schedule against a closed problem on the GPU (drop-in for verify.py:203)."""
+    verdict, _makespan, _ii = verify_warpgroup_schedules(problem, [schedule], device=device)
+    raise_for_verdict(int(verdict[0]))
+
+
+def verify_warpgroup_schedule(program: object, hardware: object, schedule: object, *, build=None, device: int = 0) -> None:
+    """Verify one schedule against its program and hardware (drop-in for verify.py:325-331).
+
+    ``build`` closes the program against the hardware; by default TileFoundry's own
+    ``build_warpgroup_problem`` (build.py:169-220) is used when it is installed.
+    """
+    if build is None:
+        try:
+            from tilefoundry.schedule.warpgroup.build import build_warpgroup_problem as build
+        except ImportError as error:
+            raise VerifierRuntimeError(
+                "closing a program against hardware needs TileFoundry's build_warpgroup_problem; "
+                "pass build= or verify a closed problem with _verify_warpgroup_schedule"
+            ) from error
+    _verify_warpgroup_schedule(build(program, hardware), schedule, device=device)
+
+
+__all__ = [
+    "CLASS_NAMES",
+    "DeviceFrames",
+    "MESSAGES",
+    "WarpgroupVerifier",
+    "_verify_warpgroup_schedule",
+    "pinned_like",
+    "raise_for_verdict",
+    "verify_warpgroup_schedule",
+    "verify_warpgroup_schedules",
+]

@@ -310,9 +310,7 @@ def pinned_like(array: np.ndarray) -> np.ndarray:
     import torch
 
     tensor = torch.from_numpy(np.ascontiguousarray(array)).pin_memory()
-    view = tensor.numpy()
-    view._pinned_owner = tensor  # type: ignore[attr-defined]
-    return view
+    return tensor.numpy()  # the array's base keeps the pinned tensor alive
 
 
 _VERIFIERS: "OrderedDict[tuple, WarpgroupVerifier]" = OrderedDict()

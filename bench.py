@@ -194,13 +194,13 @@ class ClockSampler:
             import torch
 
             pynvml.nvmlInit()
-            bus = torch.cuda.get_device_properties(torch_device).pci_bus_id.lower()
+            props = torch.cuda.get_device_properties(torch_device)
+            want = (int(props.pci_domain_id), int(props.pci_bus_id), int(props.pci_device_id))
             handle = None
             for k in range(pynvml.nvmlDeviceGetCount()):
                 h = pynvml.nvmlDeviceGetHandleByIndex(k)
-                pci = pynvml.nvmlDeviceGetPciInfo(h).busId
-                pci = pci.decode() if isinstance(pci, bytes) else pci
-                if pci.lower().endswith(bus[-12:]) or bus.endswith(pci.lower()[-12:]):
+                info = pynvml.nvmlDeviceGetPciInfo(h)
+                if (int(info.domain), int(info.bus), int(info.device)) == want:
                     handle = h
             self._nvml = pynvml
             self._handle = handle

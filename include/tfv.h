@@ -76,6 +76,7 @@ extern "C" {
 #define TFV_CLASS_CYCLE 21                    /* verify.py:321-322 (unreachable after 12,15,17,19) */
 #define TFV_CLASS_OUT_OF_RANGE (-1)           /* a time is outside [0, 2^30): no verdict */
 #define TFV_CLASS_BAD_PACKING (-2)            /* lane positions are not a permutation per lane */
+#define TFV_CLASS_DEVICE_TIMEOUT (-3)         /* a bounded device wait gave up: no verdict */
 
 /* ---- frame flags ------------------------------------------------------------------ */
 #define TFV_FRAME_MALFORMED 1       /* lanes/sync violate the record constructors -> class 1 */

@@ -92,6 +92,13 @@ int check_results(const tfv_results* r) {
     return TFV_OK;
 }
 
+// The TMA-fed kernel when its layout preconditions hold, else the plain-load kernel.
+cudaError_t launch_periodic(const tfv_problem* p, const tfv::DevFrames& f, tfv::FrameTable t, const tfv::DevPeriodic& b,
+                            tfv::DevResults r, cudaStream_t s) {
+    if (tfv::periodic_tma_supported(p->dev, b)) return tfv::launch_verify_periodic_tma(p->dev, f, t, b, r, p->sm_count, s);
+    return tfv::launch_verify_periodic(p->dev, f, t, b, r, p->sm_count, s);
+}
+
 bool frame_table_fits(const tfv_problem* p, int n_frames, size_t bytes) {
     return bytes >= tfv::frame_table_bytes(n_frames, p->dev.n_ops);
 }
@@ -292,7 +299,7 @@ int tfv_analyze_frames(const tfv_problem* p, const tfv_frames* frames, void* tab
         return fail(TFV_ERR_INVALID_ARGUMENT, "frame table too small");
     DeviceGuard guard(p->device);
     if (!guard.ok()) return fail(TFV_ERR_CUDA, "cannot select device %d", p->device);
-    cudaError_t e = tfv::launch_analyze_frames(p->dev, to_dev(*frames), tfv::frame_table_view(table, frames->n_frames),
+    cudaError_t e = tfv::launch_analyze_frames(p->dev, to_dev(*frames), tfv::frame_table_view(table, frames->n_frames, p->dev.n_ops),
                                                p->sm_count, static_cast<cudaStream_t>(stream));
     if (e != cudaSuccess) return cuda_fail(e, "analyze_frames launch");
     return TFV_OK;
@@ -315,9 +322,9 @@ int tfv_verify_periodic(const tfv_problem* p, const tfv_frames* frames, const vo
     tfv::DevPeriodic db{b->n_candidates, b->op_stride, b->base_prologue, b->base_offset,
                         b->prologue_delta, b->offset_delta, b->ii, b->frame};
     tfv::DevResults dr{r->verdict, r->makespan, r->ii};
-    cudaError_t e = tfv::launch_verify_periodic(p->dev, to_dev(*frames),
-                                                tfv::frame_table_view(const_cast<void*>(table), frames->n_frames), db, dr,
-                                                p->sm_count, static_cast<cudaStream_t>(stream));
+    cudaError_t e = launch_periodic(p, to_dev(*frames),
+                                    tfv::frame_table_view(const_cast<void*>(table), frames->n_frames, p->dev.n_ops), db, dr,
+                                    static_cast<cudaStream_t>(stream));
     if (e != cudaSuccess) return cuda_fail(e, "verify_periodic launch");
     return TFV_OK;
 }
@@ -338,7 +345,7 @@ int tfv_verify_rows(const tfv_problem* p, const tfv_frames* frames, const void* 
     tfv::DevRows db{b->n_candidates, b->start, b->issue_end, b->completion, b->frame, b->row_flags};
     tfv::DevResults dr{r->verdict, r->makespan, r->ii};
     cudaError_t e = tfv::launch_verify_rows(p->dev, to_dev(*frames),
-                                            tfv::frame_table_view(const_cast<void*>(table), frames->n_frames), db, dr,
+                                            tfv::frame_table_view(const_cast<void*>(table), frames->n_frames, p->dev.n_ops), db, dr,
                                             p->sm_count, static_cast<cudaStream_t>(stream));
     if (e != cudaSuccess) return cuda_fail(e, "verify_rows launch");
     return TFV_OK;
@@ -364,6 +371,7 @@ int tfv_verify_periodic_host(const tfv_problem* p, const tfv_frames* hf, const t
     if (!guard.ok()) return fail(TFV_ERR_CUDA, "cannot select device %d", p->device);
 
     const long long chunk = std::min<long long>(n, 1LL << 21);
+    const long long pitch = (chunk + 7) & ~7LL;  // device rows keep 16-byte strides for TMA
     const size_t table_bytes = tfv::frame_table_bytes(F, N);
     cudaStream_t streams[2] = {nullptr, nullptr};
     cudaEvent_t ready = nullptr;
@@ -390,7 +398,7 @@ int tfv_verify_periodic_host(const tfv_problem* p, const tfv_frames* hf, const t
     const size_t sz_lp = up(sizeof(uint16_t) * static_cast<size_t>(F) * N), sz_f = up(sizeof(int) * std::max(F, 1));
     const size_t sz_so = up(sizeof(int) * (S + 1)), sz_se = up(sizeof(int) * 3 * std::max(E, 1));
     const size_t sz_tab = up(table_bytes), sz_base = up(sizeof(int) * N);
-    const size_t sz_d = up(sizeof(int16_t) * N * chunk), sz_c = up(sizeof(int) * chunk);
+    const size_t sz_d = up(sizeof(int16_t) * N * pitch), sz_c = up(sizeof(int) * chunk);
     const size_t fixed = sz_lp + 3 * sz_f + sz_so + sz_se + sz_tab + 2 * sz_base;
     const size_t slot = 2 * sz_d + 2 * sz_c + 3 * sz_c;
     e = cudaMalloc(&ws, fixed + 2 * slot);
@@ -424,7 +432,7 @@ int tfv_verify_periodic_host(const tfv_problem* p, const tfv_frames* hf, const t
     if (e == cudaSuccess) e = cudaMemcpyAsync(d_bo, hb->base_offset, sizeof(int) * N, cudaMemcpyHostToDevice, s0);
     if (e != cudaSuccess) return bail(e, "frame upload");
     tfv::DevFrames df{F, d_lp, d_lc, d_fl, d_ss, S, d_so, d_se};
-    tfv::FrameTable tab = tfv::frame_table_view(d_tab, F);
+    tfv::FrameTable tab = tfv::frame_table_view(d_tab, F, N);
     e = tfv::launch_analyze_frames(p->dev, df, tab, p->sm_count, s0);
     if (e != cudaSuccess) return bail(e, "analyze_frames launch");
     e = cudaEventRecord(ready, s0);
@@ -457,7 +465,7 @@ int tfv_verify_periodic_host(const tfv_problem* p, const tfv_frames* hf, const t
         const long long len = std::min(chunk, n - c0);
         Slot& sl = slots[k & 1];
         cudaStream_t s = streams[k & 1];
-        const size_t dpitch = sizeof(int16_t) * chunk;
+        const size_t dpitch = sizeof(int16_t) * pitch;
         e = cudaMemcpy2DAsync(sl.dp, dpitch, hb->prologue_delta + c0, hpitch, sizeof(int16_t) * len, N,
                               cudaMemcpyHostToDevice, s);
         if (e == cudaSuccess)
@@ -466,9 +474,9 @@ int tfv_verify_periodic_host(const tfv_problem* p, const tfv_frames* hf, const t
         if (e == cudaSuccess) e = cudaMemcpyAsync(sl.ii, hb->ii + c0, sizeof(int) * len, cudaMemcpyHostToDevice, s);
         if (e == cudaSuccess) e = cudaMemcpyAsync(sl.fr, hb->frame + c0, sizeof(int) * len, cudaMemcpyHostToDevice, s);
         if (e != cudaSuccess) return bail(e, "candidate upload");
-        tfv::DevPeriodic db{len, chunk, d_bp, d_bo, sl.dp, sl.dq, sl.ii, sl.fr};
+        tfv::DevPeriodic db{len, pitch, d_bp, d_bo, sl.dp, sl.dq, sl.ii, sl.fr};
         tfv::DevResults dr{sl.v, sl.m, sl.iio};
-        e = tfv::launch_verify_periodic(p->dev, df, tab, db, dr, p->sm_count, s);
+        e = launch_periodic(p, df, tab, db, dr, s);
         if (e != cudaSuccess) return bail(e, "verify_periodic launch");
         e = cudaMemcpyAsync(hr->verdict + c0, sl.v, sizeof(int) * len, cudaMemcpyDeviceToHost, s);
         if (e == cudaSuccess) e = cudaMemcpyAsync(hr->makespan + c0, sl.m, sizeof(int) * len, cudaMemcpyDeviceToHost, s);

@@ -71,28 +71,38 @@ struct DevFrames {
 //   int32  first_unreached[F]   first relation (sorted order, with instances) whose
 //                               completion -> start path is absent, or -1
 //   int16  succ[F][N]           lane successor (see kWrap)
+//   uint16 order[F][N]          the operations lane by lane in program order; an entry
+//                               is op | kFirstOfLane | kLastOfLane (valid frames only)
+constexpr int kFirstOfLane = 0x8000;
+constexpr int kLastOfLane = 0x4000;
+
 struct FrameTable {
     int* frame_class;
     int* frame_flags;
     int* first_unreached;
     int16_t* succ;
+    uint16_t* order;
 };
 
-inline size_t frame_table_bytes(int n_frames, int n_ops) {
+inline size_t frame_table_head(int n_frames) {
     size_t head = 3 * sizeof(int) * static_cast<size_t>(n_frames);
-    head = (head + 15) & ~static_cast<size_t>(15);
-    return head + sizeof(int16_t) * static_cast<size_t>(n_frames) * n_ops + 16;
+    return (head + 15) & ~static_cast<size_t>(15);
 }
 
-inline FrameTable frame_table_view(void* base, int n_frames) {
+inline size_t frame_table_bytes(int n_frames, int n_ops) {
+    const size_t rows = (sizeof(int16_t) * static_cast<size_t>(n_frames) * n_ops + 15) & ~static_cast<size_t>(15);
+    return frame_table_head(n_frames) + 2 * rows + 16;
+}
+
+inline FrameTable frame_table_view(void* base, int n_frames, int n_ops) {
     FrameTable t;
     char* p = static_cast<char*>(base);
     t.frame_class = reinterpret_cast<int*>(p);
     t.frame_flags = t.frame_class + n_frames;
     t.first_unreached = t.frame_flags + n_frames;
-    size_t head = 3 * sizeof(int) * static_cast<size_t>(n_frames);
-    head = (head + 15) & ~static_cast<size_t>(15);
-    t.succ = reinterpret_cast<int16_t*>(p + head);
+    const size_t rows = (sizeof(int16_t) * static_cast<size_t>(n_frames) * n_ops + 15) & ~static_cast<size_t>(15);
+    t.succ = reinterpret_cast<int16_t*>(p + frame_table_head(n_frames));
+    t.order = reinterpret_cast<uint16_t*>(p + frame_table_head(n_frames) + rows);
     return t;
 }
 
@@ -128,6 +138,11 @@ cudaError_t launch_analyze_frames(const DevProblem& p, const DevFrames& f, Frame
 cudaError_t launch_verify_periodic(const DevProblem& p, const DevFrames& f, FrameTable t,
                                    const DevPeriodic& b, DevResults r, int sm_count,
                                    cudaStream_t stream);
+// TMA variant: needs 16-byte aligned delta arrays, op_stride % 8 == 0 and N <= 256.
+bool periodic_tma_supported(const DevProblem& p, const DevPeriodic& b);
+cudaError_t launch_verify_periodic_tma(const DevProblem& p, const DevFrames& f, FrameTable t,
+                                       const DevPeriodic& b, DevResults r, int sm_count,
+                                       cudaStream_t stream);
 cudaError_t launch_verify_rows(const DevProblem& p, const DevFrames& f, FrameTable t,
                                const DevRows& b, DevResults r, int sm_count,
                                cudaStream_t stream);

@@ -180,6 +180,17 @@ __global__ void __launch_bounds__(32) analyze_frames_kernel(DevProblem p, DevFra
             succ[a] = static_cast<int16_t>(s);
             ft.succ[static_cast<size_t>(f) * N + a] = static_cast<int16_t>(s);
         }
+        // Lane-major walk order: slot[] already lists the operations lane by lane.
+        const int placed = first[15];
+        for (int j = lane; j < N; j += 32) {
+            uint16_t e = 0;
+            if (!bad && j < placed) {
+                const int op = slot[j];
+                const int l = lane_of(lp[op]), q = pos_of(lp[op]);
+                e = static_cast<uint16_t>(op | (q == 0 ? kFirstOfLane : 0) | (q == cnt[l] - 1 ? kLastOfLane : 0));
+            }
+            ft.order[static_cast<size_t>(f) * N + j] = e;
+        }
         __syncwarp();
 
         // Register locality (verify.py:296-304).

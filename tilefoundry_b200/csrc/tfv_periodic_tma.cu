@@ -1,0 +1,348 @@
+// Periodic-candidate verification fed by TMA tiles (sm_100a).
+//
+// Layout: the per-candidate int16 deltas are op-major in global memory ([N][op_stride],
+// consecutive candidates contiguous). One CTA owns a tile of kTile candidates; a single
+// thread issues two 2-D TMA copies (cp.async.bulk.tensor) that land the tile as
+// [op][candidate] in shared memory — exactly the layout in which thread t reads its own
+// candidate's column, without bank conflicts. Candidates past the end of the batch are
+// zero-filled by the TMA unit. The copy completes on an mbarrier whose wait is bounded;
+// on a timeout every candidate of the tile reports TFV_CLASS_DEVICE_TIMEOUT and the CTA
+// returns after a second bounded wait for its copy.
+//
+// Per candidate (one thread), the checks are those of verify_periodic_kernel in
+// tfv_kernels.cu, restructured for issue efficiency:
+//   * one walk over the frame's lane-ordered operation list visits every operation once;
+//     it carries the previous operation's issue end in registers, so each lane edge
+//     (verify.py:99-112, 278-282) is a subtraction and a minimum, and the same pass
+//     collects the start minima (class 1, record constructors) and completion maxima
+//     (makespan) of the prologue row and of the periodic body rows;
+//   * sync edges (verify.py:284-292) are evaluated branch-free in sorted order with a
+//     sticky "first failing edge" class, so 13/14/15 keep the reference's precedence.
+#include <climits>
+#include <cstdint>
+
+#include <cuda.h>
+#include <cudaTypedefs.h>
+
+#include "tfv_device.cuh"
+
+namespace tfv {
+
+namespace {
+
+constexpr int kTile = 128;          // candidates per CTA tile = threads per CTA
+constexpr int kMaxTmaOps = 256;     // TMA box height limit
+constexpr long long kWaitSpins = 1LL << 22;
+
+__device__ __forceinline__ uint32_t smem_addr(const void* p) {
+    return static_cast<uint32_t>(__cvta_generic_to_shared(p));
+}
+
+__device__ __forceinline__ void mbar_init(uint64_t* bar, unsigned count) {
+    asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;" ::"r"(smem_addr(bar)), "r"(count) : "memory");
+}
+
+__device__ __forceinline__ void mbar_expect_tx(uint64_t* bar, unsigned bytes) {
+    asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(smem_addr(bar)), "r"(bytes) : "memory");
+}
+
+__device__ __forceinline__ bool mbar_try_wait(uint64_t* bar, unsigned phase) {
+    uint32_t done;
+    asm volatile(
+        "{\n\t.reg .pred p;\n\t"
+        "mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n\t"
+        "selp.u32 %0, 1, 0, p;\n\t}"
+        : "=r"(done)
+        : "r"(smem_addr(bar)), "r"(phase)
+        : "memory");
+    return done != 0;
+}
+
+__device__ __forceinline__ bool mbar_wait_bounded(uint64_t* bar, unsigned phase) {
+    for (long long spin = 0; spin < kWaitSpins; ++spin)
+        if (mbar_try_wait(bar, phase)) return true;
+    return false;
+}
+
+__device__ __forceinline__ void tma_load_2d(void* dst, const CUtensorMap* map, int x, int y, uint64_t* bar) {
+    asm volatile(
+        "cp.async.bulk.tensor.2d.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1, {%2, %3}], [%4];"
+        ::"r"(smem_addr(dst)), "l"(reinterpret_cast<uint64_t>(map)), "r"(x), "r"(y), "r"(smem_addr(bar))
+        : "memory");
+}
+
+__device__ __forceinline__ void fence_proxy_async() { asm volatile("fence.proxy.async.shared::cta;" ::: "memory"); }
+
+struct Walk {
+    int lane_min;    // minimum slack over every lane-order inequality
+    int min_p, min_o;
+    int max_pl, max_ol;
+};
+
+// One pass over the frame's operations in lane order (valid frames only).
+__device__ __forceinline__ Walk walk_lanes(const uint16_t* order, const int4* opc, const int16_t* tp, const int16_t* to,
+                                           int N, int I, int ii) {
+    Walk w{INT_MAX, INT_MAX, INT_MAX, INT_MIN, INT_MIN};
+    int end_p = 0, end_o = 0, first_o = 0;
+    const bool body = I >= 2, body2 = I >= 3;
+#pragma unroll 4
+    for (int j = 0; j < N; ++j) {
+        const int e = order[j];
+        const int s = e & 0x0FFF;
+        const int4 k = opc[s];  // issue, latency, base prologue, base offset
+        const int p = k.z + tp[s * kTile];
+        const int o = k.w + to[s * kTile];
+        if (e & kFirstOfLane) {
+            first_o = o;
+        } else {
+            w.lane_min = min(w.lane_min, p - end_p);
+            if (body) w.lane_min = min(w.lane_min, o - end_o);
+        }
+        end_p = p + k.x;
+        end_o = o + k.x;
+        if (e & kLastOfLane) {  // wrap edge (i, last) -> (i + 1, first)
+            const int next = first_o + ii;
+            if (body) w.lane_min = min(w.lane_min, next - end_p);
+            if (body2) w.lane_min = min(w.lane_min, next - end_o);
+        }
+        w.min_p = min(w.min_p, p);
+        w.min_o = min(w.min_o, o);
+        w.max_pl = max(w.max_pl, p + k.y);
+        w.max_ol = max(w.max_ol, o + k.y);
+    }
+    return w;
+}
+
+// Extremes only, in operation order (frames that failed structurally).
+__device__ __forceinline__ Walk scan_ops(const int4* opc, const int16_t* tp, const int16_t* to, int N) {
+    Walk w{INT_MAX, INT_MAX, INT_MAX, INT_MIN, INT_MIN};
+    for (int s = 0; s < N; ++s) {
+        const int4 k = opc[s];
+        const int p = k.z + tp[s * kTile];
+        const int o = k.w + to[s * kTile];
+        w.min_p = min(w.min_p, p);
+        w.min_o = min(w.min_o, o);
+        w.max_pl = max(w.max_pl, p + k.y);
+        w.max_ol = max(w.max_ol, o + k.y);
+    }
+    return w;
+}
+
+__device__ __forceinline__ int cover(int t, int p0, int o, int dur, int ii, int I) {
+    int count = (p0 <= t && t < p0 + dur) ? 1 : 0;
+    if (I == 2) {
+        const int s = o + ii;
+        count += (s <= t && t < s + dur) ? 1 : 0;
+    } else if (I >= 3) {
+        const int u = t - o;
+        const int hi = min(u >= 0 ? u / ii : -((-u + ii - 1) / ii), I - 1);
+        const int v = u - dur;
+        const int lo = max((v >= 0 ? v / ii : -((-v + ii - 1) / ii)) + 1, 1);
+        count += max(0, hi - lo + 1);
+    }
+    return count;
+}
+
+// Classes 13..20 for a candidate whose frame is valid and whose lane order holds.
+__device__ int tail_checks(const DevProblem& p, const DevFrames& fr, const FrameTable& ft, int f, const int4* opc,
+                           const int16_t* tp, const int16_t* to, int ii) {
+    const int I = p.iterations;
+    auto P = [&](int s) { return opc[s].z + tp[s * kTile]; };
+    auto O = [&](int s) { return opc[s].w + to[s * kTile]; };
+
+    const int set = fr.sync_set[f];
+    const int e0 = fr.sync_offsets[set], e1 = fr.sync_offsets[set + 1];
+    int first_bad = 0;  // class of the first failing edge in sorted order, sticky
+    for (int k = e0; k < e1; ++k) {
+        const int a = fr.sync_edges[3 * k], b = fr.sync_edges[3 * k + 1], d = fr.sync_edges[3 * k + 2];
+        int code;
+        if (a < 0 || b < 0) {
+            code = TFV_CLASS_SYNC_UNKNOWN_OP;
+        } else if (d >= I) {
+            code = TFV_CLASS_SYNC_NO_INSTANCE;
+        } else {
+            const int lat = opc[a].y;
+            const int shift = d * ii;
+            const int ob = O(b) + shift;
+            bool bad = P(a) + lat > (d == 0 ? P(b) : ob);
+            bad |= (I - d >= 2) && (O(a) + lat > ob);
+            code = bad ? TFV_CLASS_SYNC_INEQUALITY : 0;
+        }
+        first_bad = first_bad ? first_bad : code;
+    }
+    if (first_bad) return first_bad;
+    if (ft.frame_flags[f] & kFrameRegisterCross) return TFV_CLASS_REGISTER_CROSSES_LANES;
+    const int r = ft.first_unreached[f];
+    if (r >= 0) {
+        const int packed = p.relation[r];
+        const int a = packed & 0xFFF, b = (packed >> 12) & 0xFFF, d = packed >> 24;
+        const int target = d == 0 ? P(b) : O(b) + ii;
+        return P(a) + opc[a].y > target ? TFV_CLASS_RELATION_TIMING : TFV_CLASS_RELATION_NO_PATH;
+    }
+    if (I >= 2) {
+        for (int k = 0; k < p.n_carried; ++k) {
+            const int packed = p.carried[k];
+            const int u = packed & 0xFFFF, df = packed >> 16;
+            if (O(u) + opc[u].y > O(df)) return TFV_CLASS_CARRIED_SHARED_LIFETIME;
+        }
+    }
+    for (int q = 0; q < p.n_resources; ++q) {
+        const int w0 = p.res_offsets[q], w1 = p.res_offsets[q + 1];
+        const int cap = p.capacity[q];
+        for (int v = w0; v < w1; ++v) {
+            const int x = p.res_win_op[v];
+            for (int j = 0; j < I; ++j) {
+                const int t = j == 0 ? P(x) : O(x) + j * ii;
+                int demand = 0;
+                for (int w = w0; w < w1; ++w) {
+                    const int y = p.res_win_op[w];
+                    demand += p.res_win_amount[w] * cover(t, P(y), O(y), p.res_win_duration[w], ii, I);
+                }
+                if (demand > cap) return TFV_CLASS_RESOURCE_CAPACITY;
+            }
+        }
+    }
+    return TFV_CLASS_PASS;
+}
+
+__global__ void __launch_bounds__(kTile) verify_periodic_tma_kernel(DevProblem p, DevFrames fr, FrameTable ft,
+                                                                     DevPeriodic b, DevResults out, int n_tiles,
+                                                                     const __grid_constant__ CUtensorMap map_p,
+                                                                     const __grid_constant__ CUtensorMap map_o) {
+    extern __shared__ __align__(128) unsigned char smem[];
+    const int N = p.n_ops;
+    const int I = p.iterations;
+    const int t = threadIdx.x;
+    int16_t* tp = reinterpret_cast<int16_t*>(smem);           // [N][kTile]
+    int16_t* to = tp + N * kTile;                             // [N][kTile]
+    int4* opc = reinterpret_cast<int4*>(smem + 4 * N * kTile);  // [N]
+    uint64_t* bar = reinterpret_cast<uint64_t*>(opc + N);
+
+    for (int s = t; s < N; s += kTile)
+        opc[s] = make_int4(p.issue[s], p.latency[s], b.base_prologue[s], b.base_offset[s]);
+    if (t == 0) {
+        mbar_init(bar, 1);
+        asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+        fence_proxy_async();
+    }
+    __syncthreads();
+
+    const unsigned tile_bytes = static_cast<unsigned>(2 * N * kTile * sizeof(int16_t));
+    unsigned phase = 0;
+    for (int tile = blockIdx.x; tile < n_tiles; tile += gridDim.x) {
+        if (t == 0) {
+            fence_proxy_async();
+            mbar_expect_tx(bar, tile_bytes);
+            tma_load_2d(tp, &map_p, tile * kTile, 0, bar);
+            tma_load_2d(to, &map_o, tile * kTile, 0, bar);
+        }
+        const long long c = static_cast<long long>(tile) * kTile + t;
+        const bool live = c < b.n;
+        const int f = live ? b.frame[c] : 0;
+        const int ii = live ? b.ii[c] : 0;
+        const bool landed = __syncthreads_and(mbar_wait_bounded(bar, phase));
+        if (!landed) {  // report, drain the copy (bounded) and leave
+            if (live) {
+                out.verdict[c] = TFV_CLASS_DEVICE_TIMEOUT;
+                out.makespan[c] = 0;
+                out.ii[c] = 0;
+            }
+            mbar_wait_bounded(bar, phase);
+            return;
+        }
+        phase ^= 1;
+        if (live) {
+            const int16_t* mp = tp + t;
+            const int16_t* mo = to + t;
+            const bool frame_ok = static_cast<unsigned>(f) < static_cast<unsigned>(fr.n_frames);
+            const int fclass = frame_ok ? ft.frame_class[f] : TFV_CLASS_BAD_PACKING;
+            const Walk w = fclass == 0 ? walk_lanes(ft.order + static_cast<size_t>(f) * N, opc, mp, mo, N, I, ii)
+                                       : scan_ops(opc, mp, mo, N);
+            long long makespan = w.max_pl;
+            bool negative = w.min_p < 0;
+            bool out_of_range = false;
+            if (I >= 2) {
+                const long long k1 = ii, kl = static_cast<long long>(I - 1) * ii;
+                const long long lo = k1 < kl ? k1 : kl, hi = k1 < kl ? kl : k1;
+                negative |= static_cast<long long>(w.min_o) + lo < 0;
+                const long long body = static_cast<long long>(w.max_ol) + hi;
+                makespan = makespan > body ? makespan : body;
+                out_of_range |= hi >= TFV_TIME_LIMIT || lo <= -static_cast<long long>(TFV_TIME_LIMIT);
+            }
+            out_of_range |= makespan >= TFV_TIME_LIMIT;
+            int cls;
+            if (fclass == TFV_CLASS_BAD_PACKING) cls = TFV_CLASS_BAD_PACKING;
+            else if (fclass == TFV_CLASS_SCHEDULE_MALFORMED || negative) cls = TFV_CLASS_SCHEDULE_MALFORMED;
+            else if (out_of_range) cls = TFV_CLASS_OUT_OF_RANGE;
+            else if (fclass != 0) cls = fclass;
+            else if (I >= 3 && ii <= 0) cls = TFV_CLASS_II_NONPOSITIVE;
+            else if (w.lane_min < 0) cls = TFV_CLASS_LANE_ORDER;
+            else cls = tail_checks(p, fr, ft, f, opc, mp, mo, ii);
+            out.verdict[c] = cls;
+            out.makespan[c] = makespan > INT_MAX ? INT_MAX : (makespan < INT_MIN ? INT_MIN : static_cast<int>(makespan));
+            out.ii[c] = I >= 3 ? ii : 0;
+        }
+        __syncthreads();  // every thread is done with the tile before the next copy lands
+    }
+}
+
+PFN_cuTensorMapEncodeTiled_v12000 encode_fn() {
+    static PFN_cuTensorMapEncodeTiled_v12000 fn = nullptr;
+    if (!fn) {
+        void* ptr = nullptr;
+        cudaDriverEntryPointQueryResult q;
+        if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &ptr, cudaEnableDefault, &q) == cudaSuccess &&
+            q == cudaDriverEntryPointSuccess)
+            fn = reinterpret_cast<PFN_cuTensorMapEncodeTiled_v12000>(ptr);
+    }
+    return fn;
+}
+
+bool make_map(CUtensorMap* map, const int16_t* base, long long n, long long stride, int N) {
+    auto fn = encode_fn();
+    if (!fn) return false;
+    cuuint64_t dims[2] = {static_cast<cuuint64_t>(n), static_cast<cuuint64_t>(N)};
+    cuuint64_t strides[1] = {static_cast<cuuint64_t>(stride) * sizeof(int16_t)};
+    cuuint32_t box[2] = {static_cast<cuuint32_t>(kTile), static_cast<cuuint32_t>(N)};
+    cuuint32_t elem[2] = {1, 1};
+    CUresult r = fn(map, CU_TENSOR_MAP_DATA_TYPE_UINT16, 2, const_cast<int16_t*>(base), dims, strides, box, elem,
+                    CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_NONE, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                    CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+    return r == CUDA_SUCCESS;
+}
+
+size_t tma_smem_bytes(int n_ops) { return 4 * static_cast<size_t>(n_ops) * kTile + 16 * static_cast<size_t>(n_ops) + 16; }
+
+}  // namespace
+
+bool periodic_tma_supported(const DevProblem& p, const DevPeriodic& b) {
+    const auto aligned = [](const void* ptr) { return (reinterpret_cast<uintptr_t>(ptr) & 15) == 0; };
+    return p.n_ops <= kMaxTmaOps && b.stride % 8 == 0 && aligned(b.prologue_delta) && aligned(b.offset_delta) &&
+           b.n < (1LL << 31) && encode_fn() != nullptr;
+}
+
+cudaError_t launch_verify_periodic_tma(const DevProblem& p, const DevFrames& f, FrameTable t, const DevPeriodic& b,
+                                       DevResults r, int sm_count, cudaStream_t stream) {
+    if (b.n <= 0) return cudaSuccess;
+    CUtensorMap map_p, map_o;
+    if (!make_map(&map_p, b.prologue_delta, b.n, b.stride, p.n_ops) ||
+        !make_map(&map_o, b.offset_delta, b.n, b.stride, p.n_ops))
+        return cudaErrorInvalidValue;
+    const size_t smem = tma_smem_bytes(p.n_ops);
+    if (smem > 48 * 1024) {
+        cudaError_t e = cudaFuncSetAttribute(verify_periodic_tma_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                             static_cast<int>(smem));
+        if (e != cudaSuccess) return e;
+    }
+    int per_sm = 0;
+    cudaError_t e = cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, verify_periodic_tma_kernel, kTile, smem);
+    if (e != cudaSuccess) return e;
+    if (per_sm < 1) return cudaErrorInvalidConfiguration;
+    const long long tiles = (b.n + kTile - 1) / kTile;
+    const long long cap = static_cast<long long>(sm_count) * per_sm;
+    const int grid = static_cast<int>(tiles < cap ? tiles : cap);
+    verify_periodic_tma_kernel<<<grid, kTile, smem, stream>>>(p, f, t, b, r, static_cast<int>(tiles), map_p, map_o);
+    return cudaGetLastError();
+}
+
+}  // namespace tfv

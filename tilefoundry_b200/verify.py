@@ -40,6 +40,7 @@ from .errors import (
 from .problem import PackedProblem, pack_problem, problem_desc
 
 CLASS_NAMES = {
+    -3: "DEVICE_TIMEOUT",
     -2: "BAD_PACKING",
     -1: "OUT_OF_RANGE",
     0: "PASS",
@@ -348,6 +349,8 @@ def raise_for_verdict(verdict: int) -> None:
         raise VerifierRangeError("schedule times lie outside the device domain [0, 2^30)")
     if verdict == -2:
         raise VerifierRuntimeError("packed schedule violates the device packing contract")
+    if verdict == -3:
+        raise VerifierRuntimeError("a bounded device wait timed out; the candidate has no verdict")
     raise WarpgroupVerificationError(MESSAGES.get(verdict, f"verification failed (class {verdict})"))
 
 

@@ -194,3 +194,27 @@ def test_mla_example_verifies_through_public_entry():
     problem = problem_from_json(problem_text("mla"))
     lanes, sync, rows = raw_cases("mla")[0][0]
     verify_warpgroup_schedule("program", "hardware", (lanes, sync, rows), build=lambda program, hardware: problem)
+
+
+@pytest.mark.parametrize("n", [1000, 1001, 8, 7, 129])
+def test_tma_and_plain_load_paths_agree_with_oracle(verifiers, n):
+    """Strides that are multiples of 8 take the TMA-fed kernel, others the plain-load kernel."""
+    torch = _torch()
+    problem = problem_from_json(problem_text("mla"))
+    verifier = verifier_for(verifiers, "mla")
+    witness = witness_from_rows(verifier.packed, *raw_cases("mla")[0][0])
+    frames, batch, _ = mla_perturbations(verifier.packed, witness, n, seed=n, producers=shared_producers(problem))
+    dev = torch.device("cuda", verifier.device)
+    dframes = verifier.frames_to_device(frames)
+    table = verifier.analyze(dframes)
+    tensors = {
+        key: torch.from_numpy(getattr(batch, key)).to(dev)
+        for key in ("base_prologue", "base_offset", "prologue_delta", "offset_delta", "ii", "frame")
+    }
+    verdict, makespan, ii = (t.cpu().numpy() for t in verifier.verify_periodic_device(dframes, table, tensors))
+    oracle = OracleProblem(load_problem(problem_text("mla")))
+    p, o = absolute_starts(batch)
+    ov, om, oi = oracle.classify_periodic(p, o, batch.ii, frames.frames, batch.frame)
+    assert np.array_equal(verdict, ov)
+    assert np.array_equal(makespan, om)
+    assert np.array_equal(ii, oi)

@@ -416,7 +416,7 @@ def run_ours(args) -> None:
                 "frac": achieved / peak,
                 "traffic": None,
                 "peak_source": peak_src,
-                "kernel": "tfv::verify_periodic_kernel",
+                "kernel": "tfv::verify_periodic_tma_kernel",
                 "kernel_ms": statistics.mean(verify_ms),
                 "analyze_ms": statistics.mean(analyze_ms),
             },

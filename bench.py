@@ -336,10 +336,7 @@ def run_ours(args) -> None:
     arrays = frames.arrays()
     from tilefoundry_b200 import _lib
 
-    fstruct = _lib.Frames(len(frames), arrays["lane_pos"].ctypes.data, arrays["lane_count"].ctypes.data,
-                          arrays["flags"].ctypes.data, arrays["sync_set"].ctypes.data,
-                          len(arrays["sync_offsets"]) - 1, arrays["sync_offsets"].ctypes.data,
-                          arrays["sync_edges"].ctypes.data)
+    fstruct = _lib.frames_struct(arrays, len(frames))
     e2e_steps = args.e2e_steps or max(3, min(args.steps, 10))
     for _ in range(min(args.warmup, 2)):
         verifier.verify_periodic_host_arrays(fstruct, hb, host_out)

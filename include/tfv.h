@@ -35,7 +35,7 @@
 extern "C" {
 #endif
 
-#define TFV_ABI_VERSION 1
+#define TFV_ABI_VERSION 2
 
 #if defined(__GNUC__)
 #define TFV_API __attribute__((visibility("default")))
@@ -93,6 +93,7 @@ extern "C" {
 #define TFV_MAX_LANES 15
 #define TFV_MAX_OPS 4095
 #define TFV_TIME_LIMIT (1 << 30)
+#define TFV_BASE_LIMIT (1 << 28)
 
 typedef struct tfv_problem tfv_problem;
 
@@ -108,7 +109,7 @@ typedef struct tfv_problem_desc {
     int32_t iterations;   /* I >= 1 */
     int32_t warp_groups;  /* L, 1..TFV_MAX_LANES */
     const int32_t* issue_duration;     /* [N] > 0 */
-    const int32_t* completion_latency; /* [N] >= issue_duration */
+    const int32_t* completion_latency; /* [N] >= issue_duration, < 2^28 */
     const int32_t* warp_group;         /* [N] declared lane, or -1 when undeclared */
     int32_t n_relations;
     const int32_t* relation_after;     /* [R] op index */
@@ -139,6 +140,7 @@ typedef struct tfv_frames {
     const int32_t* flags;       /* [n_frames] TFV_FRAME_* */
     const int32_t* sync_set;    /* [n_frames] index into the sync sets */
     int32_t n_sync_sets;
+    int32_t n_sync_edges;        /* sync_offsets[n_sync_sets] */
     const int32_t* sync_offsets; /* [n_sync_sets + 1] */
     const int32_t* sync_edges;   /* [sync_offsets[n_sync_sets]][3]: after, before, distance;
                                     an op index of -1 names an operation the problem lacks */
@@ -187,8 +189,10 @@ TFV_API int tfv_last_error(char* buffer, size_t size);
 TFV_API int tfv_problem_create(const tfv_problem_desc* desc, int device, tfv_problem** out);
 TFV_API int tfv_problem_destroy(tfv_problem* problem);
 
-/* Bytes of device scratch ("frame table") that tfv_analyze_frames writes for n_frames. */
-TFV_API int tfv_frame_table_bytes(const tfv_problem* problem, int32_t n_frames, size_t* bytes);
+/* Bytes of device scratch ("frame table") the frames need: tfv_analyze_frames writes the
+ * structural part, tfv_verify_periodic the per-batch sync programs. Reads only the host
+ * fields of `frames` (n_frames, n_sync_sets, n_sync_edges). */
+TFV_API int tfv_frame_table_bytes(const tfv_problem* problem, const tfv_frames* frames, size_t* bytes);
 
 /* Structural analysis of every frame: lane coverage and ownership
  * (verify.py:209-236), lane successors (verify.py:99-112), register locality
@@ -198,9 +202,12 @@ TFV_API int tfv_analyze_frames(const tfv_problem* problem, const tfv_frames* fra
                        void* frame_table, size_t frame_table_bytes, void* stream);
 
 /* Verify compact periodic candidates against analysed frames
- * (verify.py:203-322 for every candidate of the batch). */
+ * (verify.py:203-322 for every candidate of the batch). Also writes the batch's sync
+ * programs (sync edges with the base starts folded in) into the frame table.
+ * Base starts must lie in (-2^28, 2^28); candidates of a batch whose base does not
+ * get TFV_CLASS_OUT_OF_RANGE. */
 TFV_API int tfv_verify_periodic(const tfv_problem* problem, const tfv_frames* frames,
-                        const void* frame_table, const tfv_periodic_batch* batch,
+                        void* frame_table, size_t frame_table_bytes, const tfv_periodic_batch* batch,
                         const tfv_results* results, void* stream);
 
 /* Verify explicit timing rows against analysed frames (general schedules). */

@@ -29,7 +29,7 @@ def test_library_exports_every_declared_function():
     for name in names:
         assert hasattr(lib, name), name
     assert set(names) == set(_lib.EXPORTS)
-    assert lib.tfv_abi_version() == 1
+    assert lib.tfv_abi_version() == _lib.ABI_VERSION == 2
 
 
 def test_invalid_arguments_are_rejected_before_cuda():
@@ -56,7 +56,7 @@ def test_invalid_arguments_are_rejected_before_cuda():
     desc.n_relations = 0
     assert lib.tfv_problem_create(ctypes.byref(desc), 0, ctypes.byref(handle)) == -1
     assert lib.tfv_problem_destroy(None) == 0
-    assert lib.tfv_verify_periodic(None, None, None, None, None, None) == -1
+    assert lib.tfv_verify_periodic(None, None, None, 0, None, None, None) == -1
     assert lib.tfv_verify_rows(None, None, None, None, None, None) == -1
     assert lib.tfv_analyze_frames(None, None, None, 0, None) == -1
     assert lib.tfv_verify_periodic_host(None, None, None, None) == -1

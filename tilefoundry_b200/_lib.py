@@ -25,8 +25,12 @@ TFV_LANE_ABSENT = 15
 TFV_MAX_LANES = 15
 TFV_MAX_OPS = 4095
 TFV_TIME_LIMIT = 1 << 30
+TFV_BASE_LIMIT = 1 << 28
+ABI_VERSION = 2
 CLASS_OUT_OF_RANGE = -1
 CLASS_BAD_PACKING = -2
+CLASS_DEVICE_TIMEOUT = -3
+
 
 _p = ctypes.c_void_p
 
@@ -66,6 +70,7 @@ class Frames(ctypes.Structure):
         ("flags", _p),
         ("sync_set", _p),
         ("n_sync_sets", ctypes.c_int32),
+        ("n_sync_edges", ctypes.c_int32),
         ("sync_offsets", _p),
         ("sync_edges", _p),
     ]
@@ -99,16 +104,31 @@ class Results(ctypes.Structure):
     _fields_ = [("verdict", _p), ("makespan", _p), ("ii", _p)]
 
 
+def frames_struct(arrays: dict, n_frames: int, pointer=lambda a: a.ctypes.data) -> "Frames":
+    """A ``tfv_frames`` over the arrays of :meth:`FrameSet.arrays` (host or device)."""
+    return Frames(
+        n_frames,
+        pointer(arrays["lane_pos"]) if n_frames else None,
+        pointer(arrays["lane_count"]) if n_frames else None,
+        pointer(arrays["flags"]) if n_frames else None,
+        pointer(arrays["sync_set"]) if n_frames else None,
+        len(arrays["sync_offsets"]) - 1,
+        int(arrays["sync_offsets"][-1]),
+        pointer(arrays["sync_offsets"]),
+        pointer(arrays["sync_edges"]),
+    )
+
+
 EXPORTS = {
     "tfv_abi_version": (ctypes.c_int, []),
     "tfv_last_error": (ctypes.c_int, [ctypes.c_char_p, ctypes.c_size_t]),
     "tfv_problem_create": (ctypes.c_int, [ctypes.POINTER(ProblemDesc), ctypes.c_int, ctypes.POINTER(_p)]),
     "tfv_problem_destroy": (ctypes.c_int, [_p]),
-    "tfv_frame_table_bytes": (ctypes.c_int, [_p, ctypes.c_int32, ctypes.POINTER(ctypes.c_size_t)]),
+    "tfv_frame_table_bytes": (ctypes.c_int, [_p, ctypes.POINTER(Frames), ctypes.POINTER(ctypes.c_size_t)]),
     "tfv_analyze_frames": (ctypes.c_int, [_p, ctypes.POINTER(Frames), _p, ctypes.c_size_t, _p]),
     "tfv_verify_periodic": (
         ctypes.c_int,
-        [_p, ctypes.POINTER(Frames), _p, ctypes.POINTER(PeriodicBatch), ctypes.POINTER(Results), _p],
+        [_p, ctypes.POINTER(Frames), _p, ctypes.c_size_t, ctypes.POINTER(PeriodicBatch), ctypes.POINTER(Results), _p],
     ),
     "tfv_verify_rows": (
         ctypes.c_int,
@@ -140,7 +160,7 @@ def load() -> ctypes.CDLL:
         fn = getattr(lib, name)
         fn.restype = restype
         fn.argtypes = argtypes
-    if lib.tfv_abi_version() != 1:
+    if lib.tfv_abi_version() != ABI_VERSION:
         raise VerifierRuntimeError("libtfv.so ABI version mismatch")
     _lib = lib
     return lib
@@ -158,7 +178,9 @@ def check(status: int, what: str) -> None:
 
 
 __all__ = [
+    "ABI_VERSION",
     "EXPORTS",
+    "frames_struct",
     "Frames",
     "PeriodicBatch",
     "ProblemDesc",

@@ -180,8 +180,8 @@ class PeriodicBatch:
             if delta.size and (delta.min() < -32768 or delta.max() > 32767):
                 raise ValueError(f"{name} starts span more than the int16 delta range around their base")
         for name, base in (("prologue", base_prologue), ("offset", base_offset)):
-            if base.size and np.abs(base).max() >= _lib.TFV_TIME_LIMIT:
-                raise ValueError(f"{name} base starts must lie in (-2^30, 2^30)")
+            if base.size and np.abs(base).max() >= _lib.TFV_BASE_LIMIT:
+                raise ValueError(f"{name} base starts must lie in (-2^28, 2^28)")
         return cls(
             base_prologue=base_prologue.astype(np.int32),
             base_offset=base_offset.astype(np.int32),

@@ -73,6 +73,7 @@ tfv::DevFrames to_dev(const tfv_frames& f) {
     d.flags = f.flags;
     d.sync_set = f.sync_set;
     d.n_sync_sets = f.n_sync_sets;
+    d.n_sync_edges = f.n_sync_edges;
     d.sync_offsets = f.sync_offsets;
     d.sync_edges = f.sync_edges;
     return d;
@@ -80,7 +81,8 @@ tfv::DevFrames to_dev(const tfv_frames& f) {
 
 int check_frames(const tfv_frames* f) {
     if (!f) return fail(TFV_ERR_INVALID_ARGUMENT, "frames is NULL");
-    if (f->n_frames < 0 || f->n_sync_sets < 1) return fail(TFV_ERR_INVALID_ARGUMENT, "frames need n_frames >= 0 and n_sync_sets >= 1");
+    if (f->n_frames < 0 || f->n_sync_sets < 1 || f->n_sync_edges < 0)
+        return fail(TFV_ERR_INVALID_ARGUMENT, "frames need n_frames >= 0, n_sync_sets >= 1 and n_sync_edges >= 0");
     if (f->n_frames > 0 && (!f->lane_pos || !f->lane_count || !f->flags || !f->sync_set))
         return fail(TFV_ERR_INVALID_ARGUMENT, "frame arrays must not be NULL");
     if (!f->sync_offsets || !f->sync_edges) return fail(TFV_ERR_INVALID_ARGUMENT, "sync set arrays must not be NULL");
@@ -99,8 +101,8 @@ cudaError_t launch_periodic(const tfv_problem* p, const tfv::DevFrames& f, tfv::
     return tfv::launch_verify_periodic(p->dev, f, t, b, r, p->sm_count, s);
 }
 
-bool frame_table_fits(const tfv_problem* p, int n_frames, size_t bytes) {
-    return bytes >= tfv::frame_table_bytes(n_frames, p->dev.n_ops);
+tfv::FrameTableShape shape_of(const tfv_problem* p, const tfv_frames* f) {
+    return tfv::FrameTableShape{f->n_frames, p->dev.n_ops, f->n_sync_sets, f->n_sync_edges};
 }
 
 }  // namespace
@@ -129,7 +131,7 @@ int tfv_problem_create(const tfv_problem_desc* d, int device, tfv_problem** out)
     for (int a = 0; a < N; ++a) {
         if (d->issue_duration[a] <= 0 || d->completion_latency[a] < d->issue_duration[a])
             return fail(TFV_ERR_INVALID_ARGUMENT, "operation %d: need 0 < issue_duration <= completion_latency", a);
-        if (d->completion_latency[a] >= TFV_TIME_LIMIT) return fail(TFV_ERR_RANGE, "operation %d latency >= 2^30", a);
+        if (d->completion_latency[a] >= TFV_BASE_LIMIT) return fail(TFV_ERR_RANGE, "operation %d latency >= 2^28", a);
         if (d->warp_group[a] < -1 || d->warp_group[a] >= L)
             return fail(TFV_ERR_INVALID_ARGUMENT, "operation %d warp_group out of range", a);
     }
@@ -285,9 +287,11 @@ int tfv_problem_destroy(tfv_problem* p) {
     return TFV_OK;
 }
 
-int tfv_frame_table_bytes(const tfv_problem* p, int32_t n_frames, size_t* bytes) {
-    if (!p || !bytes || n_frames < 0) return fail(TFV_ERR_INVALID_ARGUMENT, "invalid arguments");
-    *bytes = tfv::frame_table_bytes(n_frames, p->dev.n_ops);
+int tfv_frame_table_bytes(const tfv_problem* p, const tfv_frames* frames, size_t* bytes) {
+    if (!p || !bytes) return fail(TFV_ERR_INVALID_ARGUMENT, "invalid arguments");
+    int rc = check_frames(frames);
+    if (rc) return rc;
+    *bytes = tfv::frame_table_bytes(shape_of(p, frames));
     return TFV_OK;
 }
 
@@ -295,17 +299,17 @@ int tfv_analyze_frames(const tfv_problem* p, const tfv_frames* frames, void* tab
     if (!p) return fail(TFV_ERR_INVALID_ARGUMENT, "problem is NULL");
     int rc = check_frames(frames);
     if (rc) return rc;
-    if (frames->n_frames > 0 && (!table || !frame_table_fits(p, frames->n_frames, table_bytes)))
-        return fail(TFV_ERR_INVALID_ARGUMENT, "frame table too small");
+    if (!table || table_bytes < tfv::frame_table_bytes(shape_of(p, frames)))
+        return fail(TFV_ERR_INVALID_ARGUMENT, "frame table missing or too small");
     DeviceGuard guard(p->device);
     if (!guard.ok()) return fail(TFV_ERR_CUDA, "cannot select device %d", p->device);
-    cudaError_t e = tfv::launch_analyze_frames(p->dev, to_dev(*frames), tfv::frame_table_view(table, frames->n_frames, p->dev.n_ops),
+    cudaError_t e = tfv::launch_analyze_frames(p->dev, to_dev(*frames), tfv::frame_table_view(table, shape_of(p, frames)),
                                                p->sm_count, static_cast<cudaStream_t>(stream));
     if (e != cudaSuccess) return cuda_fail(e, "analyze_frames launch");
     return TFV_OK;
 }
 
-int tfv_verify_periodic(const tfv_problem* p, const tfv_frames* frames, const void* table,
+int tfv_verify_periodic(const tfv_problem* p, const tfv_frames* frames, void* table, size_t table_bytes,
                         const tfv_periodic_batch* b, const tfv_results* r, void* stream) {
     if (!p || !b) return fail(TFV_ERR_INVALID_ARGUMENT, "problem and batch must not be NULL");
     int rc = check_frames(frames);
@@ -315,16 +319,20 @@ int tfv_verify_periodic(const tfv_problem* p, const tfv_frames* frames, const vo
     if (b->n_candidates < 0 || b->op_stride < b->n_candidates)
         return fail(TFV_ERR_INVALID_ARGUMENT, "need 0 <= n_candidates <= op_stride");
     if (b->n_candidates == 0) return TFV_OK;
-    if (!table || !b->base_prologue || !b->base_offset || !b->prologue_delta || !b->offset_delta || !b->ii || !b->frame)
-        return fail(TFV_ERR_INVALID_ARGUMENT, "batch arrays and frame table must not be NULL");
+    if (!table || table_bytes < tfv::frame_table_bytes(shape_of(p, frames)))
+        return fail(TFV_ERR_INVALID_ARGUMENT, "frame table missing or too small");
+    if (!b->base_prologue || !b->base_offset || !b->prologue_delta || !b->offset_delta || !b->ii || !b->frame)
+        return fail(TFV_ERR_INVALID_ARGUMENT, "batch arrays must not be NULL");
     DeviceGuard guard(p->device);
     if (!guard.ok()) return fail(TFV_ERR_CUDA, "cannot select device %d", p->device);
     tfv::DevPeriodic db{b->n_candidates, b->op_stride, b->base_prologue, b->base_offset,
                         b->prologue_delta, b->offset_delta, b->ii, b->frame};
     tfv::DevResults dr{r->verdict, r->makespan, r->ii};
-    cudaError_t e = launch_periodic(p, to_dev(*frames),
-                                    tfv::frame_table_view(const_cast<void*>(table), frames->n_frames, p->dev.n_ops), db, dr,
-                                    static_cast<cudaStream_t>(stream));
+    const tfv::DevFrames df = to_dev(*frames);
+    const tfv::FrameTable view = tfv::frame_table_view(table, shape_of(p, frames));
+    const cudaStream_t s = static_cast<cudaStream_t>(stream);
+    cudaError_t e = tfv::launch_compile_sync_programs(p->dev, df, view, b->base_prologue, b->base_offset, p->sm_count, s);
+    if (e == cudaSuccess) e = launch_periodic(p, df, view, db, dr, s);
     if (e != cudaSuccess) return cuda_fail(e, "verify_periodic launch");
     return TFV_OK;
 }
@@ -345,7 +353,7 @@ int tfv_verify_rows(const tfv_problem* p, const tfv_frames* frames, const void* 
     tfv::DevRows db{b->n_candidates, b->start, b->issue_end, b->completion, b->frame, b->row_flags};
     tfv::DevResults dr{r->verdict, r->makespan, r->ii};
     cudaError_t e = tfv::launch_verify_rows(p->dev, to_dev(*frames),
-                                            tfv::frame_table_view(const_cast<void*>(table), frames->n_frames, p->dev.n_ops), db, dr,
+                                            tfv::frame_table_view(const_cast<void*>(table), shape_of(p, frames)), db, dr,
                                             p->sm_count, static_cast<cudaStream_t>(stream));
     if (e != cudaSuccess) return cuda_fail(e, "verify_rows launch");
     return TFV_OK;
@@ -365,14 +373,15 @@ int tfv_verify_periodic_host(const tfv_problem* p, const tfv_frames* hf, const t
     const int F = hf->n_frames;
     const int S = hf->n_sync_sets;
     const int E = hf->sync_offsets[S];
-    if (E < 0) return fail(TFV_ERR_INVALID_ARGUMENT, "negative sync edge count");
+    if (E < 0 || E != hf->n_sync_edges) return fail(TFV_ERR_INVALID_ARGUMENT, "sync_offsets[n_sync_sets] must equal n_sync_edges");
 
     DeviceGuard guard(p->device);
     if (!guard.ok()) return fail(TFV_ERR_CUDA, "cannot select device %d", p->device);
 
     const long long chunk = std::min<long long>(n, 1LL << 21);
     const long long pitch = (chunk + 7) & ~7LL;  // device rows keep 16-byte strides for TMA
-    const size_t table_bytes = tfv::frame_table_bytes(F, N);
+    const tfv::FrameTableShape shape{F, N, S, E};
+    const size_t table_bytes = tfv::frame_table_bytes(shape);
     cudaStream_t streams[2] = {nullptr, nullptr};
     cudaEvent_t ready = nullptr;
     char* ws = nullptr;
@@ -431,9 +440,10 @@ int tfv_verify_periodic_host(const tfv_problem* p, const tfv_frames* hf, const t
     if (e == cudaSuccess) e = cudaMemcpyAsync(d_bp, hb->base_prologue, sizeof(int) * N, cudaMemcpyHostToDevice, s0);
     if (e == cudaSuccess) e = cudaMemcpyAsync(d_bo, hb->base_offset, sizeof(int) * N, cudaMemcpyHostToDevice, s0);
     if (e != cudaSuccess) return bail(e, "frame upload");
-    tfv::DevFrames df{F, d_lp, d_lc, d_fl, d_ss, S, d_so, d_se};
-    tfv::FrameTable tab = tfv::frame_table_view(d_tab, F, N);
+    tfv::DevFrames df{F, d_lp, d_lc, d_fl, d_ss, S, E, d_so, d_se};
+    tfv::FrameTable tab = tfv::frame_table_view(d_tab, shape);
     e = tfv::launch_analyze_frames(p->dev, df, tab, p->sm_count, s0);
+    if (e == cudaSuccess) e = tfv::launch_compile_sync_programs(p->dev, df, tab, d_bp, d_bo, p->sm_count, s0);
     if (e != cudaSuccess) return bail(e, "analyze_frames launch");
     e = cudaEventRecord(ready, s0);
     if (e == cudaSuccess) e = cudaStreamWaitEvent(streams[1], ready, 0);

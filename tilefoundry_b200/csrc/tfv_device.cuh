@@ -60,21 +60,30 @@ struct DevFrames {
     const int* flags;
     const int* sync_set;
     int n_sync_sets;
+    int n_sync_edges;
     const int* sync_offsets;
     const int* sync_edges;  // [E][3]
 };
 
-// Frame table (device scratch written by the analysis kernel). Layout inside one
-// buffer, for F frames and N operations:
+// Frame table (device scratch). Layout inside one buffer, for F frames, N operations,
+// S sync sets and E sync edges (every region 16-byte aligned):
 //   int32  frame_class[F]       0 or the first structural verdict (1, 2, 4, 5, -2)
 //   int32  frame_flags[F]       kFrameRegisterCross
 //   int32  first_unreached[F]   first relation (sorted order, with instances) whose
 //                               completion -> start path is absent, or -1
 //   int16  succ[F][N]           lane successor (see kWrap)
-//   uint16 order[F][N]          the operations lane by lane in program order; an entry
-//                               is op | kFirstOfLane | kLastOfLane (valid frames only)
+//   uint16 order[F][N]          the operations lane by lane in program order; operations in
+//                               no lane follow as pseudo-lane 15
+//   uint16 lane_len[F][16]      length of each lane's run in order[]
+//   int2   set_meta[S]          {program length, class of the first statically failing edge}
+//   int4   set_prog[E]          per sync edge, base starts folded in (written per batch):
+//                               {a | b << 12 | from_offset << 24 | has_body << 25, w0, w1, distance}
+// The analysis kernel writes everything up to lane_len; tfv_verify_periodic compiles the
+// set programs for its batch's base starts.
 constexpr int kFirstOfLane = 0x8000;
 constexpr int kLastOfLane = 0x4000;
+constexpr int kProgFromOffset = 1 << 24;
+constexpr int kProgHasBody = 1 << 25;
 
 struct FrameTable {
     int* frame_class;
@@ -82,27 +91,40 @@ struct FrameTable {
     int* first_unreached;
     int16_t* succ;
     uint16_t* order;
+    uint16_t* lane_len;
+    int2* set_meta;
+    int4* set_prog;
 };
 
-inline size_t frame_table_head(int n_frames) {
-    size_t head = 3 * sizeof(int) * static_cast<size_t>(n_frames);
-    return (head + 15) & ~static_cast<size_t>(15);
+inline size_t round16(size_t x) { return (x + 15) & ~static_cast<size_t>(15); }
+
+struct FrameTableShape {
+    int frames, ops, sets, edges;
+};
+
+inline size_t frame_table_bytes(FrameTableShape s) {
+    const size_t F = static_cast<size_t>(s.frames), N = static_cast<size_t>(s.ops);
+    return round16(3 * sizeof(int) * F) + 2 * round16(sizeof(int16_t) * F * N) + round16(sizeof(uint16_t) * F * 16) +
+           round16(sizeof(int2) * static_cast<size_t>(s.sets)) + round16(sizeof(int4) * static_cast<size_t>(s.edges)) + 16;
 }
 
-inline size_t frame_table_bytes(int n_frames, int n_ops) {
-    const size_t rows = (sizeof(int16_t) * static_cast<size_t>(n_frames) * n_ops + 15) & ~static_cast<size_t>(15);
-    return frame_table_head(n_frames) + 2 * rows + 16;
-}
-
-inline FrameTable frame_table_view(void* base, int n_frames, int n_ops) {
+inline FrameTable frame_table_view(void* base, FrameTableShape s) {
+    const size_t F = static_cast<size_t>(s.frames), N = static_cast<size_t>(s.ops);
     FrameTable t;
     char* p = static_cast<char*>(base);
     t.frame_class = reinterpret_cast<int*>(p);
-    t.frame_flags = t.frame_class + n_frames;
-    t.first_unreached = t.frame_flags + n_frames;
-    const size_t rows = (sizeof(int16_t) * static_cast<size_t>(n_frames) * n_ops + 15) & ~static_cast<size_t>(15);
-    t.succ = reinterpret_cast<int16_t*>(p + frame_table_head(n_frames));
-    t.order = reinterpret_cast<uint16_t*>(p + frame_table_head(n_frames) + rows);
+    t.frame_flags = t.frame_class + F;
+    t.first_unreached = t.frame_flags + F;
+    p += round16(3 * sizeof(int) * F);
+    t.succ = reinterpret_cast<int16_t*>(p);
+    p += round16(sizeof(int16_t) * F * N);
+    t.order = reinterpret_cast<uint16_t*>(p);
+    p += round16(sizeof(int16_t) * F * N);
+    t.lane_len = reinterpret_cast<uint16_t*>(p);
+    p += round16(sizeof(uint16_t) * F * 16);
+    t.set_meta = reinterpret_cast<int2*>(p);
+    p += round16(sizeof(int2) * static_cast<size_t>(s.sets));
+    t.set_prog = reinterpret_cast<int4*>(p);
     return t;
 }
 
@@ -138,6 +160,9 @@ cudaError_t launch_analyze_frames(const DevProblem& p, const DevFrames& f, Frame
 cudaError_t launch_verify_periodic(const DevProblem& p, const DevFrames& f, FrameTable t,
                                    const DevPeriodic& b, DevResults r, int sm_count,
                                    cudaStream_t stream);
+// Per-batch sync programs: the base starts folded into every edge of every set.
+cudaError_t launch_compile_sync_programs(const DevProblem& p, const DevFrames& f, FrameTable t, const int* base_prologue,
+                                         const int* base_offset, int sm_count, cudaStream_t stream);
 // TMA variant: needs 16-byte aligned delta arrays, op_stride % 8 == 0 and N <= 256.
 bool periodic_tma_supported(const DevProblem& p, const DevPeriodic& b);
 cudaError_t launch_verify_periodic_tma(const DevProblem& p, const DevFrames& f, FrameTable t,

@@ -91,7 +91,7 @@ __global__ void __launch_bounds__(32) analyze_frames_kernel(DevProblem p, DevFra
     int* first = cnt + 16;
 
     const int* E = fr.sync_edges;
-    const int total_edges = fr.sync_offsets[fr.n_sync_sets];
+    const int total_edges = min(fr.sync_offsets[fr.n_sync_sets], fr.n_sync_edges);
 
     for (int f = blockIdx.x; f < fr.n_frames; f += gridDim.x) {
         if (lane < 16) cnt[lane] = 0;
@@ -180,16 +180,24 @@ __global__ void __launch_bounds__(32) analyze_frames_kernel(DevProblem p, DevFra
             succ[a] = static_cast<int16_t>(s);
             ft.succ[static_cast<size_t>(f) * N + a] = static_cast<int16_t>(s);
         }
-        // Lane-major walk order: slot[] already lists the operations lane by lane.
-        const int placed = first[15];
-        for (int j = lane; j < N; j += 32) {
-            uint16_t e = 0;
-            if (!bad && j < placed) {
-                const int op = slot[j];
-                const int l = lane_of(lp[op]), q = pos_of(lp[op]);
-                e = static_cast<uint16_t>(op | (q == 0 ? kFirstOfLane : 0) | (q == cnt[l] - 1 ? kLastOfLane : 0));
-            }
-            ft.order[static_cast<size_t>(f) * N + j] = e;
+        // Lane-major walk order: slot[] lists the placed operations lane by lane; the
+        // operations in no lane follow as pseudo-lane 15. Bad frames walk in index order.
+        const int placed = bad ? 0 : first[15];
+        uint16_t* order = ft.order + static_cast<size_t>(f) * N;
+        for (int j = lane; j < placed; j += 32) order[j] = static_cast<uint16_t>(slot[j]);
+        int tail = placed;
+        for (int a0 = 0; a0 < N; a0 += 32) {
+            const int a = a0 + lane;
+            const bool loose = a < N && (bad || lane_of(lp[a]) == TFV_LANE_ABSENT);
+            const unsigned m = __ballot_sync(kFull, loose);
+            if (loose) order[tail + __popc(m & ((1u << lane) - 1))] = static_cast<uint16_t>(a);
+            tail += __popc(m);
+        }
+        if (lane < 16) {
+            int len = 0;
+            if (lane == 15) len = N - placed;
+            else if (!bad) len = cnt[lane];
+            ft.lane_len[static_cast<size_t>(f) * 16 + lane] = static_cast<uint16_t>(len);
         }
         __syncwarp();
 
@@ -329,6 +337,69 @@ cudaError_t launch_analyze_frames(const DevProblem& p, const DevFrames& f, Frame
     }
     const int grid = min(f.n_frames, sm_count * 32);
     analyze_frames_kernel<<<grid, 32, smem, stream>>>(p, f, t);
+    return cudaGetLastError();
+}
+
+// ---------------------------------------------------------------------------------------
+// Per-batch sync programs
+// ---------------------------------------------------------------------------------------
+
+// One warp per sync set: finds the first edge that fails statically (an unknown operation,
+// class 13, or no finite instance, class 14; verify.py:285-289) and folds the batch's base
+// starts into the time inequalities of the edges before it (verify.py:290-292):
+//   instance 0:      start(d, b) - completion(0, a) = w0 + delta(b) - delta_prologue(a) + d * ii
+//   instances >= 1:  start(i+d, b) - completion(i, a) = w1 + delta_offset(b) - delta_offset(a) + d * ii
+// where delta(b) is b's prologue delta for d == 0 and its offset delta otherwise.
+__global__ void __launch_bounds__(32) compile_sync_programs_kernel(DevProblem p, DevFrames fr, FrameTable ft,
+                                                                     const int* base_prologue, const int* base_offset) {
+    const int N = p.n_ops, I = p.iterations;
+    const int lane = threadIdx.x;
+    const int total = min(fr.sync_offsets[fr.n_sync_sets], fr.n_sync_edges);
+    for (int s = blockIdx.x; s < fr.n_sync_sets; s += gridDim.x) {
+        int e0 = fr.sync_offsets[s], e1 = fr.sync_offsets[s + 1];
+        bool bad = e0 < 0 || e1 < e0 || e1 > total;
+        if (bad) e0 = e1 = 0;
+        int stop = e1;  // first statically failing edge
+        for (int k0 = e0; k0 < e1; k0 += 32) {
+            const int k = k0 + lane;
+            bool stat = false;
+            if (k < e1) {
+                const int a = fr.sync_edges[3 * k], b = fr.sync_edges[3 * k + 1], d = fr.sync_edges[3 * k + 2];
+                bad |= a < -1 || b < -1 || a >= N || b >= N || d < 0;
+                stat = a < 0 || b < 0 || d >= I;
+            }
+            const unsigned m = __ballot_sync(kFull, stat);
+            if (m) {
+                stop = k0 + __ffs(m) - 1;
+                break;
+            }
+        }
+        bad = __any_sync(kFull, bad);
+        int tail = 0;
+        if (bad) {
+            tail = TFV_CLASS_BAD_PACKING;
+            stop = e0;
+        } else if (stop < e1) {
+            const int a = fr.sync_edges[3 * stop], b = fr.sync_edges[3 * stop + 1];
+            tail = (a < 0 || b < 0) ? TFV_CLASS_SYNC_UNKNOWN_OP : TFV_CLASS_SYNC_NO_INSTANCE;
+        }
+        for (int k = e0 + lane; k < stop; k += 32) {
+            const int a = fr.sync_edges[3 * k], b = fr.sync_edges[3 * k + 1], d = fr.sync_edges[3 * k + 2];
+            const int lat = p.latency[a];
+            const int w0 = (d == 0 ? base_prologue[b] : base_offset[b]) - base_prologue[a] - lat;
+            const int w1 = base_offset[b] - base_offset[a] - lat;
+            const int bits = a | (b << 12) | (d == 0 ? 0 : kProgFromOffset) | (I - d >= 2 ? kProgHasBody : 0);
+            ft.set_prog[k] = make_int4(bits, w0, w1, d);
+        }
+        if (lane == 0) ft.set_meta[s] = make_int2(stop - e0, tail);
+    }
+}
+
+cudaError_t launch_compile_sync_programs(const DevProblem& p, const DevFrames& f, FrameTable t, const int* base_prologue,
+                                         const int* base_offset, int sm_count, cudaStream_t stream) {
+    if (f.n_sync_sets <= 0) return cudaSuccess;
+    const int grid = min(f.n_sync_sets, sm_count * 16);
+    compile_sync_programs_kernel<<<grid, 32, 0, stream>>>(p, f, t, base_prologue, base_offset);
     return cudaGetLastError();
 }
 

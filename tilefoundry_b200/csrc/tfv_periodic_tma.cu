@@ -73,59 +73,55 @@ __device__ __forceinline__ void tma_load_2d(void* dst, const CUtensorMap* map, i
 
 __device__ __forceinline__ void fence_proxy_async() { asm volatile("fence.proxy.async.shared::cta;" ::: "memory"); }
 
-struct Walk {
-    int lane_min;    // minimum slack over every lane-order inequality
-    int min_p, min_o;
-    int max_pl, max_ol;
+struct Extremes {
+    int min_p, min_o;    // smallest prologue / body-offset start
+    int max_pl, max_ol;  // largest prologue / body-offset completion
 };
 
-// One pass over the frame's operations in lane order (valid frames only).
-__device__ __forceinline__ Walk walk_lanes(const uint16_t* order, const int4* opc, const int16_t* tp, const int16_t* to,
-                                           int N, int I, int ii) {
-    Walk w{INT_MAX, INT_MAX, INT_MAX, INT_MIN, INT_MIN};
-    int end_p = 0, end_o = 0, first_o = 0;
-    const bool body = I >= 2, body2 = I >= 3;
-#pragma unroll 4
-    for (int j = 0; j < N; ++j) {
-        const int e = order[j];
-        const int s = e & 0x0FFF;
-        const int4 k = opc[s];  // issue, latency, base prologue, base offset
-        const int p = k.z + tp[s * kTile];
-        const int o = k.w + to[s * kTile];
-        if (e & kFirstOfLane) {
-            first_o = o;
-        } else {
-            w.lane_min = min(w.lane_min, p - end_p);
-            if (body) w.lane_min = min(w.lane_min, o - end_o);
-        }
-        end_p = p + k.x;
-        end_o = o + k.x;
-        if (e & kLastOfLane) {  // wrap edge (i, last) -> (i + 1, first)
-            const int next = first_o + ii;
-            if (body) w.lane_min = min(w.lane_min, next - end_p);
-            if (body2) w.lane_min = min(w.lane_min, next - end_o);
-        }
-        w.min_p = min(w.min_p, p);
-        w.min_o = min(w.min_o, o);
-        w.max_pl = max(w.max_pl, p + k.y);
-        w.max_ol = max(w.max_ol, o + k.y);
-    }
-    return w;
+__device__ __forceinline__ void take(Extremes& x, int p, int o, int lat) {
+    x.min_p = min(x.min_p, p);
+    x.min_o = min(x.min_o, o);
+    x.max_pl = max(x.max_pl, p + lat);
+    x.max_ol = max(x.max_ol, o + lat);
 }
 
-// Extremes only, in operation order (frames that failed structurally).
-__device__ __forceinline__ Walk scan_ops(const int4* opc, const int16_t* tp, const int16_t* to, int N) {
-    Walk w{INT_MAX, INT_MAX, INT_MAX, INT_MIN, INT_MIN};
-    for (int s = 0; s < N; ++s) {
-        const int4 k = opc[s];
-        const int p = k.z + tp[s * kTile];
-        const int o = k.w + to[s * kTile];
-        w.min_p = min(w.min_p, p);
-        w.min_o = min(w.min_o, o);
-        w.max_pl = max(w.max_pl, p + k.y);
-        w.max_ol = max(w.max_ol, o + k.y);
+// One pass over the frame's operations lane by lane (order/lane_len of the frame table).
+// Returns the smallest slack of every lane-order inequality (verify.py:99-112, 278-282):
+// same-iteration pairs in the prologue row (start) and the periodic rows (offset), and
+// the wrap from a lane's last operation to its first operation one iteration later.
+template <int kBodyRows>  // 0: I == 1, 1: I == 2, 2: I >= 3
+__device__ __forceinline__ int walk_lanes(const uint16_t* order, const uint16_t* lane_len, const int4* opc,
+                                          const int16_t* tp, const int16_t* to, int kTileOps, int ii, Extremes& x) {
+    int lane_min = INT_MAX;
+    int j = 0;
+    const int N = kTileOps;
+    for (int l = 0; l < 16; ++l) {
+        const int len = min(static_cast<int>(lane_len[l]), N - j);  // never past the frame's row
+        if (len <= 0) continue;
+        int s = min(static_cast<int>(order[j]), N - 1);
+        int4 k = opc[s];
+        int p = k.z + tp[s * kTile];
+        int o = k.w + to[s * kTile];
+        take(x, p, o, k.y);
+        const int first_o = o;
+        int end_p = p + k.x, end_o = o + k.x;
+#pragma unroll 4
+        for (int q = 1; q < len; ++q) {
+            s = min(static_cast<int>(order[j + q]), N - 1);
+            k = opc[s];
+            p = k.z + tp[s * kTile];
+            o = k.w + to[s * kTile];
+            take(x, p, o, k.y);
+            lane_min = min(lane_min, p - end_p);
+            if (kBodyRows >= 1) lane_min = min(lane_min, o - end_o);
+            end_p = p + k.x;
+            end_o = o + k.x;
+        }
+        if (kBodyRows >= 1) lane_min = min(lane_min, first_o + ii - end_p);
+        if (kBodyRows >= 2) lane_min = min(lane_min, first_o + ii - end_o);
+        j += len;
     }
-    return w;
+    return lane_min;
 }
 
 __device__ __forceinline__ int cover(int t, int p0, int o, int dur, int ii, int I) {
@@ -143,68 +139,30 @@ __device__ __forceinline__ int cover(int t, int p0, int o, int dur, int ii, int 
     return count;
 }
 
-// Classes 13..20 for a candidate whose frame is valid and whose lane order holds.
-__device__ int tail_checks(const DevProblem& p, const DevFrames& fr, const FrameTable& ft, int f, const int4* opc,
-                           const int16_t* tp, const int16_t* to, int ii) {
+// verify.py:183-200 on the periodic rows: demand at every window start.
+__device__ bool resources_exceed(const DevProblem& p, const int4* opc, const int16_t* tp, const int16_t* to, int ii) {
     const int I = p.iterations;
-    auto P = [&](int s) { return opc[s].z + tp[s * kTile]; };
-    auto O = [&](int s) { return opc[s].w + to[s * kTile]; };
-
-    const int set = fr.sync_set[f];
-    const int e0 = fr.sync_offsets[set], e1 = fr.sync_offsets[set + 1];
-    int first_bad = 0;  // class of the first failing edge in sorted order, sticky
-    for (int k = e0; k < e1; ++k) {
-        const int a = fr.sync_edges[3 * k], b = fr.sync_edges[3 * k + 1], d = fr.sync_edges[3 * k + 2];
-        int code;
-        if (a < 0 || b < 0) {
-            code = TFV_CLASS_SYNC_UNKNOWN_OP;
-        } else if (d >= I) {
-            code = TFV_CLASS_SYNC_NO_INSTANCE;
-        } else {
-            const int lat = opc[a].y;
-            const int shift = d * ii;
-            const int ob = O(b) + shift;
-            bool bad = P(a) + lat > (d == 0 ? P(b) : ob);
-            bad |= (I - d >= 2) && (O(a) + lat > ob);
-            code = bad ? TFV_CLASS_SYNC_INEQUALITY : 0;
-        }
-        first_bad = first_bad ? first_bad : code;
-    }
-    if (first_bad) return first_bad;
-    if (ft.frame_flags[f] & kFrameRegisterCross) return TFV_CLASS_REGISTER_CROSSES_LANES;
-    const int r = ft.first_unreached[f];
-    if (r >= 0) {
-        const int packed = p.relation[r];
-        const int a = packed & 0xFFF, b = (packed >> 12) & 0xFFF, d = packed >> 24;
-        const int target = d == 0 ? P(b) : O(b) + ii;
-        return P(a) + opc[a].y > target ? TFV_CLASS_RELATION_TIMING : TFV_CLASS_RELATION_NO_PATH;
-    }
-    if (I >= 2) {
-        for (int k = 0; k < p.n_carried; ++k) {
-            const int packed = p.carried[k];
-            const int u = packed & 0xFFFF, df = packed >> 16;
-            if (O(u) + opc[u].y > O(df)) return TFV_CLASS_CARRIED_SHARED_LIFETIME;
-        }
-    }
     for (int q = 0; q < p.n_resources; ++q) {
         const int w0 = p.res_offsets[q], w1 = p.res_offsets[q + 1];
         const int cap = p.capacity[q];
         for (int v = w0; v < w1; ++v) {
             const int x = p.res_win_op[v];
             for (int j = 0; j < I; ++j) {
-                const int t = j == 0 ? P(x) : O(x) + j * ii;
+                const int t = j == 0 ? opc[x].z + tp[x * kTile] : opc[x].w + to[x * kTile] + j * ii;
                 int demand = 0;
                 for (int w = w0; w < w1; ++w) {
                     const int y = p.res_win_op[w];
-                    demand += p.res_win_amount[w] * cover(t, P(y), O(y), p.res_win_duration[w], ii, I);
+                    demand += p.res_win_amount[w] *
+                              cover(t, opc[y].z + tp[y * kTile], opc[y].w + to[y * kTile], p.res_win_duration[w], ii, I);
                 }
-                if (demand > cap) return TFV_CLASS_RESOURCE_CAPACITY;
+                if (demand > cap) return true;
             }
         }
     }
-    return TFV_CLASS_PASS;
+    return false;
 }
 
+template <int kBodyRows>
 __global__ void __launch_bounds__(kTile) verify_periodic_tma_kernel(DevProblem p, DevFrames fr, FrameTable ft,
                                                                      DevPeriodic b, DevResults out, int n_tiles,
                                                                      const __grid_constant__ CUtensorMap map_p,
@@ -213,19 +171,23 @@ __global__ void __launch_bounds__(kTile) verify_periodic_tma_kernel(DevProblem p
     const int N = p.n_ops;
     const int I = p.iterations;
     const int t = threadIdx.x;
-    int16_t* tp = reinterpret_cast<int16_t*>(smem);           // [N][kTile]
-    int16_t* to = tp + N * kTile;                             // [N][kTile]
-    int4* opc = reinterpret_cast<int4*>(smem + 4 * N * kTile);  // [N]
+    int16_t* tp = reinterpret_cast<int16_t*>(smem);             // [N][kTile] prologue deltas
+    int16_t* to = tp + N * kTile;                               // [N][kTile] offset deltas
+    int4* opc = reinterpret_cast<int4*>(smem + 4 * N * kTile);  // [N] issue, latency, base starts
     uint64_t* bar = reinterpret_cast<uint64_t*>(opc + N);
 
-    for (int s = t; s < N; s += kTile)
-        opc[s] = make_int4(p.issue[s], p.latency[s], b.base_prologue[s], b.base_offset[s]);
+    bool base_ok = true;
+    for (int s = t; s < N; s += kTile) {
+        const int bp = b.base_prologue[s], bo = b.base_offset[s];
+        base_ok &= bp > -TFV_BASE_LIMIT && bp < TFV_BASE_LIMIT && bo > -TFV_BASE_LIMIT && bo < TFV_BASE_LIMIT;
+        opc[s] = make_int4(p.issue[s], p.latency[s], bp, bo);
+    }
     if (t == 0) {
         mbar_init(bar, 1);
         asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
         fence_proxy_async();
     }
-    __syncthreads();
+    base_ok = __syncthreads_and(base_ok);
 
     const unsigned tile_bytes = static_cast<unsigned>(2 * N * kTile * sizeof(int16_t));
     unsigned phase = 0;
@@ -238,7 +200,7 @@ __global__ void __launch_bounds__(kTile) verify_periodic_tma_kernel(DevProblem p
         }
         const long long c = static_cast<long long>(tile) * kTile + t;
         const bool live = c < b.n;
-        const int f = live ? b.frame[c] : 0;
+        const int f_in = live ? b.frame[c] : 0;
         const int ii = live ? b.ii[c] : 0;
         const bool landed = __syncthreads_and(mbar_wait_bounded(bar, phase));
         if (!landed) {  // report, drain the copy (bounded) and leave
@@ -251,21 +213,58 @@ __global__ void __launch_bounds__(kTile) verify_periodic_tma_kernel(DevProblem p
             return;
         }
         phase ^= 1;
-        if (live) {
+        if (live && fr.n_frames > 0) {
             const int16_t* mp = tp + t;
             const int16_t* mo = to + t;
-            const bool frame_ok = static_cast<unsigned>(f) < static_cast<unsigned>(fr.n_frames);
+            const bool frame_ok = static_cast<unsigned>(f_in) < static_cast<unsigned>(fr.n_frames);
+            const int f = frame_ok ? f_in : 0;
             const int fclass = frame_ok ? ft.frame_class[f] : TFV_CLASS_BAD_PACKING;
-            const Walk w = fclass == 0 ? walk_lanes(ft.order + static_cast<size_t>(f) * N, opc, mp, mo, N, I, ii)
-                                       : scan_ops(opc, mp, mo, N);
-            long long makespan = w.max_pl;
-            bool negative = w.min_p < 0;
-            bool out_of_range = false;
-            if (I >= 2) {
+            Extremes x{INT_MAX, INT_MAX, INT_MIN, INT_MIN};
+            const int lane_min = walk_lanes<kBodyRows>(ft.order + static_cast<size_t>(f) * N,
+                                                       ft.lane_len + static_cast<size_t>(f) * 16, opc, mp, mo, N, ii, x);
+            // Sync edges before the set's first static failure, base starts folded in.
+            const int set = fr.sync_set[f];
+            const int2 meta = (static_cast<unsigned>(set) < static_cast<unsigned>(fr.n_sync_sets))
+                                  ? ft.set_meta[set] : make_int2(0, TFV_CLASS_BAD_PACKING);
+            const int4* prog = ft.set_prog + (meta.x > 0 ? fr.sync_offsets[set] : 0);
+            int sync_min = INT_MAX;
+#pragma unroll 4
+            for (int k = 0; k < meta.x; ++k) {
+                const int4 e = prog[k];
+                const int a = e.x & 0xFFF, bb = (e.x >> 12) & 0xFFF;
+                const int dpa = mp[a * kTile], doa = mo[a * kTile];
+                const int dpb = mp[bb * kTile], dob = mo[bb * kTile];
+                const int shift = e.w * ii;
+                const int t0 = e.y + ((e.x & kProgFromOffset) ? dob : dpb) - dpa + shift;
+                const int t1 = (e.x & kProgHasBody) ? e.z + dob - doa + shift : INT_MAX;
+                sync_min = min(sync_min, min(t0, t1));
+            }
+            // First relation without a lane/sync path: timing at instance 0 decides 17 vs 18.
+            int rel_cls = 0;
+            const int r = ft.first_unreached[f];
+            if (r >= 0) {
+                const int packed = p.relation[r];
+                const int a = packed & 0xFFF, bb = (packed >> 12) & 0xFFF, d = packed >> 24;
+                const int ready = opc[a].z + mp[a * kTile] + opc[a].y;
+                const int target = d == 0 ? opc[bb].z + mp[bb * kTile] : opc[bb].w + mo[bb * kTile] + ii;
+                rel_cls = ready > target ? TFV_CLASS_RELATION_TIMING : TFV_CLASS_RELATION_NO_PATH;
+            }
+            bool carried_bad = false;
+            if (kBodyRows >= 1) {
+                for (int k = 0; k < p.n_carried; ++k) {
+                    const int packed = p.carried[k];
+                    const int u = packed & 0xFFFF, df = packed >> 16;
+                    carried_bad |= opc[u].w + mo[u * kTile] + opc[u].y > opc[df].w + mo[df * kTile];
+                }
+            }
+            long long makespan = x.max_pl;
+            bool negative = x.min_p < 0;
+            bool out_of_range = !base_ok;
+            if (kBodyRows >= 1) {
                 const long long k1 = ii, kl = static_cast<long long>(I - 1) * ii;
                 const long long lo = k1 < kl ? k1 : kl, hi = k1 < kl ? kl : k1;
-                negative |= static_cast<long long>(w.min_o) + lo < 0;
-                const long long body = static_cast<long long>(w.max_ol) + hi;
+                negative |= static_cast<long long>(x.min_o) + lo < 0;
+                const long long body = static_cast<long long>(x.max_ol) + hi;
                 makespan = makespan > body ? makespan : body;
                 out_of_range |= hi >= TFV_TIME_LIMIT || lo <= -static_cast<long long>(TFV_TIME_LIMIT);
             }
@@ -275,12 +274,22 @@ __global__ void __launch_bounds__(kTile) verify_periodic_tma_kernel(DevProblem p
             else if (fclass == TFV_CLASS_SCHEDULE_MALFORMED || negative) cls = TFV_CLASS_SCHEDULE_MALFORMED;
             else if (out_of_range) cls = TFV_CLASS_OUT_OF_RANGE;
             else if (fclass != 0) cls = fclass;
-            else if (I >= 3 && ii <= 0) cls = TFV_CLASS_II_NONPOSITIVE;
-            else if (w.lane_min < 0) cls = TFV_CLASS_LANE_ORDER;
-            else cls = tail_checks(p, fr, ft, f, opc, mp, mo, ii);
+            else if (kBodyRows >= 2 && ii <= 0) cls = TFV_CLASS_II_NONPOSITIVE;
+            else if (lane_min < 0) cls = TFV_CLASS_LANE_ORDER;
+            else if (sync_min < 0) cls = TFV_CLASS_SYNC_INEQUALITY;
+            else if (meta.y != 0) cls = meta.y;
+            else if (ft.frame_flags[f] & kFrameRegisterCross) cls = TFV_CLASS_REGISTER_CROSSES_LANES;
+            else if (rel_cls) cls = rel_cls;
+            else if (carried_bad) cls = TFV_CLASS_CARRIED_SHARED_LIFETIME;
+            else cls = (p.n_resources > 0 && resources_exceed(p, opc, mp, mo, ii)) ? TFV_CLASS_RESOURCE_CAPACITY
+                                                                                 : TFV_CLASS_PASS;
             out.verdict[c] = cls;
             out.makespan[c] = makespan > INT_MAX ? INT_MAX : (makespan < INT_MIN ? INT_MIN : static_cast<int>(makespan));
-            out.ii[c] = I >= 3 ? ii : 0;
+            out.ii[c] = kBodyRows >= 2 ? ii : 0;
+        } else if (live) {  // no frames at all: the candidate cannot name one
+            out.verdict[c] = TFV_CLASS_BAD_PACKING;
+            out.makespan[c] = 0;
+            out.ii[c] = kBodyRows >= 2 ? ii : 0;
         }
         __syncthreads();  // every thread is done with the tile before the next copy lands
     }
@@ -321,6 +330,30 @@ bool periodic_tma_supported(const DevProblem& p, const DevPeriodic& b) {
            b.n < (1LL << 31) && encode_fn() != nullptr;
 }
 
+namespace {
+
+template <int kBodyRows>
+cudaError_t launch_tma(const DevProblem& p, const DevFrames& f, FrameTable t, const DevPeriodic& b, DevResults r,
+                       int sm_count, cudaStream_t stream, const CUtensorMap& map_p, const CUtensorMap& map_o) {
+    auto kernel = verify_periodic_tma_kernel<kBodyRows>;
+    const size_t smem = tma_smem_bytes(p.n_ops);
+    if (smem > 48 * 1024) {
+        cudaError_t e = cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(smem));
+        if (e != cudaSuccess) return e;
+    }
+    int per_sm = 0;
+    cudaError_t e = cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, kernel, kTile, smem);
+    if (e != cudaSuccess) return e;
+    if (per_sm < 1) return cudaErrorInvalidConfiguration;
+    const long long tiles = (b.n + kTile - 1) / kTile;
+    const long long cap = static_cast<long long>(sm_count) * per_sm;
+    const int grid = static_cast<int>(tiles < cap ? tiles : cap);
+    kernel<<<grid, kTile, smem, stream>>>(p, f, t, b, r, static_cast<int>(tiles), map_p, map_o);
+    return cudaGetLastError();
+}
+
+}  // namespace
+
 cudaError_t launch_verify_periodic_tma(const DevProblem& p, const DevFrames& f, FrameTable t, const DevPeriodic& b,
                                        DevResults r, int sm_count, cudaStream_t stream) {
     if (b.n <= 0) return cudaSuccess;
@@ -328,21 +361,9 @@ cudaError_t launch_verify_periodic_tma(const DevProblem& p, const DevFrames& f, 
     if (!make_map(&map_p, b.prologue_delta, b.n, b.stride, p.n_ops) ||
         !make_map(&map_o, b.offset_delta, b.n, b.stride, p.n_ops))
         return cudaErrorInvalidValue;
-    const size_t smem = tma_smem_bytes(p.n_ops);
-    if (smem > 48 * 1024) {
-        cudaError_t e = cudaFuncSetAttribute(verify_periodic_tma_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                             static_cast<int>(smem));
-        if (e != cudaSuccess) return e;
-    }
-    int per_sm = 0;
-    cudaError_t e = cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, verify_periodic_tma_kernel, kTile, smem);
-    if (e != cudaSuccess) return e;
-    if (per_sm < 1) return cudaErrorInvalidConfiguration;
-    const long long tiles = (b.n + kTile - 1) / kTile;
-    const long long cap = static_cast<long long>(sm_count) * per_sm;
-    const int grid = static_cast<int>(tiles < cap ? tiles : cap);
-    verify_periodic_tma_kernel<<<grid, kTile, smem, stream>>>(p, f, t, b, r, static_cast<int>(tiles), map_p, map_o);
-    return cudaGetLastError();
+    if (p.iterations >= 3) return launch_tma<2>(p, f, t, b, r, sm_count, stream, map_p, map_o);
+    if (p.iterations == 2) return launch_tma<1>(p, f, t, b, r, sm_count, stream, map_p, map_o);
+    return launch_tma<0>(p, f, t, b, r, sm_count, stream, map_p, map_o);
 }
 
 }  // namespace tfv

@@ -148,22 +148,23 @@ class WarpgroupVerifier:
         dev = torch.device("cuda", self.device)
         arrays = frames.arrays()
         tensors = {key: torch.from_numpy(np.ascontiguousarray(value)).to(dev) for key, value in arrays.items()}
-        lane_pos = tensors["lane_pos"]
         struct = _lib.Frames(
             len(frames),
-            lane_pos.data_ptr() if lane_pos.numel() else None,
+            tensors["lane_pos"].data_ptr() if len(frames) else None,
             tensors["lane_count"].data_ptr() if len(frames) else None,
             tensors["flags"].data_ptr() if len(frames) else None,
             tensors["sync_set"].data_ptr() if len(frames) else None,
             len(arrays["sync_offsets"]) - 1,
+            int(arrays["sync_offsets"][-1]),
             tensors["sync_offsets"].data_ptr(),
             tensors["sync_edges"].data_ptr(),
         )
         return DeviceFrames(tensors, struct, len(frames))
 
-    def frame_table_bytes(self, n_frames: int) -> int:
+    def frame_table_bytes(self, frames: DeviceFrames | _lib.Frames) -> int:
+        struct = frames.struct if isinstance(frames, DeviceFrames) else frames
         size = ctypes.c_size_t()
-        _lib.check(self._lib.tfv_frame_table_bytes(self._handle, n_frames, ctypes.byref(size)), "tfv_frame_table_bytes")
+        _lib.check(self._lib.tfv_frame_table_bytes(self._handle, ctypes.byref(struct), ctypes.byref(size)), "tfv_frame_table_bytes")
         return int(size.value)
 
     def _stream(self, stream: Any) -> int | None:
@@ -175,7 +176,7 @@ class WarpgroupVerifier:
     def analyze(self, frames: DeviceFrames, table: Any = None, stream: Any = None):
         """Run the frame analysis; returns the frame-table tensor (device scratch)."""
         torch = _torch()
-        nbytes = self.frame_table_bytes(frames.n_frames)
+        nbytes = self.frame_table_bytes(frames)
         if table is None:
             table = torch.empty(nbytes, dtype=torch.uint8, device=torch.device("cuda", self.device))
         _lib.check(
@@ -213,8 +214,8 @@ class WarpgroupVerifier:
         out, results = self._results(n, out)
         _lib.check(
             self._lib.tfv_verify_periodic(
-                self._handle, ctypes.byref(frames.struct), table.data_ptr(), ctypes.byref(struct), ctypes.byref(results),
-                self._stream(stream),
+                self._handle, ctypes.byref(frames.struct), table.data_ptr(), int(table.numel()), ctypes.byref(struct),
+                ctypes.byref(results), self._stream(stream),
             ),
             "tfv_verify_periodic",
         )
@@ -252,16 +253,7 @@ class WarpgroupVerifier:
         """
         n = batch.n
         arrays = frames.arrays()
-        fstruct = _lib.Frames(
-            len(frames),
-            arrays["lane_pos"].ctypes.data if len(frames) else None,
-            arrays["lane_count"].ctypes.data if len(frames) else None,
-            arrays["flags"].ctypes.data if len(frames) else None,
-            arrays["sync_set"].ctypes.data if len(frames) else None,
-            len(arrays["sync_offsets"]) - 1,
-            arrays["sync_offsets"].ctypes.data,
-            arrays["sync_edges"].ctypes.data,
-        )
+        fstruct = _lib.frames_struct(arrays, len(frames))
         verdict = np.empty(n, dtype=np.int32)
         makespan = np.empty(n, dtype=np.int32)
         ii = np.empty(n, dtype=np.int32)

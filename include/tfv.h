@@ -94,6 +94,7 @@ extern "C" {
 #define TFV_MAX_OPS 4095
 #define TFV_TIME_LIMIT (1 << 30)
 #define TFV_BASE_LIMIT (1 << 28)
+#define TFV_STATIC_TABLE_BYTES (8u << 20) /* frame table of tfv_verify_periodic_static */
 
 typedef struct tfv_problem tfv_problem;
 
@@ -222,6 +223,20 @@ TFV_API int tfv_verify_rows(const tfv_problem* problem, const tfv_frames* frames
  * `results` are host pointers. */
 TFV_API int tfv_verify_periodic_host(const tfv_problem* problem, const tfv_frames* frames,
                              const tfv_periodic_batch* batch, const tfv_results* results);
+
+/* No counterpart in the reference. For callers that cannot allocate device memory (a
+ * process whose device memory is owned by another framework's pooled allocator, or a
+ * latency-sensitive caller that must not trigger cudaMalloc/cudaFree, which can
+ * synchronize the whole device): analyses the frames and verifies the batch like
+ * tfv_analyze_frames + tfv_verify_periodic, with the frame table in a file-scope device
+ * array of TFV_STATIC_TABLE_BYTES (8 MiB, held by every GPU that loads the library until
+ * exit). Frames needing a larger table are rejected with TFV_ERR_RANGE. Allocates
+ * nothing. The first call on a device looks up the array's device address with that
+ * device current; make it before any stream capture. All calls share the array: calls
+ * whose work overlaps on the GPU race. Device pointers, stream-ordered like
+ * tfv_verify_periodic. */
+TFV_API int tfv_verify_periodic_static(const tfv_problem* problem, const tfv_frames* frames,
+                                       const tfv_periodic_batch* batch, const tfv_results* results, void* stream);
 
 #ifdef __cplusplus
 }

@@ -138,6 +138,10 @@ EXPORTS = {
         ctypes.c_int,
         [_p, ctypes.POINTER(Frames), ctypes.POINTER(PeriodicBatch), ctypes.POINTER(Results)],
     ),
+    "tfv_verify_periodic_static": (
+        ctypes.c_int,
+        [_p, ctypes.POINTER(Frames), ctypes.POINTER(PeriodicBatch), ctypes.POINTER(Results), _p],
+    ),
 }
 
 _lib: ctypes.CDLL | None = None

@@ -504,3 +504,44 @@ int tfv_verify_periodic_host(const tfv_problem* p, const tfv_frames* hf, const t
 }
 
 }  // extern "C"
+
+// ---------------------------------------------------------------------------------------
+// Helpers for tfv_verify_periodic_static (tfv_static.cu): the analysis, sync-program
+// compilation and verification sequence on a frame table the caller does not own.
+// ---------------------------------------------------------------------------------------
+
+int tfv_internal_fail(int code, const char* message) { return fail(code, "%s", message); }
+
+int tfv_internal_device(const tfv_problem* p) { return p ? p->device : -1; }
+
+int tfv_internal_periodic_with_table(const tfv_problem* p, const tfv_frames* frames, void* table, size_t table_bytes,
+                                     const tfv_periodic_batch* b, const tfv_results* r, void* stream, bool analyze) {
+    if (!p || !b) return fail(TFV_ERR_INVALID_ARGUMENT, "problem and batch must not be NULL");
+    int rc = check_frames(frames);
+    if (rc) return rc;
+    rc = check_results(r);
+    if (rc) return rc;
+    if (b->n_candidates < 0 || b->op_stride < b->n_candidates)
+        return fail(TFV_ERR_INVALID_ARGUMENT, "need 0 <= n_candidates <= op_stride");
+    const size_t needed = tfv::frame_table_bytes(shape_of(p, frames));
+    if (needed > table_bytes)
+        return fail(TFV_ERR_RANGE, "these frames need a %zu-byte frame table; the static table holds %zu bytes", needed,
+                    table_bytes);
+    if (b->n_candidates == 0) return TFV_OK;
+    if (!b->base_prologue || !b->base_offset || !b->prologue_delta || !b->offset_delta || !b->ii || !b->frame)
+        return fail(TFV_ERR_INVALID_ARGUMENT, "batch arrays must not be NULL");
+    DeviceGuard guard(p->device);
+    if (!guard.ok()) return fail(TFV_ERR_CUDA, "cannot select device %d", p->device);
+    tfv::DevPeriodic db{b->n_candidates, b->op_stride, b->base_prologue, b->base_offset,
+                        b->prologue_delta, b->offset_delta, b->ii, b->frame};
+    tfv::DevResults dr{r->verdict, r->makespan, r->ii};
+    const tfv::DevFrames df = to_dev(*frames);
+    const tfv::FrameTable view = tfv::frame_table_view(table, shape_of(p, frames));
+    const cudaStream_t s = static_cast<cudaStream_t>(stream);
+    cudaError_t e = cudaSuccess;
+    if (analyze) e = tfv::launch_analyze_frames(p->dev, df, view, p->sm_count, s);
+    if (e == cudaSuccess) e = tfv::launch_compile_sync_programs(p->dev, df, view, b->base_prologue, b->base_offset, p->sm_count, s);
+    if (e == cudaSuccess) e = launch_periodic(p, df, view, db, dr, s);
+    if (e != cudaSuccess) return cuda_fail(e, "verify_periodic_static launch");
+    return TFV_OK;
+}

@@ -37,6 +37,10 @@ sys.path[:0] = [str(ROOT), str(ROOT / "tests")]
 METRIC = "candidate schedules verified/sec (bit-exact verdict+makespan) at 1/2/4/8 B200"
 UNIT = "candidates/s"
 FALLBACK_HBM_GBS = 6650.0
+# DRAM bytes per candidate of verify_periodic_tma_kernel measured by ncu on a 2 097 152-
+# candidate launch (dram__bytes_read.sum + dram__bytes_write.sum = 467.7 MB; see
+# profiles/verify_periodic_tma_mla.md). Traffic grows in proportion to the candidates.
+MEASURED_DRAM_BYTES_PER_CANDIDATE = 467.7e6 / 2097152
 
 
 def parse_args():
@@ -411,7 +415,8 @@ def run_ours(args) -> None:
                 "peak": peak,
                 "unit": "GB/s",
                 "frac": achieved / peak,
-                "traffic": None,
+                "traffic": MEASURED_DRAM_BYTES_PER_CANDIDATE * n,
+                "traffic_source": "ncu dram__bytes_read+write on 2097152 candidates, scaled per candidate",
                 "peak_source": peak_src,
                 "kernel": "tfv::verify_periodic_tma_kernel",
                 "kernel_ms": statistics.mean(verify_ms),

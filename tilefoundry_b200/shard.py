@@ -35,8 +35,8 @@ def gather_results(results, n_total: int, *, dst: int = 0, group=None):
     local = torch.stack([t.to(torch.int32) for t in results])
     padded = torch.zeros((3, widest), dtype=torch.int32, device=local.device)
     padded[:, : local.shape[1]] = local
-    pieces = [torch.empty_like(padded) for _ in range(world)]
-    dist.all_gather(pieces, padded, group=group)
+    pieces = [torch.empty_like(padded) for _ in range(world)] if rank == dst else None
+    dist.gather(padded, gather_list=pieces, dst=dst, group=group)
     if rank != dst:
         return None
     parts = []

@@ -76,14 +76,21 @@ struct DevFrames {
 //                               no lane follow as pseudo-lane 15
 //   uint16 lane_len[F][16]      length of each lane's run in order[]
 //   int2   set_meta[S]          {program length, class of the first statically failing edge}
-//   int4   set_prog[E]          per sync edge, base starts folded in (written per batch):
-//                               {a | b << 12 | from_offset << 24 | has_body << 25, w0, w1, distance}
+//   int4   set_prog[E]          per sync edge, base starts folded in (written per batch), in
+//                               the TMA tile's byte offsets (rows of kTmaTile int16 values):
+//                               {a_row | b_row << 16, x_row | distance << 17, w0, w1}
+//                               a_row/b_row: offsets of a's and b's prologue rows; x_row: the
+//                               row instance 0 reads for b (prologue row for distance 0, offset
+//                               row otherwise, which start N rows later); w1 = kNoBodyWeight
+//                               when the edge has no instance >= 1
 // The analysis kernel writes everything up to lane_len; tfv_verify_periodic compiles the
 // set programs for its batch's base starts.
 constexpr int kFirstOfLane = 0x8000;
 constexpr int kLastOfLane = 0x4000;
-constexpr int kProgFromOffset = 1 << 24;
-constexpr int kProgHasBody = 1 << 25;
+constexpr int kTmaTile = 128;                         // candidates per TMA tile
+constexpr int kTmaRowBytes = kTmaTile * 2;            // one op's int16 deltas in a tile
+constexpr int kNoBodyWeight = 1 << 29;                // slack that can never go negative
+constexpr int kMaxProgDistance = (1 << 14) - 1;
 
 struct FrameTable {
     int* frame_class;

@@ -349,7 +349,9 @@ cudaError_t launch_analyze_frames(const DevProblem& p, const DevFrames& f, Frame
 // starts into the time inequalities of the edges before it (verify.py:290-292):
 //   instance 0:      start(d, b) - completion(0, a) = w0 + delta(b) - delta_prologue(a) + d * ii
 //   instances >= 1:  start(i+d, b) - completion(i, a) = w1 + delta_offset(b) - delta_offset(a) + d * ii
-// where delta(b) is b's prologue delta for d == 0 and its offset delta otherwise.
+// where delta(b) is b's prologue delta for d == 0 and its offset delta otherwise. Entries
+// address the TMA tile directly (see set_prog in tfv_device.cuh); they are only consumed by
+// the TMA kernel, which requires N <= 256 and iterations <= kMaxProgDistance.
 __global__ void __launch_bounds__(32) compile_sync_programs_kernel(DevProblem p, DevFrames fr, FrameTable ft,
                                                                      const int* base_prologue, const int* base_offset) {
     const int N = p.n_ops, I = p.iterations;
@@ -383,13 +385,15 @@ __global__ void __launch_bounds__(32) compile_sync_programs_kernel(DevProblem p,
             const int a = fr.sync_edges[3 * stop], b = fr.sync_edges[3 * stop + 1];
             tail = (a < 0 || b < 0) ? TFV_CLASS_SYNC_UNKNOWN_OP : TFV_CLASS_SYNC_NO_INSTANCE;
         }
+        const int to_rows = N * kTmaRowBytes;  // the offset rows follow the N prologue rows
         for (int k = e0 + lane; k < stop; k += 32) {
             const int a = fr.sync_edges[3 * k], b = fr.sync_edges[3 * k + 1], d = fr.sync_edges[3 * k + 2];
             const int lat = p.latency[a];
             const int w0 = (d == 0 ? base_prologue[b] : base_offset[b]) - base_prologue[a] - lat;
-            const int w1 = base_offset[b] - base_offset[a] - lat;
-            const int bits = a | (b << 12) | (d == 0 ? 0 : kProgFromOffset) | (I - d >= 2 ? kProgHasBody : 0);
-            ft.set_prog[k] = make_int4(bits, w0, w1, d);
+            const int w1 = I - d >= 2 ? base_offset[b] - base_offset[a] - lat : kNoBodyWeight;
+            const int a_row = a * kTmaRowBytes, b_row = b * kTmaRowBytes;
+            const int x_row = d == 0 ? b_row : to_rows + b_row;
+            ft.set_prog[k] = make_int4(a_row | (b_row << 16), x_row | (min(d, kMaxProgDistance) << 17), w0, w1);
         }
         if (lane == 0) ft.set_meta[s] = make_int2(stop - e0, tail);
     }

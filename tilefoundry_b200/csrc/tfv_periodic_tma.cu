@@ -30,7 +30,7 @@ namespace tfv {
 
 namespace {
 
-constexpr int kTile = 128;          // candidates per CTA tile = threads per CTA
+constexpr int kTile = kTmaTile;     // candidates per CTA tile = threads per CTA
 constexpr int kMaxTmaOps = 256;     // TMA box height limit
 constexpr long long kWaitSpins = 1LL << 22;
 
@@ -88,37 +88,50 @@ __device__ __forceinline__ void take(Extremes& x, int p, int o, int lat) {
 // One pass over the frame's operations lane by lane (order/lane_len of the frame table).
 // Returns the smallest slack of every lane-order inequality (verify.py:99-112, 278-282):
 // same-iteration pairs in the prologue row (start) and the periodic rows (offset), and
-// the wrap from a lane's last operation to its first operation one iteration later.
+// the wrap from a lane's last operation to its first operation one iteration later. The
+// slack accumulates as min(start + (-previous issue end)) in one DPX instruction.
 template <int kBodyRows>  // 0: I == 1, 1: I == 2, 2: I >= 3
 __device__ __forceinline__ int walk_lanes(const uint16_t* order, const uint16_t* lane_len, const int4* opc,
-                                          const int16_t* tp, const int16_t* to, int kTileOps, int ii, Extremes& x) {
+                                          const char* row_p, int to_bytes, int N, int ii, Extremes& x) {
+    const uint4 lens_lo = reinterpret_cast<const uint4*>(lane_len)[0];
+    const uint4 lens_hi = reinterpret_cast<const uint4*>(lane_len)[1];
+    const unsigned lens[8] = {lens_lo.x, lens_lo.y, lens_lo.z, lens_lo.w, lens_hi.x, lens_hi.y, lens_hi.z, lens_hi.w};
     int lane_min = INT_MAX;
     int j = 0;
-    const int N = kTileOps;
+#pragma unroll
     for (int l = 0; l < 16; ++l) {
-        const int len = min(static_cast<int>(lane_len[l]), N - j);  // never past the frame's row
+        const int len = min(static_cast<int>((lens[l >> 1] >> ((l & 1) * 16)) & 0xFFFF), N - j);
         if (len <= 0) continue;
         int s = min(static_cast<int>(order[j]), N - 1);
         int4 k = opc[s];
-        int p = k.z + tp[s * kTile];
-        int o = k.w + to[s * kTile];
-        take(x, p, o, k.y);
+        const char* row = row_p + s * kTmaRowBytes;
+        int p = k.z + *reinterpret_cast<const int16_t*>(row);
+        int o = k.w + *reinterpret_cast<const int16_t*>(row + to_bytes);
+        x.min_p = min(x.min_p, p);
+        x.min_o = min(x.min_o, o);
+        x.max_pl = __viaddmax_s32(p, k.y, x.max_pl);
+        x.max_ol = __viaddmax_s32(o, k.y, x.max_ol);
         const int first_o = o;
-        int end_p = p + k.x, end_o = o + k.x;
+        int nend_p = -p - k.x, nend_o = -o - k.x;  // minus the issue end
 #pragma unroll 4
         for (int q = 1; q < len; ++q) {
             s = min(static_cast<int>(order[j + q]), N - 1);
             k = opc[s];
-            p = k.z + tp[s * kTile];
-            o = k.w + to[s * kTile];
-            take(x, p, o, k.y);
-            lane_min = min(lane_min, p - end_p);
-            if (kBodyRows >= 1) lane_min = min(lane_min, o - end_o);
-            end_p = p + k.x;
-            end_o = o + k.x;
+            row = row_p + s * kTmaRowBytes;
+            p = k.z + *reinterpret_cast<const int16_t*>(row);
+            o = k.w + *reinterpret_cast<const int16_t*>(row + to_bytes);
+            x.min_p = min(x.min_p, p);
+            x.min_o = min(x.min_o, o);
+            x.max_pl = __viaddmax_s32(p, k.y, x.max_pl);
+            x.max_ol = __viaddmax_s32(o, k.y, x.max_ol);
+            lane_min = __viaddmin_s32(p, nend_p, lane_min);
+            if (kBodyRows >= 1) lane_min = __viaddmin_s32(o, nend_o, lane_min);
+            nend_p = -p - k.x;
+            nend_o = -o - k.x;
         }
-        if (kBodyRows >= 1) lane_min = min(lane_min, first_o + ii - end_p);
-        if (kBodyRows >= 2) lane_min = min(lane_min, first_o + ii - end_o);
+        const int next = first_o + ii;  // the lane's first operation one iteration later
+        if (kBodyRows >= 1) lane_min = __viaddmin_s32(next, nend_p, lane_min);
+        if (kBodyRows >= 2) lane_min = __viaddmin_s32(next, nend_o, lane_min);
         j += len;
     }
     return lane_min;
@@ -220,8 +233,11 @@ __global__ void __launch_bounds__(kTile) verify_periodic_tma_kernel(DevProblem p
             const int f = frame_ok ? f_in : 0;
             const int fclass = frame_ok ? ft.frame_class[f] : TFV_CLASS_BAD_PACKING;
             Extremes x{INT_MAX, INT_MAX, INT_MIN, INT_MIN};
+            const char* row_p = reinterpret_cast<const char*>(mp);
+            const int to_bytes = N * kTmaRowBytes;
             const int lane_min = walk_lanes<kBodyRows>(ft.order + static_cast<size_t>(f) * N,
-                                                       ft.lane_len + static_cast<size_t>(f) * 16, opc, mp, mo, N, ii, x);
+                                                       ft.lane_len + static_cast<size_t>(f) * 16, opc, row_p, to_bytes,
+                                                       N, ii, x);
             // Sync edges before the set's first static failure, base starts folded in.
             const int set = fr.sync_set[f];
             const int2 meta = (static_cast<unsigned>(set) < static_cast<unsigned>(fr.n_sync_sets))
@@ -231,13 +247,15 @@ __global__ void __launch_bounds__(kTile) verify_periodic_tma_kernel(DevProblem p
 #pragma unroll 4
             for (int k = 0; k < meta.x; ++k) {
                 const int4 e = prog[k];
-                const int a = e.x & 0xFFF, bb = (e.x >> 12) & 0xFFF;
-                const int dpa = mp[a * kTile], doa = mo[a * kTile];
-                const int dpb = mp[bb * kTile], dob = mo[bb * kTile];
-                const int shift = e.w * ii;
-                const int t0 = e.y + ((e.x & kProgFromOffset) ? dob : dpb) - dpa + shift;
-                const int t1 = (e.x & kProgHasBody) ? e.z + dob - doa + shift : INT_MAX;
-                sync_min = min(sync_min, min(t0, t1));
+                const int a_row = e.x & 0xFFFF, b_row = static_cast<unsigned>(e.x) >> 16;
+                const int x_row = e.y & 0x1FFFF, d = static_cast<unsigned>(e.y) >> 17;
+                const int dpa = *reinterpret_cast<const int16_t*>(row_p + a_row);
+                const int doa = *reinterpret_cast<const int16_t*>(row_p + to_bytes + a_row);
+                const int dob = *reinterpret_cast<const int16_t*>(row_p + to_bytes + b_row);
+                const int xb = *reinterpret_cast<const int16_t*>(row_p + x_row);
+                const int shift = d * ii;
+                sync_min = __viaddmin_s32(e.z + xb - dpa, shift, sync_min);  // instance 0
+                sync_min = __viaddmin_s32(e.w + dob - doa, shift, sync_min);  // instances >= 1
             }
             // First relation without a lane/sync path: timing at instance 0 decides 17 vs 18.
             int rel_cls = 0;
@@ -326,8 +344,8 @@ size_t tma_smem_bytes(int n_ops) { return 4 * static_cast<size_t>(n_ops) * kTile
 
 bool periodic_tma_supported(const DevProblem& p, const DevPeriodic& b) {
     const auto aligned = [](const void* ptr) { return (reinterpret_cast<uintptr_t>(ptr) & 15) == 0; };
-    return p.n_ops <= kMaxTmaOps && b.stride % 8 == 0 && aligned(b.prologue_delta) && aligned(b.offset_delta) &&
-           b.n < (1LL << 31) && encode_fn() != nullptr;
+    return p.n_ops <= kMaxTmaOps && p.iterations <= kMaxProgDistance && b.stride % 8 == 0 && aligned(b.prologue_delta) &&
+           aligned(b.offset_delta) && b.n < (1LL << 31) && encode_fn() != nullptr;
 }
 
 namespace {

@@ -33,7 +33,6 @@ namespace {
 constexpr int kTile = kTmaTile;     // candidates per CTA tile = threads per CTA
 constexpr int kMaxTmaOps = 256;     // TMA box height limit
 constexpr long long kWaitSpins = 1LL << 22;
-constexpr int kProgCache = 48;      // sync-program entries of the cached frame
 
 __device__ __forceinline__ uint32_t smem_addr(const void* p) {
     return static_cast<uint32_t>(__cvta_generic_to_shared(p));
@@ -188,17 +187,7 @@ __global__ void __launch_bounds__(kTile) verify_periodic_tma_kernel(DevProblem p
     int16_t* tp = reinterpret_cast<int16_t*>(smem);             // [N][kTile] prologue deltas
     int16_t* to = tp + N * kTile;                               // [N][kTile] offset deltas
     int4* opc = reinterpret_cast<int4*>(smem + 4 * N * kTile);  // [N] issue, latency, base starts
-    // Cache of the frame most candidates of recent tiles use: its walk order, lane lengths,
-    // structural verdict and sync program. Threads whose frame it is read it from shared
-    // memory; the others read the frame table, through the same generic pointers, so a
-    // warp with mixed frames does not diverge.
-    uint16_t* c_order = reinterpret_cast<uint16_t*>(opc + N);         // [round8(N)]
-    uint16_t* c_lens = c_order + ((N + 7) & ~7);                      // [16]
-    int4* c_prog = reinterpret_cast<int4*>(c_lens + 16);              // [kProgCache]
-    int4* c_head = c_prog + kProgCache;                               // class, flags, unreached, set
-    int4* c_meta = c_head + 1;                                        // program length, tail class, cached?
-    uint64_t* bar = reinterpret_cast<uint64_t*>(c_meta + 1);
-    int cached_frame = -1;
+    uint64_t* bar = reinterpret_cast<uint64_t*>(opc + N);
 
     bool base_ok = true;
     for (int s = t; s < N; s += kTile) {
@@ -226,29 +215,7 @@ __global__ void __launch_bounds__(kTile) verify_periodic_tma_kernel(DevProblem p
         const bool live = c < b.n;
         const int f_in = live ? b.frame[c] : 0;
         const int ii = live ? b.ii[c] : 0;
-        // The tile's leading frame is cached when it holds the majority of the tile.
-        const long long c0 = static_cast<long long>(tile) * kTile;
-        const int f_lead = b.frame[c0];
-        const int live_count = static_cast<int>(b.n - c0 < kTile ? b.n - c0 : kTile);
-        const int votes = __syncthreads_count(live && f_in == f_lead);
-        const bool restage = 2 * votes > live_count && f_lead != cached_frame &&
-                             static_cast<unsigned>(f_lead) < static_cast<unsigned>(fr.n_frames);
-        if (restage) {
-            const int set = fr.sync_set[f_lead];
-            const bool set_ok = static_cast<unsigned>(set) < static_cast<unsigned>(fr.n_sync_sets);
-            const int2 meta = set_ok ? ft.set_meta[set] : make_int2(0, TFV_CLASS_BAD_PACKING);
-            const bool prog_fits = meta.x <= kProgCache;
-            for (int j = t; j < N; j += kTile) c_order[j] = ft.order[static_cast<size_t>(f_lead) * N + j];
-            if (t < 16) c_lens[t] = ft.lane_len[static_cast<size_t>(f_lead) * 16 + t];
-            if (prog_fits)
-                for (int k = t; k < meta.x; k += kTile) c_prog[k] = ft.set_prog[fr.sync_offsets[set] + k];
-            if (t == 0) {
-                *c_head = make_int4(ft.frame_class[f_lead], ft.frame_flags[f_lead], ft.first_unreached[f_lead], set);
-                *c_meta = make_int4(meta.x, meta.y, prog_fits ? 1 : 0, 0);
-            }
-            cached_frame = f_lead;
-        }
-        const bool landed = __syncthreads_and(mbar_wait_bounded(bar, phase));  // also publishes the cache
+        const bool landed = __syncthreads_and(mbar_wait_bounded(bar, phase));
         if (!landed) {  // report, drain the copy (bounded) and leave
             if (live) {
                 out.verdict[c] = TFV_CLASS_DEVICE_TIMEOUT;
@@ -264,30 +231,18 @@ __global__ void __launch_bounds__(kTile) verify_periodic_tma_kernel(DevProblem p
             const int16_t* mo = to + t;
             const bool frame_ok = static_cast<unsigned>(f_in) < static_cast<unsigned>(fr.n_frames);
             const int f = frame_ok ? f_in : 0;
-            const bool hit = frame_ok && f == cached_frame;
-            const int4 head = hit ? *c_head
-                                  : make_int4(frame_ok ? ft.frame_class[f] : TFV_CLASS_BAD_PACKING, ft.frame_flags[f],
-                                              ft.first_unreached[f], fr.sync_set[f]);
-            const int fclass = frame_ok ? head.x : TFV_CLASS_BAD_PACKING;
+            const int fclass = frame_ok ? ft.frame_class[f] : TFV_CLASS_BAD_PACKING;
             Extremes x{INT_MAX, INT_MAX, INT_MIN, INT_MIN};
             const char* row_p = reinterpret_cast<const char*>(mp);
             const int to_bytes = N * kTmaRowBytes;
-            const uint16_t* order = hit ? c_order : ft.order + static_cast<size_t>(f) * N;
-            const uint16_t* lens = hit ? c_lens : ft.lane_len + static_cast<size_t>(f) * 16;
-            const int lane_min = walk_lanes<kBodyRows>(order, lens, opc, row_p, to_bytes, N, ii, x);
+            const int lane_min = walk_lanes<kBodyRows>(ft.order + static_cast<size_t>(f) * N,
+                                                       ft.lane_len + static_cast<size_t>(f) * 16, opc, row_p, to_bytes,
+                                                       N, ii, x);
             // Sync edges before the set's first static failure, base starts folded in.
-            const int set = head.w;
-            int2 meta;
-            const int4* prog;
-            if (hit) {
-                const int4 cm = *c_meta;
-                meta = make_int2(cm.x, cm.y);
-                prog = cm.z ? c_prog : ft.set_prog + (cm.x > 0 ? fr.sync_offsets[set] : 0);
-            } else {
-                meta = (static_cast<unsigned>(set) < static_cast<unsigned>(fr.n_sync_sets))
-                           ? ft.set_meta[set] : make_int2(0, TFV_CLASS_BAD_PACKING);
-                prog = ft.set_prog + (meta.x > 0 ? fr.sync_offsets[set] : 0);
-            }
+            const int set = fr.sync_set[f];
+            const int2 meta = (static_cast<unsigned>(set) < static_cast<unsigned>(fr.n_sync_sets))
+                                  ? ft.set_meta[set] : make_int2(0, TFV_CLASS_BAD_PACKING);
+            const int4* prog = ft.set_prog + (meta.x > 0 ? fr.sync_offsets[set] : 0);
             int sync_min = INT_MAX;
 #pragma unroll 4
             for (int k = 0; k < meta.x; ++k) {
@@ -304,7 +259,7 @@ __global__ void __launch_bounds__(kTile) verify_periodic_tma_kernel(DevProblem p
             }
             // First relation without a lane/sync path: timing at instance 0 decides 17 vs 18.
             int rel_cls = 0;
-            const int r = head.z;
+            const int r = ft.first_unreached[f];
             if (r >= 0) {
                 const int packed = p.relation[r];
                 const int a = packed & 0xFFF, bb = (packed >> 12) & 0xFFF, d = packed >> 24;
@@ -341,7 +296,7 @@ __global__ void __launch_bounds__(kTile) verify_periodic_tma_kernel(DevProblem p
             else if (lane_min < 0) cls = TFV_CLASS_LANE_ORDER;
             else if (sync_min < 0) cls = TFV_CLASS_SYNC_INEQUALITY;
             else if (meta.y != 0) cls = meta.y;
-            else if (head.y & kFrameRegisterCross) cls = TFV_CLASS_REGISTER_CROSSES_LANES;
+            else if (ft.frame_flags[f] & kFrameRegisterCross) cls = TFV_CLASS_REGISTER_CROSSES_LANES;
             else if (rel_cls) cls = rel_cls;
             else if (carried_bad) cls = TFV_CLASS_CARRIED_SHARED_LIFETIME;
             else cls = (p.n_resources > 0 && resources_exceed(p, opc, mp, mo, ii)) ? TFV_CLASS_RESOURCE_CAPACITY
@@ -383,10 +338,7 @@ bool make_map(CUtensorMap* map, const int16_t* base, long long n, long long stri
     return r == CUDA_SUCCESS;
 }
 
-size_t tma_smem_bytes(int n_ops) {
-    const size_t n = static_cast<size_t>(n_ops);
-    return 4 * n * kTile + 16 * n + 2 * ((n + 7) & ~static_cast<size_t>(7)) + 32 + 16 * (kProgCache + 2) + 16;
-}
+size_t tma_smem_bytes(int n_ops) { return 4 * static_cast<size_t>(n_ops) * kTile + 16 * static_cast<size_t>(n_ops) + 16; }
 
 }  // namespace
 

@@ -95,3 +95,34 @@ def raw_mutations(packed, witness, count: int, seed: int):
                     r[4] -= r[0] * cut
         out.append((lanes, sync, [tuple(r) for r in rows]))
     return out
+
+
+def resource_heavy(seed: int, count: int):
+    """A problem without dependencies whose candidates overlap iterations freely.
+
+    Every operation reads only the external input, so there are no relations and sync is
+    empty; lanes hold one or a few operations. Random prologue/offset starts and IIs make
+    the resource capacity (class 20) the deciding check for most candidates, with the
+    middle/boundary iterations of the periodic demand all exercised.
+    """
+    from tilefoundry_b200 import pack_problem
+    from tilefoundry_b200.batch import FrameSet, PeriodicBatch
+
+    rng = np.random.default_rng(seed)
+    n = int(rng.integers(2, 16))
+    problem = random_dag_problem(
+        n, layers=1, lanes=n, n_resources=int(rng.integers(1, 4)), iterations=int(rng.choice([1, 2, 3, 5, 8, 13])),
+        seed=seed, latency=(2, 40), capacity=(2, int(rng.integers(6, 40))), demand=(1, 4), windows_per_op=(1, 3),
+        carried=0.0, declared=0.0,
+    )
+    packed = pack_problem(problem)
+    frames = FrameSet(packed)
+    frame = frames.add([[op] for op in packed.op_ids], [])  # one operation per lane
+    span = int(packed.latency.max()) * 3
+    issue = packed.issue.astype(np.int64)
+    ii = rng.integers(int(issue.max()), span, size=count)
+    prologue = rng.integers(0, span, size=(count, n))
+    slack = np.maximum(ii[:, None] - issue[None, :], 0)
+    offset = prologue + (rng.random((count, n)) * (slack + 1)).astype(np.int64)  # wrap edges hold
+    batch = PeriodicBatch.from_starts(prologue, offset, ii, np.full(count, frame))
+    return problem, packed, frames, batch

@@ -218,3 +218,42 @@ def test_tma_and_plain_load_paths_agree_with_oracle(verifiers, n):
     assert np.array_equal(verdict, ov)
     assert np.array_equal(makespan, om)
     assert np.array_equal(ii, oi)
+
+
+@pytest.mark.parametrize("seed", range(16))
+def test_resource_capacity_matches_oracle(seed):
+    from random_cases import resource_heavy
+
+    problem, packed, frames, batch = resource_heavy(seed, 4000)
+    with WarpgroupVerifier(packed) as verifier:
+        verdict, makespan, ii = verifier.verify_periodic(frames, batch)
+    oracle = OracleProblem(load_problem(problem_to_json(problem)))
+    p, o = absolute_starts(batch)
+    ov, om, oi = oracle.classify_periodic(p, o, batch.ii, frames.frames, batch.frame)
+    assert np.array_equal(verdict, ov)
+    assert np.array_equal(makespan, om)
+    assert np.array_equal(ii, oi)
+
+
+@pytest.mark.parametrize("name,count", [("gemm", 4000), ("fa", 4000), ("dag", 300), ("stress", 3)])
+def test_kernel_body_configs_match_oracle(name, count):
+    """The GEMM mainloop, FlashAttention, 256-op DAG and 1024-op stress bodies (global-read kernel)."""
+    from tilefoundry_b200 import workloads
+
+    problem = {
+        "gemm": workloads.gemm_mainloop_problem,
+        "fa": workloads.flash_attention_problem,
+        "dag": workloads.dag_problem,
+        "stress": workloads.stress_problem,
+    }[name]()
+    packed = pack_problem(problem)
+    witness = workloads.list_schedule_witness(packed, seed=1)
+    frames, batch = neighbourhood(packed, witness, count, seed=3, jitter=64)
+    with WarpgroupVerifier(packed) as verifier:
+        verdict, makespan, ii = verifier.verify_periodic(frames, batch)
+    oracle = OracleProblem(load_problem(problem_to_json(problem)))
+    p, o = absolute_starts(batch)
+    ov, om, oi = oracle.classify_periodic(p, o, batch.ii, frames.frames, batch.frame)
+    assert np.array_equal(verdict, ov)
+    assert np.array_equal(makespan, om)
+    assert np.array_equal(ii, oi)

@@ -268,8 +268,7 @@ int tfv_problem_create(const tfv_problem_desc* d, int device, tfv_problem** out)
     dp.res_win_amount = base + o_wam;
     dp.res_win_duration = base + o_wdu;
 
-    if (tfv::analyze_smem_bytes(N, L) > static_cast<size_t>(p->max_smem_optin) ||
-        tfv::periodic_tile(N) == 0) {
+    if (tfv::analyze_smem_bytes(N, L) > static_cast<size_t>(p->max_smem_optin)) {
         cudaFree(p->buffer);
         delete p;
         return fail(TFV_ERR_UNSUPPORTED, "problem with %d ops and %d lanes exceeds shared memory", N, L);

@@ -28,6 +28,7 @@
 #include <cstdint>
 
 #include "tfv_device.cuh"
+#include "tfv_resources.cuh"
 
 namespace tfv {
 
@@ -39,10 +40,6 @@ __host__ __device__ inline size_t align16(size_t x) { return (x + 15) & ~static_
 
 __device__ __forceinline__ int lane_of(uint16_t v) { return v >> TFV_LANE_SHIFT; }
 __device__ __forceinline__ int pos_of(uint16_t v) { return v & TFV_POS_MASK; }
-
-__device__ __forceinline__ int floor_div(int u, int d) {  // d > 0
-    return u >= 0 ? u / d : -((-u + d - 1) / d);
-}
 
 }  // namespace
 
@@ -424,46 +421,32 @@ size_t periodic_smem_bytes(const DevProblem& p, int tile) {
 
 namespace {
 
-// Demand of resource window w at time t, counting every iteration's copy
-// (verify.py:183-200 nets +amount at start and -amount at start + duration).
-__device__ __forceinline__ int window_cover(int t, int p0, int o, int dur, int ii, int I) {
-    int count = (p0 <= t && t < p0 + dur) ? 1 : 0;
-    if (I == 2) {
-        const int s = o + ii;
-        count += (s <= t && t < s + dur) ? 1 : 0;
-    } else if (I >= 3) {
-        const int u = t - o;
-        const int hi = min(floor_div(u, ii), I - 1);
-        const int lo = max(floor_div(u - dur, ii) + 1, 1);
-        count += max(0, hi - lo + 1);
-    }
-    return count;
-}
+// Candidate values staged as int32 in shared memory, column t of an [N][T] tile.
+struct StagedView {
+    const int* P;
+    const int* O;
+    int T;
+    __device__ __forceinline__ int p(int a) const { return P[a * T]; }
+    __device__ __forceinline__ int o(int a) const { return O[a * T]; }
+};
 
-__device__ int periodic_resources(const DevProblem& p, const int* P, const int* O, int T, int ii, int I) {
-    for (int q = 0; q < p.n_resources; ++q) {
-        const int w0 = p.res_offsets[q], w1 = p.res_offsets[q + 1];
-        const int cap = p.capacity[q];
-        for (int v = w0; v < w1; ++v) {
-            const int x = p.res_win_op[v];
-            for (int j = 0; j < I; ++j) {
-                const int t = (j == 0) ? P[x * T] : O[x * T] + j * ii;
-                int demand = 0;
-                for (int w = w0; w < w1; ++w) {
-                    const int y = p.res_win_op[w];
-                    demand += p.res_win_amount[w] * window_cover(t, P[y * T], O[y * T], p.res_win_duration[w], ii, I);
-                }
-                if (demand > cap) return TFV_CLASS_RESOURCE_CAPACITY;
-            }
-        }
-    }
-    return 0;
-}
+// Candidate values read from the op-major delta arrays in global memory (any N).
+struct GlobalView {
+    const int* bp;  // base starts in shared memory
+    const int* bo;
+    const int16_t* dp;
+    const int16_t* dq;
+    long long stride;
+    long long c;
+    __device__ __forceinline__ int p(int a) const { return bp[a] + dp[a * stride + c]; }
+    __device__ __forceinline__ int o(int a) const { return bo[a] + dq[a * stride + c]; }
+};
 
 // Checks 10..20 of one periodic candidate whose times are in range and whose frame is
-// structurally valid. P/O point at the candidate's column (stride T) in shared memory.
-__device__ int periodic_checks(const DevProblem& p, const DevFrames& fr, const FrameTable& ft, int f,
-                               const int* P, const int* O, int T, const int* issue, const int* lat, int ii) {
+// structurally valid.
+template <class View>
+__device__ int periodic_checks(const DevProblem& p, const DevFrames& fr, const FrameTable& ft, int f, const View& V,
+                               const int* issue, const int* lat, int ii) {
     const int N = p.n_ops;
     const int I = p.iterations;
     if (I >= 3 && ii <= 0) return TFV_CLASS_II_NONPOSITIVE;  // verify.py:262-264
@@ -474,13 +457,13 @@ __device__ int periodic_checks(const DevProblem& p, const DevFrames& fr, const F
     bool lane_bad = false;
     for (int a = 0; a < N; ++a) {
         const int s = succ[a];
-        const int pa = P[a * T] + issue[a];
-        const int oa = O[a * T] + issue[a];
+        const int pa = V.p(a) + issue[a];
+        const int oa = V.o(a) + issue[a];
         if (!(s & kWrap)) {
-            lane_bad |= pa > P[s * T];
-            lane_bad |= (I >= 2) & (oa > O[s * T]);
+            lane_bad |= pa > V.p(s);
+            lane_bad |= (I >= 2) & (oa > V.o(s));
         } else {
-            const int next = O[(s & kSuccMask) * T] + ii;
+            const int next = V.o(s & kSuccMask) + ii;
             lane_bad |= (I >= 2) & (pa > next);
             lane_bad |= (I >= 3) & (oa > next);
         }
@@ -494,11 +477,11 @@ __device__ int periodic_checks(const DevProblem& p, const DevFrames& fr, const F
         const int a = fr.sync_edges[3 * k], b = fr.sync_edges[3 * k + 1], d = fr.sync_edges[3 * k + 2];
         if (a < 0 || b < 0) return TFV_CLASS_SYNC_UNKNOWN_OP;
         if (d >= I) return TFV_CLASS_SYNC_NO_INSTANCE;
-        const int ready0 = P[a * T] + lat[a];
+        const int ready0 = V.p(a) + lat[a];
         const int shift = d * ii;
-        const int target0 = (d == 0) ? P[b * T] : O[b * T] + shift;
+        const int target0 = (d == 0) ? V.p(b) : V.o(b) + shift;
         if (ready0 > target0) return TFV_CLASS_SYNC_INEQUALITY;
-        if (I - d >= 2 && O[a * T] + lat[a] > O[b * T] + shift) return TFV_CLASS_SYNC_INEQUALITY;
+        if (I - d >= 2 && V.o(a) + lat[a] > V.o(b) + shift) return TFV_CLASS_SYNC_INEQUALITY;
     }
 
     if (ft.frame_flags[f] & kFrameRegisterCross) return TFV_CLASS_REGISTER_CROSSES_LANES;
@@ -507,19 +490,51 @@ __device__ int periodic_checks(const DevProblem& p, const DevFrames& fr, const F
     if (r >= 0) {
         const int packed = p.relation[r];
         const int a = packed & 0xFFF, b = (packed >> 12) & 0xFFF, d = packed >> 24;
-        const int target = (d == 0) ? P[b * T] : O[b * T] + ii;
-        return (P[a * T] + lat[a] > target) ? TFV_CLASS_RELATION_TIMING : TFV_CLASS_RELATION_NO_PATH;
+        const int target = (d == 0) ? V.p(b) : V.o(b) + ii;
+        return (V.p(a) + lat[a] > target) ? TFV_CLASS_RELATION_TIMING : TFV_CLASS_RELATION_NO_PATH;
     }
 
     if (I >= 2) {  // verify.py:315-318, iterations 1..I-1 share the periodic offsets
         for (int k = 0; k < p.n_carried; ++k) {
             const int packed = p.carried[k];
             const int u = packed & 0xFFFF, df = packed >> 16;
-            if (O[u * T] + lat[u] > O[df * T]) return TFV_CLASS_CARRIED_SHARED_LIFETIME;
+            if (V.o(u) + lat[u] > V.o(df)) return TFV_CLASS_CARRIED_SHARED_LIFETIME;
         }
     }
-    if (p.n_resources > 0) return periodic_resources(p, P, O, T, ii, I);
+    if (p.n_resources > 0 && periodic_resources_exceed(p, V, ii)) return TFV_CLASS_RESOURCE_CAPACITY;
     return TFV_CLASS_PASS;
+}
+
+// Verdict, makespan and II of one periodic candidate from its start extremes.
+template <class View>
+__device__ void finish_candidate(const DevProblem& p, const DevFrames& fr, const FrameTable& ft, const View& V,
+                                 const int* issue, const int* lat, int f, int ii, int min_p, int max_pl, int min_o,
+                                 int max_ol, DevResults out, long long c) {
+    const int I = p.iterations;
+    // Starts of iterations >= 1 are offset + i * ii: extremes at i = 1 and i = I - 1.
+    long long makespan = max_pl;
+    bool negative = min_p < 0;
+    bool out_of_range = false;
+    if (I >= 2) {
+        const long long k1 = ii, kl = static_cast<long long>(I - 1) * ii;
+        const long long lo = k1 < kl ? k1 : kl, hi = k1 < kl ? kl : k1;
+        negative |= static_cast<long long>(min_o) + lo < 0;
+        const long long body = static_cast<long long>(max_ol) + hi;
+        makespan = makespan > body ? makespan : body;
+        out_of_range |= hi >= TFV_TIME_LIMIT || lo <= -static_cast<long long>(TFV_TIME_LIMIT);
+    }
+    out_of_range |= makespan >= TFV_TIME_LIMIT;
+    int cls;
+    const bool frame_ok = static_cast<unsigned>(f) < static_cast<unsigned>(fr.n_frames);
+    const int fclass = frame_ok ? ft.frame_class[f] : TFV_CLASS_BAD_PACKING;
+    if (fclass == TFV_CLASS_BAD_PACKING) cls = TFV_CLASS_BAD_PACKING;
+    else if (fclass == TFV_CLASS_SCHEDULE_MALFORMED || negative) cls = TFV_CLASS_SCHEDULE_MALFORMED;
+    else if (out_of_range) cls = TFV_CLASS_OUT_OF_RANGE;
+    else if (fclass != 0) cls = fclass;
+    else cls = periodic_checks(p, fr, ft, f, V, issue, lat, ii);
+    out.verdict[c] = cls;
+    out.makespan[c] = makespan > INT_MAX ? INT_MAX : (makespan < INT_MIN ? INT_MIN : static_cast<int>(makespan));
+    out.ii[c] = I >= 3 ? ii : 0;
 }
 
 }  // namespace
@@ -527,7 +542,6 @@ __device__ int periodic_checks(const DevProblem& p, const DevFrames& fr, const F
 __global__ void verify_periodic_kernel(DevProblem p, DevFrames fr, FrameTable ft, DevPeriodic b, DevResults out) {
     extern __shared__ __align__(16) int psm[];
     const int N = p.n_ops;
-    const int I = p.iterations;
     const int T = blockDim.x;
     const int t = threadIdx.x;
     int* issue_s = psm;
@@ -549,8 +563,6 @@ __global__ void verify_periodic_kernel(DevProblem p, DevFrames fr, FrameTable ft
         if (c >= b.n) continue;
         int* P = Ps + t;
         int* O = Os + t;
-        const int f = b.frame[c];
-        const int ii = b.ii[c];
         int min_p = INT_MAX, max_pl = INT_MIN, min_o = INT_MAX, max_ol = INT_MIN;
         for (int a = 0; a < N; ++a) {
             const int pv = bp_s[a] + b.prologue_delta[a * b.stride + c];
@@ -562,32 +574,39 @@ __global__ void verify_periodic_kernel(DevProblem p, DevFrames fr, FrameTable ft
             min_o = min(min_o, ov);
             max_ol = max(max_ol, ov + lat_s[a]);
         }
-        // Starts of iterations >= 1 are offset + i * ii: extremes at i = 1 and i = I - 1.
-        long long makespan = max_pl;
-        bool negative = min_p < 0;
-        bool out_of_range = false;
-        if (I >= 2) {
-            const long long k1 = ii, kl = static_cast<long long>(I - 1) * ii;
-            const long long lo = k1 < kl ? k1 : kl, hi = k1 < kl ? kl : k1;
-            negative |= static_cast<long long>(min_o) + lo < 0;
-            const long long body = static_cast<long long>(max_ol) + hi;
-            makespan = makespan > body ? makespan : body;
-            out_of_range |= hi >= TFV_TIME_LIMIT || lo <= -static_cast<long long>(TFV_TIME_LIMIT);
+        finish_candidate(p, fr, ft, StagedView{P, O, T}, issue_s, lat_s, b.frame[c], b.ii[c], min_p, max_pl, min_o,
+                         max_ol, out, c);
+    }
+}
+
+// Any number of operations: values are read from the delta arrays on demand.
+__global__ void __launch_bounds__(128) verify_periodic_global_kernel(DevProblem p, DevFrames fr, FrameTable ft,
+                                                                      DevPeriodic b, DevResults out) {
+    extern __shared__ __align__(16) int gsm[];
+    const int N = p.n_ops;
+    int* issue_s = gsm;
+    int* lat_s = gsm + N;
+    int* bp_s = gsm + 2 * N;
+    int* bo_s = gsm + 3 * N;
+    for (int a = threadIdx.x; a < N; a += blockDim.x) {
+        issue_s[a] = p.issue[a];
+        lat_s[a] = p.latency[a];
+        bp_s[a] = b.base_prologue[a];
+        bo_s[a] = b.base_offset[a];
+    }
+    __syncthreads();
+    const long long step = static_cast<long long>(gridDim.x) * blockDim.x;
+    for (long long c = static_cast<long long>(blockIdx.x) * blockDim.x + threadIdx.x; c < b.n; c += step) {
+        const GlobalView V{bp_s, bo_s, b.prologue_delta, b.offset_delta, b.stride, c};
+        int min_p = INT_MAX, max_pl = INT_MIN, min_o = INT_MAX, max_ol = INT_MIN;
+        for (int a = 0; a < N; ++a) {
+            const int pv = V.p(a), ov = V.o(a);
+            min_p = min(min_p, pv);
+            max_pl = max(max_pl, pv + lat_s[a]);
+            min_o = min(min_o, ov);
+            max_ol = max(max_ol, ov + lat_s[a]);
         }
-        out_of_range |= makespan >= TFV_TIME_LIMIT;
-
-        int cls;
-        const bool frame_ok = static_cast<unsigned>(f) < static_cast<unsigned>(fr.n_frames);
-        const int fclass = frame_ok ? ft.frame_class[f] : TFV_CLASS_BAD_PACKING;
-        if (fclass == TFV_CLASS_BAD_PACKING) cls = TFV_CLASS_BAD_PACKING;
-        else if (fclass == TFV_CLASS_SCHEDULE_MALFORMED || negative) cls = TFV_CLASS_SCHEDULE_MALFORMED;
-        else if (out_of_range) cls = TFV_CLASS_OUT_OF_RANGE;
-        else if (fclass != 0) cls = fclass;
-        else cls = periodic_checks(p, fr, ft, f, P, O, T, issue_s, lat_s, ii);
-
-        out.verdict[c] = cls;
-        out.makespan[c] = makespan > INT_MAX ? INT_MAX : (makespan < INT_MIN ? INT_MIN : static_cast<int>(makespan));
-        out.ii[c] = I >= 3 ? ii : 0;
+        finish_candidate(p, fr, ft, V, issue_s, lat_s, b.frame[c], b.ii[c], min_p, max_pl, min_o, max_ol, out, c);
     }
 }
 
@@ -595,7 +614,18 @@ cudaError_t launch_verify_periodic(const DevProblem& p, const DevFrames& f, Fram
                                    DevResults r, int sm_count, cudaStream_t stream) {
     if (b.n <= 0) return cudaSuccess;
     const int tile = periodic_tile(p.n_ops);
-    if (tile == 0) return cudaErrorInvalidValue;
+    if (tile == 0) {  // too many operations to stage a tile: read the deltas on demand
+        const size_t smem = static_cast<size_t>(4) * p.n_ops * sizeof(int);
+        if (smem > 48 * 1024) {
+            cudaError_t e = cudaFuncSetAttribute(verify_periodic_global_kernel,
+                                                 cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(smem));
+            if (e != cudaSuccess) return e;
+        }
+        const long long blocks = (b.n + 127) / 128;
+        const long long cap = static_cast<long long>(sm_count) * 16;
+        verify_periodic_global_kernel<<<static_cast<int>(blocks < cap ? blocks : cap), 128, smem, stream>>>(p, f, t, b, r);
+        return cudaGetLastError();
+    }
     const size_t smem = periodic_smem_bytes(p, tile);
     if (smem > 48 * 1024) {
         cudaError_t e = cudaFuncSetAttribute(verify_periodic_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,

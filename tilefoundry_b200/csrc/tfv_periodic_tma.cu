@@ -25,6 +25,7 @@
 #include <cudaTypedefs.h>
 
 #include "tfv_device.cuh"
+#include "tfv_resources.cuh"
 
 namespace tfv {
 
@@ -78,13 +79,6 @@ struct Extremes {
     int max_pl, max_ol;  // largest prologue / body-offset completion
 };
 
-__device__ __forceinline__ void take(Extremes& x, int p, int o, int lat) {
-    x.min_p = min(x.min_p, p);
-    x.min_o = min(x.min_o, o);
-    x.max_pl = max(x.max_pl, p + lat);
-    x.max_ol = max(x.max_ol, o + lat);
-}
-
 // One pass over the frame's operations lane by lane (order/lane_len of the frame table).
 // Returns the smallest slack of every lane-order inequality (verify.py:99-112, 278-282):
 // same-iteration pairs in the prologue row (start) and the periodic rows (offset), and
@@ -137,43 +131,14 @@ __device__ __forceinline__ int walk_lanes(const uint16_t* order, const uint16_t*
     return lane_min;
 }
 
-__device__ __forceinline__ int cover(int t, int p0, int o, int dur, int ii, int I) {
-    int count = (p0 <= t && t < p0 + dur) ? 1 : 0;
-    if (I == 2) {
-        const int s = o + ii;
-        count += (s <= t && t < s + dur) ? 1 : 0;
-    } else if (I >= 3) {
-        const int u = t - o;
-        const int hi = min(u >= 0 ? u / ii : -((-u + ii - 1) / ii), I - 1);
-        const int v = u - dur;
-        const int lo = max((v >= 0 ? v / ii : -((-v + ii - 1) / ii)) + 1, 1);
-        count += max(0, hi - lo + 1);
-    }
-    return count;
-}
-
-// verify.py:183-200 on the periodic rows: demand at every window start.
-__device__ bool resources_exceed(const DevProblem& p, const int4* opc, const int16_t* tp, const int16_t* to, int ii) {
-    const int I = p.iterations;
-    for (int q = 0; q < p.n_resources; ++q) {
-        const int w0 = p.res_offsets[q], w1 = p.res_offsets[q + 1];
-        const int cap = p.capacity[q];
-        for (int v = w0; v < w1; ++v) {
-            const int x = p.res_win_op[v];
-            for (int j = 0; j < I; ++j) {
-                const int t = j == 0 ? opc[x].z + tp[x * kTile] : opc[x].w + to[x * kTile] + j * ii;
-                int demand = 0;
-                for (int w = w0; w < w1; ++w) {
-                    const int y = p.res_win_op[w];
-                    demand += p.res_win_amount[w] *
-                              cover(t, opc[y].z + tp[y * kTile], opc[y].w + to[y * kTile], p.res_win_duration[w], ii, I);
-                }
-                if (demand > cap) return true;
-            }
-        }
-    }
-    return false;
-}
+// Candidate values of thread t's tile column: base start + int16 delta.
+struct TileView {
+    const int4* opc;
+    const int16_t* mp;
+    const int16_t* mo;
+    __device__ __forceinline__ int p(int a) const { return opc[a].z + mp[a * kTile]; }
+    __device__ __forceinline__ int o(int a) const { return opc[a].w + mo[a * kTile]; }
+};
 
 template <int kBodyRows>
 __global__ void __launch_bounds__(kTile) verify_periodic_tma_kernel(DevProblem p, DevFrames fr, FrameTable ft,
@@ -299,8 +264,8 @@ __global__ void __launch_bounds__(kTile) verify_periodic_tma_kernel(DevProblem p
             else if (ft.frame_flags[f] & kFrameRegisterCross) cls = TFV_CLASS_REGISTER_CROSSES_LANES;
             else if (rel_cls) cls = rel_cls;
             else if (carried_bad) cls = TFV_CLASS_CARRIED_SHARED_LIFETIME;
-            else cls = (p.n_resources > 0 && resources_exceed(p, opc, mp, mo, ii)) ? TFV_CLASS_RESOURCE_CAPACITY
-                                                                                 : TFV_CLASS_PASS;
+            else cls = (p.n_resources > 0 && periodic_resources_exceed(p, TileView{opc, mp, mo}, ii))
+                           ? TFV_CLASS_RESOURCE_CAPACITY : TFV_CLASS_PASS;
             out.verdict[c] = cls;
             out.makespan[c] = makespan > INT_MAX ? INT_MAX : (makespan < INT_MIN ? INT_MIN : static_cast<int>(makespan));
             out.ii[c] = kBodyRows >= 2 ? ii : 0;

@@ -279,8 +279,8 @@ def list_schedule_witness(packed: PackedProblem, *, seed: int = 0, lane_of: list
     """A valid periodic witness by list scheduling one iteration.
 
     Lanes follow the declared warp groups (undeclared operations get a seeded lane);
-    each lane runs its operations in index order, which is a topological order of every
-    same-iteration constraint of the problems built here. Operations start as early as
+    each lane runs its operations in a topological order of the same-iteration
+    constraints (distance-0 relations and carried-lifetime pairs). Operations start as early as
     their lane predecessor's issue end, their distance-0 relations' completions, the
     carried-lifetime users' completions and the resource capacities allow. Body
     iterations repeat the prologue one span later (offset = prologue, II = span), so
@@ -318,7 +318,28 @@ def list_schedule_witness(packed: PackedProblem, *, seed: int = 0, lane_of: list
                     return False
         return True
 
+    # Kahn's algorithm over the same-iteration constraints, smallest index first.
+    import heapq
+
+    succs: list[list[int]] = [[] for _ in range(N)]
+    indeg = [0] * N
     for k in range(N):
+        for a in preds[k]:
+            succs[a].append(k)
+            indeg[k] += 1
+    ready = [k for k in range(N) if indeg[k] == 0]
+    heapq.heapify(ready)
+    topo: list[int] = []
+    while ready:
+        k = heapq.heappop(ready)
+        topo.append(k)
+        for b in succs[k]:
+            indeg[b] -= 1
+            if indeg[b] == 0:
+                heapq.heappush(ready, b)
+    if len(topo) != N:
+        raise ValueError("same-iteration constraints are cyclic: no single-iteration witness exists")
+    for k in topo:
         for q in {w[0] for w in windows[k]}:
             if sum(amount for r, amount, _ in windows[k] if r == q) > int(packed.capacity[q]):
                 raise ValueError(f"operation {packed.op_ids[k]!r} alone exceeds resource {packed.resource_ids[q]!r}")
@@ -335,7 +356,7 @@ def list_schedule_witness(packed: PackedProblem, *, seed: int = 0, lane_of: list
             placed[q].append((t, t + dur, amount))
         lane_tail[lane_of[k]] = k
     span = int((start + packed.latency).max())
-    lanes = [[packed.op_ids[k] for k in range(N) if lane_of[k] == l] for l in range(L)]
+    lanes = [[packed.op_ids[k] for k in topo if lane_of[k] == l] for l in range(L)]
     sync = [(packed.op_ids[a], packed.op_ids[b], int(d)) for a, b, d in packed.relations if d < I]
     return Witness(lanes, sync, start.copy(), start.copy(), max(span, 1))
 
@@ -413,3 +434,97 @@ def neighbourhood(
         frame=frame,
     )
     return frames, batch
+
+
+# ---------------------------------------------------------------------------------------
+# Kernel-body problems: GEMM mainloop and FlashAttention forward
+# ---------------------------------------------------------------------------------------
+
+
+def _body_problem(ops_spec, lanes: int, iterations: int, capacities: dict, iter_args=(), inputs=("%gmem",)):
+    """Closed problem from ``(id, warp_group, issue, latency, [(resource, amount, duration)], out, space, uses)``."""
+    from .model import (
+        LoopIterArg,
+        OperationOutput,
+        ProblemLoop,
+        ProblemOperation,
+        ProgramInput,
+        ResourceCapacity,
+        ResourceWindow,
+        TensorType,
+        ValueRef,
+        ValueUses,
+        WarpgroupProblem,
+    )
+
+    kinds = {"register": "reg", "shared": "smem"}
+    ops = tuple(
+        ProblemOperation(
+            op_id,
+            (OperationOutput(out, kinds[space], ValueUses(tuple(uses))),),
+            wg,
+            issue,
+            latency,
+            tuple(ResourceWindow(r, a, d) for r, a, d in windows),
+        )
+        for op_id, wg, issue, latency, windows, out, space, uses in ops_spec
+    )
+    return WarpgroupProblem(
+        "cycle",
+        lanes,
+        tuple(ResourceCapacity(r, c) for r, c in capacities.items()),
+        (TensorType("gmem", "global"), TensorType("reg", "register"), TensorType("smem", "shared")),
+        tuple(ProgramInput(i, "gmem") for i in inputs),
+        ProblemLoop("%k", iterations, tuple(LoopIterArg(a, ValueRef(y)) for a, y in iter_args), ops),
+    )
+
+
+def gemm_mainloop_problem(iterations: int = 8):
+    """GEMM mainloop body: TMA loads of A (128x64 bf16, 16 KB) and B (256x64 bf16, 32 KB)
+    by the producer warpgroup, a 128x256x64 tcgen05 MMA (latency 512) and a barrier
+    arrive by the consumer, and an epilogue store of the 128x256 fp32 accumulator.
+    Resources: shared memory in KB (227), TMEM columns (512), mbarriers, TMA slots; a
+    4-stage ring bounds the loads in flight through the TMA-slot capacity."""
+    spec = [
+        ("load_a", 0, 24, 700, [("smem_kb", 16, 700), ("tma_slots", 1, 700)], "%a", "shared", ["%gmem"]),
+        ("load_b", 0, 24, 900, [("smem_kb", 32, 900), ("tma_slots", 1, 900)], "%b", "shared", ["%gmem"]),
+        ("mma", 1, 64, 512, [("tmem_cols", 256, 512)], "%acc", "shared", ["%a", "%b", "%acc_prev"]),
+        ("arrive", 1, 4, 4, [("mbarrier", 1, 4)], "%bar", "register", ["%acc"]),
+        ("store", 1, 160, 420, [("smem_kb", 96, 420)], "%out", "register", ["%acc", "%bar"]),
+    ]
+    caps = {"smem_kb": 227, "tmem_cols": 512, "mbarrier": 8, "tma_slots": 8}
+    return _body_problem(spec, 2, iterations, caps, iter_args=[("%acc_prev", "%acc")])
+
+
+def flash_attention_problem(iterations: int = 16):
+    """FlashAttention-forward body (Q 128x128, K/V 128x128 bf16 tiles): loads of K and V
+    (load warpgroup), S = QK^T and P.V MMAs (MMA warpgroup), rowmax, exp2, rowsum and the O
+    rescale (softmax warpgroup). Shared memory 227 KB, TMEM 512 columns."""
+    spec = [
+        ("load_k", 0, 24, 800, [("smem_kb", 32, 800)], "%k", "shared", ["%gmem"]),
+        ("load_v", 0, 24, 800, [("smem_kb", 32, 800)], "%v", "shared", ["%gmem"]),
+        ("qk", 1, 48, 384, [("tmem_cols", 128, 384)], "%s", "shared", ["%gmem", "%k"]),
+        ("rowmax", 2, 90, 110, [], "%m", "register", ["%s", "%m_prev"]),
+        ("exp2", 2, 220, 240, [("smem_kb", 32, 240)], "%p", "shared", ["%s", "%m"]),
+        ("rowsum", 2, 80, 96, [], "%l", "register", ["%p", "%l_prev"]),
+        ("rescale", 2, 140, 160, [("tmem_cols", 128, 160)], "%o_scaled", "shared", ["%o_prev", "%m", "%m_prev"]),
+        ("pv", 1, 48, 384, [("tmem_cols", 128, 384)], "%o", "shared", ["%p", "%v", "%o_scaled"]),
+    ]
+    caps = {"smem_kb": 227, "tmem_cols": 512}
+    return _body_problem(
+        spec, 3, iterations, caps, iter_args=[("%m_prev", "%m"), ("%l_prev", "%l"), ("%o_prev", "%o")]
+    )
+
+
+def dag_problem(seed: int = 0):
+    """Random layered DAG: 256 ops in 16 layers, fan-in 1-4, latencies U[20, 2000],
+    8 warpgroups, 6 resources with capacities U[4, 64] and demands 1-8, 32 iterations."""
+    return random_dag_problem(256, layers=16, lanes=8, n_resources=6, iterations=32, seed=seed)
+
+
+def stress_problem(seed: int = 0):
+    """Stress body: a 1024-op random DAG (same generator), 12 warpgroups, 64 iterations,
+    heavy-tailed demands (Pareto alpha = 1.5, capped at the capacity)."""
+    return random_dag_problem(
+        1024, layers=32, lanes=12, n_resources=6, iterations=64, seed=seed, pareto_alpha=1.5, demand=(1, 8)
+    )

@@ -49,7 +49,8 @@ def parse_args():
     p.add_argument("--steps", type=int, default=20)
     p.add_argument("--warmup", type=int, default=5)
     p.add_argument("--impl", choices=["ours", "reference"], default="ours")
-    p.add_argument("--candidates", type=int, default=1 << 23, help="candidates per GPU")
+    p.add_argument("--workload", choices=sorted(WORKLOADS), default="mla")
+    p.add_argument("--candidates", type=int, default=None, help="candidates per GPU (default per workload)")
     p.add_argument("--seed", type=int, default=2026)
     p.add_argument("--e2e-steps", type=int, default=None)
     p.add_argument("--no-cpu-baseline", action="store_true")
@@ -72,6 +73,43 @@ def mla_workload(n: int, seed: int):
     return problem, packed, frames, batch
 
 
+def body_workload(builder):
+    def make(n: int, seed: int):
+        from tilefoundry_b200 import pack_problem
+        from tilefoundry_b200.workloads import list_schedule_witness, neighbourhood
+
+        problem = builder()
+        packed = pack_problem(problem)
+        witness = list_schedule_witness(packed, seed=1)
+        frames, batch = neighbourhood(packed, witness, n, seed=seed, jitter=64)
+        return problem, packed, frames, batch
+
+    return make
+
+
+def _builder(name):
+    def build():
+        from tilefoundry_b200 import workloads
+
+        return getattr(workloads, name)()
+
+    return build
+
+
+# name: (generator, default candidates per GPU, description)
+WORKLOADS = {
+    "mla": (mla_workload, 1 << 23, "mla-decode-perturbations"),
+    "gemm": (body_workload(_builder("gemm_mainloop_problem")), 1 << 24, "gemm-mainloop-neighbourhood"),
+    "fa": (body_workload(_builder("flash_attention_problem")), 1 << 23, "flash-attention-fwd-neighbourhood"),
+    "dag": (body_workload(_builder("dag_problem")), 1 << 21, "layered-dag-256-neighbourhood"),
+    "stress": (body_workload(_builder("stress_problem")), 1 << 16, "stress-dag-1024-neighbourhood"),
+}
+
+
+def workload(name: str, n: int, seed: int):
+    return WORKLOADS[name][0](n, seed)
+
+
 def algorithmic_bytes_per_candidate(n_ops: int) -> int:
     """Inputs: int16 prologue and offset deltas per op, int32 II and frame; outputs: 3 x int32."""
     return 2 * 2 * n_ops + 4 + 4 + 12
@@ -80,13 +118,15 @@ def algorithmic_bytes_per_candidate(n_ops: int) -> int:
 # --------------------------------------------------------------------------- oracle timing
 
 
+ORACLE_PROBLEM = None  # closed-problem JSON text of the workload, set before the pool starts
+
+
 def _oracle_worker(args):
-    name, chunk = args
-    from golden_data import problem_text
+    text, chunk = args
     from oracle import verify_port as port
     from oracle.problem_doc import load_problem
 
-    problem = load_problem(problem_text(name))
+    problem = load_problem(text)
     return [port.classify(problem, *case)[0] for case in chunk]
 
 
@@ -115,7 +155,7 @@ def time_oracle(pool, workers: int, frames, batch, packed, start: int, count: in
     cases = oracle_sample(frames, batch, packed, start, count)
     chunks = [cases[k::workers] for k in range(workers)]
     t0 = time.perf_counter()
-    list(pool.map(_oracle_worker, [("mla", chunk) for chunk in chunks if chunk]))
+    list(pool.map(_oracle_worker, [(ORACLE_PROBLEM, chunk) for chunk in chunks if chunk]))
     return time.perf_counter() - t0
 
 
@@ -132,8 +172,12 @@ def run_reference(args) -> None:
     if rank != 0:
         return
     pool, workers = make_pool()
+    global ORACLE_PROBLEM
     n = max(4096, args.steps * 64)
-    _problem, packed, frames, batch = mla_workload(n, args.seed)
+    problem, packed, frames, batch = workload(args.workload, n, args.seed)
+    from tilefoundry_b200 import problem_to_json
+
+    ORACLE_PROBLEM = problem_to_json(problem)
     sample = args.cpu_sample or max(16, 4 * workers)
     with pool:
         for w in range(args.warmup):
@@ -156,8 +200,9 @@ def run_reference(args) -> None:
         "scaling": "weak",
         "vs_baseline": None,
         "dtype": "int64",
-        "data": "synthetic: seeded MLA perturbations (same generator and seed as the GPU arm)",
-        "config": {"workload": "mla-decode-perturbations", "ops": 51, "iterations": 16, "warpgroups": 3},
+        "data": "synthetic: seeded candidates of the workload (same generator and seed as the GPU arm)",
+        "config": {"workload": WORKLOADS[args.workload][2], "ops": packed.n_ops, "iterations": packed.iterations,
+                   "warpgroups": packed.warp_groups},
         "cpu_baseline": {
             "value": value,
             "unit": UNIT,
@@ -258,7 +303,7 @@ def run_ours(args) -> None:
     world = int(os.environ.get("WORLD_SIZE", "1"))
     rank = int(os.environ.get("RANK", "0"))
     local = int(os.environ.get("LOCAL_RANK", "0"))
-    want_cpu = world == 1 and rank == 0 and not args.no_cpu_baseline
+    want_cpu = world == 1 and rank == 0 and not args.no_cpu_baseline and args.workload in ("mla", "gemm", "fa")
     pool, workers = make_pool() if want_cpu else (None, 0)  # spawned before any CUDA call
 
     import numpy as np
@@ -277,8 +322,12 @@ def run_ours(args) -> None:
     from tilefoundry_b200 import WarpgroupVerifier
     from tilefoundry_b200.verify import pinned_like
 
-    n = args.candidates
-    _problem, packed, frames, batch = mla_workload(n, args.seed + rank)
+    global ORACLE_PROBLEM
+    n = args.candidates or WORKLOADS[args.workload][1]
+    problem, packed, frames, batch = workload(args.workload, n, args.seed + rank)
+    from tilefoundry_b200 import problem_to_json
+
+    ORACLE_PROBLEM = problem_to_json(problem)
     verifier = WarpgroupVerifier(packed, device=local)
     dframes = verifier.frames_to_device(frames)
     tensors = {
@@ -412,9 +461,10 @@ def run_ours(args) -> None:
             "scaling": "weak",
             "vs_baseline": None,
             "dtype": "int32",
-            "data": "synthetic: seeded perturbations of the MLA example's verified witness (per-rank seed)",
+            "data": ("synthetic: seeded perturbations of the MLA example's verified witness (per-rank seed)"
+                     if args.workload == "mla" else "synthetic: seeded neighbourhood of a list-scheduled witness (per-rank seed)"),
             "config": {
-                "workload": "mla-decode-perturbations",
+                "workload": WORKLOADS[args.workload][2],
                 "candidates_per_gpu": n,
                 "ops": packed.n_ops,
                 "iterations": packed.iterations,
@@ -433,10 +483,10 @@ def run_ours(args) -> None:
                 "peak": peak,
                 "unit": "GB/s",
                 "frac": achieved / peak,
-                "traffic": MEASURED_DRAM_BYTES_PER_CANDIDATE * n,
+                "traffic": MEASURED_DRAM_BYTES_PER_CANDIDATE * n if args.workload == "mla" else None,
                 "traffic_source": "ncu dram__bytes_read+write on 2097152 candidates, scaled per candidate",
                 "peak_source": peak_src,
-                "kernel": "tfv::verify_periodic_tma_kernel",
+                "kernel": "tfv::verify_periodic_tma_kernel" if packed.n_ops <= 256 else "tfv::verify_periodic_global_kernel",
                 "kernel_ms": statistics.mean(verify_ms),
                 "analyze_ms": statistics.mean(analyze_ms),
             },

@@ -126,3 +126,77 @@ def resource_heavy(seed: int, count: int):
     offset = prologue + (rng.random((count, n)) * (slack + 1)).astype(np.int64)  # wrap edges hold
     batch = PeriodicBatch.from_starts(prologue, offset, ii, np.full(count, frame))
     return problem, packed, frames, batch
+
+
+def resource_wide(seed: int, count: int, n_ops: int, n_resources: int, iterations: int = 4, lanes: int = 8):
+    """Many operations on few resources: lanes of back-to-back operations, no dependencies.
+
+    Each candidate draws its own gaps between the operations of a lane (prologue and body
+    separately) and an II above its lane span for 85% of the batch, so the lane order
+    holds for most candidates and the capacity check (class 20) decides them; each
+    capacity is the median peak demand of a sample. With ``n_ops`` above 256 the
+    global-read kernel runs, and a resource with more than 256 windows takes the
+    one-thread-per-candidate path.
+    """
+    from tilefoundry_b200.batch import FrameSet, PeriodicBatch
+
+    rng = np.random.default_rng(seed)
+    problem = random_dag_problem(
+        n_ops, layers=1, lanes=lanes, n_resources=n_resources, iterations=iterations, seed=seed,
+        latency=(30, 200), capacity=(8, 160), demand=(1, 4), windows_per_op=(1, 1), carried=0.0, declared=0.0,
+    )
+    packed = pack_problem(problem)
+    frames = FrameSet(packed)
+    lane_of = np.arange(n_ops) % lanes
+    frame = frames.add([[op for k, op in enumerate(packed.op_ids) if lane_of[k] == l] for l in range(lanes)], [])
+    issue = packed.issue.astype(np.int64)
+
+    def lane_starts():  # back-to-back lanes with per-candidate gaps of 0..7 cycles
+        gaps = issue[None, :] + rng.integers(0, 8, size=(count, n_ops))
+        starts = np.zeros((count, n_ops), dtype=np.int64)
+        ends = np.zeros(count, dtype=np.int64)
+        for l in range(lanes):
+            ks = np.flatnonzero(lane_of == l)
+            run = np.cumsum(gaps[:, ks], axis=1)
+            starts[:, ks] = run - gaps[:, ks]
+            ends = np.maximum(ends, run[:, -1])
+        return starts, ends
+
+    prologue, span_p = lane_starts()
+    offset, span_o = lane_starts()
+    prologue += rng.integers(0, 50, size=(count, 1))
+    offset += rng.integers(0, 50, size=(count, 1))
+    span = np.maximum(span_p, span_o)
+    ii = span + rng.integers(60, 200, size=count)
+    short = rng.random(count) < 0.15
+    ii[short] = (span[short] * rng.uniform(0.5, 1.0, size=int(short.sum()))).astype(np.int64) + 1
+    # Capacity of each resource: the median peak demand of a sample of the candidates, so
+    # that about half of the lane-valid candidates exceed it.
+    import dataclasses
+
+    caps = []
+    for q in range(n_resources):
+        peaks = []
+        for c in np.flatnonzero(~short)[:64]:
+            events: dict[int, int] = {}
+            for k in range(n_ops):
+                for w in range(packed.window_offsets[k], packed.window_offsets[k + 1]):
+                    if packed.window_resource[w] != q:
+                        continue
+                    for i in range(iterations):
+                        s = int(prologue[c, k]) if i == 0 else int(offset[c, k] + i * ii[c])
+                        events[s] = events.get(s, 0) + int(packed.window_amount[w])
+                        events[s + int(packed.window_duration[w])] = events.get(s + int(packed.window_duration[w]), 0) - int(packed.window_amount[w])
+            level = peak = 0
+            for t in sorted(events):
+                level += events[t]
+                peak = max(peak, level)
+            peaks.append(peak)
+        caps.append(max(1, int(np.median(peaks))))
+    resources = tuple(dataclasses.replace(r, capacity=caps[q]) for q, r in enumerate(problem.resources))
+    problem = dataclasses.replace(problem, resources=resources)
+    packed = pack_problem(problem)
+    frames = FrameSet(packed)
+    frame = frames.add([[op for k, op in enumerate(packed.op_ids) if lane_of[k] == l] for l in range(lanes)], [])
+    batch = PeriodicBatch.from_starts(prologue, offset, ii, np.full(count, frame))
+    return problem, packed, frames, batch

@@ -235,6 +235,57 @@ def test_resource_capacity_matches_oracle(seed):
     assert np.array_equal(ii, oi)
 
 
+@pytest.mark.parametrize("seed", range(4))
+def test_resource_capacity_plain_kernel_matches_oracle(seed):
+    """An odd candidate count (stride not a multiple of 8) takes the staged plain-load kernel."""
+    from random_cases import resource_heavy
+
+    torch = _torch()
+    problem, packed, frames, batch = resource_heavy(100 + seed, 3001)
+    with WarpgroupVerifier(packed) as verifier:
+        dev = torch.device("cuda", verifier.device)
+        dframes = verifier.frames_to_device(frames)
+        table = verifier.analyze(dframes)
+        tensors = {
+            key: torch.from_numpy(getattr(batch, key)).to(dev)
+            for key in ("base_prologue", "base_offset", "prologue_delta", "offset_delta", "ii", "frame")
+        }
+        verdict, makespan, ii = (t.cpu().numpy() for t in verifier.verify_periodic_device(dframes, table, tensors))
+    oracle = OracleProblem(load_problem(problem_to_json(problem)))
+    p, o = absolute_starts(batch)
+    ov, om, oi = oracle.classify_periodic(p, o, batch.ii, frames.frames, batch.frame)
+    assert np.array_equal(verdict, ov)
+    assert np.array_equal(makespan, om)
+    assert np.array_equal(ii, oi)
+
+
+@pytest.mark.parametrize(
+    "seed,n_ops,n_resources,iterations",
+    [
+        (0, 100, 1, 4),  # TMA kernel, 100 windows on one resource (several per lane)
+        (1, 60, 2, 13),
+        (2, 300, 2, 5),  # global-read kernel, about 150 windows per resource
+        (3, 300, 1, 3),  # 300 windows on one resource: one thread per candidate
+        (4, 40, 1, 2),
+        (5, 40, 1, 1),
+    ],
+)
+def test_resource_capacity_many_windows_match_oracle(seed, n_ops, n_resources, iterations):
+    from random_cases import resource_wide
+
+    problem, packed, frames, batch = resource_wide(seed, 2000, n_ops, n_resources, iterations)
+    with WarpgroupVerifier(packed) as verifier:
+        verdict, makespan, ii = verifier.verify_periodic(frames, batch)
+    oracle = OracleProblem(load_problem(problem_to_json(problem)))
+    p, o = absolute_starts(batch)
+    ov, om, oi = oracle.classify_periodic(p, o, batch.ii, frames.frames, batch.frame)
+    assert np.array_equal(verdict, ov)
+    assert np.array_equal(makespan, om)
+    assert np.array_equal(ii, oi)
+    classes = set(np.unique(ov).tolist())
+    assert 20 in classes or iterations == 1
+
+
 @pytest.mark.parametrize("name,count", [("gemm", 4000), ("fa", 4000), ("dag", 300), ("stress", 3)])
 def test_kernel_body_configs_match_oracle(name, count):
     """The GEMM mainloop, FlashAttention, 256-op DAG and 1024-op stress bodies (global-read kernel)."""

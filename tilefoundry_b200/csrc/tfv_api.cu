@@ -255,6 +255,8 @@ int tfv_problem_create(const tfv_problem_desc* d, int device, tfv_problem** out)
     dp.n_register_groups = d->n_register_groups;
     dp.n_resources = Q;
     dp.n_windows = static_cast<int>(win_op.size());
+    dp.res_max_windows = 0;
+    for (int q = 0; q < Q; ++q) dp.res_max_windows = std::max(dp.res_max_windows, res_offsets[q + 1] - res_offsets[q]);
     dp.issue = base + o_issue;
     dp.latency = base + o_lat;
     dp.warp_group = base + o_wg;

@@ -33,6 +33,7 @@ struct DevProblem {
     int n_register_groups;
     int n_resources;
     int n_windows;
+    int res_max_windows;  // most windows of any one resource
     // [N] per operation
     const int* issue;       // issue_duration
     const int* latency;     // completion_latency

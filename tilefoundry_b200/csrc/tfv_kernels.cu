@@ -54,6 +54,7 @@ size_t analyze_smem_bytes(int n, int lanes) {
     b += align16(sizeof(int16_t) * n);           // succ
     b += align16(sizeof(int) * n) * 2;           // adjacency [lo, hi) into the sync set
     b += align16(sizeof(uint16_t) * n * lanes) * 2;  // M0, M1
+    b += align16(sizeof(int16_t) * n);           // closure round of each op
     b += sizeof(int) * 32;                       // per-lane counts and starts
     return b;
 }
@@ -84,6 +85,8 @@ __global__ void __launch_bounds__(32) analyze_frames_kernel(DevProblem p, DevFra
     cur += align16(sizeof(uint16_t) * N * L);
     uint16_t* M1 = reinterpret_cast<uint16_t*>(cur);
     cur += align16(sizeof(uint16_t) * N * L);
+    int16_t* round_of = reinterpret_cast<int16_t*>(cur);
+    cur += align16(sizeof(int16_t) * N);
     int* cnt = reinterpret_cast<int*>(cur);
     int* first = cnt + 16;
 
@@ -229,26 +232,72 @@ __global__ void __launch_bounds__(32) analyze_frames_kernel(DevProblem p, DevFra
                 M0[idx] = (lane_of(lp[a]) == l) ? static_cast<uint16_t>(pos_of(lp[a])) : kInfPos;
             }
             __syncwarp();
-            // Closure within one iteration: lane successor and distance-0 sync targets.
-            for (int round = 0; round <= N + 1; ++round) {
-                bool changed = false;
+            // Closure within one iteration over the lane successor and the distance-0 sync
+            // targets. Operations are finished in rounds: an operation whose targets were all
+            // finished in earlier rounds takes their minima once, so each operation is visited
+            // with final inputs (round_of records when). The rounds end after the longest
+            // same-iteration path. Operations left over lie on or above a cycle; then the
+            // plain fixed-point iteration below finishes the closure.
+            for (int a = lane; a < N; a += 32) round_of[a] = -1;
+            __syncwarp();
+            int rounds = 0;
+            bool all_done = false;
+            for (int r = 0; r <= N; ++r) {
+                bool progress = false, left = false;
                 for (int a = lane; a < N; a += 32) {
+                    if (round_of[a] >= 0) continue;
                     const int s = succ[a];
                     const bool same = !(s & kWrap);
                     const int lo = adj_lo[a], hi = adj_hi[a];
+                    bool ready = !same || (round_of[s] >= 0 && round_of[s] < r);
+                    for (int k = lo; k < hi && ready; ++k)
+                        if (E[3 * k + 2] == 0) {
+                            const int t = round_of[E[3 * k + 1]];
+                            ready = t >= 0 && t < r;
+                        }
+                    if (!ready) {
+                        left = true;
+                        continue;
+                    }
                     for (int l = 0; l < L; ++l) {
                         uint16_t m = M0[a * L + l];
                         if (same) m = min(m, M0[s * L + l]);
                         for (int k = lo; k < hi; ++k)
                             if (E[3 * k + 2] == 0) m = min(m, M0[E[3 * k + 1] * L + l]);
-                        if (m < M0[a * L + l]) {
-                            M0[a * L + l] = m;
-                            changed = true;
-                        }
+                        M0[a * L + l] = m;
                     }
+                    round_of[a] = static_cast<int16_t>(r);
+                    progress = true;
                 }
                 __syncwarp();
-                if (!__any_sync(kFull, changed)) break;
+                rounds = r + 1;
+                if (!__any_sync(kFull, left)) {
+                    all_done = true;
+                    break;
+                }
+                if (!__any_sync(kFull, progress)) break;
+            }
+            if (!all_done) {
+                for (int round = 0; round <= N + 1; ++round) {
+                    bool changed = false;
+                    for (int a = lane; a < N; a += 32) {
+                        const int s = succ[a];
+                        const bool same = !(s & kWrap);
+                        const int lo = adj_lo[a], hi = adj_hi[a];
+                        for (int l = 0; l < L; ++l) {
+                            uint16_t m = M0[a * L + l];
+                            if (same) m = min(m, M0[s * L + l]);
+                            for (int k = lo; k < hi; ++k)
+                                if (E[3 * k + 2] == 0) m = min(m, M0[E[3 * k + 1] * L + l]);
+                            if (m < M0[a * L + l]) {
+                                M0[a * L + l] = m;
+                                changed = true;
+                            }
+                        }
+                    }
+                    __syncwarp();
+                    if (!__any_sync(kFull, changed)) break;
+                }
             }
             // Next-iteration reach: entered through a wrap edge or a distance-1 sync edge.
             for (int a = lane; a < N; a += 32) {
@@ -263,25 +312,45 @@ __global__ void __launch_bounds__(32) analyze_frames_kernel(DevProblem p, DevFra
                 }
             }
             __syncwarp();
-            for (int round = 0; round <= N + 1; ++round) {
-                bool changed = false;
-                for (int a = lane; a < N; a += 32) {
-                    const int s = succ[a];
-                    const bool same = !(s & kWrap);
-                    const int lo = adj_lo[a], hi = adj_hi[a];
-                    for (int l = 0; l < L; ++l) {
-                        uint16_t m = M1[a * L + l];
-                        if (same) m = min(m, M1[s * L + l]);
-                        for (int k = lo; k < hi; ++k)
-                            if (E[3 * k + 2] == 0) m = min(m, M1[E[3 * k + 1] * L + l]);
-                        if (m < M1[a * L + l]) {
+            // The same same-iteration graph closes M1: the rounds of M0 are a valid order.
+            if (all_done) {
+                for (int r = 0; r < rounds; ++r) {
+                    for (int a = lane; a < N; a += 32) {
+                        if (round_of[a] != r) continue;
+                        const int s = succ[a];
+                        const bool same = !(s & kWrap);
+                        const int lo = adj_lo[a], hi = adj_hi[a];
+                        for (int l = 0; l < L; ++l) {
+                            uint16_t m = M1[a * L + l];
+                            if (same) m = min(m, M1[s * L + l]);
+                            for (int k = lo; k < hi; ++k)
+                                if (E[3 * k + 2] == 0) m = min(m, M1[E[3 * k + 1] * L + l]);
                             M1[a * L + l] = m;
-                            changed = true;
                         }
                     }
+                    __syncwarp();
                 }
-                __syncwarp();
-                if (!__any_sync(kFull, changed)) break;
+            } else {
+                for (int round = 0; round <= N + 1; ++round) {
+                    bool changed = false;
+                    for (int a = lane; a < N; a += 32) {
+                        const int s = succ[a];
+                        const bool same = !(s & kWrap);
+                        const int lo = adj_lo[a], hi = adj_hi[a];
+                        for (int l = 0; l < L; ++l) {
+                            uint16_t m = M1[a * L + l];
+                            if (same) m = min(m, M1[s * L + l]);
+                            for (int k = lo; k < hi; ++k)
+                                if (E[3 * k + 2] == 0) m = min(m, M1[E[3 * k + 1] * L + l]);
+                            if (m < M1[a * L + l]) {
+                                M1[a * L + l] = m;
+                                changed = true;
+                            }
+                        }
+                    }
+                    __syncwarp();
+                    if (!__any_sync(kFull, changed)) break;
+                }
             }
             // Queries from completion(a): its sync targets always; its lane successor only
             // through the completion -> issue_end edge of issue_duration == latency ops.
@@ -416,7 +485,8 @@ int periodic_tile(int n) {
 }
 
 size_t periodic_smem_bytes(const DevProblem& p, int tile) {
-    return static_cast<size_t>(4) * p.n_ops * sizeof(int) + static_cast<size_t>(2) * p.n_ops * tile * sizeof(int);
+    return static_cast<size_t>(4) * p.n_ops * sizeof(int) + static_cast<size_t>(2) * p.n_ops * tile * sizeof(int) +
+           static_cast<size_t>(tile / 32) * warp_resource_scratch_bytes(p);
 }
 
 namespace {
@@ -501,15 +571,21 @@ __device__ int periodic_checks(const DevProblem& p, const DevFrames& fr, const F
             if (V.o(u) + lat[u] > V.o(df)) return TFV_CLASS_CARRIED_SHARED_LIFETIME;
         }
     }
-    if (p.n_resources > 0 && periodic_resources_exceed(p, V, ii)) return TFV_CLASS_RESOURCE_CAPACITY;
-    return TFV_CLASS_PASS;
+    if (p.n_resources == 0) return TFV_CLASS_PASS;
+    if (warp_resources_used(p)) return kResourcesPending;  // the warp checks the capacities next
+    return thread_resources_exceed(p, V, ii) ? TFV_CLASS_RESOURCE_CAPACITY : TFV_CLASS_PASS;
 }
 
-// Verdict, makespan and II of one periodic candidate from its start extremes.
+struct Verdict {
+    int cls;       // verdict class, or kResourcesPending
+    int makespan;  // clamped to int32
+};
+
+// Verdict and makespan of one periodic candidate from its start extremes.
 template <class View>
-__device__ void finish_candidate(const DevProblem& p, const DevFrames& fr, const FrameTable& ft, const View& V,
-                                 const int* issue, const int* lat, int f, int ii, int min_p, int max_pl, int min_o,
-                                 int max_ol, DevResults out, long long c) {
+__device__ Verdict finish_candidate(const DevProblem& p, const DevFrames& fr, const FrameTable& ft, const View& V,
+                                    const int* issue, const int* lat, int f, int ii, int min_p, int max_pl, int min_o,
+                                    int max_ol) {
     const int I = p.iterations;
     // Starts of iterations >= 1 are offset + i * ii: extremes at i = 1 and i = I - 1.
     long long makespan = max_pl;
@@ -532,8 +608,27 @@ __device__ void finish_candidate(const DevProblem& p, const DevFrames& fr, const
     else if (out_of_range) cls = TFV_CLASS_OUT_OF_RANGE;
     else if (fclass != 0) cls = fclass;
     else cls = periodic_checks(p, fr, ft, f, V, issue, lat, ii);
+    return Verdict{cls, makespan > INT_MAX ? INT_MAX : (makespan < INT_MIN ? INT_MIN : static_cast<int>(makespan))};
+}
+
+// Resolves the warp's pending capacity checks (class 20), one candidate at a time with
+// every lane; view(src) is the candidate of lane src. All 32 lanes must call it.
+template <class ViewOf>
+__device__ void resolve_pending(const DevProblem& p, int& cls, int ii, int4* scratch, ViewOf view) {
+    const int lane = threadIdx.x & 31;
+    unsigned pending = __ballot_sync(kFull, cls == kResourcesPending);
+    while (pending) {
+        const int src = __ffs(pending) - 1;
+        pending &= pending - 1;
+        const int src_ii = __shfl_sync(kFull, ii, src);
+        const bool exceed = warp_resources_exceed(p, view(src), src_ii, scratch, lane);
+        if (lane == src) cls = exceed ? TFV_CLASS_RESOURCE_CAPACITY : TFV_CLASS_PASS;
+    }
+}
+
+__device__ __forceinline__ void write_result(DevResults out, long long c, int cls, int makespan, int ii, int I) {
     out.verdict[c] = cls;
-    out.makespan[c] = makespan > INT_MAX ? INT_MAX : (makespan < INT_MIN ? INT_MIN : static_cast<int>(makespan));
+    out.makespan[c] = makespan;
     out.ii[c] = I >= 3 ? ii : 0;
 }
 
@@ -550,6 +645,8 @@ __global__ void verify_periodic_kernel(DevProblem p, DevFrames fr, FrameTable ft
     int* bo_s = psm + 3 * N;
     int* Ps = psm + 4 * N;
     int* Os = Ps + static_cast<size_t>(N) * T;
+    int4* scratch = reinterpret_cast<int4*>(Os + static_cast<size_t>(N) * T) + (t >> 5) * 2 * p.res_max_windows;
+    const bool warp_path = warp_resources_used(p);
     for (int a = t; a < N; a += T) {
         issue_s[a] = p.issue[a];
         lat_s[a] = p.latency[a];
@@ -560,22 +657,35 @@ __global__ void verify_periodic_kernel(DevProblem p, DevFrames fr, FrameTable ft
 
     for (long long c0 = static_cast<long long>(blockIdx.x) * T; c0 < b.n; c0 += static_cast<long long>(gridDim.x) * T) {
         const long long c = c0 + t;
-        if (c >= b.n) continue;
-        int* P = Ps + t;
-        int* O = Os + t;
-        int min_p = INT_MAX, max_pl = INT_MIN, min_o = INT_MAX, max_ol = INT_MIN;
-        for (int a = 0; a < N; ++a) {
-            const int pv = bp_s[a] + b.prologue_delta[a * b.stride + c];
-            const int ov = bo_s[a] + b.offset_delta[a * b.stride + c];
-            P[a * T] = pv;
-            O[a * T] = ov;
-            min_p = min(min_p, pv);
-            max_pl = max(max_pl, pv + lat_s[a]);
-            min_o = min(min_o, ov);
-            max_ol = max(max_ol, ov + lat_s[a]);
+        const bool live = c < b.n;
+        int cls = 0, ms = 0, ii = 0;
+        if (live) {
+            int* P = Ps + t;
+            int* O = Os + t;
+            int min_p = INT_MAX, max_pl = INT_MIN, min_o = INT_MAX, max_ol = INT_MIN;
+            for (int a = 0; a < N; ++a) {
+                const int pv = bp_s[a] + b.prologue_delta[a * b.stride + c];
+                const int ov = bo_s[a] + b.offset_delta[a * b.stride + c];
+                P[a * T] = pv;
+                O[a * T] = ov;
+                min_p = min(min_p, pv);
+                max_pl = max(max_pl, pv + lat_s[a]);
+                min_o = min(min_o, ov);
+                max_ol = max(max_ol, ov + lat_s[a]);
+            }
+            ii = b.ii[c];
+            const Verdict v = finish_candidate(p, fr, ft, StagedView{P, O, T}, issue_s, lat_s, b.frame[c], ii, min_p,
+                                               max_pl, min_o, max_ol);
+            cls = v.cls;
+            ms = v.makespan;
         }
-        finish_candidate(p, fr, ft, StagedView{P, O, T}, issue_s, lat_s, b.frame[c], b.ii[c], min_p, max_pl, min_o,
-                         max_ol, out, c);
+        if (warp_path)
+            resolve_pending(p, cls, ii, scratch, [&](int src) {
+                const int col = (t & ~31) + src;
+                return StagedView{Ps + col, Os + col, T};
+            });
+        if (live) write_result(out, c, cls, ms, ii, p.iterations);
+        __syncthreads();  // the staged columns are rewritten by the next round
     }
 }
 
@@ -588,6 +698,8 @@ __global__ void __launch_bounds__(128) verify_periodic_global_kernel(DevProblem 
     int* lat_s = gsm + N;
     int* bp_s = gsm + 2 * N;
     int* bo_s = gsm + 3 * N;
+    int4* scratch = reinterpret_cast<int4*>(gsm + 4 * N) + (threadIdx.x >> 5) * 2 * p.res_max_windows;
+    const bool warp_path = warp_resources_used(p);
     for (int a = threadIdx.x; a < N; a += blockDim.x) {
         issue_s[a] = p.issue[a];
         lat_s[a] = p.latency[a];
@@ -596,17 +708,31 @@ __global__ void __launch_bounds__(128) verify_periodic_global_kernel(DevProblem 
     }
     __syncthreads();
     const long long step = static_cast<long long>(gridDim.x) * blockDim.x;
-    for (long long c = static_cast<long long>(blockIdx.x) * blockDim.x + threadIdx.x; c < b.n; c += step) {
-        const GlobalView V{bp_s, bo_s, b.prologue_delta, b.offset_delta, b.stride, c};
-        int min_p = INT_MAX, max_pl = INT_MIN, min_o = INT_MAX, max_ol = INT_MIN;
-        for (int a = 0; a < N; ++a) {
-            const int pv = V.p(a), ov = V.o(a);
-            min_p = min(min_p, pv);
-            max_pl = max(max_pl, pv + lat_s[a]);
-            min_o = min(min_o, ov);
-            max_ol = max(max_ol, ov + lat_s[a]);
+    for (long long c0 = static_cast<long long>(blockIdx.x) * blockDim.x; c0 < b.n; c0 += step) {
+        const long long c = c0 + threadIdx.x;
+        const bool live = c < b.n;
+        int cls = 0, ms = 0, ii = 0;
+        if (live) {
+            const GlobalView V{bp_s, bo_s, b.prologue_delta, b.offset_delta, b.stride, c};
+            int min_p = INT_MAX, max_pl = INT_MIN, min_o = INT_MAX, max_ol = INT_MIN;
+            for (int a = 0; a < N; ++a) {
+                const int pv = V.p(a), ov = V.o(a);
+                min_p = min(min_p, pv);
+                max_pl = max(max_pl, pv + lat_s[a]);
+                min_o = min(min_o, ov);
+                max_ol = max(max_ol, ov + lat_s[a]);
+            }
+            ii = b.ii[c];
+            const Verdict v = finish_candidate(p, fr, ft, V, issue_s, lat_s, b.frame[c], ii, min_p, max_pl, min_o, max_ol);
+            cls = v.cls;
+            ms = v.makespan;
         }
-        finish_candidate(p, fr, ft, V, issue_s, lat_s, b.frame[c], b.ii[c], min_p, max_pl, min_o, max_ol, out, c);
+        if (warp_path)
+            resolve_pending(p, cls, ii, scratch, [&](int src) {
+                return GlobalView{bp_s, bo_s, b.prologue_delta, b.offset_delta, b.stride,
+                                  c0 + (threadIdx.x & ~31) + src};
+            });
+        if (live) write_result(out, c, cls, ms, ii, p.iterations);
     }
 }
 
@@ -615,7 +741,7 @@ cudaError_t launch_verify_periodic(const DevProblem& p, const DevFrames& f, Fram
     if (b.n <= 0) return cudaSuccess;
     const int tile = periodic_tile(p.n_ops);
     if (tile == 0) {  // too many operations to stage a tile: read the deltas on demand
-        const size_t smem = static_cast<size_t>(4) * p.n_ops * sizeof(int);
+        const size_t smem = static_cast<size_t>(4) * p.n_ops * sizeof(int) + 4 * warp_resource_scratch_bytes(p);
         if (smem > 48 * 1024) {
             cudaError_t e = cudaFuncSetAttribute(verify_periodic_global_kernel,
                                                  cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(smem));

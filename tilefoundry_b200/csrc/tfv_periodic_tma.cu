@@ -153,6 +153,10 @@ __global__ void __launch_bounds__(kTile) verify_periodic_tma_kernel(DevProblem p
     int16_t* to = tp + N * kTile;                               // [N][kTile] offset deltas
     int4* opc = reinterpret_cast<int4*>(smem + 4 * N * kTile);  // [N] issue, latency, base starts
     uint64_t* bar = reinterpret_cast<uint64_t*>(opc + N);
+    const int lane = t & 31;
+    // capacity-check records of this warp (warp path only)
+    int4* scratch = reinterpret_cast<int4*>(bar + 2) + (t >> 5) * 2 * p.res_max_windows;
+    const bool warp_path = warp_resources_used(p);
 
     bool base_ok = true;
     for (int s = t; s < N; s += kTile) {
@@ -191,6 +195,7 @@ __global__ void __launch_bounds__(kTile) verify_periodic_tma_kernel(DevProblem p
             return;
         }
         phase ^= 1;
+        int cls = 0, ms = 0;  // this thread's verdict and makespan
         if (live && fr.n_frames > 0) {
             const int16_t* mp = tp + t;
             const int16_t* mo = to + t;
@@ -252,7 +257,6 @@ __global__ void __launch_bounds__(kTile) verify_periodic_tma_kernel(DevProblem p
                 out_of_range |= hi >= TFV_TIME_LIMIT || lo <= -static_cast<long long>(TFV_TIME_LIMIT);
             }
             out_of_range |= makespan >= TFV_TIME_LIMIT;
-            int cls;
             if (fclass == TFV_CLASS_BAD_PACKING) cls = TFV_CLASS_BAD_PACKING;
             else if (fclass == TFV_CLASS_SCHEDULE_MALFORMED || negative) cls = TFV_CLASS_SCHEDULE_MALFORMED;
             else if (out_of_range) cls = TFV_CLASS_OUT_OF_RANGE;
@@ -264,14 +268,28 @@ __global__ void __launch_bounds__(kTile) verify_periodic_tma_kernel(DevProblem p
             else if (ft.frame_flags[f] & kFrameRegisterCross) cls = TFV_CLASS_REGISTER_CROSSES_LANES;
             else if (rel_cls) cls = rel_cls;
             else if (carried_bad) cls = TFV_CLASS_CARRIED_SHARED_LIFETIME;
-            else cls = (p.n_resources > 0 && periodic_resources_exceed(p, TileView{opc, mp, mo}, ii))
-                           ? TFV_CLASS_RESOURCE_CAPACITY : TFV_CLASS_PASS;
-            out.verdict[c] = cls;
-            out.makespan[c] = makespan > INT_MAX ? INT_MAX : (makespan < INT_MIN ? INT_MIN : static_cast<int>(makespan));
-            out.ii[c] = kBodyRows >= 2 ? ii : 0;
+            else if (p.n_resources == 0) cls = TFV_CLASS_PASS;
+            else if (warp_path) cls = kResourcesPending;
+            else cls = thread_resources_exceed(p, TileView{opc, mp, mo}, ii) ? TFV_CLASS_RESOURCE_CAPACITY
+                                                                               : TFV_CLASS_PASS;
+            ms = makespan > INT_MAX ? INT_MAX : (makespan < INT_MIN ? INT_MIN : static_cast<int>(makespan));
         } else if (live) {  // no frames at all: the candidate cannot name one
-            out.verdict[c] = TFV_CLASS_BAD_PACKING;
-            out.makespan[c] = 0;
+            cls = TFV_CLASS_BAD_PACKING;
+        }
+        if (warp_path) {  // capacity (class 20): the warp checks its pending candidates one by one
+            unsigned pending = __ballot_sync(0xFFFFFFFFu, cls == kResourcesPending);
+            while (pending) {
+                const int src = __ffs(pending) - 1;
+                pending &= pending - 1;
+                const int src_ii = __shfl_sync(0xFFFFFFFFu, ii, src);
+                const int col = (t & ~31) + src;
+                const bool exceed = warp_resources_exceed(p, TileView{opc, tp + col, to + col}, src_ii, scratch, lane);
+                if (lane == src) cls = exceed ? TFV_CLASS_RESOURCE_CAPACITY : TFV_CLASS_PASS;
+            }
+        }
+        if (live) {
+            out.verdict[c] = cls;
+            out.makespan[c] = ms;
             out.ii[c] = kBodyRows >= 2 ? ii : 0;
         }
         __syncthreads();  // every thread is done with the tile before the next copy lands
@@ -303,7 +321,11 @@ bool make_map(CUtensorMap* map, const int16_t* base, long long n, long long stri
     return r == CUDA_SUCCESS;
 }
 
-size_t tma_smem_bytes(int n_ops) { return 4 * static_cast<size_t>(n_ops) * kTile + 16 * static_cast<size_t>(n_ops) + 16; }
+// Tiles, per-op constants, the mbarrier (16 bytes) and the warps' capacity-check records.
+size_t tma_smem_bytes(const DevProblem& p) {
+    return 4 * static_cast<size_t>(p.n_ops) * kTile + 16 * static_cast<size_t>(p.n_ops) + 16 +
+           (kTile / 32) * warp_resource_scratch_bytes(p);
+}
 
 }  // namespace
 
@@ -319,7 +341,7 @@ template <int kBodyRows>
 cudaError_t launch_tma(const DevProblem& p, const DevFrames& f, FrameTable t, const DevPeriodic& b, DevResults r,
                        int sm_count, cudaStream_t stream, const CUtensorMap& map_p, const CUtensorMap& map_o) {
     auto kernel = verify_periodic_tma_kernel<kBodyRows>;
-    const size_t smem = tma_smem_bytes(p.n_ops);
+    const size_t smem = tma_smem_bytes(p);
     if (smem > 48 * 1024) {
         cudaError_t e = cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(smem));
         if (e != cudaSuccess) return e;

@@ -3,85 +3,273 @@
 // The reference nets +amount at every window start and -amount at its end and sweeps the
 // timestamps; the demand can only exceed the capacity at some window start, so evaluating
 // the demand at every window start is exact. Window w of operation y covers
-// [P_y, P_y + D_w) in iteration 0 and [O_y + i*II, O_y + i*II + D_w) for i = 1..I-1.
+// [P_y, P_y + D_w) in iteration 0 and [S_y + i*T, S_y + i*T + D_w) for i = 0..n-1, where
+// S_y = O_y + T is its first body start, T the II and n = I - 1 the number of body copies.
 //
-// At a body start t = O_v + j*II of window v, the copies i of window w that cover t are
-// those with k = j - i in the fixed range [a_vw, b_vw] (a_vw = ceil((O_w - O_v)/II),
-// b_vw = ceil((O_w - O_v + D_w)/II) - 1), clipped to k in [j-I+1, j-1]. As a function of
-// j each term rises, stays flat at b_vw - a_vw + 1 and falls, so the body demand is
-// largest (and constant) on the middle iterations where no term is clipped; prologue
-// windows only add at small j. The demand is therefore evaluated explicitly for the low
-// iterations that the clipping or a prologue window can reach, once for a middle iteration,
-// and for every iteration only when no middle exists.
+// No division in the inner loops. Each window's first body start and duration are split
+// by T (S = qs*T + rs, D = m*T + e) with a multiply-shift divider. Unclipped by the
+// iteration range, the body demand F(t) is T-periodic and
+// F(S_v) = sum_w a_w * (m_w + [(rs_v - rs_w) mod T < e_w]). On
+// [max_w(S_w + D_w) - T, min_w S_w + n*T) the clipped body demand equals F; when that range
+// spans a full period (min S + n*T >= max(S + D)) every phase of F occurs at a real body
+// start, so the largest F decides every start at or after the end E of the last prologue
+// window (where the demand is the body demand, at most F). The starts before E — every
+// prologue start and the body starts S_v + j*T < E — are evaluated exactly; with no full
+// period, every start is. The clipped copy count of a window at t = qt*T + rt needs only
+// compares.
+//
+// Two drivers share that evaluation:
+//   * thread_resources_exceed: one thread per candidate, window values recomputed where
+//     they are used (cheapest for a few windows per resource);
+//   * warp_resources_exceed: one warp per candidate, the window values staged once in
+//     shared memory and the starts split across the lanes.
 #pragma once
+
+#include <climits>
 
 #include "tfv_device.cuh"
 
 namespace tfv {
 
-__device__ __forceinline__ int fdiv(int u, int d) { return u >= 0 ? u / d : -((-u + d - 1) / d); }  // d > 0
-__device__ __forceinline__ int cdiv(int u, int d) { return -fdiv(-u, d); }
+// Windows of one resource that the warp path stages (two int4 records each per warp).
+constexpr int kWarpWindowCap = 256;
+// Up to this many windows per resource the one-thread-per-candidate driver is used.
+constexpr int kThreadWindowMax = 8;
+// Internal verdict: classes 1..19 passed and the capacity check is still to be done.
+constexpr int kResourcesPending = 0x7FFF;
 
-// Demand of the windows [w0, w1) at time t (direct count, any II; I >= 1).
+__host__ __device__ inline bool warp_resources_used(const DevProblem& p) {
+    return p.n_resources > 0 && p.res_max_windows > kThreadWindowMax && p.res_max_windows <= kWarpWindowCap;
+}
+// Shared-memory records one warp needs for the warp path.
+inline size_t warp_resource_scratch_bytes(const DevProblem& p) {
+    return warp_resources_used(p) ? 2 * sizeof(int4) * static_cast<size_t>(p.res_max_windows) : 0;
+}
+
+// floor(x / d) for x in [0, 2^30) and d in [1, 2^30) by one multiply and a shift:
+// Granlund and Montgomery, "Division by Invariant Integers using Multiplication" (PLDI
+// 1994), Theorem 4.2 with N = 30, l = ceil(log2 d) and m = ceil(2^(N + l) / d) < 2^31.
+struct Divider {
+    unsigned long long m;
+    int shift;
+    __host__ __device__ explicit Divider(int d) {
+        const unsigned du = static_cast<unsigned>(d);
+#ifdef __CUDA_ARCH__
+        const int l = du <= 1 ? 0 : 32 - __clz(du - 1);
+#else
+        int l = 0;
+        while ((1u << l) < du) ++l;
+#endif
+        shift = 30 + l;
+        m = ((1ull << shift) + du - 1) / du;
+    }
+    __host__ __device__ __forceinline__ int quot(int x) const {
+        return static_cast<int>((static_cast<unsigned long long>(static_cast<unsigned>(x)) * m) >> shift);
+    }
+};
+
+// One window at one candidate.
+struct Win {
+    int P;   // prologue start
+    int D;   // duration
+    int a;   // amount
+    int S;   // first body start O + T
+    int qs;  // S = qs*T + rs
+    int rs;
+    int m;   // D = m*T + e
+    int e;
+};
+
+// Window values recomputed from the candidate's starts (thread driver).
 template <class Vals>
-__device__ int demand_at(const DevProblem& p, const Vals& V, int w0, int w1, int t, int ii, int I) {
-    int demand = 0;
-    for (int w = w0; w < w1; ++w) {
-        const int y = p.res_win_op[w], dur = p.res_win_duration[w];
-        const int p0 = V.p(y);
-        int count = (p0 <= t && t < p0 + dur) ? 1 : 0;
-        if (I == 2) {
-            const int s = V.o(y) + ii;
-            count += (s <= t && t < s + dur) ? 1 : 0;
-        } else if (I >= 3) {
-            const int u = t - V.o(y);
-            const int hi = min(fdiv(u, ii), I - 1);
-            const int lo = max(fdiv(u - dur, ii) + 1, 1);
-            count += max(0, hi - lo + 1);
+struct LiveWindows {
+    const DevProblem& p;
+    const Vals& V;
+    const Divider& div;
+    int w0, T, I;
+    __device__ __forceinline__ Win operator()(int w) const {
+        Win x;
+        const int y = p.res_win_op[w0 + w];
+        x.a = p.res_win_amount[w0 + w];
+        x.D = p.res_win_duration[w0 + w];
+        x.P = V.p(y);
+        x.S = I >= 2 ? V.o(y) + T : 0;
+        if (I >= 3) {
+            x.qs = div.quot(x.S);
+            x.rs = x.S - x.qs * T;
+            x.m = div.quot(x.D);
+            x.e = x.D - x.m * T;
+        } else {
+            x.qs = x.rs = x.m = x.e = 0;
         }
-        demand += p.res_win_amount[w] * count;
+        return x;
+    }
+};
+
+// Window values staged in shared memory as {rs, e, a, m}, {P, D, qs, S} (warp driver).
+struct StagedWindows {
+    const int4* rec;
+    const int4* rec2;
+    __device__ __forceinline__ Win operator()(int w) const {
+        const int4 r = rec[w], r2 = rec2[w];
+        return Win{r2.x, r2.y, r.z, r2.w, r2.z, r.x, r.w, r.y};
+    }
+};
+
+// Per-resource sums the evaluation needs.
+struct ResourceSums {
+    int E;     // end of the last prologue window
+    int Smin;  // earliest first body start
+    int Lend;  // latest end of a first body copy
+    int sumA;  // sum of amounts: bound of the prologue demand alone
+    int sumF;  // bound of F
+    int C0;    // sum of a*m (with m <= n)
+};
+
+__device__ __forceinline__ void add_window(ResourceSums& s, const Win& x, int n) {
+    s.E = max(s.E, x.P + x.D);
+    s.Smin = min(s.Smin, x.S);
+    s.Lend = max(s.Lend, x.S + x.D);
+    s.sumA += x.a;
+    const int mc = min(x.m, n);
+    s.sumF += x.a * (mc + (x.e > 0 ? 1 : 0));
+    s.C0 += x.a * mc;
+}
+
+// Demand at a start t = qt*T + rt from the prologue copy and the clipped body copies.
+template <class Src>
+__device__ __forceinline__ int clipped_demand(const Src& src, int W, int t, int qt, int rt, int T, int n) {
+    int demand = 0;
+    for (int w = 0; w < W; ++w) {
+        const Win x = src(w);
+        int cnt = static_cast<unsigned>(t - x.P) < static_cast<unsigned>(x.D) ? 1 : 0;  // P <= t < P + D
+        // body copies i with S + i*T <= t < S + i*T + D: i = hi - c + 1 .. hi
+        const int d = rt - x.rs;
+        const int k0 = d < 0 ? 1 : 0;
+        const int c = x.m + (d + k0 * T < x.e ? 1 : 0);
+        const int hi = qt - x.qs - k0;
+        cnt += max(0, min(hi, n - 1) - max(hi - c + 1, 0) + 1);
+        demand += x.a * cnt;
     }
     return demand;
 }
 
-// True when some resource's demand exceeds its capacity. Requires ii > 0 when I >= 3
-// (class 10 is decided before resources).
-template <class Vals>
-__device__ bool periodic_resources_exceed(const DevProblem& p, const Vals& V, int ii) {
-    const int I = p.iterations;
-    for (int q = 0; q < p.n_resources; ++q) {
-        const int w0 = p.res_offsets[q], w1 = p.res_offsets[q + 1];
-        const int cap = p.capacity[q];
-        for (int v = w0; v < w1; ++v) {
-            const int x = p.res_win_op[v];
-            // iteration 0: the window's prologue start
-            if (demand_at(p, V, w0, w1, V.p(x), ii, I) > cap) return true;
-            if (I < 3) {
-                if (I == 2 && demand_at(p, V, w0, w1, V.o(x) + ii, ii, I) > cap) return true;
-                continue;
-            }
-            const int ox = V.o(x);
-            int k_hi = INT_MIN, k_lo = INT_MAX, j_pro = 0;
-            for (int w = w0; w < w1; ++w) {
-                const int y = p.res_win_op[w], dur = p.res_win_duration[w];
-                const int delta = V.o(y) - ox;
-                k_lo = min(k_lo, cdiv(delta, ii));
-                k_hi = max(k_hi, cdiv(delta + dur, ii) - 1);
-                // last iteration j whose start ox + j*ii a prologue window of w can still cover
-                j_pro = max(j_pro, fdiv(V.p(y) + dur - 1 - ox, ii));
-            }
-            const int mid_lo = max(k_hi + 1, j_pro + 1);  // first j unclipped and past the prologue
-            const int mid_hi = k_lo + I - 1;               // last j unclipped
-            if (mid_lo <= mid_hi && mid_lo >= 1 && mid_lo <= I - 1) {
-                const int last_low = min(mid_lo - 1, I - 1);
-                for (int j = 1; j <= last_low; ++j)
-                    if (demand_at(p, V, w0, w1, ox + j * ii, ii, I) > cap) return true;
-                if (demand_at(p, V, w0, w1, ox + mid_lo * ii, ii, I) > cap) return true;
-            } else {
-                for (int j = 1; j < I; ++j)
-                    if (demand_at(p, V, w0, w1, ox + j * ii, ii, I) > cap) return true;
-            }
+// Demand at t of the prologue copies alone (no body copy has started by t).
+template <class Src>
+__device__ __forceinline__ int prologue_demand(const Src& src, int W, int t) {
+    int demand = 0;
+    for (int w = 0; w < W; ++w) {
+        const Win x = src(w);
+        demand += static_cast<unsigned>(t - x.P) < static_cast<unsigned>(x.D) ? x.a : 0;
+    }
+    return demand;
+}
+
+// Demand at t for I <= 2: the prologue copy and, for I == 2, the one body copy at S.
+template <class Src>
+__device__ __forceinline__ int short_demand(const Src& src, int W, int t, int I) {
+    int demand = 0;
+    for (int w = 0; w < W; ++w) {
+        const Win x = src(w);
+        demand += static_cast<unsigned>(t - x.P) < static_cast<unsigned>(x.D) ? x.a : 0;
+        if (I == 2) demand += static_cast<unsigned>(t - x.S) < static_cast<unsigned>(x.D) ? x.a : 0;
+    }
+    return demand;
+}
+
+// F at the phase rv of a first body start.
+template <class Src>
+__device__ __forceinline__ int periodic_demand(const Src& src, int W, int rv, int C0, int T) {
+    int F = C0;
+    for (int w = 0; w < W; ++w) {
+        const Win x = src(w);
+        const int d = rv - x.rs;
+        const unsigned u = min(static_cast<unsigned>(d), static_cast<unsigned>(d + T));  // (rv - rs) mod T
+        F += u < static_cast<unsigned>(x.e) ? x.a : 0;
+    }
+    return F;
+}
+
+// Whether a start of the windows v = v0, v0 + step, ... exceeds cap (see the file comment).
+template <class Src>
+__device__ bool starts_exceed(const Src& src, int W, int v0, int step, const ResourceSums& s, int cap, int T, int I,
+                              const Divider& div) {
+    if (I <= 2) {
+        for (int v = v0; v < W; v += step) {
+            const Win x = src(v);
+            if (short_demand(src, W, x.P, I) > cap) return true;
+            if (I == 2 && short_demand(src, W, x.S, I) > cap) return true;
         }
+        return false;
+    }
+    const int n = I - 1;
+    const bool middle = s.Smin + n * T >= s.Lend;  // the unclipped range spans a full period
+    if (middle && s.sumF > cap) {
+        for (int v = v0; v < W; v += step)
+            if (periodic_demand(src, W, src(v).rs, s.C0, T) > cap) return true;
+    }
+    const int horizon = middle ? s.E : INT_MAX;
+    for (int v = v0; v < W; v += step) {
+        const Win x = src(v);
+        if (x.P < s.Smin) {
+            if (s.sumA > cap && prologue_demand(src, W, x.P) > cap) return true;
+        } else {
+            const int qp = div.quot(x.P);
+            if (clipped_demand(src, W, x.P, qp, x.P - qp * T, T, n) > cap) return true;
+        }
+        int t = x.S;
+        for (int j = 0; j < n && t < horizon; ++j, t += T)
+            if (clipped_demand(src, W, t, x.qs + j, x.rs, T, n) > cap) return true;
+    }
+    return false;
+}
+
+// One thread per candidate. Requires T > 0 when I >= 3 (class 10 is decided before
+// resources) and every materialised start in [0, 2^30) (classes 1 and -1 before).
+template <class Vals>
+__device__ bool thread_resources_exceed(const DevProblem& p, const Vals& V, int T) {
+    const int I = p.iterations;
+    const Divider div(I >= 3 ? T : 1);
+    for (int q = 0; q < p.n_resources; ++q) {
+        const int w0 = p.res_offsets[q], W = p.res_offsets[q + 1] - w0;
+        const LiveWindows<Vals> src{p, V, div, w0, T, I};
+        ResourceSums s{INT_MIN, INT_MAX, INT_MIN, 0, 0, 0};
+        for (int w = 0; w < W; ++w) add_window(s, src(w), I - 1);
+        if (starts_exceed(src, W, 0, 1, s, p.capacity[q], T, I, div)) return true;
+    }
+    return false;
+}
+
+// One warp per candidate: every lane passes the same V and T. Same requirements as the
+// thread driver, plus warp_resources_used and scratch for 2 * res_max_windows int4
+// records private to the warp.
+template <class Vals>
+__device__ bool warp_resources_exceed(const DevProblem& p, const Vals& V, int T, int4* scratch, int lane) {
+    const unsigned full = 0xFFFFFFFFu;
+    const int I = p.iterations;
+    int4* rec = scratch;
+    int4* rec2 = scratch + p.res_max_windows;
+    const Divider div(I >= 3 ? T : 1);
+    for (int q = 0; q < p.n_resources; ++q) {
+        const int w0 = p.res_offsets[q], W = p.res_offsets[q + 1] - w0;
+        const LiveWindows<Vals> live{p, V, div, w0, T, I};
+        ResourceSums s{INT_MIN, INT_MAX, INT_MIN, 0, 0, 0};
+        for (int w = lane; w < W; w += 32) {
+            const Win x = live(w);
+            rec[w] = make_int4(x.rs, x.e, x.a, x.m);
+            rec2[w] = make_int4(x.P, x.D, x.qs, x.S);
+            add_window(s, x, I - 1);
+        }
+        s.E = __reduce_max_sync(full, s.E);
+        s.Smin = __reduce_min_sync(full, s.Smin);
+        s.Lend = __reduce_max_sync(full, s.Lend);
+        s.sumA = __reduce_add_sync(full, s.sumA);
+        s.sumF = __reduce_add_sync(full, s.sumF);
+        s.C0 = __reduce_add_sync(full, s.C0);
+        __syncwarp();
+        const bool exceed = starts_exceed(StagedWindows{rec, rec2}, W, lane, 32, s, p.capacity[q], T, I, div);
+        if (__any_sync(full, exceed)) return true;
+        __syncwarp();  // every lane is done with this resource's records
     }
     return false;
 }

@@ -24,6 +24,7 @@
 //       timing inequality at every instance. The first failing relation is therefore
 //       the first relation whose path is absent; its class is 17 if its timing fails at
 //       instance 0 (checked first, verify.py:311) and 18 otherwise.
+#include <algorithm>
 #include <climits>
 #include <cstdint>
 
@@ -54,8 +55,10 @@ size_t analyze_smem_bytes(int n, int lanes) {
     b += align16(sizeof(int16_t) * n);           // succ
     b += align16(sizeof(int) * n) * 2;           // adjacency [lo, hi) into the sync set
     b += align16(sizeof(uint16_t) * n * lanes) * 2;  // M0, M1
-    b += align16(sizeof(int16_t) * n);           // closure round of each op
+    b += align16(sizeof(int) * n);               // same-iteration in-degree
+    b += align16(sizeof(int16_t) * n);           // topological order
     b += sizeof(int) * 32;                       // per-lane counts and starts
+    b += sizeof(int) * 4;                        // queue tail
     return b;
 }
 
@@ -63,7 +66,7 @@ size_t analyze_smem_bytes(int n, int lanes) {
 //           from start(y) (suffixes of a lane are closed under reachability, because
 //           start -> issue_end -> next start follows the lane, verify.py:132-137).
 // M1[y][l]: the same for lane l in the next iteration.
-__global__ void __launch_bounds__(32) analyze_frames_kernel(DevProblem p, DevFrames fr, FrameTable ft) {
+__global__ void __launch_bounds__(32) analyze_frames_kernel(DevProblem p, DevFrames fr, FrameTable ft, int edge_cap) {
     extern __shared__ __align__(16) unsigned char smem[];
     const int N = p.n_ops;
     const int L = p.warp_groups;
@@ -85,10 +88,15 @@ __global__ void __launch_bounds__(32) analyze_frames_kernel(DevProblem p, DevFra
     cur += align16(sizeof(uint16_t) * N * L);
     uint16_t* M1 = reinterpret_cast<uint16_t*>(cur);
     cur += align16(sizeof(uint16_t) * N * L);
-    int16_t* round_of = reinterpret_cast<int16_t*>(cur);
+    int* indeg = reinterpret_cast<int*>(cur);
+    cur += align16(sizeof(int) * N);
+    int16_t* topo = reinterpret_cast<int16_t*>(cur);
     cur += align16(sizeof(int16_t) * N);
     int* cnt = reinterpret_cast<int*>(cur);
     int* first = cnt + 16;
+    int* qtail = cnt + 32;
+    // the frame's sync set as target | distance << 12 (distance clamped to 3), when it fits
+    uint16_t* staged = reinterpret_cast<uint16_t*>(cnt + 36);
 
     const int* E = fr.sync_edges;
     const int total_edges = min(fr.sync_offsets[fr.n_sync_sets], fr.n_sync_edges);
@@ -216,6 +224,12 @@ __global__ void __launch_bounds__(32) analyze_frames_kernel(DevProblem p, DevFra
         // Reachability of every required relation (verify.py:122-160, 306-314).
         int first_unreached = -1;
         if (cls == 0 && !unusable_for_paths) {
+            const bool fits = e1 - e0 <= edge_cap;
+            if (fits)
+                for (int k = e0 + lane; k < e1; k += 32)
+                    staged[k - e0] = static_cast<uint16_t>(E[3 * k + 1] | (min(E[3 * k + 2], 3) << 12));
+            // every target is an operation and every distance is below I here
+            auto edge = [&](int k) -> int { return fits ? staged[k - e0] : E[3 * k + 1] | (min(E[3 * k + 2], 3) << 12); };
             for (int a = lane; a < N; a += 32) {
                 adj_lo[a] = e0;
                 adj_hi[a] = e0;
@@ -232,154 +246,119 @@ __global__ void __launch_bounds__(32) analyze_frames_kernel(DevProblem p, DevFra
                 M0[idx] = (lane_of(lp[a]) == l) ? static_cast<uint16_t>(pos_of(lp[a])) : kInfPos;
             }
             __syncwarp();
-            // Closure within one iteration over the lane successor and the distance-0 sync
-            // targets. Operations are finished in rounds: an operation whose targets were all
-            // finished in earlier rounds takes their minima once, so each operation is visited
-            // with final inputs (round_of records when). The rounds end after the longest
-            // same-iteration path. Operations left over lie on or above a cycle; then the
-            // plain fixed-point iteration below finishes the closure.
-            for (int a = lane; a < N; a += 32) round_of[a] = -1;
+            // Closure over the same-iteration graph: lane successors and distance-0 sync
+            // targets. Kahn's algorithm gives a topological order; the closure then visits the
+            // operations in reverse, so each reads finished targets only, and the L columns
+            // are independent (one warp lane each).
+            for (int a = lane; a < N; a += 32) indeg[a] = 0;
             __syncwarp();
-            int rounds = 0;
-            bool all_done = false;
-            for (int r = 0; r <= N; ++r) {
-                bool progress = false, left = false;
-                for (int a = lane; a < N; a += 32) {
-                    if (round_of[a] >= 0) continue;
-                    const int s = succ[a];
-                    const bool same = !(s & kWrap);
-                    const int lo = adj_lo[a], hi = adj_hi[a];
-                    bool ready = !same || (round_of[s] >= 0 && round_of[s] < r);
-                    for (int k = lo; k < hi && ready; ++k)
-                        if (E[3 * k + 2] == 0) {
-                            const int t = round_of[E[3 * k + 1]];
-                            ready = t >= 0 && t < r;
-                        }
-                    if (!ready) {
-                        left = true;
-                        continue;
-                    }
-                    for (int l = 0; l < L; ++l) {
-                        uint16_t m = M0[a * L + l];
-                        if (same) m = min(m, M0[s * L + l]);
-                        for (int k = lo; k < hi; ++k)
-                            if (E[3 * k + 2] == 0) m = min(m, M0[E[3 * k + 1] * L + l]);
-                        M0[a * L + l] = m;
-                    }
-                    round_of[a] = static_cast<int16_t>(r);
-                    progress = true;
-                }
-                __syncwarp();
-                rounds = r + 1;
-                if (!__any_sync(kFull, left)) {
-                    all_done = true;
-                    break;
-                }
-                if (!__any_sync(kFull, progress)) break;
-            }
-            if (!all_done) {
-                for (int round = 0; round <= N + 1; ++round) {
-                    bool changed = false;
-                    for (int a = lane; a < N; a += 32) {
-                        const int s = succ[a];
-                        const bool same = !(s & kWrap);
-                        const int lo = adj_lo[a], hi = adj_hi[a];
-                        for (int l = 0; l < L; ++l) {
-                            uint16_t m = M0[a * L + l];
-                            if (same) m = min(m, M0[s * L + l]);
-                            for (int k = lo; k < hi; ++k)
-                                if (E[3 * k + 2] == 0) m = min(m, M0[E[3 * k + 1] * L + l]);
-                            if (m < M0[a * L + l]) {
-                                M0[a * L + l] = m;
-                                changed = true;
-                            }
-                        }
-                    }
-                    __syncwarp();
-                    if (!__any_sync(kFull, changed)) break;
-                }
-            }
-            // Next-iteration reach: entered through a wrap edge or a distance-1 sync edge.
             for (int a = lane; a < N; a += 32) {
                 const int s = succ[a];
-                const int lo = adj_lo[a], hi = adj_hi[a];
-                for (int l = 0; l < L; ++l) {
-                    uint16_t m = kInfPos;
-                    if (s & kWrap) m = min(m, M0[(s & kSuccMask) * L + l]);
-                    for (int k = lo; k < hi; ++k)
-                        if (E[3 * k + 2] == 1) m = min(m, M0[E[3 * k + 1] * L + l]);
-                    M1[a * L + l] = m;
+                if (!(s & kWrap)) atomicAdd(&indeg[s], 1);
+                for (int k = adj_lo[a]; k < adj_hi[a]; ++k) {
+                    const int v = edge(k);
+                    if ((v >> 12) == 0) atomicAdd(&indeg[v & 0xFFF], 1);
                 }
             }
             __syncwarp();
-            // The same same-iteration graph closes M1: the rounds of M0 are a valid order.
-            if (all_done) {
-                for (int r = 0; r < rounds; ++r) {
-                    for (int a = lane; a < N; a += 32) {
-                        if (round_of[a] != r) continue;
-                        const int s = succ[a];
-                        const bool same = !(s & kWrap);
-                        const int lo = adj_lo[a], hi = adj_hi[a];
-                        for (int l = 0; l < L; ++l) {
-                            uint16_t m = M1[a * L + l];
-                            if (same) m = min(m, M1[s * L + l]);
-                            for (int k = lo; k < hi; ++k)
-                                if (E[3 * k + 2] == 0) m = min(m, M1[E[3 * k + 1] * L + l]);
-                            M1[a * L + l] = m;
-                        }
-                    }
-                    __syncwarp();
-                }
-            } else {
-                for (int round = 0; round <= N + 1; ++round) {
-                    bool changed = false;
-                    for (int a = lane; a < N; a += 32) {
-                        const int s = succ[a];
-                        const bool same = !(s & kWrap);
-                        const int lo = adj_lo[a], hi = adj_hi[a];
-                        for (int l = 0; l < L; ++l) {
-                            uint16_t m = M1[a * L + l];
-                            if (same) m = min(m, M1[s * L + l]);
-                            for (int k = lo; k < hi; ++k)
-                                if (E[3 * k + 2] == 0) m = min(m, M1[E[3 * k + 1] * L + l]);
-                            if (m < M1[a * L + l]) {
-                                M1[a * L + l] = m;
-                                changed = true;
-                            }
-                        }
-                    }
-                    __syncwarp();
-                    if (!__any_sync(kFull, changed)) break;
-                }
+            int tail = 0;
+            for (int a0 = 0; a0 < N; a0 += 32) {
+                const int a = a0 + lane;
+                const bool source = a < N && indeg[a] == 0;
+                const unsigned m = __ballot_sync(kFull, source);
+                if (source) topo[tail + __popc(m & ((1u << lane) - 1))] = static_cast<int16_t>(a);
+                tail += __popc(m);
             }
-            // Queries from completion(a): its sync targets always; its lane successor only
-            // through the completion -> issue_end edge of issue_duration == latency ops.
-            for (int r0 = 0; r0 < p.n_relations; r0 += 32) {
-                const int r = r0 + lane;
-                bool unreached = false;
-                if (r < p.n_relations) {
-                    const int packed = p.relation[r];
-                    const int a = packed & 0xFFF, b = (packed >> 12) & 0xFFF, d = packed >> 24;
-                    if (d < I) {
-                        const int lb = lane_of(lp[b]), qb = pos_of(lp[b]);
-                        int best = kInfPos;
-                        for (int k = adj_lo[a]; k < adj_hi[a]; ++k) {
-                            const int t = E[3 * k + 1], dd = E[3 * k + 2];
-                            if (dd == 0) best = min(best, static_cast<int>(d == 0 ? M0[t * L + lb] : M1[t * L + lb]));
-                            else if (dd == 1 && d == 1) best = min(best, static_cast<int>(M0[t * L + lb]));
-                        }
-                        if (p.issue[a] == p.latency[a]) {
-                            const int s = succ[a];
-                            if (!(s & kWrap)) best = min(best, static_cast<int>(d == 0 ? M0[s * L + lb] : M1[s * L + lb]));
-                            else if (d == 1) best = min(best, static_cast<int>(M0[(s & kSuccMask) * L + lb]));
-                        }
-                        unreached = qb < best;
+            // Kahn's algorithm, one lane: a chain-like graph has about as many levels as
+            // operations, so level-synchronous rounds would cost a warp round trip each.
+            if (lane == 0) {
+                for (int head = 0; head < tail; ++head) {
+                    const int a = topo[head];
+                    const int s = succ[a];
+                    if (!(s & kWrap) && --indeg[s] == 0) topo[tail++] = static_cast<int16_t>(s);
+                    for (int k = adj_lo[a]; k < adj_hi[a]; ++k) {
+                        const int v = edge(k);
+                        if ((v >> 12) == 0 && --indeg[v & 0xFFF] == 0) topo[tail++] = static_cast<int16_t>(v & 0xFFF);
                     }
                 }
-                const unsigned m = __ballot_sync(kFull, unreached);
-                if (m) {
-                    first_unreached = r0 + __ffs(m) - 1;
-                    break;
+                *qtail = tail;
+            }
+            __syncwarp();
+            // A same-iteration cycle of lane and distance-0 sync edges would need every start
+            // on it to exceed its predecessor's (issue and latency are positive), so a
+            // candidate of such a frame always fails a lane-order or sync check (classes
+            // 12-15) before the relation checks: the closure is only needed for acyclic frames.
+            const bool ordered = *qtail == N;
+
+            // One closure step of operation a on lane l of M: its own value, its same-iteration
+            // lane successor and its distance-0 sync targets.
+            auto step = [&](uint16_t* M, int a, int l) -> uint16_t {
+                const int s = succ[a];
+                uint16_t m = M[a * L + l];
+                if (!(s & kWrap)) m = min(m, M[s * L + l]);
+                for (int k = adj_lo[a]; k < adj_hi[a]; ++k) {
+                    const int v = edge(k);
+                    if ((v >> 12) == 0) m = min(m, M[(v & 0xFFF) * L + l]);
+                }
+                return m;
+            };
+            // lane l closes column l of M in reverse topological order
+            auto close = [&](uint16_t* M) {
+                if (lane < L)
+                    for (int i = N - 1; i >= 0; --i) {
+                        const int a = topo[i];
+                        M[a * L + lane] = step(M, a, lane);
+                    }
+                __syncwarp();
+            };
+            if (ordered) {
+                close(M0);
+                // Next-iteration reach: entered through a wrap edge or a distance-1 sync edge.
+                for (int a = lane; a < N; a += 32) {
+                    const int s = succ[a];
+                    const int lo = adj_lo[a], hi = adj_hi[a];
+                    for (int l = 0; l < L; ++l) {
+                        uint16_t m = kInfPos;
+                        if (s & kWrap) m = min(m, M0[(s & kSuccMask) * L + l]);
+                        for (int k = lo; k < hi; ++k) {
+                            const int v = edge(k);
+                            if ((v >> 12) == 1) m = min(m, M0[(v & 0xFFF) * L + l]);
+                        }
+                        M1[a * L + l] = m;
+                    }
+                }
+                __syncwarp();
+                close(M1);  // the same graph: M1 of a is the least M1 seed reachable from a
+                // Queries from completion(a): its sync targets always; its lane successor only
+                // through the completion -> issue_end edge of issue_duration == latency ops.
+                for (int r0 = 0; r0 < p.n_relations; r0 += 32) {
+                    const int r = r0 + lane;
+                    bool unreached = false;
+                    if (r < p.n_relations) {
+                        const int packed = p.relation[r];
+                        const int a = packed & 0xFFF, b = (packed >> 12) & 0xFFF, d = packed >> 24;
+                        if (d < I) {
+                            const int lb = lane_of(lp[b]), qb = pos_of(lp[b]);
+                            int best = kInfPos;
+                            for (int k = adj_lo[a]; k < adj_hi[a]; ++k) {
+                                const int v = edge(k);
+                                const int t = v & 0xFFF, dd = v >> 12;
+                                if (dd == 0) best = min(best, static_cast<int>(d == 0 ? M0[t * L + lb] : M1[t * L + lb]));
+                                else if (dd == 1 && d == 1) best = min(best, static_cast<int>(M0[t * L + lb]));
+                            }
+                            if (p.issue[a] == p.latency[a]) {
+                                const int s = succ[a];
+                                if (!(s & kWrap)) best = min(best, static_cast<int>(d == 0 ? M0[s * L + lb] : M1[s * L + lb]));
+                                else if (d == 1) best = min(best, static_cast<int>(M0[(s & kSuccMask) * L + lb]));
+                            }
+                            unreached = qb < best;
+                        }
+                    }
+                    const unsigned m = __ballot_sync(kFull, unreached);
+                    if (m) {
+                        first_unreached = r0 + __ffs(m) - 1;
+                        break;
+                    }
                 }
             }
         }
@@ -395,14 +374,21 @@ __global__ void __launch_bounds__(32) analyze_frames_kernel(DevProblem p, DevFra
 cudaError_t launch_analyze_frames(const DevProblem& p, const DevFrames& f, FrameTable t, int sm_count,
                                   cudaStream_t stream) {
     if (f.n_frames <= 0) return cudaSuccess;
-    const size_t smem = analyze_smem_bytes(p.n_ops, p.warp_groups);
+    // Stage each frame's sync set in shared memory when the device has room for it.
+    int device = 0, optin = 48 * 1024;
+    cudaError_t e = cudaGetDevice(&device);
+    if (e == cudaSuccess) e = cudaDeviceGetAttribute(&optin, cudaDevAttrMaxSharedMemoryPerBlockOptin, device);
+    if (e != cudaSuccess) return e;
+    const size_t base = analyze_smem_bytes(p.n_ops, p.warp_groups);
+    const size_t room = static_cast<size_t>(optin) > base ? (static_cast<size_t>(optin) - base) / sizeof(uint16_t) : 0;
+    const int edge_cap = static_cast<int>(std::min<size_t>({room, static_cast<size_t>(f.n_sync_edges), 16384}));
+    const size_t smem = base + align16(sizeof(uint16_t) * static_cast<size_t>(edge_cap));
     if (smem > 48 * 1024) {
-        cudaError_t e = cudaFuncSetAttribute(analyze_frames_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                             static_cast<int>(smem));
+        e = cudaFuncSetAttribute(analyze_frames_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(smem));
         if (e != cudaSuccess) return e;
     }
     const int grid = min(f.n_frames, sm_count * 32);
-    analyze_frames_kernel<<<grid, 32, smem, stream>>>(p, f, t);
+    analyze_frames_kernel<<<grid, 32, smem, stream>>>(p, f, t, edge_cap);
     return cudaGetLastError();
 }
 

@@ -51,6 +51,8 @@ def parse_args():
     p.add_argument("--impl", choices=["ours", "reference"], default="ours")
     p.add_argument("--workload", choices=sorted(WORKLOADS), default="mla")
     p.add_argument("--candidates", type=int, default=None, help="candidates per GPU (default per workload)")
+    p.add_argument("--iis", type=int, default=None,
+                   help="initiation intervals per candidate over [II_lb, 2 II_lb] (default 16 for stress, else 1)")
     p.add_argument("--seed", type=int, default=2026)
     p.add_argument("--e2e-steps", type=int, default=None)
     p.add_argument("--no-cpu-baseline", action="store_true")
@@ -324,6 +326,7 @@ def run_ours(args) -> None:
 
     global ORACLE_PROBLEM
     n = args.candidates or WORKLOADS[args.workload][1]
+    n_ii = args.iis or (16 if args.workload == "stress" else 1)
     problem, packed, frames, batch = workload(args.workload, n, args.seed + rank)
     from tilefoundry_b200 import problem_to_json
 
@@ -334,10 +337,15 @@ def run_ours(args) -> None:
         key: torch.from_numpy(np.ascontiguousarray(getattr(batch, key))).to(dev)
         for key in ("base_prologue", "base_offset", "prologue_delta", "offset_delta", "ii", "frame")
     }
-    # Results live in [3, n] tensors (verdict, makespan, ii rows), double-buffered so that
+    # Results live in [3, n_ii, n] tensors (verdict, makespan, ii), double-buffered so that
     # the gather of one step's results to rank 0 overlaps the next step's verification.
-    results = [torch.empty((3, n), dtype=torch.int32, device=dev) for _ in range(2)]
-    gathered = [[torch.empty((3, n), dtype=torch.int32, device=dev) for _ in range(world)] if rank == 0 else None
+    # With n_ii > 1 every candidate is verified at n_ii IIs spread over [II_lb, 2 II_lb].
+    from tilefoundry_b200.workloads import ii_lower_bound, ii_sweep
+
+    sweep = np.repeat(ii_sweep(ii_lower_bound(packed), n_ii)[:, None], n, axis=1).astype(np.int32) if n_ii > 1 else None
+    ii_values = torch.from_numpy(sweep).to(dev) if sweep is not None else None
+    results = [torch.empty((3, n_ii, n), dtype=torch.int32, device=dev) for _ in range(2)]
+    gathered = [[torch.empty((3, n_ii, n), dtype=torch.int32, device=dev) for _ in range(world)] if rank == 0 else None
                 for _ in range(2)] if world > 1 else None
     pending = [None, None]
     table = verifier.analyze(dframes)
@@ -358,7 +366,10 @@ def run_ours(args) -> None:
         if events is not None:
             events[1].record(stream)
         out = results[buf]
-        verifier.verify_periodic_device(dframes, table, tensors, out=(out[0], out[1], out[2]))
+        if ii_values is None:
+            verifier.verify_periodic_device(dframes, table, tensors, out=(out[0, 0], out[1, 0], out[2, 0]))
+        else:
+            verifier.verify_periodic_sweep_device(dframes, table, tensors, ii_values, out=(out[0], out[1], out[2]))
         if events is not None:
             events[2].record(stream)
         if dist is not None:
@@ -395,7 +406,7 @@ def run_ours(args) -> None:
         t = torch.tensor([elapsed_ms], device=dev)
         dist.all_reduce(t, op=dist.ReduceOp.MAX)
         elapsed_ms = float(t.item())
-    value = n * world * args.steps / (elapsed_ms / 1e3)
+    value = n * n_ii * world * args.steps / (elapsed_ms / 1e3)
 
     # End to end through the C ABI host-buffer entry: pinned inputs in, host results out.
     from tilefoundry_b200.batch import PeriodicBatch
@@ -408,27 +419,39 @@ def run_ours(args) -> None:
 
     fstruct = _lib.frames_struct(arrays, len(frames))
     e2e_steps = args.e2e_steps or max(3, min(args.steps, 10))
+    if sweep is None:
+        def e2e_call():
+            verifier.verify_periodic_host_arrays(fstruct, hb, host_out)
+            return host_out
+        e2e_entry = "tfv_verify_periodic_host"
+    else:
+        def e2e_call():  # host arrays in, host arrays out, through the public sweep entry
+            return verifier.verify_periodic_sweep(frames, hb, sweep)
+        e2e_entry = "WarpgroupVerifier.verify_periodic_sweep"
     for _ in range(min(args.warmup, 2)):
-        verifier.verify_periodic_host_arrays(fstruct, hb, host_out)
+        e2e_call()
     barrier()
     t0 = time.perf_counter()
     for _ in range(e2e_steps):
-        verifier.verify_periodic_host_arrays(fstruct, hb, host_out)
+        e2e_out = e2e_call()
     e2e_s = time.perf_counter() - t0
     barrier()
     if dist is not None:
         t = torch.tensor([e2e_s], device=dev, dtype=torch.float64)
         dist.all_reduce(t, op=dist.ReduceOp.MAX)
         e2e_s = float(t.item())
-    e2e_value = n * world * e2e_steps / e2e_s
+    e2e_value = n * n_ii * world * e2e_steps / e2e_s
     last = results[(args.steps - 1) % 2]
-    assert np.array_equal(host_out[0], last[0].cpu().numpy()), "host-buffer and device entries disagree"
+    assert np.array_equal(np.asarray(e2e_out[0]).reshape(n_ii, n), last[0].cpu().numpy()), \
+        "host-buffer and device entries disagree"
     h2d = sum(int(np.asarray(v).nbytes) for v in arrays.values()) + sum(
-        int(getattr(batch, k).nbytes) for k in ("base_prologue", "base_offset", "prologue_delta", "offset_delta", "ii", "frame"))
-    d2h = 3 * 4 * n
+        int(getattr(batch, k).nbytes) for k in ("base_prologue", "base_offset", "prologue_delta", "offset_delta", "frame"))
+    h2d += int(sweep.nbytes) if sweep is not None else int(batch.ii.nbytes)
+    d2h = 3 * 4 * n * n_ii
 
     if rank == 0:
-        per_launch = algorithmic_bytes_per_candidate(packed.n_ops) * n
+        # deltas and frame once per candidate; II and the three results once per (candidate, II)
+        per_launch = (algorithmic_bytes_per_candidate(packed.n_ops) + 16 * (n_ii - 1)) * n
         mean_verify_s = statistics.mean(verify_ms) / 1e3
         achieved = per_launch / mean_verify_s / 1e9
         peak, peak_src = FALLBACK_HBM_GBS, "fallback"
@@ -448,7 +471,7 @@ def run_ours(args) -> None:
                 "kind": "port",
                 "sample": f"{sample} candidates of this batch through oracle/verify_port.py in {workers} processes ({secs:.1f} s)",
             }
-        verdicts = np.bincount(last[0].cpu().numpy() + 3, minlength=25)
+        verdicts = np.bincount(last[0].cpu().numpy().ravel() + 3, minlength=25)
         line = {
             "metric": METRIC,
             "value": value,
@@ -466,6 +489,7 @@ def run_ours(args) -> None:
             "config": {
                 "workload": WORKLOADS[args.workload][2],
                 "candidates_per_gpu": n,
+                "iis_per_candidate": n_ii,
                 "ops": packed.n_ops,
                 "iterations": packed.iterations,
                 "warpgroups": packed.warp_groups,
@@ -475,7 +499,7 @@ def run_ours(args) -> None:
                 "bytes_per_candidate": algorithmic_bytes_per_candidate(packed.n_ops),
                 "l2": f"inputs {per_launch / 1e9:.2f} GB per GPU per step, larger than the 126 MB L2",
                 "parallelism": f"dp{world} (contiguous candidate shards, gather to rank 0)",
-                "valid_fraction": float(verdicts[3] / n),
+                "valid_fraction": float(verdicts[3] / (n * n_ii)),
             },
             "roofline": {
                 "bound": "hbm",
@@ -492,7 +516,7 @@ def run_ours(args) -> None:
             },
             "cpu_baseline": cpu,
             "e2e": {"value": e2e_value, "unit": UNIT, "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h,
-                    "steps": e2e_steps, "entry": "tfv_verify_periodic_host"},
+                    "steps": e2e_steps, "entry": e2e_entry},
             "gpu_launches": 3 * args.steps,  # frame analysis, sync-program compile, verification
             "clocks": clocks.summary(),
         }

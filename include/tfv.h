@@ -35,7 +35,7 @@
 extern "C" {
 #endif
 
-#define TFV_ABI_VERSION 2
+#define TFV_ABI_VERSION 3
 
 #if defined(__GNUC__)
 #define TFV_API __attribute__((visibility("default")))
@@ -210,6 +210,19 @@ TFV_API int tfv_analyze_frames(const tfv_problem* problem, const tfv_frames* fra
 TFV_API int tfv_verify_periodic(const tfv_problem* problem, const tfv_frames* frames,
                         void* frame_table, size_t frame_table_bytes, const tfv_periodic_batch* batch,
                         const tfv_results* results, void* stream);
+
+/* The II search's bulk oracle: every candidate of `batch` verified at n_ii initiation
+ * intervals. The reference's solver fixes the body offsets and minimises the II from
+ * max(issue durations, resource bound) upward (solve.py:255-270, 452) and materialises a
+ * periodic schedule at a given II by _materialize_periodic_times (solve.py:206-231);
+ * here the offsets of each candidate are read once and checked at every II.
+ * `ii_values` is [n_ii][n_candidates] int32 on the device (row k holds every candidate's
+ * k-th II; batch->ii is not read), and each result array is [n_ii][n_candidates].
+ * Otherwise like tfv_verify_periodic. */
+TFV_API int tfv_verify_periodic_sweep(const tfv_problem* problem, const tfv_frames* frames,
+                                      void* frame_table, size_t frame_table_bytes,
+                                      const tfv_periodic_batch* batch, int n_ii, const int32_t* ii_values,
+                                      const tfv_results* results, void* stream);
 
 /* Verify explicit timing rows against analysed frames (general schedules). */
 TFV_API int tfv_verify_rows(const tfv_problem* problem, const tfv_frames* frames,

@@ -308,3 +308,63 @@ def test_kernel_body_configs_match_oracle(name, count):
     assert np.array_equal(verdict, ov)
     assert np.array_equal(makespan, om)
     assert np.array_equal(ii, oi)
+
+
+def _oracle_rows(problem, frames, batch, ii_values):
+    oracle = OracleProblem(load_problem(problem_to_json(problem)))
+    p, o = absolute_starts(batch)
+    return [oracle.classify_periodic(p, o, row, frames.frames, batch.frame) for row in ii_values]
+
+
+def _assert_sweep(got, want):
+    verdict, makespan, ii = got
+    for k, (ov, om, oi) in enumerate(want):
+        assert np.array_equal(verdict[k], ov), f"II row {k}"
+        assert np.array_equal(makespan[k], om), f"II row {k}"
+        assert np.array_equal(ii[k], oi), f"II row {k}"
+
+
+@pytest.mark.parametrize("n", [4096, 3001])
+def test_ii_sweep_matches_oracle_mla(verifiers, n):
+    """Each candidate at six IIs of its own (TMA kernel for n = 4096, staged kernel for 3001)."""
+    problem = problem_from_json(problem_text("mla"))
+    verifier = verifier_for(verifiers, "mla")
+    witness = witness_from_rows(verifier.packed, *raw_cases("mla")[0][0])
+    frames, batch, _ = mla_perturbations(verifier.packed, witness, n, seed=n + 5, producers=shared_producers(problem))
+    shifts = np.array([-40, -10, 0, 7, 30, 200])
+    ii_values = (batch.ii[None, :].astype(np.int64) + shifts[:, None]).astype(np.int32)
+    got = verifier.verify_periodic_sweep(frames, batch, ii_values)
+    _assert_sweep(got, _oracle_rows(problem, frames, batch, ii_values))
+    # row k equals a plain verification of the batch at those IIs
+    single = PeriodicBatch(batch.base_prologue, batch.base_offset, batch.prologue_delta, batch.offset_delta,
+                           ii_values[3].copy(), batch.frame)
+    verdict, makespan, ii = verifier.verify_periodic(frames, single)
+    assert np.array_equal(verdict, got[0][3]) and np.array_equal(makespan, got[1][3])
+
+
+def test_ii_sweep_matches_oracle_resources():
+    from random_cases import resource_wide
+    from tilefoundry_b200.workloads import ii_lower_bound, ii_sweep
+
+    problem, packed, frames, batch = resource_wide(7, 600, 80, 2, 6)
+    ii_values = np.repeat(ii_sweep(max(ii_lower_bound(packed), int(batch.ii.min()) // 2), 5)[:, None], 600, axis=1)
+    with WarpgroupVerifier(packed) as verifier:
+        got = verifier.verify_periodic_sweep(frames, batch, ii_values.astype(np.int32))
+    want = _oracle_rows(problem, frames, batch, ii_values)
+    _assert_sweep(got, want)
+    assert {0, 20} <= set(np.unique(np.concatenate([w[0] for w in want])).tolist())
+
+
+def test_ii_sweep_stress_body_matches_oracle():
+    """The 1024-op stress body at four IIs over [II_lb, 2 II_lb] (global-read kernel)."""
+    from tilefoundry_b200 import workloads
+
+    problem = workloads.stress_problem()
+    packed = pack_problem(problem)
+    witness = workloads.list_schedule_witness(packed, seed=1)
+    frames, batch = neighbourhood(packed, witness, 2, seed=5, jitter=64)
+    ii_values = np.repeat(workloads.ii_sweep(workloads.ii_lower_bound(packed), 4)[:, None], 2, axis=1)
+    ii_values[-1] = witness.ii  # one row at the witness II
+    with WarpgroupVerifier(packed) as verifier:
+        got = verifier.verify_periodic_sweep(frames, batch, ii_values.astype(np.int32))
+    _assert_sweep(got, _oracle_rows(problem, frames, batch, ii_values))

@@ -189,3 +189,25 @@ def test_gather_results_two_gloo_ranks():
         assert proc.exitcode == 0
     assert full[0] == list(range(11))
     assert full[2] == [3 * v for v in range(11)]
+
+
+def test_ii_lower_bound_and_sweep():
+    """solve.py:186-204, 261-264 from the problem records: max issue duration and, per
+    resource, ceil(sum of duration * amount / capacity)."""
+    from tilefoundry_b200 import pack_problem
+    from tilefoundry_b200.workloads import ii_lower_bound, ii_sweep, random_dag_problem
+
+    for seed in range(6):
+        problem = random_dag_problem(40, layers=4, lanes=4, n_resources=3, iterations=4, seed=seed,
+                                     latency=(2, 300), capacity=(2, 9))
+        held: dict[str, int] = {}
+        for op in problem.loop.ops:
+            for w in op.resource_windows:
+                held[w.resource_id] = held.get(w.resource_id, 0) + w.duration * w.amount
+        capacity = {r.id: r.capacity for r in problem.resources}
+        want = max([max(op.issue_duration for op in problem.loop.ops)] +
+                   [-(-total // capacity[rid]) for rid, total in held.items()])
+        assert ii_lower_bound(pack_problem(problem)) == want
+    values = ii_sweep(100, 16)
+    assert values[0] == 100 and values[-1] == 200 and len(values) == 16 and np.all(np.diff(values) > 0)
+    assert ii_sweep(7, 1).tolist() == [7]

@@ -26,7 +26,7 @@ TFV_MAX_LANES = 15
 TFV_MAX_OPS = 4095
 TFV_TIME_LIMIT = 1 << 30
 TFV_BASE_LIMIT = 1 << 28
-ABI_VERSION = 2
+ABI_VERSION = 3
 CLASS_OUT_OF_RANGE = -1
 CLASS_BAD_PACKING = -2
 CLASS_DEVICE_TIMEOUT = -3
@@ -129,6 +129,11 @@ EXPORTS = {
     "tfv_verify_periodic": (
         ctypes.c_int,
         [_p, ctypes.POINTER(Frames), _p, ctypes.c_size_t, ctypes.POINTER(PeriodicBatch), ctypes.POINTER(Results), _p],
+    ),
+    "tfv_verify_periodic_sweep": (
+        ctypes.c_int,
+        [_p, ctypes.POINTER(Frames), _p, ctypes.c_size_t, ctypes.POINTER(PeriodicBatch), ctypes.c_int, _p,
+         ctypes.POINTER(Results), _p],
     ),
     "tfv_verify_rows": (
         ctypes.c_int,

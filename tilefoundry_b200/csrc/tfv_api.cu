@@ -105,6 +105,38 @@ tfv::FrameTableShape shape_of(const tfv_problem* p, const tfv_frames* f) {
     return tfv::FrameTableShape{f->n_frames, p->dev.n_ops, f->n_sync_sets, f->n_sync_edges};
 }
 
+// Verification of a device-resident periodic batch at n_ii IIs per candidate: ii_values is
+// [n_ii][n_candidates] and the result arrays have the same shape.
+int verify_periodic_sweep(const tfv_problem* p, const tfv_frames* frames, void* table, size_t table_bytes,
+                          const tfv_periodic_batch* b, int n_ii, const int32_t* ii_values, const tfv_results* r,
+                          void* stream) {
+    if (!p || !b) return fail(TFV_ERR_INVALID_ARGUMENT, "problem and batch must not be NULL");
+    int rc = check_frames(frames);
+    if (rc) return rc;
+    rc = check_results(r);
+    if (rc) return rc;
+    if (b->n_candidates < 0 || b->op_stride < b->n_candidates)
+        return fail(TFV_ERR_INVALID_ARGUMENT, "need 0 <= n_candidates <= op_stride");
+    if (n_ii < 1) return fail(TFV_ERR_INVALID_ARGUMENT, "need at least one II per candidate");
+    if (b->n_candidates == 0) return TFV_OK;
+    if (!table || table_bytes < tfv::frame_table_bytes(shape_of(p, frames)))
+        return fail(TFV_ERR_INVALID_ARGUMENT, "frame table missing or too small");
+    if (!b->base_prologue || !b->base_offset || !b->prologue_delta || !b->offset_delta || !ii_values || !b->frame)
+        return fail(TFV_ERR_INVALID_ARGUMENT, "batch arrays must not be NULL");
+    DeviceGuard guard(p->device);
+    if (!guard.ok()) return fail(TFV_ERR_CUDA, "cannot select device %d", p->device);
+    tfv::DevPeriodic db{b->n_candidates, b->op_stride, b->base_prologue, b->base_offset,
+                        b->prologue_delta, b->offset_delta, ii_values, b->frame, n_ii, b->n_candidates};
+    tfv::DevResults dr{r->verdict, r->makespan, r->ii};
+    const tfv::DevFrames df = to_dev(*frames);
+    const tfv::FrameTable view = tfv::frame_table_view(table, shape_of(p, frames));
+    const cudaStream_t s = static_cast<cudaStream_t>(stream);
+    cudaError_t e = tfv::launch_compile_sync_programs(p->dev, df, view, b->base_prologue, b->base_offset, p->sm_count, s);
+    if (e == cudaSuccess) e = launch_periodic(p, df, view, db, dr, s);
+    if (e != cudaSuccess) return cuda_fail(e, "verify_periodic launch");
+    return TFV_OK;
+}
+
 }  // namespace
 
 extern "C" {
@@ -312,30 +344,13 @@ int tfv_analyze_frames(const tfv_problem* p, const tfv_frames* frames, void* tab
 
 int tfv_verify_periodic(const tfv_problem* p, const tfv_frames* frames, void* table, size_t table_bytes,
                         const tfv_periodic_batch* b, const tfv_results* r, void* stream) {
-    if (!p || !b) return fail(TFV_ERR_INVALID_ARGUMENT, "problem and batch must not be NULL");
-    int rc = check_frames(frames);
-    if (rc) return rc;
-    rc = check_results(r);
-    if (rc) return rc;
-    if (b->n_candidates < 0 || b->op_stride < b->n_candidates)
-        return fail(TFV_ERR_INVALID_ARGUMENT, "need 0 <= n_candidates <= op_stride");
-    if (b->n_candidates == 0) return TFV_OK;
-    if (!table || table_bytes < tfv::frame_table_bytes(shape_of(p, frames)))
-        return fail(TFV_ERR_INVALID_ARGUMENT, "frame table missing or too small");
-    if (!b->base_prologue || !b->base_offset || !b->prologue_delta || !b->offset_delta || !b->ii || !b->frame)
-        return fail(TFV_ERR_INVALID_ARGUMENT, "batch arrays must not be NULL");
-    DeviceGuard guard(p->device);
-    if (!guard.ok()) return fail(TFV_ERR_CUDA, "cannot select device %d", p->device);
-    tfv::DevPeriodic db{b->n_candidates, b->op_stride, b->base_prologue, b->base_offset,
-                        b->prologue_delta, b->offset_delta, b->ii, b->frame};
-    tfv::DevResults dr{r->verdict, r->makespan, r->ii};
-    const tfv::DevFrames df = to_dev(*frames);
-    const tfv::FrameTable view = tfv::frame_table_view(table, shape_of(p, frames));
-    const cudaStream_t s = static_cast<cudaStream_t>(stream);
-    cudaError_t e = tfv::launch_compile_sync_programs(p->dev, df, view, b->base_prologue, b->base_offset, p->sm_count, s);
-    if (e == cudaSuccess) e = launch_periodic(p, df, view, db, dr, s);
-    if (e != cudaSuccess) return cuda_fail(e, "verify_periodic launch");
-    return TFV_OK;
+    return verify_periodic_sweep(p, frames, table, table_bytes, b, 1, b ? b->ii : nullptr, r, stream);
+}
+
+int tfv_verify_periodic_sweep(const tfv_problem* p, const tfv_frames* frames, void* table, size_t table_bytes,
+                              const tfv_periodic_batch* b, int n_ii, const int32_t* ii_values, const tfv_results* r,
+                              void* stream) {
+    return verify_periodic_sweep(p, frames, table, table_bytes, b, n_ii, ii_values, r, stream);
 }
 
 int tfv_verify_rows(const tfv_problem* p, const tfv_frames* frames, const void* table, const tfv_rows_batch* b,
@@ -485,7 +500,7 @@ int tfv_verify_periodic_host(const tfv_problem* p, const tfv_frames* hf, const t
         if (e == cudaSuccess) e = cudaMemcpyAsync(sl.ii, hb->ii + c0, sizeof(int) * len, cudaMemcpyHostToDevice, s);
         if (e == cudaSuccess) e = cudaMemcpyAsync(sl.fr, hb->frame + c0, sizeof(int) * len, cudaMemcpyHostToDevice, s);
         if (e != cudaSuccess) return bail(e, "candidate upload");
-        tfv::DevPeriodic db{len, pitch, d_bp, d_bo, sl.dp, sl.dq, sl.ii, sl.fr};
+        tfv::DevPeriodic db{len, pitch, d_bp, d_bo, sl.dp, sl.dq, sl.ii, sl.fr, 1, len};
         tfv::DevResults dr{sl.v, sl.m, sl.iio};
         e = launch_periodic(p, df, tab, db, dr, s);
         if (e != cudaSuccess) return bail(e, "verify_periodic launch");
@@ -534,7 +549,7 @@ int tfv_internal_periodic_with_table(const tfv_problem* p, const tfv_frames* fra
     DeviceGuard guard(p->device);
     if (!guard.ok()) return fail(TFV_ERR_CUDA, "cannot select device %d", p->device);
     tfv::DevPeriodic db{b->n_candidates, b->op_stride, b->base_prologue, b->base_offset,
-                        b->prologue_delta, b->offset_delta, b->ii, b->frame};
+                        b->prologue_delta, b->offset_delta, b->ii, b->frame, 1, b->n_candidates};
     tfv::DevResults dr{r->verdict, r->makespan, r->ii};
     const tfv::DevFrames df = to_dev(*frames);
     const tfv::FrameTable view = tfv::frame_table_view(table, shape_of(p, frames));

@@ -143,8 +143,10 @@ struct DevPeriodic {
     const int* base_offset;
     const int16_t* prologue_delta;
     const int16_t* offset_delta;
-    const int* ii;
+    const int* ii;  // [n_ii][ii_stride]: every candidate is verified at each of n_ii IIs
     const int* frame;
+    int n_ii;
+    long long ii_stride;  // also the row stride of the [n_ii][ii_stride] results
 };
 
 struct DevRows {

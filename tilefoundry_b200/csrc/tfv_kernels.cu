@@ -644,11 +644,10 @@ __global__ void verify_periodic_kernel(DevProblem p, DevFrames fr, FrameTable ft
     for (long long c0 = static_cast<long long>(blockIdx.x) * T; c0 < b.n; c0 += static_cast<long long>(gridDim.x) * T) {
         const long long c = c0 + t;
         const bool live = c < b.n;
-        int cls = 0, ms = 0, ii = 0;
+        int* P = Ps + t;
+        int* O = Os + t;
+        int min_p = INT_MAX, max_pl = INT_MIN, min_o = INT_MAX, max_ol = INT_MIN;
         if (live) {
-            int* P = Ps + t;
-            int* O = Os + t;
-            int min_p = INT_MAX, max_pl = INT_MIN, min_o = INT_MAX, max_ol = INT_MIN;
             for (int a = 0; a < N; ++a) {
                 const int pv = bp_s[a] + b.prologue_delta[a * b.stride + c];
                 const int ov = bo_s[a] + b.offset_delta[a * b.stride + c];
@@ -659,18 +658,25 @@ __global__ void verify_periodic_kernel(DevProblem p, DevFrames fr, FrameTable ft
                 min_o = min(min_o, ov);
                 max_ol = max(max_ol, ov + lat_s[a]);
             }
-            ii = b.ii[c];
-            const Verdict v = finish_candidate(p, fr, ft, StagedView{P, O, T}, issue_s, lat_s, b.frame[c], ii, min_p,
-                                               max_pl, min_o, max_ol);
-            cls = v.cls;
-            ms = v.makespan;
         }
-        if (warp_path)
-            resolve_pending(p, cls, ii, scratch, [&](int src) {
-                const int col = (t & ~31) + src;
-                return StagedView{Ps + col, Os + col, T};
-            });
-        if (live) write_result(out, c, cls, ms, ii, p.iterations);
+        const int f = live ? b.frame[c] : 0;
+        for (int k = 0; k < b.n_ii; ++k) {  // each II of the sweep reuses the staged column
+            const long long o = k * b.ii_stride + c;
+            int cls = 0, ms = 0, ii = 0;
+            if (live) {
+                ii = b.ii[o];
+                const Verdict v = finish_candidate(p, fr, ft, StagedView{P, O, T}, issue_s, lat_s, f, ii, min_p, max_pl,
+                                                   min_o, max_ol);
+                cls = v.cls;
+                ms = v.makespan;
+            }
+            if (warp_path)
+                resolve_pending(p, cls, ii, scratch, [&](int src) {
+                    const int col = (t & ~31) + src;
+                    return StagedView{Ps + col, Os + col, T};
+                });
+            if (live) write_result(out, o, cls, ms, ii, p.iterations);
+        }
         __syncthreads();  // the staged columns are rewritten by the next round
     }
 }
@@ -697,10 +703,9 @@ __global__ void __launch_bounds__(128) verify_periodic_global_kernel(DevProblem 
     for (long long c0 = static_cast<long long>(blockIdx.x) * blockDim.x; c0 < b.n; c0 += step) {
         const long long c = c0 + threadIdx.x;
         const bool live = c < b.n;
-        int cls = 0, ms = 0, ii = 0;
+        const GlobalView V{bp_s, bo_s, b.prologue_delta, b.offset_delta, b.stride, c};
+        int min_p = INT_MAX, max_pl = INT_MIN, min_o = INT_MAX, max_ol = INT_MIN;
         if (live) {
-            const GlobalView V{bp_s, bo_s, b.prologue_delta, b.offset_delta, b.stride, c};
-            int min_p = INT_MAX, max_pl = INT_MIN, min_o = INT_MAX, max_ol = INT_MIN;
             for (int a = 0; a < N; ++a) {
                 const int pv = V.p(a), ov = V.o(a);
                 min_p = min(min_p, pv);
@@ -708,17 +713,24 @@ __global__ void __launch_bounds__(128) verify_periodic_global_kernel(DevProblem 
                 min_o = min(min_o, ov);
                 max_ol = max(max_ol, ov + lat_s[a]);
             }
-            ii = b.ii[c];
-            const Verdict v = finish_candidate(p, fr, ft, V, issue_s, lat_s, b.frame[c], ii, min_p, max_pl, min_o, max_ol);
-            cls = v.cls;
-            ms = v.makespan;
         }
-        if (warp_path)
-            resolve_pending(p, cls, ii, scratch, [&](int src) {
-                return GlobalView{bp_s, bo_s, b.prologue_delta, b.offset_delta, b.stride,
-                                  c0 + (threadIdx.x & ~31) + src};
-            });
-        if (live) write_result(out, c, cls, ms, ii, p.iterations);
+        const int f = live ? b.frame[c] : 0;
+        for (int k = 0; k < b.n_ii; ++k) {  // each II of the sweep
+            const long long o = k * b.ii_stride + c;
+            int cls = 0, ms = 0, ii = 0;
+            if (live) {
+                ii = b.ii[o];
+                const Verdict v = finish_candidate(p, fr, ft, V, issue_s, lat_s, f, ii, min_p, max_pl, min_o, max_ol);
+                cls = v.cls;
+                ms = v.makespan;
+            }
+            if (warp_path)
+                resolve_pending(p, cls, ii, scratch, [&](int src) {
+                    return GlobalView{bp_s, bo_s, b.prologue_delta, b.offset_delta, b.stride,
+                                      c0 + (threadIdx.x & ~31) + src};
+                });
+            if (live) write_result(out, o, cls, ms, ii, p.iterations);
+        }
     }
 }
 

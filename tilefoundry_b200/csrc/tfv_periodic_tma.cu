@@ -183,114 +183,120 @@ __global__ void __launch_bounds__(kTile) verify_periodic_tma_kernel(DevProblem p
         const long long c = static_cast<long long>(tile) * kTile + t;
         const bool live = c < b.n;
         const int f_in = live ? b.frame[c] : 0;
-        const int ii = live ? b.ii[c] : 0;
+        const int ii_first = live ? b.ii[c] : 0;
         const bool landed = __syncthreads_and(mbar_wait_bounded(bar, phase));
         if (!landed) {  // report, drain the copy (bounded) and leave
-            if (live) {
-                out.verdict[c] = TFV_CLASS_DEVICE_TIMEOUT;
-                out.makespan[c] = 0;
-                out.ii[c] = 0;
-            }
+            if (live)
+                for (int k = 0; k < b.n_ii; ++k) {
+                    const long long o = k * b.ii_stride + c;
+                    out.verdict[o] = TFV_CLASS_DEVICE_TIMEOUT;
+                    out.makespan[o] = 0;
+                    out.ii[o] = 0;
+                }
             mbar_wait_bounded(bar, phase);
             return;
         }
         phase ^= 1;
-        int cls = 0, ms = 0;  // this thread's verdict and makespan
-        if (live && fr.n_frames > 0) {
-            const int16_t* mp = tp + t;
-            const int16_t* mo = to + t;
-            const bool frame_ok = static_cast<unsigned>(f_in) < static_cast<unsigned>(fr.n_frames);
-            const int f = frame_ok ? f_in : 0;
-            const int fclass = frame_ok ? ft.frame_class[f] : TFV_CLASS_BAD_PACKING;
-            Extremes x{INT_MAX, INT_MAX, INT_MIN, INT_MIN};
-            const char* row_p = reinterpret_cast<const char*>(mp);
-            const int to_bytes = N * kTmaRowBytes;
-            const int lane_min = walk_lanes<kBodyRows>(ft.order + static_cast<size_t>(f) * N,
-                                                       ft.lane_len + static_cast<size_t>(f) * 16, opc, row_p, to_bytes,
-                                                       N, ii, x);
-            // Sync edges before the set's first static failure, base starts folded in.
-            const int set = fr.sync_set[f];
-            const int2 meta = (static_cast<unsigned>(set) < static_cast<unsigned>(fr.n_sync_sets))
-                                  ? ft.set_meta[set] : make_int2(0, TFV_CLASS_BAD_PACKING);
-            const int4* prog = ft.set_prog + (meta.x > 0 ? fr.sync_offsets[set] : 0);
-            int sync_min = INT_MAX;
-#pragma unroll 4
-            for (int k = 0; k < meta.x; ++k) {
-                const int4 e = prog[k];
-                const int a_row = e.x & 0xFFFF, b_row = static_cast<unsigned>(e.x) >> 16;
-                const int x_row = e.y & 0x1FFFF, d = static_cast<unsigned>(e.y) >> 17;
-                const int dpa = *reinterpret_cast<const int16_t*>(row_p + a_row);
-                const int doa = *reinterpret_cast<const int16_t*>(row_p + to_bytes + a_row);
-                const int dob = *reinterpret_cast<const int16_t*>(row_p + to_bytes + b_row);
-                const int xb = *reinterpret_cast<const int16_t*>(row_p + x_row);
-                const int shift = d * ii;
-                sync_min = __viaddmin_s32(e.z + xb - dpa, shift, sync_min);  // instance 0
-                sync_min = __viaddmin_s32(e.w + dob - doa, shift, sync_min);  // instances >= 1
+        for (int k = 0; k < b.n_ii; ++k) {  // each II of the sweep reuses the staged tile
+            const long long o = k * b.ii_stride + c;
+            const int ii = k == 0 ? ii_first : (live ? b.ii[o] : 0);
+            int cls = 0, ms = 0;  // this thread's verdict and makespan
+            if (live && fr.n_frames > 0) {
+                const int16_t* mp = tp + t;
+                const int16_t* mo = to + t;
+                const bool frame_ok = static_cast<unsigned>(f_in) < static_cast<unsigned>(fr.n_frames);
+                const int f = frame_ok ? f_in : 0;
+                const int fclass = frame_ok ? ft.frame_class[f] : TFV_CLASS_BAD_PACKING;
+                Extremes x{INT_MAX, INT_MAX, INT_MIN, INT_MIN};
+                const char* row_p = reinterpret_cast<const char*>(mp);
+                const int to_bytes = N * kTmaRowBytes;
+                const int lane_min = walk_lanes<kBodyRows>(ft.order + static_cast<size_t>(f) * N,
+                                                           ft.lane_len + static_cast<size_t>(f) * 16, opc, row_p, to_bytes,
+                                                           N, ii, x);
+                // Sync edges before the set's first static failure, base starts folded in.
+                const int set = fr.sync_set[f];
+                const int2 meta = (static_cast<unsigned>(set) < static_cast<unsigned>(fr.n_sync_sets))
+                                      ? ft.set_meta[set] : make_int2(0, TFV_CLASS_BAD_PACKING);
+                const int4* prog = ft.set_prog + (meta.x > 0 ? fr.sync_offsets[set] : 0);
+                int sync_min = INT_MAX;
+    #pragma unroll 4
+                for (int k = 0; k < meta.x; ++k) {
+                    const int4 e = prog[k];
+                    const int a_row = e.x & 0xFFFF, b_row = static_cast<unsigned>(e.x) >> 16;
+                    const int x_row = e.y & 0x1FFFF, d = static_cast<unsigned>(e.y) >> 17;
+                    const int dpa = *reinterpret_cast<const int16_t*>(row_p + a_row);
+                    const int doa = *reinterpret_cast<const int16_t*>(row_p + to_bytes + a_row);
+                    const int dob = *reinterpret_cast<const int16_t*>(row_p + to_bytes + b_row);
+                    const int xb = *reinterpret_cast<const int16_t*>(row_p + x_row);
+                    const int shift = d * ii;
+                    sync_min = __viaddmin_s32(e.z + xb - dpa, shift, sync_min);  // instance 0
+                    sync_min = __viaddmin_s32(e.w + dob - doa, shift, sync_min);  // instances >= 1
+                }
+                // First relation without a lane/sync path: timing at instance 0 decides 17 vs 18.
+                int rel_cls = 0;
+                const int r = ft.first_unreached[f];
+                if (r >= 0) {
+                    const int packed = p.relation[r];
+                    const int a = packed & 0xFFF, bb = (packed >> 12) & 0xFFF, d = packed >> 24;
+                    const int ready = opc[a].z + mp[a * kTile] + opc[a].y;
+                    const int target = d == 0 ? opc[bb].z + mp[bb * kTile] : opc[bb].w + mo[bb * kTile] + ii;
+                    rel_cls = ready > target ? TFV_CLASS_RELATION_TIMING : TFV_CLASS_RELATION_NO_PATH;
+                }
+                bool carried_bad = false;
+                if (kBodyRows >= 1) {
+                    for (int k = 0; k < p.n_carried; ++k) {
+                        const int packed = p.carried[k];
+                        const int u = packed & 0xFFFF, df = packed >> 16;
+                        carried_bad |= opc[u].w + mo[u * kTile] + opc[u].y > opc[df].w + mo[df * kTile];
+                    }
+                }
+                long long makespan = x.max_pl;
+                bool negative = x.min_p < 0;
+                bool out_of_range = !base_ok;
+                if (kBodyRows >= 1) {
+                    const long long k1 = ii, kl = static_cast<long long>(I - 1) * ii;
+                    const long long lo = k1 < kl ? k1 : kl, hi = k1 < kl ? kl : k1;
+                    negative |= static_cast<long long>(x.min_o) + lo < 0;
+                    const long long body = static_cast<long long>(x.max_ol) + hi;
+                    makespan = makespan > body ? makespan : body;
+                    out_of_range |= hi >= TFV_TIME_LIMIT || lo <= -static_cast<long long>(TFV_TIME_LIMIT);
+                }
+                out_of_range |= makespan >= TFV_TIME_LIMIT;
+                if (fclass == TFV_CLASS_BAD_PACKING) cls = TFV_CLASS_BAD_PACKING;
+                else if (fclass == TFV_CLASS_SCHEDULE_MALFORMED || negative) cls = TFV_CLASS_SCHEDULE_MALFORMED;
+                else if (out_of_range) cls = TFV_CLASS_OUT_OF_RANGE;
+                else if (fclass != 0) cls = fclass;
+                else if (kBodyRows >= 2 && ii <= 0) cls = TFV_CLASS_II_NONPOSITIVE;
+                else if (lane_min < 0) cls = TFV_CLASS_LANE_ORDER;
+                else if (sync_min < 0) cls = TFV_CLASS_SYNC_INEQUALITY;
+                else if (meta.y != 0) cls = meta.y;
+                else if (ft.frame_flags[f] & kFrameRegisterCross) cls = TFV_CLASS_REGISTER_CROSSES_LANES;
+                else if (rel_cls) cls = rel_cls;
+                else if (carried_bad) cls = TFV_CLASS_CARRIED_SHARED_LIFETIME;
+                else if (p.n_resources == 0) cls = TFV_CLASS_PASS;
+                else if (warp_path) cls = kResourcesPending;
+                else cls = thread_resources_exceed(p, TileView{opc, mp, mo}, ii) ? TFV_CLASS_RESOURCE_CAPACITY
+                                                                                   : TFV_CLASS_PASS;
+                ms = makespan > INT_MAX ? INT_MAX : (makespan < INT_MIN ? INT_MIN : static_cast<int>(makespan));
+            } else if (live) {  // no frames at all: the candidate cannot name one
+                cls = TFV_CLASS_BAD_PACKING;
             }
-            // First relation without a lane/sync path: timing at instance 0 decides 17 vs 18.
-            int rel_cls = 0;
-            const int r = ft.first_unreached[f];
-            if (r >= 0) {
-                const int packed = p.relation[r];
-                const int a = packed & 0xFFF, bb = (packed >> 12) & 0xFFF, d = packed >> 24;
-                const int ready = opc[a].z + mp[a * kTile] + opc[a].y;
-                const int target = d == 0 ? opc[bb].z + mp[bb * kTile] : opc[bb].w + mo[bb * kTile] + ii;
-                rel_cls = ready > target ? TFV_CLASS_RELATION_TIMING : TFV_CLASS_RELATION_NO_PATH;
-            }
-            bool carried_bad = false;
-            if (kBodyRows >= 1) {
-                for (int k = 0; k < p.n_carried; ++k) {
-                    const int packed = p.carried[k];
-                    const int u = packed & 0xFFFF, df = packed >> 16;
-                    carried_bad |= opc[u].w + mo[u * kTile] + opc[u].y > opc[df].w + mo[df * kTile];
+            if (warp_path) {  // capacity (class 20): the warp checks its pending candidates one by one
+                unsigned pending = __ballot_sync(0xFFFFFFFFu, cls == kResourcesPending);
+                while (pending) {
+                    const int src = __ffs(pending) - 1;
+                    pending &= pending - 1;
+                    const int src_ii = __shfl_sync(0xFFFFFFFFu, ii, src);
+                    const int col = (t & ~31) + src;
+                    const bool exceed = warp_resources_exceed(p, TileView{opc, tp + col, to + col}, src_ii, scratch, lane);
+                    if (lane == src) cls = exceed ? TFV_CLASS_RESOURCE_CAPACITY : TFV_CLASS_PASS;
                 }
             }
-            long long makespan = x.max_pl;
-            bool negative = x.min_p < 0;
-            bool out_of_range = !base_ok;
-            if (kBodyRows >= 1) {
-                const long long k1 = ii, kl = static_cast<long long>(I - 1) * ii;
-                const long long lo = k1 < kl ? k1 : kl, hi = k1 < kl ? kl : k1;
-                negative |= static_cast<long long>(x.min_o) + lo < 0;
-                const long long body = static_cast<long long>(x.max_ol) + hi;
-                makespan = makespan > body ? makespan : body;
-                out_of_range |= hi >= TFV_TIME_LIMIT || lo <= -static_cast<long long>(TFV_TIME_LIMIT);
+            if (live) {
+                out.verdict[o] = cls;
+                out.makespan[o] = ms;
+                out.ii[o] = kBodyRows >= 2 ? ii : 0;
             }
-            out_of_range |= makespan >= TFV_TIME_LIMIT;
-            if (fclass == TFV_CLASS_BAD_PACKING) cls = TFV_CLASS_BAD_PACKING;
-            else if (fclass == TFV_CLASS_SCHEDULE_MALFORMED || negative) cls = TFV_CLASS_SCHEDULE_MALFORMED;
-            else if (out_of_range) cls = TFV_CLASS_OUT_OF_RANGE;
-            else if (fclass != 0) cls = fclass;
-            else if (kBodyRows >= 2 && ii <= 0) cls = TFV_CLASS_II_NONPOSITIVE;
-            else if (lane_min < 0) cls = TFV_CLASS_LANE_ORDER;
-            else if (sync_min < 0) cls = TFV_CLASS_SYNC_INEQUALITY;
-            else if (meta.y != 0) cls = meta.y;
-            else if (ft.frame_flags[f] & kFrameRegisterCross) cls = TFV_CLASS_REGISTER_CROSSES_LANES;
-            else if (rel_cls) cls = rel_cls;
-            else if (carried_bad) cls = TFV_CLASS_CARRIED_SHARED_LIFETIME;
-            else if (p.n_resources == 0) cls = TFV_CLASS_PASS;
-            else if (warp_path) cls = kResourcesPending;
-            else cls = thread_resources_exceed(p, TileView{opc, mp, mo}, ii) ? TFV_CLASS_RESOURCE_CAPACITY
-                                                                               : TFV_CLASS_PASS;
-            ms = makespan > INT_MAX ? INT_MAX : (makespan < INT_MIN ? INT_MIN : static_cast<int>(makespan));
-        } else if (live) {  // no frames at all: the candidate cannot name one
-            cls = TFV_CLASS_BAD_PACKING;
-        }
-        if (warp_path) {  // capacity (class 20): the warp checks its pending candidates one by one
-            unsigned pending = __ballot_sync(0xFFFFFFFFu, cls == kResourcesPending);
-            while (pending) {
-                const int src = __ffs(pending) - 1;
-                pending &= pending - 1;
-                const int src_ii = __shfl_sync(0xFFFFFFFFu, ii, src);
-                const int col = (t & ~31) + src;
-                const bool exceed = warp_resources_exceed(p, TileView{opc, tp + col, to + col}, src_ii, scratch, lane);
-                if (lane == src) cls = exceed ? TFV_CLASS_RESOURCE_CAPACITY : TFV_CLASS_PASS;
-            }
-        }
-        if (live) {
-            out.verdict[c] = cls;
-            out.makespan[c] = ms;
-            out.ii[c] = kBodyRows >= 2 ? ii : 0;
         }
         __syncthreads();  // every thread is done with the tile before the next copy lands
     }

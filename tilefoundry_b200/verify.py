@@ -221,6 +221,64 @@ class WarpgroupVerifier:
         )
         return out
 
+    def verify_periodic_sweep_device(self, frames: DeviceFrames, table, batch: dict, ii_values, out=None,
+                                     stream: Any = None):
+        """Verify every device-resident periodic candidate at several IIs.
+
+        ``batch`` is as for :meth:`verify_periodic_device` (its ``ii`` is not read);
+        ``ii_values`` is an int32 tensor [n_ii, n] on this device, row k holding every
+        candidate's k-th II. Returns ``(verdict, makespan, ii)`` int32 tensors [n_ii, n].
+        """
+        torch = _torch()
+        n = int(batch["frame"].shape[0])
+        if ii_values.dtype != torch.int32 or ii_values.dim() != 2 or int(ii_values.shape[1]) != n:
+            raise ValueError("ii_values must be an int32 tensor of shape [n_ii, n_candidates]")
+        ii_values = ii_values.contiguous()
+        n_ii = int(ii_values.shape[0])
+        struct = _lib.PeriodicBatch(
+            n,
+            int(batch["prologue_delta"].stride(0)),
+            batch["base_prologue"].data_ptr(),
+            batch["base_offset"].data_ptr(),
+            batch["prologue_delta"].data_ptr(),
+            batch["offset_delta"].data_ptr(),
+            None,
+            batch["frame"].data_ptr(),
+        )
+        if out is None:
+            dev = torch.device("cuda", self.device)
+            out = tuple(torch.empty((n_ii, n), dtype=torch.int32, device=dev) for _ in range(3))
+        verdict, makespan, ii = out
+        results = _lib.Results(verdict.data_ptr(), makespan.data_ptr(), ii.data_ptr())
+        _lib.check(
+            self._lib.tfv_verify_periodic_sweep(
+                self._handle, ctypes.byref(frames.struct), table.data_ptr(), int(table.numel()), ctypes.byref(struct),
+                n_ii, ii_values.data_ptr(), ctypes.byref(results), self._stream(stream),
+            ),
+            "tfv_verify_periodic_sweep",
+        )
+        return out
+
+    def verify_periodic_sweep(self, frames, batch, ii_values):
+        """Host-array convenience for :meth:`verify_periodic_sweep_device`.
+
+        ``frames`` is a :class:`~tilefoundry_b200.batch.FrameSet`, ``batch`` a
+        :class:`~tilefoundry_b200.batch.PeriodicBatch` and ``ii_values`` an integer array
+        [n_ii, n]. Returns numpy ``(verdict, makespan, ii)`` arrays [n_ii, n].
+        """
+        torch = _torch()
+        dev = torch.device("cuda", self.device)
+        dframes = self.frames_to_device(frames)
+        tensors = {
+            key: torch.from_numpy(np.ascontiguousarray(getattr(batch, key))).to(dev)
+            for key in ("base_prologue", "base_offset", "prologue_delta", "offset_delta", "frame")
+        }
+        ii_t = torch.from_numpy(np.ascontiguousarray(ii_values, dtype=np.int32)).to(dev)
+        table = self.analyze(dframes)
+        out = self.verify_periodic_sweep_device(dframes, table, tensors, ii_t)
+        torch.cuda.synchronize(dev)
+        return tuple(t.cpu().numpy() for t in out)
+
     def verify_rows_device(self, frames: DeviceFrames, table, batch: dict, out=None, stream: Any = None):
         """Verify device-resident explicit rows (``start``/``issue_end``/``completion`` [n, I, N])."""
         n = int(batch["frame"].shape[0])

@@ -528,3 +528,24 @@ def stress_problem(seed: int = 0):
     return random_dag_problem(
         1024, layers=32, lanes=12, n_resources=6, iterations=64, seed=seed, pareto_alpha=1.5, demand=(1, 8)
     )
+
+
+def ii_lower_bound(packed: PackedProblem) -> int:
+    """The solver's II lower bound: the longest issue duration, and per resource the
+    held amount-cycles of one iteration over its capacity, rounded up
+    (solve.py:186-204, 261-264)."""
+    bound = int(packed.issue.max()) if packed.n_ops else 1
+    held: dict[int, int] = {}
+    for w in range(len(packed.window_resource)):
+        q = int(packed.window_resource[w])
+        held[q] = held.get(q, 0) + int(packed.window_duration[w]) * int(packed.window_amount[w])
+    for q, total in held.items():
+        bound = max(bound, -(-total // int(packed.capacity[q])))
+    return max(bound, 1)
+
+
+def ii_sweep(ii_lb: int, n_ii: int = 16) -> np.ndarray:
+    """``n_ii`` initiation intervals spread evenly over [ii_lb, 2 * ii_lb]."""
+    if n_ii == 1:
+        return np.array([ii_lb], dtype=np.int64)
+    return ii_lb + (np.arange(n_ii, dtype=np.int64) * ii_lb) // (n_ii - 1)

@@ -202,6 +202,21 @@ TFV_API int tfv_frame_table_bytes(const tfv_problem* problem, const tfv_frames* 
 TFV_API int tfv_analyze_frames(const tfv_problem* problem, const tfv_frames* frames,
                        void* frame_table, size_t frame_table_bytes, void* stream);
 
+/* Canonical synchronization export of every frame (sync.py:21-62): the analysis of
+ * tfv_analyze_frames plus, per frame, which edges of its sync set are retained.
+ * Each frame's sync set must be the complete candidate set: the problem's required
+ * completion relations with a finite instance (distance < iterations), in sorted order
+ * (sync.py:41-45). Edges are decided in that order; an edge is dropped when every one of
+ * its instances stays reachable through the lanes and the edges still retained
+ * (sync.py:49-58). keep[f * keep_stride + j] (device, n_frames * keep_stride bytes,
+ * keep_stride >= the longest set) is 1 when edge j of frame f's set is retained, 0 when
+ * dropped. A frame that is structurally bad, cyclic, or whose set holds an edge with an
+ * unknown operation or no instance keeps every edge; the reference rejects those
+ * schedules before reducing (sync.py:46-47), which callers check with a verification
+ * of the complete schedule. */
+TFV_API int tfv_export_sync(const tfv_problem* problem, const tfv_frames* frames, void* frame_table,
+                            size_t frame_table_bytes, uint8_t* keep, int keep_stride, void* stream);
+
 /* Verify compact periodic candidates against analysed frames
  * (verify.py:203-322 for every candidate of the batch). Also writes the batch's sync
  * programs (sync edges with the base starts folded in) into the frame table.

@@ -542,3 +542,35 @@ def materialize_periodic(problem, prologue: dict, offset: dict, ii: int):
                 )
             )
     return rows
+
+
+# ---------------------------------------------------------------------------
+# Canonical synchronization export (sync.py:21-62)
+# ---------------------------------------------------------------------------
+
+
+def export_sync(problem, lanes, times_rows):
+    """Restate ``export_warpgroup_schedule`` (sync.py:21-62) for one solve result.
+
+    ``lanes`` is a tuple of op-id tuples and ``times_rows`` canonical rows. Returns
+    ``("ok", retained)`` with the retained relations in candidate order, or
+    ``("fail", class_id)`` when the schedule with every candidate relation does not
+    verify (sync.py:46-47). The candidates are the required completion relations with a
+    finite instance (sync.py:41-45); each is dropped, in order, when every one of its
+    instances stays reachable through the lanes and the relations still retained
+    (sync.py:49-58).
+    """
+    iterations = problem.loop.iterations
+    candidates = tuple(edge for edge in required_completion_relations(problem) if edge[2] < iterations)
+    try:
+        verify_canonical(problem, lanes, tuple(sorted(candidates)), times_rows)
+    except OracleFailure as failure:
+        return "fail", failure.class_id
+    retained = list(candidates)
+    for candidate in candidates:
+        trial = tuple(item for item in retained if item != candidate)
+        control = completion_event_edges(problem, lanes, trial)
+        if all(event_reachable(control, after, before) for after, before in expand_relation(candidate, iterations)):
+            retained.remove(candidate)
+    verify_canonical(problem, lanes, tuple(sorted(retained)), times_rows)  # sync.py:60-61
+    return "ok", tuple(retained)

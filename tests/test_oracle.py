@@ -74,3 +74,14 @@ def test_golden_covers_every_reachable_class():
         seen.update(v[0] for v in raw_cases(name)[1])
         seen.update(int(v) for v in periodic_cases(name)["verdict"])
     assert seen >= {0, 1, 2, 4, 5, 7, 8, 9, 10, 11, 12, 13, 14, 15, 16, 17, 18, 19, 20}
+
+
+def test_port_export_reproduces_the_reference_exported_mla_sync():
+    """The committed MLA schedule was exported by the reference (sync.py:21-62): exporting
+    its lanes and times again keeps exactly its 48 sync edges."""
+    problem = load_problem(problem_text("mla"))
+    lanes, sync, rows = raw_cases("mla")[0][0]
+    clanes, csync, crows = port.construct(lanes, sync, rows)
+    status, kept = port.export_sync(problem, clanes, crows)
+    assert status == "ok"
+    assert sorted(kept) == sorted(csync) and len(kept) == 48

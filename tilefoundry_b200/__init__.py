@@ -31,9 +31,11 @@ from .model import (
     WarpgroupLane,
     WarpgroupProblem,
     WarpgroupSchedule,
+    WarpgroupSolveResult,
 )
 from .problem import PackedProblem, pack_problem
 from .serialization import problem_from_json, problem_to_json, schedule_from_json, schedule_to_json
+from .sync import export_warpgroup_schedule, export_warpgroup_schedules
 from .verify import (
     CLASS_NAMES,
     WarpgroupVerifier,
@@ -58,6 +60,9 @@ __all__ = [
     "ResourceWindow",
     "SCHEDULE_FORMAT",
     "SynchronizationEdge",
+    "WarpgroupSolveResult",
+    "export_warpgroup_schedule",
+    "export_warpgroup_schedules",
     "TensorType",
     "TimedOperation",
     "ValueRef",

@@ -130,6 +130,7 @@ EXPORTS = {
         ctypes.c_int,
         [_p, ctypes.POINTER(Frames), _p, ctypes.c_size_t, ctypes.POINTER(PeriodicBatch), ctypes.POINTER(Results), _p],
     ),
+    "tfv_export_sync": (ctypes.c_int, [_p, ctypes.POINTER(Frames), _p, ctypes.c_size_t, _p, ctypes.c_int, _p]),
     "tfv_verify_periodic_sweep": (
         ctypes.c_int,
         [_p, ctypes.POINTER(Frames), _p, ctypes.c_size_t, ctypes.POINTER(PeriodicBatch), ctypes.c_int, _p,

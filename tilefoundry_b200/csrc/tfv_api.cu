@@ -342,6 +342,23 @@ int tfv_analyze_frames(const tfv_problem* p, const tfv_frames* frames, void* tab
     return TFV_OK;
 }
 
+int tfv_export_sync(const tfv_problem* p, const tfv_frames* frames, void* table, size_t table_bytes, uint8_t* keep,
+                    int keep_stride, void* stream) {
+    if (!p) return fail(TFV_ERR_INVALID_ARGUMENT, "problem is NULL");
+    int rc = check_frames(frames);
+    if (rc) return rc;
+    if (!table || table_bytes < tfv::frame_table_bytes(shape_of(p, frames)))
+        return fail(TFV_ERR_INVALID_ARGUMENT, "frame table missing or too small");
+    if (frames->n_frames > 0 && (!keep || keep_stride <= 0))
+        return fail(TFV_ERR_INVALID_ARGUMENT, "keep must hold n_frames * keep_stride bytes with keep_stride > 0");
+    DeviceGuard guard(p->device);
+    if (!guard.ok()) return fail(TFV_ERR_CUDA, "cannot select device %d", p->device);
+    cudaError_t e = tfv::launch_analyze_frames(p->dev, to_dev(*frames), tfv::frame_table_view(table, shape_of(p, frames)),
+                                               p->sm_count, static_cast<cudaStream_t>(stream), keep, keep_stride);
+    if (e != cudaSuccess) return cuda_fail(e, "export_sync launch");
+    return TFV_OK;
+}
+
 int tfv_verify_periodic(const tfv_problem* p, const tfv_frames* frames, void* table, size_t table_bytes,
                         const tfv_periodic_batch* b, const tfv_results* r, void* stream) {
     return verify_periodic_sweep(p, frames, table, table_bytes, b, 1, b ? b->ii : nullptr, r, stream);

@@ -165,8 +165,12 @@ struct DevResults {
 };
 
 // Launchers (tfv_kernels.cu). Each returns the cudaError_t of its launch.
+// With keep != nullptr the analysis also exports each frame's sync set (sync.py:21-62):
+// keep[f * keep_stride + j] = 1 when edge j of frame f's set is retained. The sets must
+// be the complete candidate sets (required relations with a finite instance, sorted);
+// frames that are structurally bad, cyclic or whose set has a 13/14 edge keep every edge.
 cudaError_t launch_analyze_frames(const DevProblem& p, const DevFrames& f, FrameTable t,
-                                  int sm_count, cudaStream_t stream);
+                                  int sm_count, cudaStream_t stream, uint8_t* keep = nullptr, int keep_stride = 0);
 cudaError_t launch_verify_periodic(const DevProblem& p, const DevFrames& f, FrameTable t,
                                    const DevPeriodic& b, DevResults r, int sm_count,
                                    cudaStream_t stream);

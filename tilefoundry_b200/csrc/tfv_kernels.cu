@@ -66,7 +66,10 @@ size_t analyze_smem_bytes(int n, int lanes) {
 //           from start(y) (suffixes of a lane are closed under reachability, because
 //           start -> issue_end -> next start follows the lane, verify.py:132-137).
 // M1[y][l]: the same for lane l in the next iteration.
-__global__ void __launch_bounds__(32) analyze_frames_kernel(DevProblem p, DevFrames fr, FrameTable ft, int edge_cap) {
+// With `keep` set, also writes the canonical sync export of every frame (see
+// launch_analyze_frames in tfv_device.cuh): keep[f * keep_stride + j] for edge j of the set.
+__global__ void __launch_bounds__(32) analyze_frames_kernel(DevProblem p, DevFrames fr, FrameTable ft, int edge_cap,
+                                                            uint8_t* keep, int keep_stride) {
     extern __shared__ __align__(16) unsigned char smem[];
     const int N = p.n_ops;
     const int L = p.warp_groups;
@@ -223,6 +226,7 @@ __global__ void __launch_bounds__(32) analyze_frames_kernel(DevProblem p, DevFra
 
         // Reachability of every required relation (verify.py:122-160, 306-314).
         int first_unreached = -1;
+        bool exported = false;
         if (cls == 0 && !unusable_for_paths) {
             const bool fits = e1 - e0 <= edge_cap;
             if (fits)
@@ -360,8 +364,46 @@ __global__ void __launch_bounds__(32) analyze_frames_kernel(DevProblem p, DevFra
                         break;
                     }
                 }
+                // Canonical sync export (sync.py:49-58): the edges of the set are the candidate
+                // relations in sorted order, so each operation's out-edges form one run and are
+                // decided in that order. Edge (a, b, d) is dropped when completion(a) still
+                // reaches start(b) d iterations later through another edge kept so far (a sync
+                // edge of a, or its lane successor when issue == latency). Dropping an edge
+                // that another path implies leaves every reachability unchanged, so the closure
+                // of the complete set answers every later query too.
+                if (keep) {
+                    uint8_t* kf = keep + static_cast<size_t>(f) * keep_stride;
+                    for (int a = lane; a < N; a += 32) {
+                        const int lo = adj_lo[a], hi = adj_hi[a];
+                        const int s = succ[a];
+                        const bool through_lane = p.issue[a] == p.latency[a];
+                        for (int k = lo; k < hi; ++k) {
+                            const int v = edge(k);
+                            const int b = v & 0xFFF, d = v >> 12;
+                            bool implied = false;
+                            if (d <= 1) {
+                                const int lb = lane_of(lp[b]), qb = pos_of(lp[b]);
+                                for (int k2 = lo; k2 < hi && !implied; ++k2) {
+                                    if (k2 == k || (k2 < k && kf[k2 - e0] == 0)) continue;
+                                    const int v2 = edge(k2);
+                                    const int t = v2 & 0xFFF, d2 = v2 >> 12;
+                                    if (d2 == 0) implied = (d == 0 ? M0[t * L + lb] : M1[t * L + lb]) <= qb;
+                                    else if (d2 == 1 && d == 1) implied = M0[t * L + lb] <= qb;
+                                }
+                                if (!implied && through_lane) {
+                                    if (!(s & kWrap)) implied = (d == 0 ? M0[s * L + lb] : M1[s * L + lb]) <= qb;
+                                    else if (d == 1) implied = M0[(s & kSuccMask) * L + lb] <= qb;
+                                }
+                            }
+                            kf[k - e0] = implied ? 0 : 1;
+                        }
+                    }
+                    exported = true;
+                }
             }
         }
+        if (keep && !exported)  // no export for this frame: every edge stays
+            for (int j = lane; j < keep_stride; j += 32) keep[static_cast<size_t>(f) * keep_stride + j] = 1;
         if (lane == 0) {
             ft.frame_class[f] = cls;
             ft.frame_flags[f] = out_flags;
@@ -372,7 +414,7 @@ __global__ void __launch_bounds__(32) analyze_frames_kernel(DevProblem p, DevFra
 }
 
 cudaError_t launch_analyze_frames(const DevProblem& p, const DevFrames& f, FrameTable t, int sm_count,
-                                  cudaStream_t stream) {
+                                  cudaStream_t stream, uint8_t* keep, int keep_stride) {
     if (f.n_frames <= 0) return cudaSuccess;
     // Stage each frame's sync set in shared memory when the device has room for it.
     int device = 0, optin = 48 * 1024;
@@ -388,7 +430,7 @@ cudaError_t launch_analyze_frames(const DevProblem& p, const DevFrames& f, Frame
         if (e != cudaSuccess) return e;
     }
     const int grid = min(f.n_frames, sm_count * 32);
-    analyze_frames_kernel<<<grid, 32, smem, stream>>>(p, f, t, edge_cap);
+    analyze_frames_kernel<<<grid, 32, smem, stream>>>(p, f, t, edge_cap, keep, keep_stride);
     return cudaGetLastError();
 }
 

@@ -140,7 +140,7 @@ struct TileView {
     __device__ __forceinline__ int o(int a) const { return opc[a].w + mo[a * kTile]; }
 };
 
-template <int kBodyRows>
+template <int kBodyRows, bool kSweep>  // kSweep: more than one II per candidate
 __global__ void __launch_bounds__(kTile) verify_periodic_tma_kernel(DevProblem p, DevFrames fr, FrameTable ft,
                                                                      DevPeriodic b, DevResults out, int n_tiles,
                                                                      const __grid_constant__ CUtensorMap map_p,
@@ -157,6 +157,7 @@ __global__ void __launch_bounds__(kTile) verify_periodic_tma_kernel(DevProblem p
     // capacity-check records of this warp (warp path only)
     int4* scratch = reinterpret_cast<int4*>(bar + 2) + (t >> 5) * 2 * p.res_max_windows;
     const bool warp_path = warp_resources_used(p);
+    const int n_ii = kSweep ? b.n_ii : 1;
 
     bool base_ok = true;
     for (int s = t; s < N; s += kTile) {
@@ -187,7 +188,7 @@ __global__ void __launch_bounds__(kTile) verify_periodic_tma_kernel(DevProblem p
         const bool landed = __syncthreads_and(mbar_wait_bounded(bar, phase));
         if (!landed) {  // report, drain the copy (bounded) and leave
             if (live)
-                for (int k = 0; k < b.n_ii; ++k) {
+                for (int k = 0; k < n_ii; ++k) {
                     const long long o = k * b.ii_stride + c;
                     out.verdict[o] = TFV_CLASS_DEVICE_TIMEOUT;
                     out.makespan[o] = 0;
@@ -197,7 +198,7 @@ __global__ void __launch_bounds__(kTile) verify_periodic_tma_kernel(DevProblem p
             return;
         }
         phase ^= 1;
-        for (int k = 0; k < b.n_ii; ++k) {  // each II of the sweep reuses the staged tile
+        for (int k = 0; k < n_ii; ++k) {  // each II of the sweep reuses the staged tile
             const long long o = k * b.ii_stride + c;
             const int ii = k == 0 ? ii_first : (live ? b.ii[o] : 0);
             int cls = 0, ms = 0;  // this thread's verdict and makespan
@@ -343,10 +344,10 @@ bool periodic_tma_supported(const DevProblem& p, const DevPeriodic& b) {
 
 namespace {
 
-template <int kBodyRows>
+template <int kBodyRows, bool kSweep>
 cudaError_t launch_tma(const DevProblem& p, const DevFrames& f, FrameTable t, const DevPeriodic& b, DevResults r,
                        int sm_count, cudaStream_t stream, const CUtensorMap& map_p, const CUtensorMap& map_o) {
-    auto kernel = verify_periodic_tma_kernel<kBodyRows>;
+    auto kernel = verify_periodic_tma_kernel<kBodyRows, kSweep>;
     const size_t smem = tma_smem_bytes(p);
     if (smem > 48 * 1024) {
         cudaError_t e = cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(smem));
@@ -372,9 +373,14 @@ cudaError_t launch_verify_periodic_tma(const DevProblem& p, const DevFrames& f, 
     if (!make_map(&map_p, b.prologue_delta, b.n, b.stride, p.n_ops) ||
         !make_map(&map_o, b.offset_delta, b.n, b.stride, p.n_ops))
         return cudaErrorInvalidValue;
-    if (p.iterations >= 3) return launch_tma<2>(p, f, t, b, r, sm_count, stream, map_p, map_o);
-    if (p.iterations == 2) return launch_tma<1>(p, f, t, b, r, sm_count, stream, map_p, map_o);
-    return launch_tma<0>(p, f, t, b, r, sm_count, stream, map_p, map_o);
+    if (b.n_ii > 1) {
+        if (p.iterations >= 3) return launch_tma<2, true>(p, f, t, b, r, sm_count, stream, map_p, map_o);
+        if (p.iterations == 2) return launch_tma<1, true>(p, f, t, b, r, sm_count, stream, map_p, map_o);
+        return launch_tma<0, true>(p, f, t, b, r, sm_count, stream, map_p, map_o);
+    }
+    if (p.iterations >= 3) return launch_tma<2, false>(p, f, t, b, r, sm_count, stream, map_p, map_o);
+    if (p.iterations == 2) return launch_tma<1, false>(p, f, t, b, r, sm_count, stream, map_p, map_o);
+    return launch_tma<0, false>(p, f, t, b, r, sm_count, stream, map_p, map_o);
 }
 
 }  // namespace tfv

@@ -356,6 +356,33 @@ class WarpgroupSchedule:
         object.__setattr__(self, "times", tuple(sorted(times)))
 
 
+@dataclass(frozen=True, slots=True)
+class WarpgroupSolveResult:
+    """A solver's lane program and timing witness (solve.py:33-60)."""
+
+    status: str
+    lanes: tuple[WarpgroupLane, ...]
+    times: tuple[TimedOperation, ...]
+    initiation_interval: int | None = None
+
+    def __post_init__(self) -> None:
+        if self.status not in ("OPTIMAL", "FEASIBLE_NOT_PROVEN"):
+            raise WarpgroupValidationError(f"invalid warpgroup solve status {self.status!r}")
+        if type(self.lanes) is not tuple or not all(type(item) is WarpgroupLane for item in self.lanes):
+            raise WarpgroupValidationError("solve lanes must contain exact WarpgroupLane records")
+        if type(self.times) is not tuple or not all(type(item) is TimedOperation for item in self.times):
+            raise WarpgroupValidationError("solve times must contain exact TimedOperation records")
+        if self.initiation_interval is not None and (
+            type(self.initiation_interval) is not int or self.initiation_interval <= 0
+        ):
+            raise WarpgroupValidationError("initiation interval must be a positive integer")
+
+    @property
+    def makespan(self) -> int:
+        """The finite makespan of the timing witness."""
+        return max((item.completion for item in self.times), default=0)
+
+
 def value_references(expression: object) -> tuple[str, ...]:
     """SSA values read by one expression, in traversal order.
 
@@ -399,6 +426,7 @@ __all__ = [
     "ResourceCapacity",
     "ResourceWindow",
     "SCHEDULE_FORMAT",
+    "WarpgroupSolveResult",
     "SynchronizationEdge",
     "TensorType",
     "TimedOperation",

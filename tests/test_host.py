@@ -211,3 +211,19 @@ def test_ii_lower_bound_and_sweep():
     values = ii_sweep(100, 16)
     assert values[0] == 100 and values[-1] == 200 and len(values) == 16 and np.all(np.diff(values) > 0)
     assert ii_sweep(7, 1).tolist() == [7]
+
+
+def test_closed_problem_is_built_once_per_document_pair():
+    from tilefoundry_b200.verify import closed_problem
+
+    calls = []
+
+    def build(program, hardware):
+        calls.append((program, hardware))
+        return ("problem", len(calls))
+
+    program, hardware, other = object(), object(), object()
+    first = closed_problem(program, hardware, build)
+    assert closed_problem(program, hardware, build) is first
+    assert closed_problem(program, other, build) is not first
+    assert len(calls) == 2

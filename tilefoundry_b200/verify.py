@@ -410,11 +410,36 @@ def _verify_warpgroup_schedule(problem: object, schedule: object, *, device: int
     raise_for_verdict(int(verdict[0]))
 
 
+_CLOSED: "OrderedDict[tuple, tuple]" = OrderedDict()
+
+
+def closed_problem(program: object, hardware: object, build) -> object:
+    """``build(program, hardware)``, cached for the last 8 (program, hardware, build) triples.
+
+    The reference's public entry closes the program on every call (verify.py:325-331,
+    build.py:169-220); the closure depends only on the two documents, so repeated calls
+    with the same objects reuse it (and with it the device tables of the problem). The
+    cache keys on object identity and keeps the objects alive while they are cached,
+    so a key cannot be reused by another object; the records are immutable.
+    """
+    key = (id(program), id(hardware), id(build))
+    found = _CLOSED.get(key)
+    if found is not None and found[0] is program and found[1] is hardware and found[2] is build:
+        _CLOSED.move_to_end(key)
+        return found[3]
+    problem = build(program, hardware)
+    _CLOSED[key] = (program, hardware, build, problem)
+    while len(_CLOSED) > 8:
+        _CLOSED.popitem(last=False)
+    return problem
+
+
 def verify_warpgroup_schedule(program: object, hardware: object, schedule: object, *, build=None, device: int = 0) -> None:
     """Verify one schedule against its program and hardware (drop-in for verify.py:325-331).
 
     ``build`` closes the program against the hardware; by default TileFoundry's own
-    ``build_warpgroup_problem`` (build.py:169-220) is used when it is installed.
+    ``build_warpgroup_problem`` (build.py:169-220) is used when it is installed. The
+    closed problem is cached per (program, hardware) object pair (see closed_problem).
     """
     if build is None:
         try:
@@ -424,7 +449,7 @@ def verify_warpgroup_schedule(program: object, hardware: object, schedule: objec
                 "closing a program against hardware needs TileFoundry's build_warpgroup_problem; "
                 "pass build= or verify a closed problem with _verify_warpgroup_schedule"
             ) from error
-    _verify_warpgroup_schedule(build(program, hardware), schedule, device=device)
+    _verify_warpgroup_schedule(closed_problem(program, hardware, build), schedule, device=device)
 
 
 __all__ = [
@@ -433,6 +458,7 @@ __all__ = [
     "MESSAGES",
     "WarpgroupVerifier",
     "_verify_warpgroup_schedule",
+    "closed_problem",
     "pinned_like",
     "raise_for_verdict",
     "verify_warpgroup_schedule",

@@ -266,6 +266,36 @@ TFV_API int tfv_verify_periodic_host(const tfv_problem* problem, const tfv_frame
 TFV_API int tfv_verify_periodic_static(const tfv_problem* problem, const tfv_frames* frames,
                                        const tfv_periodic_batch* batch, const tfv_results* results, void* stream);
 
+/* ---------------------------------------------------------------------------------------
+ * Native decode of schedule documents (serialization.py:679-727) into the packed layout.
+ * ------------------------------------------------------------------------------------- */
+
+#define TFV_SCHEDULE_FORMAT "tilefoundry.warpgroup_schedule"
+
+/* Deduplicated frames (lanes + sync sets) of one problem, filled by tfv_decode_schedules.
+ * `op_ids` are the problem's operation ids in strictly increasing byte order (the
+ * operation order of tfv_problem_desc); they name the operations in documents. */
+typedef struct tfv_frameset tfv_frameset;
+TFV_API int tfv_frameset_create(int n_ops, int iterations, const char* const* op_ids, tfv_frameset** out);
+TFV_API int tfv_frameset_destroy(tfv_frameset* frameset);
+/* Host view of the frames in the layout of tfv_frames; the pointers stay valid until the
+ * next tfv_decode_schedules into this frame set or its destruction. */
+TFV_API int tfv_frameset_view(const tfv_frameset* frameset, tfv_frames* out);
+
+/* Decode n UTF-8 schedule documents (documents[c], lengths[c] bytes) with the
+ * reference's strict JSON rules and record constructors. status[c] is 0 for a decoded
+ * document and 1 where the reference raises WarpgroupSerializationError. A decoded
+ * document's rows fill start/issue_end/completion[c] ([n][iterations][n_ops] int32, host)
+ * like the Python packer: instances outside the grid or missing set row_flags[c]
+ * (TFV_ROWS_COVERAGE), and for those makespan_override[c] / ii_override[c] hold the
+ * makespan and II over the rows as listed. frame[c] indexes the frame set (frames are
+ * numbered in document order), -1 for an undecoded document. `threads` <= 0 uses every
+ * hardware thread. */
+TFV_API int tfv_decode_schedules(tfv_frameset* frameset, int64_t n, const char* const* documents,
+                                 const size_t* lengths, int32_t* start, int32_t* issue_end, int32_t* completion,
+                                 int32_t* frame, int32_t* row_flags, int32_t* makespan_override,
+                                 int32_t* ii_override, int32_t* status, int threads);
+
 #ifdef __cplusplus
 }
 #endif

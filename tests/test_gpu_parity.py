@@ -368,3 +368,33 @@ def test_ii_sweep_stress_body_matches_oracle():
     with WarpgroupVerifier(packed) as verifier:
         got = verifier.verify_periodic_sweep(frames, batch, ii_values.astype(np.int32))
     _assert_sweep(got, _oracle_rows(problem, frames, batch, ii_values))
+
+
+@pytest.mark.parametrize("name", ["mla", "resource_c4_w5", "shared_init_i4", "tiny_free"])
+def test_verify_documents_matches_record_path(name):
+    """Native document decode + rows kernel equals the record path, rejects included."""
+    import json
+
+    from tilefoundry_b200 import SCHEDULE_FORMAT, WarpgroupSerializationError, schedule_from_json
+    from tilefoundry_b200.decode import CLASS_DECODE_FAILED
+
+    problem = problem_from_json(problem_text(name))
+    cases, _verdicts = raw_cases(name)
+    docs = [json.dumps({"format": SCHEDULE_FORMAT, "lanes": [list(l) for l in lanes],
+                        "sync": [{"after": a, "before": b, "distance": d} for a, b, d in sync],
+                        "times": [list(r) for r in rows]}) for lanes, sync, rows in cases[:300]]
+    docs += [d.replace("1", "1.0", 1) for d in docs[:5]]
+    with WarpgroupVerifier(pack_problem(problem)) as verifier:
+        verdict, makespan, ii = verifier.verify_documents(docs)
+        records, index = [], []
+        for k, d in enumerate(docs):
+            try:
+                records.append(schedule_from_json(d))
+                index.append(k)
+            except WarpgroupSerializationError:
+                assert verdict[k] == CLASS_DECODE_FAILED
+        rv, rm, ri = verifier.verify_schedules(records)
+    assert np.array_equal(verdict[index], rv)
+    assert np.array_equal(makespan[index], rm)
+    assert np.array_equal(ii[index], ri)
+    assert len(index) < len(docs)

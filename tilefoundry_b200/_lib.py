@@ -130,6 +130,13 @@ EXPORTS = {
         ctypes.c_int,
         [_p, ctypes.POINTER(Frames), _p, ctypes.c_size_t, ctypes.POINTER(PeriodicBatch), ctypes.POINTER(Results), _p],
     ),
+    "tfv_frameset_create": (ctypes.c_int, [ctypes.c_int, ctypes.c_int, ctypes.POINTER(ctypes.c_char_p), ctypes.POINTER(_p)]),
+    "tfv_frameset_destroy": (ctypes.c_int, [_p]),
+    "tfv_frameset_view": (ctypes.c_int, [_p, ctypes.POINTER(Frames)]),
+    "tfv_decode_schedules": (
+        ctypes.c_int,
+        [_p, ctypes.c_int64, ctypes.POINTER(ctypes.c_char_p), ctypes.POINTER(ctypes.c_size_t)] + [_p] * 8 + [ctypes.c_int],
+    ),
     "tfv_export_sync": (ctypes.c_int, [_p, ctypes.POINTER(Frames), _p, ctypes.c_size_t, _p, ctypes.c_int, _p]),
     "tfv_verify_periodic_sweep": (
         ctypes.c_int,

@@ -144,6 +144,7 @@ class WarpgroupVerifier:
 
     # ------------------------------------------------------------------ device tensors
     def frames_to_device(self, frames: FrameSet) -> DeviceFrames:
+        """Upload a frame set (``FrameSet`` or ``NativeFrameSet``) for the kernels."""
         torch = _torch()
         dev = torch.device("cuda", self.device)
         arrays = frames.arrays()
@@ -353,6 +354,42 @@ class WarpgroupVerifier:
             verdict, makespan, ii = (t.cpu().numpy() for t in self.verify_rows_device(dframes, table, batch))
         makespan = np.where(rows.override, rows.override_makespan, makespan)
         ii = np.where(rows.override, rows.override_ii, ii)
+        return verdict, makespan, ii
+
+
+    def verify_documents(self, documents, *, threads: int = 0) -> tuple[np.ndarray, np.ndarray, np.ndarray]:
+        """Verify schedule JSON documents: native decode (``tfv_decode_schedules``) + rows kernel.
+
+        Documents the reference would reject with WarpgroupSerializationError get verdict
+        ``CLASS_DECODE_FAILED`` (-4), makespan and II 0.
+        """
+        from .decode import CLASS_DECODE_FAILED, NativeFrameSet, decode_schedule_documents
+
+        torch = _torch()
+        native = NativeFrameSet(self.packed)
+        try:
+            decoded = decode_schedule_documents(native, documents, threads=threads)
+            rows = decoded.rows
+            dev = torch.device("cuda", self.device)
+            with torch.cuda.device(dev):
+                dframes = self.frames_to_device(native)  # a NativeFrameSet has FrameSet's arrays()
+                table = self.analyze(dframes)
+                batch = {
+                    "start": torch.from_numpy(rows.start).to(dev),
+                    "issue_end": torch.from_numpy(rows.issue_end).to(dev),
+                    "completion": torch.from_numpy(rows.completion).to(dev),
+                    "frame": torch.from_numpy(rows.frame).to(dev),
+                    "row_flags": torch.from_numpy(rows.row_flags).to(dev),
+                }
+                verdict, makespan, ii = (t.cpu().numpy() for t in self.verify_rows_device(dframes, table, batch))
+        finally:
+            native.close()
+        makespan = np.where(rows.override, rows.override_makespan, makespan)
+        ii = np.where(rows.override, rows.override_ii, ii)
+        failed = decoded.status != 0
+        verdict = np.where(failed, CLASS_DECODE_FAILED, verdict).astype(np.int32)
+        makespan = np.where(failed, 0, makespan).astype(np.int32)
+        ii = np.where(failed, 0, ii).astype(np.int32)
         return verdict, makespan, ii
 
 

@@ -28,8 +28,10 @@
 #ifndef TFV_H_
 #define TFV_H_
 
+#ifndef __CUDACC_RTC__ /* the run-time compiler gets these types from its prelude */
 #include <stddef.h>
 #include <stdint.h>
+#endif
 
 #ifdef __cplusplus
 extern "C" {
@@ -238,6 +240,25 @@ TFV_API int tfv_verify_periodic_sweep(const tfv_problem* problem, const tfv_fram
                                       void* frame_table, size_t frame_table_bytes,
                                       const tfv_periodic_batch* batch, int n_ii, const int32_t* ii_values,
                                       const tfv_results* results, void* stream);
+
+/* Frame-specialised verification. A plan holds a kernel generated for one frame (its lane
+ * walk and sync inequalities as straight-line code, the batch's base starts folded into
+ * constants) and compiled at run time with NVRTC (libnvrtc.so.12 must be loadable). Its
+ * verification gives the same results as tfv_verify_periodic; the candidates of that
+ * frame take the generated code, the others the frame-table path. `host_frames` are host
+ * pointers; `frame` indexes them. Needs N <= 256 and the TMA layout of the batch
+ * (16-byte aligned deltas, op_stride % 8 == 0). tfv_verify_periodic_planned takes the
+ * device frames and frame table like tfv_verify_periodic; `spec_frame` must index a frame
+ * identical to the plan's (same lanes and sync set); a plan serves one stream at a time
+ * (its constants live in the module). */
+typedef struct tfv_plan tfv_plan;
+TFV_API int tfv_plan_create(const tfv_problem* problem, const tfv_frames* host_frames, int frame, tfv_plan** out);
+TFV_API int tfv_plan_destroy(tfv_plan* plan);
+/* The generated CUDA source of a plan (truncated to size - 1 bytes). */
+TFV_API int tfv_plan_source(const tfv_plan* plan, char* buffer, size_t size);
+TFV_API int tfv_verify_periodic_planned(const tfv_plan* plan, const tfv_frames* frames, void* frame_table,
+                                        size_t frame_table_bytes, const tfv_periodic_batch* batch, int spec_frame,
+                                        const tfv_results* results, void* stream);
 
 /* Verify explicit timing rows against analysed frames (general schedules). */
 TFV_API int tfv_verify_rows(const tfv_problem* problem, const tfv_frames* frames,

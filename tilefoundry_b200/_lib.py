@@ -137,6 +137,14 @@ EXPORTS = {
         ctypes.c_int,
         [_p, ctypes.c_int64, ctypes.POINTER(ctypes.c_char_p), ctypes.POINTER(ctypes.c_size_t)] + [_p] * 8 + [ctypes.c_int],
     ),
+    "tfv_plan_create": (ctypes.c_int, [_p, ctypes.POINTER(Frames), ctypes.c_int, ctypes.POINTER(_p)]),
+    "tfv_plan_destroy": (ctypes.c_int, [_p]),
+    "tfv_plan_source": (ctypes.c_int, [_p, ctypes.c_char_p, ctypes.c_size_t]),
+    "tfv_verify_periodic_planned": (
+        ctypes.c_int,
+        [_p, ctypes.POINTER(Frames), _p, ctypes.c_size_t, ctypes.POINTER(PeriodicBatch), ctypes.c_int,
+         ctypes.POINTER(Results), _p],
+    ),
     "tfv_export_sync": (ctypes.c_int, [_p, ctypes.POINTER(Frames), _p, ctypes.c_size_t, _p, ctypes.c_int, _p]),
     "tfv_verify_periodic_sweep": (
         ctypes.c_int,

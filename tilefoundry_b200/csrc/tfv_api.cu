@@ -15,6 +15,7 @@ struct tfv_problem {
     int max_smem_optin = 0;
     void* buffer = nullptr;  // one device allocation holding every table
     tfv::DevProblem dev{};
+    std::vector<int> issue_h, latency_h;  // host copies for generated code
 };
 
 namespace {
@@ -286,6 +287,8 @@ int tfv_problem_create(const tfv_problem_desc* d, int device, tfv_problem** out)
     dp.n_carried = d->n_carried;
     dp.n_register_groups = d->n_register_groups;
     dp.n_resources = Q;
+    p->issue_h.assign(d->issue_duration, d->issue_duration + N);
+    p->latency_h.assign(d->completion_latency, d->completion_latency + N);
     dp.n_windows = static_cast<int>(win_op.size());
     dp.res_max_windows = 0;
     for (int q = 0; q < Q; ++q) dp.res_max_windows = std::max(dp.res_max_windows, res_offsets[q + 1] - res_offsets[q]);
@@ -546,6 +549,22 @@ int tfv_verify_periodic_host(const tfv_problem* p, const tfv_frames* hf, const t
 int tfv_internal_fail(int code, const char* message) { return fail(code, "%s", message); }
 
 int tfv_internal_device(const tfv_problem* p) { return p ? p->device : -1; }
+
+const tfv::DevProblem* tfv_internal_dev(const tfv_problem* p) { return p ? &p->dev : nullptr; }
+
+int tfv_internal_sm_count(const tfv_problem* p) { return p ? p->sm_count : 0; }
+
+const int* tfv_internal_issue_host(const tfv_problem* p) { return p ? p->issue_h.data() : nullptr; }
+
+const int* tfv_internal_latency_host(const tfv_problem* p) { return p ? p->latency_h.data() : nullptr; }
+
+int tfv_internal_check_frames(const tfv_frames* frames) { return check_frames(frames); }
+
+int tfv_internal_cuda_fail(cudaError_t e, const char* what) { return cuda_fail(e, what); }
+
+tfv::FrameTableShape tfv_internal_shape(const tfv_problem* p, const tfv_frames* f) { return shape_of(p, f); }
+
+tfv::DevFrames tfv_internal_to_dev(const tfv_frames& f) { return to_dev(f); }
 
 int tfv_internal_periodic_with_table(const tfv_problem* p, const tfv_frames* frames, void* table, size_t table_bytes,
                                      const tfv_periodic_batch* b, const tfv_results* r, void* stream, bool analyze) {

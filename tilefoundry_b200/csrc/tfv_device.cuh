@@ -5,10 +5,12 @@
 // pointers and counts, all immutable after tfv_problem_create.
 #pragma once
 
+#ifndef __CUDACC_RTC__  // the run-time compiler gets these from the prelude of tfv_jit.cu
 #include <cstddef>
 #include <cstdint>
 
 #include <cuda_runtime.h>
+#endif
 
 #include "tfv.h"
 
@@ -90,6 +92,7 @@ constexpr int kFirstOfLane = 0x8000;
 constexpr int kLastOfLane = 0x4000;
 constexpr int kTmaTile = 128;                         // candidates per TMA tile
 constexpr int kTmaRowBytes = kTmaTile * 2;            // one op's int16 deltas in a tile
+constexpr int kSpecSmemBytes = (kTmaTile + 32) * 4;   // tile permutation of a frame-specialised kernel
 constexpr int kNoBodyWeight = 1 << 29;                // slack that can never go negative
 constexpr int kMaxProgDistance = (1 << 14) - 1;
 
@@ -164,6 +167,7 @@ struct DevResults {
     int* ii;
 };
 
+#ifndef __CUDACC_RTC__
 // Launchers (tfv_kernels.cu). Each returns the cudaError_t of its launch.
 // With keep != nullptr the analysis also exports each frame's sync set (sync.py:21-62):
 // keep[f * keep_stride + j] = 1 when edge j of frame f's set is retained. The sets must
@@ -190,5 +194,6 @@ cudaError_t launch_verify_rows(const DevProblem& p, const DevFrames& f, FrameTab
 size_t analyze_smem_bytes(int n_ops, int lanes);
 int periodic_tile(int n_ops);
 size_t periodic_smem_bytes(const DevProblem& p, int tile);
+#endif  // __CUDACC_RTC__
 
 }  // namespace tfv

@@ -1,0 +1,489 @@
+// Frame-specialised verification kernels, generated and compiled at run time.
+//
+// The TMA kernel reads each candidate's frame (lane order and sync program) from the frame
+// table, so every operation costs a frame-table load, an index computation and a shared
+// memory address per use. For the frame that most candidates of a batch share, this file
+// writes the lane walk and the sync inequalities of that frame as straight-line CUDA: the
+// operations' rows are compile-time offsets into the candidate's tile column, and the
+// batch's base starts, issue durations and latencies are folded into constants held in the
+// module's constant bank, so that each inequality is an add and a minimum. NVRTC compiles
+// the generated code together with the generic kernel body (tfv_periodic_tma.cuh), whose
+// tile permutation hands that frame's candidates to whole warps; the remaining candidates
+// of each tile take the frame-table path. Verdicts are identical: the generated code
+// computes the same extremes and the same signs of every lane and sync slack.
+#include <dlfcn.h>
+
+#include <algorithm>
+#include <cstdio>
+#include <cstring>
+#include <mutex>
+#include <string>
+#include <vector>
+
+#include <cuda.h>
+#include <cudaTypedefs.h>
+
+#include "tfv_device.cuh"
+#include "tfv_jit_sources.inc"
+
+int tfv_internal_fail(int code, const char* message);
+const tfv::DevProblem* tfv_internal_dev(const tfv_problem* p);
+int tfv_internal_sm_count(const tfv_problem* p);
+int tfv_internal_device(const tfv_problem* p);
+const int* tfv_internal_issue_host(const tfv_problem* p);
+const int* tfv_internal_latency_host(const tfv_problem* p);
+int tfv_internal_check_frames(const tfv_frames* frames);
+int tfv_internal_cuda_fail(cudaError_t e, const char* what);
+tfv::FrameTableShape tfv_internal_shape(const tfv_problem* p, const tfv_frames* f);
+tfv::DevFrames tfv_internal_to_dev(const tfv_frames& f);
+
+namespace tfv {
+bool make_map(CUtensorMap* map, const int16_t* base, long long n, long long stride, int N);
+size_t tma_smem_bytes(const DevProblem& p);
+bool periodic_tma_supported(const DevProblem& p, const DevPeriodic& b);
+}  // namespace tfv
+
+namespace {
+
+// ---------------------------------------------------------------------------------------
+// NVRTC (loaded at run time) and the driver's module API
+// ---------------------------------------------------------------------------------------
+
+// Signatures of NVRTC's public C API (nvrtcProgram is an opaque pointer).
+using NvrtcCreate = int (*)(void**, const char*, const char*, int, const char* const*, const char* const*);
+using NvrtcCompile = int (*)(void*, int, const char* const*);
+using NvrtcSize = int (*)(void*, size_t*);
+using NvrtcGet = int (*)(void*, char*);
+using NvrtcDestroy = int (*)(void**);
+
+struct Nvrtc {
+    NvrtcCreate create = nullptr;
+    NvrtcCompile compile = nullptr;
+    NvrtcSize log_size = nullptr, cubin_size = nullptr;
+    NvrtcGet log = nullptr, cubin = nullptr;
+    NvrtcDestroy destroy = nullptr;
+    bool ok = false;
+};
+
+const Nvrtc& nvrtc() {
+    static Nvrtc n;
+    static std::once_flag once;
+    std::call_once(once, [] {
+        const char* names[] = {"libnvrtc.so.12", "libnvrtc.so", "/usr/local/cuda/lib64/libnvrtc.so.12"};
+        void* h = nullptr;
+        for (const char* name : names)
+            if ((h = dlopen(name, RTLD_NOW | RTLD_LOCAL)) != nullptr) break;
+        if (!h) return;
+        n.create = reinterpret_cast<NvrtcCreate>(dlsym(h, "nvrtcCreateProgram"));
+        n.compile = reinterpret_cast<NvrtcCompile>(dlsym(h, "nvrtcCompileProgram"));
+        n.log_size = reinterpret_cast<NvrtcSize>(dlsym(h, "nvrtcGetProgramLogSize"));
+        n.log = reinterpret_cast<NvrtcGet>(dlsym(h, "nvrtcGetProgramLog"));
+        n.cubin_size = reinterpret_cast<NvrtcSize>(dlsym(h, "nvrtcGetCUBINSize"));
+        n.cubin = reinterpret_cast<NvrtcGet>(dlsym(h, "nvrtcGetCUBIN"));
+        n.destroy = reinterpret_cast<NvrtcDestroy>(dlsym(h, "nvrtcDestroyProgram"));
+        n.ok = n.create && n.compile && n.log_size && n.log && n.cubin_size && n.cubin && n.destroy;
+    });
+    return n;
+}
+
+struct Driver {
+    PFN_cuModuleLoadData_v2000 load = nullptr;
+    PFN_cuModuleUnload_v2000 unload = nullptr;
+    PFN_cuModuleGetFunction_v2000 function = nullptr;
+    PFN_cuModuleGetGlobal_v3020 global = nullptr;
+    PFN_cuLaunchKernel_v4000 launch = nullptr;
+    PFN_cuFuncSetAttribute_v9000 set_attribute = nullptr;
+    PFN_cuOccupancyMaxActiveBlocksPerMultiprocessor_v6050 occupancy = nullptr;
+    PFN_cuMemcpyDtoDAsync_v3020 copy = nullptr;
+    bool ok = false;
+};
+
+template <class F>
+void entry(const char* name, F& fn) {
+    void* ptr = nullptr;
+    cudaDriverEntryPointQueryResult q;
+    if (cudaGetDriverEntryPoint(name, &ptr, cudaEnableDefault, &q) == cudaSuccess && q == cudaDriverEntryPointSuccess)
+        fn = reinterpret_cast<F>(ptr);
+}
+
+const Driver& driver() {
+    static Driver d;
+    static std::once_flag once;
+    std::call_once(once, [] {
+        entry("cuModuleLoadData", d.load);
+        entry("cuModuleUnload", d.unload);
+        entry("cuModuleGetFunction", d.function);
+        entry("cuModuleGetGlobal", d.global);
+        entry("cuLaunchKernel", d.launch);
+        entry("cuFuncSetAttribute", d.set_attribute);
+        entry("cuOccupancyMaxActiveBlocksPerMultiprocessor", d.occupancy);
+        entry("cuMemcpyDtoDAsync", d.copy);
+        d.ok = d.load && d.unload && d.function && d.global && d.launch && d.set_attribute && d.occupancy && d.copy;
+    });
+    return d;
+}
+
+// ---------------------------------------------------------------------------------------
+// Code generation
+// ---------------------------------------------------------------------------------------
+
+struct FrameInput {
+    int N = 0, I = 0;
+    std::vector<std::vector<int>> lanes;  // operations of each lane in program order
+    std::vector<int> ea, eb, ed;          // sync edges before the set's first static failure
+};
+
+class Gen {
+  public:
+    std::string eval, consts;
+    int n_consts = 0;
+
+    // A new constant computed by the constants kernel from bp[], bo[] and immediates.
+    int constant(const std::string& expr) {
+        consts += "    c[" + std::to_string(n_consts) + "] = " + expr + ";\n";
+        return n_consts++;
+    }
+    void line(const std::string& s) { eval += "        " + s + "\n"; }
+};
+
+std::string I2S(long long v) { return std::to_string(v); }
+
+std::string generate(const FrameInput& in, const int* issue, const int* lat, int body_rows) {
+    const int N = in.N;
+    Gen g;
+    const auto bp = [](int k) { return "bp[" + I2S(k) + "]"; };
+    const auto bo = [](int k) { return "bo[" + I2S(k) + "]"; };
+    const auto P = [](int k) { return "p" + I2S(k); };
+    const auto O = [](int k) { return "o" + I2S(k); };
+    const auto C = [](int i) { return "tfv_spec_c[" + I2S(i) + "]"; };
+    // Lane walk: each operation's values are loaded once, when its lane reaches it, and
+    // feed the start/completion extremes and the lane inequalities with its predecessor;
+    // the inequalities without II go to l0, the wraps (+ ii) to l1.
+    g.line("int mnp = INT_MAX, mno = INT_MAX, mxp = INT_MIN, mxo = INT_MIN;");
+    g.line("int l0 = INT_MAX, l1 = INT_MAX;");
+    std::vector<char> seen(N, 0);
+    auto load = [&](int k) {
+        g.line("const int " + P(k) + " = P[" + I2S(k * tfv::kTmaTile) + "];");
+        if (body_rows >= 1) g.line("const int " + O(k) + " = O[" + I2S(k * tfv::kTmaTile) + "];");
+        g.line("mnp = __viaddmin_s32(" + P(k) + ", " + C(g.constant(bp(k))) + ", mnp);");
+        g.line("mxp = __viaddmax_s32(" + P(k) + ", " + C(g.constant(bp(k) + " + " + I2S(lat[k]))) + ", mxp);");
+        if (body_rows >= 1) {
+            g.line("mno = __viaddmin_s32(" + O(k) + ", " + C(g.constant(bo(k))) + ", mno);");
+            g.line("mxo = __viaddmax_s32(" + O(k) + ", " + C(g.constant(bo(k) + " + " + I2S(lat[k]))) + ", mxo);");
+        }
+        seen[k] = 1;
+    };
+    bool wraps = false;
+    for (const auto& lane : in.lanes) {
+        for (size_t q = 0; q < lane.size(); ++q) {
+            const int b = lane[q];
+            load(b);
+            if (q == 0) continue;
+            const int a = lane[q - 1];
+            g.line("l0 = min(l0, " + P(b) + " - " + P(a) + " + " +
+                   C(g.constant(bp(b) + " - " + bp(a) + " - " + I2S(issue[a]))) + ");");
+            if (body_rows >= 1)
+                g.line("l0 = min(l0, " + O(b) + " - " + O(a) + " + " +
+                       C(g.constant(bo(b) + " - " + bo(a) + " - " + I2S(issue[a]))) + ");");
+        }
+        if (!lane.empty() && body_rows >= 1) {
+            const int f = lane.front(), l = lane.back();
+            g.line("l1 = min(l1, " + O(f) + " - " + P(l) + " + " +
+                   C(g.constant(bo(f) + " - " + bp(l) + " - " + I2S(issue[l]))) + ");");
+            if (body_rows >= 2)
+                g.line("l1 = min(l1, " + O(f) + " - " + O(l) + " + " +
+                       C(g.constant(bo(f) + " - " + bo(l) + " - " + I2S(issue[l]))) + ");");
+            wraps = true;
+        }
+    }
+    for (int k = 0; k < N; ++k)
+        if (!seen[k]) load(k);  // operations in no lane still count for the extremes
+    g.line("x.min_p = mnp; x.max_pl = mxp; x.min_o = mno; x.max_ol = mxo;");
+    g.line(wraps ? "lane_min = min(l0, l1 + ii);" : "lane_min = l0;");
+    // Sync inequalities (verify.py:284-292), grouped by distance d and shifted by d * ii at
+    // the end. Values are read again here through volatile loads, so that the walk's
+    // registers need not live until their last use (the edges run in source order, one
+    // reload of the source's values per run).
+    std::vector<int> dists;
+    for (int d : in.ed)
+        if (std::find(dists.begin(), dists.end(), d) == dists.end()) dists.push_back(d);
+    for (int d : dists) g.line("int s" + I2S(d) + " = INT_MAX;");
+    const auto VP = [](int k) { return "VP[" + I2S(k * tfv::kTmaTile) + "]"; };
+    const auto VO = [](int k) { return "VO[" + I2S(k * tfv::kTmaTile) + "]"; };
+    int run = -1, run_id = 0;
+    for (size_t e = 0; e < in.ea.size(); ++e) {
+        const int a = in.ea[e], b = in.eb[e], d = in.ed[e];
+        if (a != run) {
+            run = a;
+            ++run_id;
+            g.line("const int sa" + I2S(run_id) + " = " + VP(a) + ";");
+            if (body_rows >= 1) g.line("const int soa" + I2S(run_id) + " = " + VO(a) + ";");
+        }
+        const std::string s = "s" + I2S(d), pa = "sa" + I2S(run_id), oa = "soa" + I2S(run_id);
+        const bool body = in.I - d >= 2;
+        g.line("{");
+        if (d == 0) g.line("    const int xb = " + VP(b) + ";");
+        if (d != 0 || body) g.line("    const int ob = " + VO(b) + ";");
+        g.line("    " + s + " = min(" + s + ", " + (d == 0 ? "xb" : "ob") + " - " + pa + " + " +
+               C(g.constant((d == 0 ? bp(b) : bo(b)) + " - " + bp(a) + " - " + I2S(lat[a]))) + ");");
+        if (body)
+            g.line("    " + s + " = min(" + s + ", ob - " + oa + " + " +
+                   C(g.constant(bo(b) + " - " + bo(a) + " - " + I2S(lat[a]))) + ");");
+        g.line("}");
+    }
+    std::string sync = "INT_MAX";
+    for (int d : dists) sync = "min(" + sync + ", s" + I2S(d) + (d ? " + " + I2S(d) + " * ii" : std::string()) + ")";
+    g.line("sync_min = " + sync + ";");
+
+    std::string src;
+    src += "// Generated by tfv_jit.cu for one frame.\n";
+    src += "typedef signed char int8_t; typedef unsigned char uint8_t; typedef short int16_t;\n";
+    src += "typedef unsigned short uint16_t; typedef int int32_t; typedef unsigned int uint32_t;\n";
+    src += "typedef long long int64_t; typedef unsigned long long uint64_t; typedef unsigned long uintptr_t;\n";
+    src += "typedef unsigned long size_t;\n";
+    src += "#define INT_MAX 2147483647\n#define INT_MIN (-2147483647 - 1)\n";
+    src += "struct alignas(64) CUtensorMap_st { unsigned long long opaque[16]; };\n";
+    src += "typedef CUtensorMap_st CUtensorMap;\n";
+    src += "#include \"tfv_periodic_tma.cuh\"\n";
+    src += "__constant__ int tfv_spec_c[" + I2S(std::max(1, g.n_consts)) + "];\n";
+    src += "struct Spec {\n    static constexpr bool kEnabled = true;\n";
+    src += "    __device__ __forceinline__ static void eval(const char* rp, int ii, tfv::Extremes& x, int& lane_min,\n";
+    src += "                                                int& sync_min) {\n";
+    src += "        const int16_t* P = reinterpret_cast<const int16_t*>(rp);\n";
+    src += "        const int16_t* O = reinterpret_cast<const int16_t*>(rp + " + I2S(static_cast<long long>(N) * tfv::kTmaRowBytes) + ");\n";
+    src += "        const volatile int16_t* VP = P;\n";
+    src += "        const volatile int16_t* VO = O;\n";
+    src += "        (void)O; (void)VP; (void)VO;\n";
+    src += g.eval;
+    src += "    }\n};\n";
+    src += "extern \"C\" __global__ void tfv_spec_consts(const int* bp, const int* bo, int* c) {\n";
+    src += "    if (threadIdx.x != 0 || blockIdx.x != 0) return;\n";
+    src += g.consts;
+    src += "}\n";
+    src += "extern \"C\" __global__ void __launch_bounds__(" + I2S(tfv::kTmaTile) + ") tfv_spec_kernel(\n";
+    src += "    tfv::DevProblem p, tfv::DevFrames fr, tfv::FrameTable ft, tfv::DevPeriodic b, tfv::DevResults out, int n_tiles,\n";
+    src += "    const __grid_constant__ CUtensorMap map_p, const __grid_constant__ CUtensorMap map_o, int spec_frame) {\n";
+    src += "    tfv::tma_verify_body<" + I2S(body_rows) + ", false, Spec>(p, fr, ft, b, out, n_tiles, &map_p, &map_o, spec_frame);\n";
+    src += "}\n";
+    return src;
+}
+
+}  // namespace
+
+// ---------------------------------------------------------------------------------------
+// Plans
+// ---------------------------------------------------------------------------------------
+
+struct tfv_plan {
+    const tfv_problem* problem = nullptr;
+    int device = 0;
+    int body_rows = 0;
+    int n_consts = 0;
+    CUmodule module = nullptr;
+    CUfunction kernel = nullptr, consts_kernel = nullptr;
+    CUdeviceptr consts_symbol = 0;
+    void* consts_scratch = nullptr;  // device buffer the constants kernel writes
+    size_t smem = 0;
+    int per_sm = 0;
+    std::string source;
+};
+
+namespace {
+
+int build_input(const tfv_problem* p, const tfv_frames* f, int frame, FrameInput& in) {
+    const tfv::DevProblem& d = *tfv_internal_dev(p);
+    in.N = d.n_ops;
+    in.I = d.iterations;
+    if (frame < 0 || frame >= f->n_frames) return tfv_internal_fail(TFV_ERR_INVALID_ARGUMENT, "frame index out of range");
+    if (f->flags[frame] != 0) return tfv_internal_fail(TFV_ERR_UNSUPPORTED, "the frame breaks the record rules");
+    const int L = f->lane_count[frame];
+    if (L < 1 || L > TFV_MAX_LANES) return tfv_internal_fail(TFV_ERR_UNSUPPORTED, "lane count out of range");
+    in.lanes.assign(L, {});
+    std::vector<std::vector<int>> slot(L);
+    const uint16_t* pos = f->lane_pos + static_cast<size_t>(frame) * in.N;
+    for (int k = 0; k < in.N; ++k) {
+        const int l = pos[k] >> TFV_LANE_SHIFT, q = pos[k] & TFV_POS_MASK;
+        if (l == TFV_LANE_ABSENT) continue;
+        if (l >= L) return tfv_internal_fail(TFV_ERR_UNSUPPORTED, "lane index out of range");
+        if (static_cast<int>(slot[l].size()) <= q) slot[l].resize(q + 1, -1);
+        if (slot[l][q] != -1) return tfv_internal_fail(TFV_ERR_UNSUPPORTED, "two operations share a lane position");
+        slot[l][q] = k;
+    }
+    for (int l = 0; l < L; ++l)
+        for (int k : slot[l]) {
+            if (k < 0) return tfv_internal_fail(TFV_ERR_UNSUPPORTED, "lane positions are not contiguous");
+            in.lanes[l].push_back(k);
+        }
+    const int set = f->sync_set[frame];
+    if (set < 0 || set >= f->n_sync_sets) return tfv_internal_fail(TFV_ERR_UNSUPPORTED, "sync set out of range");
+    for (int e = f->sync_offsets[set]; e < f->sync_offsets[set + 1]; ++e) {
+        const int a = f->sync_edges[3 * e], b = f->sync_edges[3 * e + 1], dd = f->sync_edges[3 * e + 2];
+        if (a < -1 || b < -1 || a >= in.N || b >= in.N || dd < 0)
+            return tfv_internal_fail(TFV_ERR_UNSUPPORTED, "sync edge out of range");
+        if (a < 0 || b < 0 || dd >= in.I) break;  // the set's first static failure ends the program
+        in.ea.push_back(a);
+        in.eb.push_back(b);
+        in.ed.push_back(std::min(dd, tfv::kMaxProgDistance));
+    }
+    return TFV_OK;
+}
+
+}  // namespace
+
+extern "C" {
+
+int tfv_plan_create(const tfv_problem* p, const tfv_frames* host_frames, int frame, tfv_plan** out) {
+    if (!p || !out) return tfv_internal_fail(TFV_ERR_INVALID_ARGUMENT, "problem and out must not be NULL");
+    int rc = tfv_internal_check_frames(host_frames);
+    if (rc) return rc;
+    const tfv::DevProblem& d = *tfv_internal_dev(p);
+    if (d.n_ops > 256 || d.iterations > tfv::kMaxProgDistance)
+        return tfv_internal_fail(TFV_ERR_UNSUPPORTED, "frame-specialised kernels need N <= 256");
+    if (!nvrtc().ok) return tfv_internal_fail(TFV_ERR_UNSUPPORTED, "the run-time compiler (libnvrtc) is not available");
+    if (!driver().ok) return tfv_internal_fail(TFV_ERR_UNSUPPORTED, "the driver's module API is not available");
+    FrameInput in;
+    rc = build_input(p, host_frames, frame, in);
+    if (rc) return rc;
+    const int body_rows = d.iterations >= 3 ? 2 : (d.iterations == 2 ? 1 : 0);
+    auto* plan = new tfv_plan();
+    plan->problem = p;
+    plan->device = tfv_internal_device(p);
+    plan->body_rows = body_rows;
+    plan->source = generate(in, tfv_internal_issue_host(p), tfv_internal_latency_host(p), body_rows);
+
+    const Nvrtc& nv = nvrtc();
+    void* prog = nullptr;
+    if (nv.create(&prog, plan->source.c_str(), "tfv_spec.cu", kJitHeaderCount, kJitHeaders, kJitHeaderNames) != 0) {
+        delete plan;
+        return tfv_internal_fail(TFV_ERR_UNSUPPORTED, "nvrtcCreateProgram failed");
+    }
+    const char* options[] = {"--gpu-architecture=sm_100a", "-default-device", "--std=c++17", "-lineinfo"};
+    const int compiled = nv.compile(prog, 4, options);
+    if (compiled != 0) {
+        size_t n = 0;
+        nv.log_size(prog, &n);
+        std::string log(n, '\0');
+        nv.log(prog, log.data());
+        nv.destroy(&prog);
+        delete plan;
+        std::fprintf(stderr, "tfv_plan_create: run-time compilation failed:\n%s\n", log.c_str());
+        return tfv_internal_fail(TFV_ERR_UNSUPPORTED, "run-time compilation of the frame-specialised kernel failed");
+    }
+    size_t bytes = 0;
+    nv.cubin_size(prog, &bytes);
+    std::vector<char> cubin(bytes);
+    nv.cubin(prog, cubin.data());
+    nv.destroy(&prog);
+
+    const Driver& drv = driver();
+    cudaError_t e = cudaSetDevice(plan->device);
+    if (e == cudaSuccess) e = cudaFree(nullptr);  // the primary context is current from here on
+    if (e != cudaSuccess) {
+        delete plan;
+        return tfv_internal_cuda_fail(e, "tfv_plan_create");
+    }
+    size_t sym_bytes = 0;
+    if (drv.load(&plan->module, cubin.data()) != CUDA_SUCCESS ||
+        drv.function(&plan->kernel, plan->module, "tfv_spec_kernel") != CUDA_SUCCESS ||
+        drv.function(&plan->consts_kernel, plan->module, "tfv_spec_consts") != CUDA_SUCCESS ||
+        drv.global(&plan->consts_symbol, &sym_bytes, plan->module, "tfv_spec_c") != CUDA_SUCCESS) {
+        if (plan->module) drv.unload(plan->module);
+        delete plan;
+        return tfv_internal_fail(TFV_ERR_CUDA, "loading the frame-specialised module failed");
+    }
+    plan->smem = tfv::tma_smem_bytes(d) + tfv::kSpecSmemBytes;
+    if (drv.set_attribute(plan->kernel, CU_FUNC_ATTRIBUTE_MAX_DYNAMIC_SHARED_SIZE_BYTES, static_cast<int>(plan->smem)) !=
+            CUDA_SUCCESS ||
+        drv.occupancy(&plan->per_sm, plan->kernel, tfv::kTmaTile, plan->smem) != CUDA_SUCCESS || plan->per_sm < 1) {
+        drv.unload(plan->module);
+        delete plan;
+        return tfv_internal_fail(TFV_ERR_CUDA, "the frame-specialised kernel cannot be resident");
+    }
+    e = cudaMalloc(&plan->consts_scratch, sizeof(int) * std::max<size_t>(1, sym_bytes / sizeof(int)));
+    if (e != cudaSuccess) {
+        drv.unload(plan->module);
+        delete plan;
+        return tfv_internal_cuda_fail(e, "tfv_plan_create");
+    }
+    plan->n_consts = static_cast<int>(sym_bytes / sizeof(int));
+    *out = plan;
+    return TFV_OK;
+}
+
+int tfv_plan_destroy(tfv_plan* plan) {
+    if (!plan) return TFV_OK;
+    cudaSetDevice(plan->device);
+    if (plan->consts_scratch) cudaFree(plan->consts_scratch);
+    if (plan->module) driver().unload(plan->module);
+    delete plan;
+    return TFV_OK;
+}
+
+int tfv_plan_source(const tfv_plan* plan, char* buffer, size_t size) {
+    if (!plan || !buffer || size == 0) return tfv_internal_fail(TFV_ERR_INVALID_ARGUMENT, "invalid arguments");
+    std::snprintf(buffer, size, "%s", plan->source.c_str());
+    return TFV_OK;
+}
+
+int tfv_verify_periodic_planned(const tfv_plan* plan, const tfv_frames* frames, void* table, size_t table_bytes,
+                                const tfv_periodic_batch* b, int spec_frame, const tfv_results* r, void* stream) {
+    if (!plan || !b || !r) return tfv_internal_fail(TFV_ERR_INVALID_ARGUMENT, "plan, batch and results must not be NULL");
+    const tfv_problem* p = plan->problem;
+    int rc = tfv_internal_check_frames(frames);
+    if (rc) return rc;
+    if (!r->verdict || !r->makespan || !r->ii) return tfv_internal_fail(TFV_ERR_INVALID_ARGUMENT, "result arrays must not be NULL");
+    if (b->n_candidates < 0 || b->op_stride < b->n_candidates)
+        return tfv_internal_fail(TFV_ERR_INVALID_ARGUMENT, "need 0 <= n_candidates <= op_stride");
+    if (b->n_candidates == 0) return TFV_OK;
+    if (!table || table_bytes < tfv::frame_table_bytes(tfv_internal_shape(p, frames)))
+        return tfv_internal_fail(TFV_ERR_INVALID_ARGUMENT, "frame table missing or too small");
+    if (!b->base_prologue || !b->base_offset || !b->prologue_delta || !b->offset_delta || !b->ii || !b->frame)
+        return tfv_internal_fail(TFV_ERR_INVALID_ARGUMENT, "batch arrays must not be NULL");
+    int previous = 0;
+    cudaGetDevice(&previous);
+    cudaError_t e = cudaSetDevice(plan->device);
+    if (e != cudaSuccess) return tfv_internal_cuda_fail(e, "tfv_verify_periodic_planned");
+    const tfv::DevProblem& d = *tfv_internal_dev(p);
+    tfv::DevPeriodic db{b->n_candidates, b->op_stride, b->base_prologue, b->base_offset,
+                        b->prologue_delta, b->offset_delta, b->ii, b->frame, 1, b->n_candidates};
+    tfv::DevResults dr{r->verdict, r->makespan, r->ii};
+    tfv::DevFrames df = tfv_internal_to_dev(*frames);
+    tfv::FrameTable view = tfv::frame_table_view(table, tfv_internal_shape(p, frames));
+    const cudaStream_t s = static_cast<cudaStream_t>(stream);
+    e = tfv::launch_compile_sync_programs(d, df, view, b->base_prologue, b->base_offset, tfv_internal_sm_count(p), s);
+    CUtensorMap map_p, map_o;
+    if (e == cudaSuccess && !tfv::periodic_tma_supported(d, db)) e = cudaErrorInvalidValue;
+    if (e == cudaSuccess && (!tfv::make_map(&map_p, db.prologue_delta, db.n, db.stride, d.n_ops) ||
+                             !tfv::make_map(&map_o, db.offset_delta, db.n, db.stride, d.n_ops)))
+        e = cudaErrorInvalidValue;
+    if (e != cudaSuccess) {
+        cudaSetDevice(previous);
+        return e == cudaErrorInvalidValue
+                   ? tfv_internal_fail(TFV_ERR_UNSUPPORTED, "the batch layout does not allow the TMA-fed kernel")
+                   : tfv_internal_cuda_fail(e, "tfv_verify_periodic_planned");
+    }
+    const Driver& drv = driver();
+    // constants of this batch's base starts -> the module's constant bank
+    const int* bp = b->base_prologue;
+    const int* bo = b->base_offset;
+    void* cptr = plan->consts_scratch;
+    void* cargs[] = {&bp, &bo, &cptr};
+    CUresult cr = drv.launch(plan->consts_kernel, 1, 1, 1, 32, 1, 1, 0, reinterpret_cast<CUstream>(s), cargs, nullptr);
+    if (cr == CUDA_SUCCESS)
+        cr = drv.copy(plan->consts_symbol, reinterpret_cast<CUdeviceptr>(plan->consts_scratch),
+                      sizeof(int) * static_cast<size_t>(plan->n_consts), reinterpret_cast<CUstream>(s));
+    const long long tiles = (db.n + tfv::kTmaTile - 1) / tfv::kTmaTile;
+    const long long cap = static_cast<long long>(tfv_internal_sm_count(p)) * plan->per_sm;
+    const int grid = static_cast<int>(tiles < cap ? tiles : cap);
+    int n_tiles = static_cast<int>(tiles);
+    tfv::DevProblem dp = d;
+    void* args[] = {&dp, &df, &view, &db, &dr, &n_tiles, &map_p, &map_o, &spec_frame};
+    if (cr == CUDA_SUCCESS)
+        cr = drv.launch(plan->kernel, grid, 1, 1, tfv::kTmaTile, 1, 1, static_cast<unsigned>(plan->smem),
+                        reinterpret_cast<CUstream>(s), args, nullptr);
+    cudaSetDevice(previous);
+    if (cr != CUDA_SUCCESS) return tfv_internal_fail(TFV_ERR_CUDA, "launching the frame-specialised kernel failed");
+    return TFV_OK;
+}
+
+}  // extern "C"

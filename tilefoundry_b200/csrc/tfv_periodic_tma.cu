@@ -1,307 +1,28 @@
-// Periodic-candidate verification fed by TMA tiles (sm_100a).
-//
-// Layout: the per-candidate int16 deltas are op-major in global memory ([N][op_stride],
-// consecutive candidates contiguous). One CTA owns a tile of kTile candidates; a single
-// thread issues two 2-D TMA copies (cp.async.bulk.tensor) that land the tile as
-// [op][candidate] in shared memory — exactly the layout in which thread t reads its own
-// candidate's column, without bank conflicts. Candidates past the end of the batch are
-// zero-filled by the TMA unit. The copy completes on an mbarrier whose wait is bounded;
-// on a timeout every candidate of the tile reports TFV_CLASS_DEVICE_TIMEOUT and the CTA
-// returns after a second bounded wait for its copy.
-//
-// Per candidate (one thread), the checks are those of verify_periodic_kernel in
-// tfv_kernels.cu, restructured for issue efficiency:
-//   * one walk over the frame's lane-ordered operation list visits every operation once;
-//     it carries the previous operation's issue end in registers, so each lane edge
-//     (verify.py:99-112, 278-282) is a subtraction and a minimum, and the same pass
-//     collects the start minima (class 1, record constructors) and completion maxima
-//     (makespan) of the prologue row and of the periodic body rows;
-//   * sync edges (verify.py:284-292) are evaluated branch-free in sorted order with a
-//     sticky "first failing edge" class, so 13/14/15 keep the reference's precedence.
+// Periodic-candidate verification fed by TMA tiles (sm_100a): kernels and launchers.
+// The device code is in tfv_periodic_tma.cuh.
 #include <climits>
 #include <cstdint>
 
 #include <cuda.h>
 #include <cudaTypedefs.h>
 
-#include "tfv_device.cuh"
-#include "tfv_resources.cuh"
+#include "tfv_periodic_tma.cuh"
 
 namespace tfv {
 
 namespace {
 
-constexpr int kTile = kTmaTile;     // candidates per CTA tile = threads per CTA
-constexpr int kMaxTmaOps = 256;     // TMA box height limit
-constexpr long long kWaitSpins = 1LL << 22;
+constexpr int kMaxTmaOps = 256;  // TMA box height limit
 
-__device__ __forceinline__ uint32_t smem_addr(const void* p) {
-    return static_cast<uint32_t>(__cvta_generic_to_shared(p));
-}
-
-__device__ __forceinline__ void mbar_init(uint64_t* bar, unsigned count) {
-    asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;" ::"r"(smem_addr(bar)), "r"(count) : "memory");
-}
-
-__device__ __forceinline__ void mbar_expect_tx(uint64_t* bar, unsigned bytes) {
-    asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(smem_addr(bar)), "r"(bytes) : "memory");
-}
-
-__device__ __forceinline__ bool mbar_try_wait(uint64_t* bar, unsigned phase) {
-    uint32_t done;
-    asm volatile(
-        "{\n\t.reg .pred p;\n\t"
-        "mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n\t"
-        "selp.u32 %0, 1, 0, p;\n\t}"
-        : "=r"(done)
-        : "r"(smem_addr(bar)), "r"(phase)
-        : "memory");
-    return done != 0;
-}
-
-__device__ __forceinline__ bool mbar_wait_bounded(uint64_t* bar, unsigned phase) {
-    for (long long spin = 0; spin < kWaitSpins; ++spin)
-        if (mbar_try_wait(bar, phase)) return true;
-    return false;
-}
-
-__device__ __forceinline__ void tma_load_2d(void* dst, const CUtensorMap* map, int x, int y, uint64_t* bar) {
-    asm volatile(
-        "cp.async.bulk.tensor.2d.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1, {%2, %3}], [%4];"
-        ::"r"(smem_addr(dst)), "l"(reinterpret_cast<uint64_t>(map)), "r"(x), "r"(y), "r"(smem_addr(bar))
-        : "memory");
-}
-
-__device__ __forceinline__ void fence_proxy_async() { asm volatile("fence.proxy.async.shared::cta;" ::: "memory"); }
-
-struct Extremes {
-    int min_p, min_o;    // smallest prologue / body-offset start
-    int max_pl, max_ol;  // largest prologue / body-offset completion
-};
-
-// One pass over the frame's operations lane by lane (order/lane_len of the frame table).
-// Returns the smallest slack of every lane-order inequality (verify.py:99-112, 278-282):
-// same-iteration pairs in the prologue row (start) and the periodic rows (offset), and
-// the wrap from a lane's last operation to its first operation one iteration later. The
-// slack accumulates as min(start + (-previous issue end)) in one DPX instruction.
-template <int kBodyRows>  // 0: I == 1, 1: I == 2, 2: I >= 3
-__device__ __forceinline__ int walk_lanes(const uint16_t* order, const uint16_t* lane_len, const int4* opc,
-                                          const char* row_p, int to_bytes, int N, int ii, Extremes& x) {
-    const uint4 lens_lo = reinterpret_cast<const uint4*>(lane_len)[0];
-    const uint4 lens_hi = reinterpret_cast<const uint4*>(lane_len)[1];
-    const unsigned lens[8] = {lens_lo.x, lens_lo.y, lens_lo.z, lens_lo.w, lens_hi.x, lens_hi.y, lens_hi.z, lens_hi.w};
-    int lane_min = INT_MAX;
-    int j = 0;
-#pragma unroll
-    for (int l = 0; l < 16; ++l) {
-        const int len = min(static_cast<int>((lens[l >> 1] >> ((l & 1) * 16)) & 0xFFFF), N - j);
-        if (len <= 0) continue;
-        int s = min(static_cast<int>(order[j]), N - 1);
-        int4 k = opc[s];
-        const char* row = row_p + s * kTmaRowBytes;
-        int p = k.z + *reinterpret_cast<const int16_t*>(row);
-        int o = k.w + *reinterpret_cast<const int16_t*>(row + to_bytes);
-        x.min_p = min(x.min_p, p);
-        x.min_o = min(x.min_o, o);
-        x.max_pl = __viaddmax_s32(p, k.y, x.max_pl);
-        x.max_ol = __viaddmax_s32(o, k.y, x.max_ol);
-        const int first_o = o;
-        int nend_p = -p - k.x, nend_o = -o - k.x;  // minus the issue end
-#pragma unroll 4
-        for (int q = 1; q < len; ++q) {
-            s = min(static_cast<int>(order[j + q]), N - 1);
-            k = opc[s];
-            row = row_p + s * kTmaRowBytes;
-            p = k.z + *reinterpret_cast<const int16_t*>(row);
-            o = k.w + *reinterpret_cast<const int16_t*>(row + to_bytes);
-            x.min_p = min(x.min_p, p);
-            x.min_o = min(x.min_o, o);
-            x.max_pl = __viaddmax_s32(p, k.y, x.max_pl);
-            x.max_ol = __viaddmax_s32(o, k.y, x.max_ol);
-            lane_min = __viaddmin_s32(p, nend_p, lane_min);
-            if (kBodyRows >= 1) lane_min = __viaddmin_s32(o, nend_o, lane_min);
-            nend_p = -p - k.x;
-            nend_o = -o - k.x;
-        }
-        const int next = first_o + ii;  // the lane's first operation one iteration later
-        if (kBodyRows >= 1) lane_min = __viaddmin_s32(next, nend_p, lane_min);
-        if (kBodyRows >= 2) lane_min = __viaddmin_s32(next, nend_o, lane_min);
-        j += len;
-    }
-    return lane_min;
-}
-
-// Candidate values of thread t's tile column: base start + int16 delta.
-struct TileView {
-    const int4* opc;
-    const int16_t* mp;
-    const int16_t* mo;
-    __device__ __forceinline__ int p(int a) const { return opc[a].z + mp[a * kTile]; }
-    __device__ __forceinline__ int o(int a) const { return opc[a].w + mo[a * kTile]; }
-};
-
-template <int kBodyRows, bool kSweep>  // kSweep: more than one II per candidate
+template <int kBodyRows, bool kSweep>
 __global__ void __launch_bounds__(kTile) verify_periodic_tma_kernel(DevProblem p, DevFrames fr, FrameTable ft,
                                                                      DevPeriodic b, DevResults out, int n_tiles,
                                                                      const __grid_constant__ CUtensorMap map_p,
                                                                      const __grid_constant__ CUtensorMap map_o) {
-    extern __shared__ __align__(128) unsigned char smem[];
-    const int N = p.n_ops;
-    const int I = p.iterations;
-    const int t = threadIdx.x;
-    int16_t* tp = reinterpret_cast<int16_t*>(smem);             // [N][kTile] prologue deltas
-    int16_t* to = tp + N * kTile;                               // [N][kTile] offset deltas
-    int4* opc = reinterpret_cast<int4*>(smem + 4 * N * kTile);  // [N] issue, latency, base starts
-    uint64_t* bar = reinterpret_cast<uint64_t*>(opc + N);
-    const int lane = t & 31;
-    // capacity-check records of this warp (warp path only)
-    int4* scratch = reinterpret_cast<int4*>(bar + 2) + (t >> 5) * 2 * p.res_max_windows;
-    const bool warp_path = warp_resources_used(p);
-    const int n_ii = kSweep ? b.n_ii : 1;
-
-    bool base_ok = true;
-    for (int s = t; s < N; s += kTile) {
-        const int bp = b.base_prologue[s], bo = b.base_offset[s];
-        base_ok &= bp > -TFV_BASE_LIMIT && bp < TFV_BASE_LIMIT && bo > -TFV_BASE_LIMIT && bo < TFV_BASE_LIMIT;
-        opc[s] = make_int4(p.issue[s], p.latency[s], bp, bo);
-    }
-    if (t == 0) {
-        mbar_init(bar, 1);
-        asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
-        fence_proxy_async();
-    }
-    base_ok = __syncthreads_and(base_ok);
-
-    const unsigned tile_bytes = static_cast<unsigned>(2 * N * kTile * sizeof(int16_t));
-    unsigned phase = 0;
-    for (int tile = blockIdx.x; tile < n_tiles; tile += gridDim.x) {
-        if (t == 0) {
-            fence_proxy_async();
-            mbar_expect_tx(bar, tile_bytes);
-            tma_load_2d(tp, &map_p, tile * kTile, 0, bar);
-            tma_load_2d(to, &map_o, tile * kTile, 0, bar);
-        }
-        const long long c = static_cast<long long>(tile) * kTile + t;
-        const bool live = c < b.n;
-        const int f_in = live ? b.frame[c] : 0;
-        const int ii_first = live ? b.ii[c] : 0;
-        const bool landed = __syncthreads_and(mbar_wait_bounded(bar, phase));
-        if (!landed) {  // report, drain the copy (bounded) and leave
-            if (live)
-                for (int k = 0; k < n_ii; ++k) {
-                    const long long o = k * b.ii_stride + c;
-                    out.verdict[o] = TFV_CLASS_DEVICE_TIMEOUT;
-                    out.makespan[o] = 0;
-                    out.ii[o] = 0;
-                }
-            mbar_wait_bounded(bar, phase);
-            return;
-        }
-        phase ^= 1;
-        for (int k = 0; k < n_ii; ++k) {  // each II of the sweep reuses the staged tile
-            const long long o = k * b.ii_stride + c;
-            const int ii = k == 0 ? ii_first : (live ? b.ii[o] : 0);
-            int cls = 0, ms = 0;  // this thread's verdict and makespan
-            if (live && fr.n_frames > 0) {
-                const int16_t* mp = tp + t;
-                const int16_t* mo = to + t;
-                const bool frame_ok = static_cast<unsigned>(f_in) < static_cast<unsigned>(fr.n_frames);
-                const int f = frame_ok ? f_in : 0;
-                const int fclass = frame_ok ? ft.frame_class[f] : TFV_CLASS_BAD_PACKING;
-                Extremes x{INT_MAX, INT_MAX, INT_MIN, INT_MIN};
-                const char* row_p = reinterpret_cast<const char*>(mp);
-                const int to_bytes = N * kTmaRowBytes;
-                const int lane_min = walk_lanes<kBodyRows>(ft.order + static_cast<size_t>(f) * N,
-                                                           ft.lane_len + static_cast<size_t>(f) * 16, opc, row_p, to_bytes,
-                                                           N, ii, x);
-                // Sync edges before the set's first static failure, base starts folded in.
-                const int set = fr.sync_set[f];
-                const int2 meta = (static_cast<unsigned>(set) < static_cast<unsigned>(fr.n_sync_sets))
-                                      ? ft.set_meta[set] : make_int2(0, TFV_CLASS_BAD_PACKING);
-                const int4* prog = ft.set_prog + (meta.x > 0 ? fr.sync_offsets[set] : 0);
-                int sync_min = INT_MAX;
-    #pragma unroll 4
-                for (int k = 0; k < meta.x; ++k) {
-                    const int4 e = prog[k];
-                    const int a_row = e.x & 0xFFFF, b_row = static_cast<unsigned>(e.x) >> 16;
-                    const int x_row = e.y & 0x1FFFF, d = static_cast<unsigned>(e.y) >> 17;
-                    const int dpa = *reinterpret_cast<const int16_t*>(row_p + a_row);
-                    const int doa = *reinterpret_cast<const int16_t*>(row_p + to_bytes + a_row);
-                    const int dob = *reinterpret_cast<const int16_t*>(row_p + to_bytes + b_row);
-                    const int xb = *reinterpret_cast<const int16_t*>(row_p + x_row);
-                    const int shift = d * ii;
-                    sync_min = __viaddmin_s32(e.z + xb - dpa, shift, sync_min);  // instance 0
-                    sync_min = __viaddmin_s32(e.w + dob - doa, shift, sync_min);  // instances >= 1
-                }
-                // First relation without a lane/sync path: timing at instance 0 decides 17 vs 18.
-                int rel_cls = 0;
-                const int r = ft.first_unreached[f];
-                if (r >= 0) {
-                    const int packed = p.relation[r];
-                    const int a = packed & 0xFFF, bb = (packed >> 12) & 0xFFF, d = packed >> 24;
-                    const int ready = opc[a].z + mp[a * kTile] + opc[a].y;
-                    const int target = d == 0 ? opc[bb].z + mp[bb * kTile] : opc[bb].w + mo[bb * kTile] + ii;
-                    rel_cls = ready > target ? TFV_CLASS_RELATION_TIMING : TFV_CLASS_RELATION_NO_PATH;
-                }
-                bool carried_bad = false;
-                if (kBodyRows >= 1) {
-                    for (int k = 0; k < p.n_carried; ++k) {
-                        const int packed = p.carried[k];
-                        const int u = packed & 0xFFFF, df = packed >> 16;
-                        carried_bad |= opc[u].w + mo[u * kTile] + opc[u].y > opc[df].w + mo[df * kTile];
-                    }
-                }
-                long long makespan = x.max_pl;
-                bool negative = x.min_p < 0;
-                bool out_of_range = !base_ok;
-                if (kBodyRows >= 1) {
-                    const long long k1 = ii, kl = static_cast<long long>(I - 1) * ii;
-                    const long long lo = k1 < kl ? k1 : kl, hi = k1 < kl ? kl : k1;
-                    negative |= static_cast<long long>(x.min_o) + lo < 0;
-                    const long long body = static_cast<long long>(x.max_ol) + hi;
-                    makespan = makespan > body ? makespan : body;
-                    out_of_range |= hi >= TFV_TIME_LIMIT || lo <= -static_cast<long long>(TFV_TIME_LIMIT);
-                }
-                out_of_range |= makespan >= TFV_TIME_LIMIT;
-                if (fclass == TFV_CLASS_BAD_PACKING) cls = TFV_CLASS_BAD_PACKING;
-                else if (fclass == TFV_CLASS_SCHEDULE_MALFORMED || negative) cls = TFV_CLASS_SCHEDULE_MALFORMED;
-                else if (out_of_range) cls = TFV_CLASS_OUT_OF_RANGE;
-                else if (fclass != 0) cls = fclass;
-                else if (kBodyRows >= 2 && ii <= 0) cls = TFV_CLASS_II_NONPOSITIVE;
-                else if (lane_min < 0) cls = TFV_CLASS_LANE_ORDER;
-                else if (sync_min < 0) cls = TFV_CLASS_SYNC_INEQUALITY;
-                else if (meta.y != 0) cls = meta.y;
-                else if (ft.frame_flags[f] & kFrameRegisterCross) cls = TFV_CLASS_REGISTER_CROSSES_LANES;
-                else if (rel_cls) cls = rel_cls;
-                else if (carried_bad) cls = TFV_CLASS_CARRIED_SHARED_LIFETIME;
-                else if (p.n_resources == 0) cls = TFV_CLASS_PASS;
-                else if (warp_path) cls = kResourcesPending;
-                else cls = thread_resources_exceed(p, TileView{opc, mp, mo}, ii) ? TFV_CLASS_RESOURCE_CAPACITY
-                                                                                   : TFV_CLASS_PASS;
-                ms = makespan > INT_MAX ? INT_MAX : (makespan < INT_MIN ? INT_MIN : static_cast<int>(makespan));
-            } else if (live) {  // no frames at all: the candidate cannot name one
-                cls = TFV_CLASS_BAD_PACKING;
-            }
-            if (warp_path) {  // capacity (class 20): the warp checks its pending candidates one by one
-                unsigned pending = __ballot_sync(0xFFFFFFFFu, cls == kResourcesPending);
-                while (pending) {
-                    const int src = __ffs(pending) - 1;
-                    pending &= pending - 1;
-                    const int src_ii = __shfl_sync(0xFFFFFFFFu, ii, src);
-                    const int col = (t & ~31) + src;
-                    const bool exceed = warp_resources_exceed(p, TileView{opc, tp + col, to + col}, src_ii, scratch, lane);
-                    if (lane == src) cls = exceed ? TFV_CLASS_RESOURCE_CAPACITY : TFV_CLASS_PASS;
-                }
-            }
-            if (live) {
-                out.verdict[o] = cls;
-                out.makespan[o] = ms;
-                out.ii[o] = kBodyRows >= 2 ? ii : 0;
-            }
-        }
-        __syncthreads();  // every thread is done with the tile before the next copy lands
-    }
+    tma_verify_body<kBodyRows, kSweep, NoSpec>(p, fr, ft, b, out, n_tiles, &map_p, &map_o, -1);
 }
+
+}  // namespace
 
 PFN_cuTensorMapEncodeTiled_v12000 encode_fn() {
     static PFN_cuTensorMapEncodeTiled_v12000 fn = nullptr;
@@ -333,8 +54,6 @@ size_t tma_smem_bytes(const DevProblem& p) {
     return 4 * static_cast<size_t>(p.n_ops) * kTile + 16 * static_cast<size_t>(p.n_ops) + 16 +
            (kTile / 32) * warp_resource_scratch_bytes(p);
 }
-
-}  // namespace
 
 bool periodic_tma_supported(const DevProblem& p, const DevPeriodic& b) {
     const auto aligned = [](const void* ptr) { return (reinterpret_cast<uintptr_t>(ptr) & 15) == 0; };

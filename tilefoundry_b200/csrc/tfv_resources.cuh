@@ -25,7 +25,9 @@
 //     shared memory and the starts split across the lanes.
 #pragma once
 
+#ifndef __CUDACC_RTC__
 #include <climits>
+#endif
 
 #include "tfv_device.cuh"
 

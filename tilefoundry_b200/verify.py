@@ -109,6 +109,26 @@ class DeviceFrames:
     n_frames: int
 
 
+class FramePlan:
+    """A frame-specialised kernel (``tfv_plan``) of one verifier and one frame content."""
+
+    def __init__(self, lib: ctypes.CDLL, handle: ctypes.c_void_p, key: tuple) -> None:
+        self._lib = lib
+        self.handle = handle
+        self.key = key
+
+    def source(self) -> str:
+        """The generated CUDA source."""
+        buf = ctypes.create_string_buffer(1 << 22)
+        _lib.check(self._lib.tfv_plan_source(self.handle, buf, len(buf)), "tfv_plan_source")
+        return buf.value.decode()
+
+    def close(self) -> None:
+        if self.handle is not None and self.handle.value:
+            self._lib.tfv_plan_destroy(self.handle)
+            self.handle = None
+
+
 class WarpgroupVerifier:
     """One closed problem resident on one GPU."""
 
@@ -120,9 +140,13 @@ class WarpgroupVerifier:
         handle = ctypes.c_void_p()
         _lib.check(self._lib.tfv_problem_create(ctypes.byref(desc), self.device, ctypes.byref(handle)), "tfv_problem_create")
         self._handle = handle
+        self._plans: dict[tuple, FramePlan] = {}
 
     # ------------------------------------------------------------------ lifetime
     def close(self) -> None:
+        for plan in getattr(self, "_plans", {}).values():
+            plan.close()
+        self._plans = {}
         if getattr(self, "_handle", None) is not None and self._handle.value:
             self._lib.tfv_problem_destroy(self._handle)
             self._handle = None
@@ -194,12 +218,29 @@ class WarpgroupVerifier:
         verdict, makespan, ii = out
         return out, _lib.Results(verdict.data_ptr(), makespan.data_ptr(), ii.data_ptr())
 
-    def verify_periodic_device(self, frames: DeviceFrames, table, batch: dict, out=None, stream: Any = None):
+    def plan(self, frames: FrameSet, frame: int) -> "FramePlan":
+        """A frame-specialised kernel for ``frames``' frame ``frame`` (compiled once per frame content)."""
+        key = frames.frames[frame]
+        found = self._plans.get(key)
+        if found is None:
+            arrays = frames.arrays()
+            struct = _lib.frames_struct(arrays, len(frames))
+            handle = ctypes.c_void_p()
+            _lib.check(self._lib.tfv_plan_create(self._handle, ctypes.byref(struct), int(frame), ctypes.byref(handle)),
+                       "tfv_plan_create")
+            found = FramePlan(self._lib, handle, key)
+            self._plans[key] = found
+        return found
+
+    def verify_periodic_device(self, frames: DeviceFrames, table, batch: dict, out=None, stream: Any = None,
+                               plan: "FramePlan | None" = None, spec_frame: int = -1):
         """Verify device-resident periodic candidates.
 
         ``batch`` holds torch tensors on this device: ``base_prologue``/``base_offset``
         [N] int32, ``prologue_delta``/``offset_delta`` [N, stride] int16 (op-major),
         ``ii`` and ``frame`` [n] int32. Returns ``(verdict, makespan, ii)`` int32 tensors.
+        With ``plan`` (see :meth:`plan`), the candidates of frame ``spec_frame`` — which
+        must be the plan's frame — run its generated code; results are unchanged.
         """
         n = int(batch["ii"].shape[0])
         struct = _lib.PeriodicBatch(
@@ -213,6 +254,15 @@ class WarpgroupVerifier:
             batch["frame"].data_ptr(),
         )
         out, results = self._results(n, out)
+        if plan is not None:
+            _lib.check(
+                self._lib.tfv_verify_periodic_planned(
+                    plan.handle, ctypes.byref(frames.struct), table.data_ptr(), int(table.numel()), ctypes.byref(struct),
+                    int(spec_frame), ctypes.byref(results), self._stream(stream),
+                ),
+                "tfv_verify_periodic_planned",
+            )
+            return out
         _lib.check(
             self._lib.tfv_verify_periodic(
                 self._handle, ctypes.byref(frames.struct), table.data_ptr(), int(table.numel()), ctypes.byref(struct),

@@ -92,7 +92,6 @@ constexpr int kFirstOfLane = 0x8000;
 constexpr int kLastOfLane = 0x4000;
 constexpr int kTmaTile = 128;                         // candidates per TMA tile
 constexpr int kTmaRowBytes = kTmaTile * 2;            // one op's int16 deltas in a tile
-constexpr int kSpecSmemBytes = (kTmaTile + 32) * 4;   // tile permutation of a frame-specialised kernel
 constexpr int kNoBodyWeight = 1 << 29;                // slack that can never go negative
 constexpr int kMaxProgDistance = (1 << 14) - 1;
 

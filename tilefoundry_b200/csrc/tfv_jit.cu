@@ -23,8 +23,8 @@
 #include <cuda.h>
 #include <cudaTypedefs.h>
 
-#include "tfv_device.cuh"
 #include "tfv_jit_sources.inc"
+#include "tfv_periodic_tma.cuh"
 
 int tfv_internal_fail(int code, const char* message);
 const tfv::DevProblem* tfv_internal_dev(const tfv_problem* p);
@@ -39,7 +39,6 @@ tfv::DevFrames tfv_internal_to_dev(const tfv_frames& f);
 
 namespace tfv {
 bool make_map(CUtensorMap* map, const int16_t* base, long long n, long long stride, int N);
-size_t tma_smem_bytes(const DevProblem& p);
 bool periodic_tma_supported(const DevProblem& p, const DevPeriodic& b);
 }  // namespace tfv
 
@@ -127,6 +126,10 @@ const Driver& driver() {
 // Code generation
 // ---------------------------------------------------------------------------------------
 
+// Tiles per CTA iteration of a specialised kernel: the frame's candidates of two tiles fill
+// whole warps more often than those of one; bodies too large for two tiles take one.
+constexpr int kSpecSuperMax = 2;
+
 struct FrameInput {
     int N = 0, I = 0;
     std::vector<std::vector<int>> lanes;  // operations of each lane in program order
@@ -148,7 +151,7 @@ class Gen {
 
 std::string I2S(long long v) { return std::to_string(v); }
 
-std::string generate(const FrameInput& in, const int* issue, const int* lat, int body_rows) {
+std::string generate(const FrameInput& in, const int* issue, const int* lat, int body_rows, int super) {
     const int N = in.N;
     Gen g;
     const auto bp = [](int k) { return "bp[" + I2S(k) + "]"; };
@@ -246,7 +249,7 @@ std::string generate(const FrameInput& in, const int* issue, const int* lat, int
     src += "typedef CUtensorMap_st CUtensorMap;\n";
     src += "#include \"tfv_periodic_tma.cuh\"\n";
     src += "__constant__ int tfv_spec_c[" + I2S(std::max(1, g.n_consts)) + "];\n";
-    src += "struct Spec {\n    static constexpr bool kEnabled = true;\n";
+    src += "struct Spec {\n    static constexpr bool kEnabled = true;\n    static constexpr int kSuper = " + I2S(super) + ";\n";
     src += "    __device__ __forceinline__ static void eval(const char* rp, int ii, tfv::Extremes& x, int& lane_min,\n";
     src += "                                                int& sync_min) {\n";
     src += "        const int16_t* P = reinterpret_cast<const int16_t*>(rp);\n";
@@ -260,7 +263,7 @@ std::string generate(const FrameInput& in, const int* issue, const int* lat, int
     src += "    if (threadIdx.x != 0 || blockIdx.x != 0) return;\n";
     src += g.consts;
     src += "}\n";
-    src += "extern \"C\" __global__ void __launch_bounds__(" + I2S(tfv::kTmaTile) + ") tfv_spec_kernel(\n";
+    src += "extern \"C\" __global__ void __launch_bounds__(" + I2S(tfv::kTmaTile * super) + ") tfv_spec_kernel(\n";
     src += "    tfv::DevProblem p, tfv::DevFrames fr, tfv::FrameTable ft, tfv::DevPeriodic b, tfv::DevResults out, int n_tiles,\n";
     src += "    const __grid_constant__ CUtensorMap map_p, const __grid_constant__ CUtensorMap map_o, int spec_frame) {\n";
     src += "    tfv::tma_verify_body<" + I2S(body_rows) + ", false, Spec>(p, fr, ft, b, out, n_tiles, &map_p, &map_o, spec_frame);\n";
@@ -278,6 +281,7 @@ struct tfv_plan {
     const tfv_problem* problem = nullptr;
     int device = 0;
     int body_rows = 0;
+    int super = 1;  // tiles per CTA iteration
     int n_consts = 0;
     CUmodule module = nullptr;
     CUfunction kernel = nullptr, consts_kernel = nullptr;
@@ -349,7 +353,11 @@ int tfv_plan_create(const tfv_problem* p, const tfv_frames* host_frames, int fra
     plan->problem = p;
     plan->device = tfv_internal_device(p);
     plan->body_rows = body_rows;
-    plan->source = generate(in, tfv_internal_issue_host(p), tfv_internal_latency_host(p), body_rows);
+    int optin = 0;
+    if (cudaDeviceGetAttribute(&optin, cudaDevAttrMaxSharedMemoryPerBlockOptin, plan->device) != cudaSuccess) optin = 0;
+    plan->super = kSpecSuperMax;
+    while (plan->super > 1 && tfv::tma_body_smem_bytes(d, plan->super, true) > static_cast<size_t>(optin)) --plan->super;
+    plan->source = generate(in, tfv_internal_issue_host(p), tfv_internal_latency_host(p), body_rows, plan->super);
 
     const Nvrtc& nv = nvrtc();
     void* prog = nullptr;
@@ -391,10 +399,11 @@ int tfv_plan_create(const tfv_problem* p, const tfv_frames* host_frames, int fra
         delete plan;
         return tfv_internal_fail(TFV_ERR_CUDA, "loading the frame-specialised module failed");
     }
-    plan->smem = tfv::tma_smem_bytes(d) + tfv::kSpecSmemBytes;
+    plan->smem = tfv::tma_body_smem_bytes(d, plan->super, true);
     if (drv.set_attribute(plan->kernel, CU_FUNC_ATTRIBUTE_MAX_DYNAMIC_SHARED_SIZE_BYTES, static_cast<int>(plan->smem)) !=
             CUDA_SUCCESS ||
-        drv.occupancy(&plan->per_sm, plan->kernel, tfv::kTmaTile, plan->smem) != CUDA_SUCCESS || plan->per_sm < 1) {
+        drv.occupancy(&plan->per_sm, plan->kernel, tfv::kTmaTile * plan->super, plan->smem) != CUDA_SUCCESS ||
+        plan->per_sm < 1) {
         drv.unload(plan->module);
         delete plan;
         return tfv_internal_fail(TFV_ERR_CUDA, "the frame-specialised kernel cannot be resident");
@@ -473,13 +482,14 @@ int tfv_verify_periodic_planned(const tfv_plan* plan, const tfv_frames* frames, 
         cr = drv.copy(plan->consts_symbol, reinterpret_cast<CUdeviceptr>(plan->consts_scratch),
                       sizeof(int) * static_cast<size_t>(plan->n_consts), reinterpret_cast<CUstream>(s));
     const long long tiles = (db.n + tfv::kTmaTile - 1) / tfv::kTmaTile;
+    const long long supers = (tiles + plan->super - 1) / plan->super;
     const long long cap = static_cast<long long>(tfv_internal_sm_count(p)) * plan->per_sm;
-    const int grid = static_cast<int>(tiles < cap ? tiles : cap);
+    const int grid = static_cast<int>(supers < cap ? supers : cap);
     int n_tiles = static_cast<int>(tiles);
     tfv::DevProblem dp = d;
     void* args[] = {&dp, &df, &view, &db, &dr, &n_tiles, &map_p, &map_o, &spec_frame};
     if (cr == CUDA_SUCCESS)
-        cr = drv.launch(plan->kernel, grid, 1, 1, tfv::kTmaTile, 1, 1, static_cast<unsigned>(plan->smem),
+        cr = drv.launch(plan->kernel, grid, 1, 1, tfv::kTmaTile * plan->super, 1, 1, static_cast<unsigned>(plan->smem),
                         reinterpret_cast<CUstream>(s), args, nullptr);
     cudaSetDevice(previous);
     if (cr != CUDA_SUCCESS) return tfv_internal_fail(TFV_ERR_CUDA, "launching the frame-specialised kernel failed");

@@ -135,27 +135,41 @@ struct TileView {
     __device__ __forceinline__ int o(int a) const { return opc[a].w + mo[a * kTile]; }
 };
 
-// The frame-independent default: every candidate takes the frame-table path.
+// The frame-independent default: every candidate takes the frame-table path, one tile of
+// kTile candidates per CTA iteration.
 struct NoSpec {
     static constexpr bool kEnabled = false;
+    static constexpr int kSuper = 1;
     __device__ __forceinline__ static void eval(const char*, int, Extremes&, int&, int&) {}
 };
 
+// Shared-memory bytes of the body: kSuper tiles, per-op constants, the mbarrier, the warps'
+// capacity-check records and (specialised kernels) the permutation of the candidates.
+__host__ __device__ inline size_t tma_body_smem_bytes(const DevProblem& p, int super, bool permuted) {
+    const size_t threads = static_cast<size_t>(kTile) * super;
+    return 4 * static_cast<size_t>(p.n_ops) * kTile * super + 16 * static_cast<size_t>(p.n_ops) + 16 +
+           (threads / 32) * warp_resource_scratch_bytes(p) + (permuted ? (threads + 32) * 4 : 0);
+}
+
 // The verification of one launch (tiles of kTile candidates, one thread per candidate).
 // kSweep: more than one II per candidate. Spec: code generated for one frame of the batch
-// (spec_frame); its candidates are gathered to the first threads of each tile, so that
-// whole warps run the generated code, and the rest take the frame-table path.
+// (spec_frame). A CTA then takes Spec::kSuper tiles per iteration and gathers that frame's
+// candidates to its first threads: whole warps of them run the generated code, and the
+// rest (including the remainder short of a warp) take the frame-table path, so no warp
+// runs both.
 template <int kBodyRows, bool kSweep, class Spec>
 __device__ __forceinline__ void tma_verify_body(const DevProblem& p, const DevFrames& fr, const FrameTable& ft,
                                                 const DevPeriodic& b, const DevResults& out, int n_tiles,
                                                 const CUtensorMap* map_p, const CUtensorMap* map_o, int spec_frame) {
     extern __shared__ __align__(128) unsigned char smem[];
+    constexpr int kSuper = Spec::kSuper;      // tiles per CTA iteration
+    constexpr int kThreads = kTile * kSuper;  // threads per CTA = candidates per iteration
     const int N = p.n_ops;
     const int I = p.iterations;
     const int t = threadIdx.x;
-    int16_t* tp = reinterpret_cast<int16_t*>(smem);             // [N][kTile] prologue deltas
-    int16_t* to = tp + N * kTile;                               // [N][kTile] offset deltas
-    int4* opc = reinterpret_cast<int4*>(smem + 4 * N * kTile);  // [N] issue, latency, base starts
+    // tile j: [N][kTile] prologue deltas, then [N][kTile] offset deltas
+    const auto tile_p = [&](int j) { return reinterpret_cast<int16_t*>(smem + static_cast<size_t>(j) * 4 * N * kTile); };
+    int4* opc = reinterpret_cast<int4*>(smem + static_cast<size_t>(kSuper) * 4 * N * kTile);  // issue, latency, bases
     uint64_t* bar = reinterpret_cast<uint64_t*>(opc + N);
     const int lane = t & 31;
     // capacity-check records of this warp (warp path only)
@@ -164,12 +178,12 @@ __device__ __forceinline__ void tma_verify_body(const DevProblem& p, const DevFr
     const int records = warp_path ? 2 * p.res_max_windows : 0;
     int4* scratch = reinterpret_cast<int4*>(bar + 2) + (t >> 5) * records;
     // tile permutation of the specialised kernel, after every warp's records
-    int* perm = reinterpret_cast<int*>(reinterpret_cast<int4*>(bar + 2) + (kTile / 32) * records);
-    int* warp_count = perm + kTile;
+    int* perm = reinterpret_cast<int*>(reinterpret_cast<int4*>(bar + 2) + (kThreads / 32) * records);
+    int* warp_count = perm + kThreads;
     const int n_ii = kSweep ? b.n_ii : 1;
 
     bool base_ok = true;
-    for (int s = t; s < N; s += kTile) {
+    for (int s = t; s < N; s += kThreads) {
         const int bp = b.base_prologue[s], bo = b.base_offset[s];
         base_ok &= bp > -TFV_BASE_LIMIT && bp < TFV_BASE_LIMIT && bo > -TFV_BASE_LIMIT && bo < TFV_BASE_LIMIT;
         opc[s] = make_int4(p.issue[s], p.latency[s], bp, bo);
@@ -183,14 +197,18 @@ __device__ __forceinline__ void tma_verify_body(const DevProblem& p, const DevFr
 
     const unsigned tile_bytes = static_cast<unsigned>(2 * N * kTile * sizeof(int16_t));
     unsigned phase = 0;
-    for (int tile = blockIdx.x; tile < n_tiles; tile += gridDim.x) {
+    const int n_super = (n_tiles + kSuper - 1) / kSuper;
+    for (int sup = blockIdx.x; sup < n_super; sup += gridDim.x) {
         if (t == 0) {
+            const int loaded = min(kSuper, n_tiles - sup * kSuper);  // no copy for a tile past the end
             fence_proxy_async();
-            mbar_expect_tx(bar, tile_bytes);
-            tma_load_2d(tp, map_p, tile * kTile, 0, bar);
-            tma_load_2d(to, map_o, tile * kTile, 0, bar);
+            mbar_expect_tx(bar, tile_bytes * loaded);
+            for (int j = 0; j < loaded; ++j) {
+                tma_load_2d(tile_p(j), map_p, (sup * kSuper + j) * kTile, 0, bar);
+                tma_load_2d(tile_p(j) + N * kTile, map_o, (sup * kSuper + j) * kTile, 0, bar);
+            }
         }
-        const long long c_own = static_cast<long long>(tile) * kTile + t;
+        const long long c_own = static_cast<long long>(sup) * kThreads + t;
         const bool live_own = c_own < b.n;
         const int f_own = live_own ? b.frame[c_own] : 0;
         const int ii_own = live_own ? b.ii[c_own] : 0;
@@ -210,13 +228,14 @@ __device__ __forceinline__ void tma_verify_body(const DevProblem& p, const DevFr
         // The tile column this thread verifies: its own, or with a specialised frame the
         // column the permutation gives it (that frame's candidates first, in order).
         int col = t;
+        bool spec = false;
         if constexpr (Spec::kEnabled) {
             const bool mine = live_own && f_own == spec_frame;
             const unsigned m = __ballot_sync(0xFFFFFFFFu, mine);
             if (lane == 0) warp_count[t >> 5] = __popc(m);
             __syncthreads();
             int before = 0, total = 0;
-            for (int w = 0; w < kTile / 32; ++w) {
+            for (int w = 0; w < kThreads / 32; ++w) {
                 const int cw = warp_count[w];
                 before += w < (t >> 5) ? cw : 0;
                 total += cw;
@@ -225,19 +244,23 @@ __device__ __forceinline__ void tma_verify_body(const DevProblem& p, const DevFr
             perm[mine ? lower : total + t - lower] = t;
             __syncthreads();
             col = perm[t];
+            spec = t < (total & ~31);  // whole warps of the frame's candidates
         }
-        const long long c = static_cast<long long>(tile) * kTile + col;
+        // the candidate's tile and its column there
+        int16_t* const tp = tile_p(col / kTile);
+        int16_t* const to = tp + N * kTile;
+        const int tc = col % kTile;
+        const long long c = static_cast<long long>(sup) * kThreads + col;
         const bool live = c < b.n;
         const int f_in = Spec::kEnabled ? (live ? b.frame[c] : 0) : f_own;
         const int ii_first = Spec::kEnabled ? (live ? b.ii[c] : 0) : ii_own;
-        const bool spec = Spec::kEnabled && live && f_in == spec_frame;
         for (int k = 0; k < n_ii; ++k) {  // each II of the sweep reuses the staged tile
             const long long o = k * b.ii_stride + c;
             const int ii = k == 0 ? ii_first : (live ? b.ii[o] : 0);
             int cls = 0, ms = 0;  // this thread's verdict and makespan
             if (live && fr.n_frames > 0) {
-                const int16_t* mp = tp + col;
-                const int16_t* mo = to + col;
+                const int16_t* mp = tp + tc;
+                const int16_t* mo = to + tc;
                 const bool frame_ok = static_cast<unsigned>(f_in) < static_cast<unsigned>(fr.n_frames);
                 const int f = frame_ok ? f_in : 0;
                 const int fclass = frame_ok ? ft.frame_class[f] : TFV_CLASS_BAD_PACKING;
@@ -327,8 +350,9 @@ __device__ __forceinline__ void tma_verify_body(const DevProblem& p, const DevFr
                     pending &= pending - 1;
                     const int src_ii = __shfl_sync(0xFFFFFFFFu, ii, src);
                     const int src_col = __shfl_sync(0xFFFFFFFFu, col, src);
-                    const bool exceed =
-                        warp_resources_exceed(p, TileView{opc, tp + src_col, to + src_col}, src_ii, scratch, lane);
+                    int16_t* const sp = tile_p(src_col / kTile);
+                    const bool exceed = warp_resources_exceed(
+                        p, TileView{opc, sp + src_col % kTile, sp + N * kTile + src_col % kTile}, src_ii, scratch, lane);
                     if (lane == src) cls = exceed ? TFV_CLASS_RESOURCE_CAPACITY : TFV_CLASS_PASS;
                 }
             }

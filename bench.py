@@ -325,7 +325,7 @@ def run_ours(args) -> None:
 
         dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=300), device_id=dev)
 
-    from tilefoundry_b200 import WarpgroupVerifier
+    from tilefoundry_b200 import VerifierRuntimeError, WarpgroupVerifier
     from tilefoundry_b200.verify import pinned_like
 
     global ORACLE_PROBLEM
@@ -366,7 +366,11 @@ def run_ours(args) -> None:
     plan, spec_frame = None, -1
     if not args.no_plan and n_ii == 1 and packed.n_ops <= 256:
         spec_frame = int(np.argmax(np.bincount(batch.frame, minlength=len(frames))))
-        plan = verifier.plan(frames, spec_frame)
+        try:
+            plan = verifier.plan(frames, spec_frame)
+        except VerifierRuntimeError as error:  # no run-time compiler here: the frame-table kernel serves all
+            print(f"# frame-specialised kernel unavailable ({error}); frame-table kernel only", file=sys.stderr)
+            plan, spec_frame = None, -1
 
     def barrier():
         if dist is not None:

@@ -126,9 +126,15 @@ const Driver& driver() {
 // Code generation
 // ---------------------------------------------------------------------------------------
 
-// Tiles per CTA iteration of a specialised kernel: the frame's candidates of two tiles fill
-// whole warps more often than those of one; bodies too large for two tiles take one.
-constexpr int kSpecSuperMax = 2;
+// Iteration shapes of a specialised kernel, first fit in shared memory wins: tiles per CTA
+// iteration and candidates per thread. Two tiles give the frame's candidates more whole
+// warps than one; bodies too large for two tiles take one. (Four tiles with two passes per
+// thread balance the warps of a CTA better but halve the resident warps; measured slower
+// on the MLA batch: 1.106 ms against 0.962 ms for two tiles.)
+struct Shape {
+    int super, passes;
+};
+constexpr Shape kShapes[] = {{2, 1}, {1, 1}};
 
 struct FrameInput {
     int N = 0, I = 0;
@@ -151,7 +157,7 @@ class Gen {
 
 std::string I2S(long long v) { return std::to_string(v); }
 
-std::string generate(const FrameInput& in, const int* issue, const int* lat, int body_rows, int super) {
+std::string generate(const FrameInput& in, const int* issue, const int* lat, int body_rows, Shape shape) {
     const int N = in.N;
     Gen g;
     const auto bp = [](int k) { return "bp[" + I2S(k) + "]"; };
@@ -249,7 +255,9 @@ std::string generate(const FrameInput& in, const int* issue, const int* lat, int
     src += "typedef CUtensorMap_st CUtensorMap;\n";
     src += "#include \"tfv_periodic_tma.cuh\"\n";
     src += "__constant__ int tfv_spec_c[" + I2S(std::max(1, g.n_consts)) + "];\n";
-    src += "struct Spec {\n    static constexpr bool kEnabled = true;\n    static constexpr int kSuper = " + I2S(super) + ";\n";
+    src += "struct Spec {\n    static constexpr bool kEnabled = true;\n";
+    src += "    static constexpr int kSuper = " + I2S(shape.super) + ";\n";
+    src += "    static constexpr int kPasses = " + I2S(shape.passes) + ";\n";
     src += "    __device__ __forceinline__ static void eval(const char* rp, int ii, tfv::Extremes& x, int& lane_min,\n";
     src += "                                                int& sync_min) {\n";
     src += "        const int16_t* P = reinterpret_cast<const int16_t*>(rp);\n";
@@ -263,7 +271,8 @@ std::string generate(const FrameInput& in, const int* issue, const int* lat, int
     src += "    if (threadIdx.x != 0 || blockIdx.x != 0) return;\n";
     src += g.consts;
     src += "}\n";
-    src += "extern \"C\" __global__ void __launch_bounds__(" + I2S(tfv::kTmaTile * super) + ") tfv_spec_kernel(\n";
+    src += "extern \"C\" __global__ void __launch_bounds__(" + I2S(tfv::kTmaTile * shape.super / shape.passes) +
+           ") tfv_spec_kernel(\n";
     src += "    tfv::DevProblem p, tfv::DevFrames fr, tfv::FrameTable ft, tfv::DevPeriodic b, tfv::DevResults out, int n_tiles,\n";
     src += "    const __grid_constant__ CUtensorMap map_p, const __grid_constant__ CUtensorMap map_o, int spec_frame) {\n";
     src += "    tfv::tma_verify_body<" + I2S(body_rows) + ", false, Spec>(p, fr, ft, b, out, n_tiles, &map_p, &map_o, spec_frame);\n";
@@ -281,7 +290,9 @@ struct tfv_plan {
     const tfv_problem* problem = nullptr;
     int device = 0;
     int body_rows = 0;
-    int super = 1;  // tiles per CTA iteration
+    int super = 1;   // tiles per CTA iteration
+    int passes = 1;  // candidates per thread and iteration
+    int threads = 0;
     int n_consts = 0;
     CUmodule module = nullptr;
     CUfunction kernel = nullptr, consts_kernel = nullptr;
@@ -355,9 +366,16 @@ int tfv_plan_create(const tfv_problem* p, const tfv_frames* host_frames, int fra
     plan->body_rows = body_rows;
     int optin = 0;
     if (cudaDeviceGetAttribute(&optin, cudaDevAttrMaxSharedMemoryPerBlockOptin, plan->device) != cudaSuccess) optin = 0;
-    plan->super = kSpecSuperMax;
-    while (plan->super > 1 && tfv::tma_body_smem_bytes(d, plan->super, true) > static_cast<size_t>(optin)) --plan->super;
-    plan->source = generate(in, tfv_internal_issue_host(p), tfv_internal_latency_host(p), body_rows, plan->super);
+    Shape shape = kShapes[sizeof(kShapes) / sizeof(kShapes[0]) - 1];
+    for (const Shape& candidate : kShapes)
+        if (tfv::tma_body_smem_bytes(d, candidate.super, candidate.passes, true) <= static_cast<size_t>(optin)) {
+            shape = candidate;
+            break;
+        }
+    plan->super = shape.super;
+    plan->passes = shape.passes;
+    plan->threads = tfv::kTmaTile * shape.super / shape.passes;
+    plan->source = generate(in, tfv_internal_issue_host(p), tfv_internal_latency_host(p), body_rows, shape);
 
     const Nvrtc& nv = nvrtc();
     void* prog = nullptr;
@@ -399,10 +417,10 @@ int tfv_plan_create(const tfv_problem* p, const tfv_frames* host_frames, int fra
         delete plan;
         return tfv_internal_fail(TFV_ERR_CUDA, "loading the frame-specialised module failed");
     }
-    plan->smem = tfv::tma_body_smem_bytes(d, plan->super, true);
+    plan->smem = tfv::tma_body_smem_bytes(d, plan->super, plan->passes, true);
     if (drv.set_attribute(plan->kernel, CU_FUNC_ATTRIBUTE_MAX_DYNAMIC_SHARED_SIZE_BYTES, static_cast<int>(plan->smem)) !=
             CUDA_SUCCESS ||
-        drv.occupancy(&plan->per_sm, plan->kernel, tfv::kTmaTile * plan->super, plan->smem) != CUDA_SUCCESS ||
+        drv.occupancy(&plan->per_sm, plan->kernel, plan->threads, plan->smem) != CUDA_SUCCESS ||
         plan->per_sm < 1) {
         drv.unload(plan->module);
         delete plan;
@@ -489,7 +507,7 @@ int tfv_verify_periodic_planned(const tfv_plan* plan, const tfv_frames* frames, 
     tfv::DevProblem dp = d;
     void* args[] = {&dp, &df, &view, &db, &dr, &n_tiles, &map_p, &map_o, &spec_frame};
     if (cr == CUDA_SUCCESS)
-        cr = drv.launch(plan->kernel, grid, 1, 1, tfv::kTmaTile * plan->super, 1, 1, static_cast<unsigned>(plan->smem),
+        cr = drv.launch(plan->kernel, grid, 1, 1, plan->threads, 1, 1, static_cast<unsigned>(plan->smem),
                         reinterpret_cast<CUstream>(s), args, nullptr);
     cudaSetDevice(previous);
     if (cr != CUDA_SUCCESS) return tfv_internal_fail(TFV_ERR_CUDA, "launching the frame-specialised kernel failed");

@@ -50,7 +50,7 @@ bool make_map(CUtensorMap* map, const int16_t* base, long long n, long long stri
 }
 
 // Tiles, per-op constants, the mbarrier (16 bytes) and the warps' capacity-check records.
-size_t tma_smem_bytes(const DevProblem& p) { return tma_body_smem_bytes(p, 1, false); }
+size_t tma_smem_bytes(const DevProblem& p) { return tma_body_smem_bytes(p, 1, 1, false); }
 
 bool periodic_tma_supported(const DevProblem& p, const DevPeriodic& b) {
     const auto aligned = [](const void* ptr) { return (reinterpret_cast<uintptr_t>(ptr) & 15) == 0; };

@@ -139,16 +139,19 @@ struct TileView {
 // kTile candidates per CTA iteration.
 struct NoSpec {
     static constexpr bool kEnabled = false;
-    static constexpr int kSuper = 1;
+    static constexpr int kSuper = 1;   // tiles per CTA iteration
+    static constexpr int kPasses = 1;  // candidates per thread and iteration
     __device__ __forceinline__ static void eval(const char*, int, Extremes&, int&, int&) {}
 };
 
-// Shared-memory bytes of the body: kSuper tiles, per-op constants, the mbarrier, the warps'
-// capacity-check records and (specialised kernels) the permutation of the candidates.
-__host__ __device__ inline size_t tma_body_smem_bytes(const DevProblem& p, int super, bool permuted) {
-    const size_t threads = static_cast<size_t>(kTile) * super;
+// Shared-memory bytes of the body: `super` tiles, per-op constants, the mbarrier, the warps'
+// capacity-check records (kTile * super / passes threads) and (specialised kernels) the
+// permutation of the candidates with per-warp counts.
+__host__ __device__ inline size_t tma_body_smem_bytes(const DevProblem& p, int super, int passes, bool permuted) {
+    const size_t candidates = static_cast<size_t>(kTile) * super;
+    const size_t threads = candidates / passes;
     return 4 * static_cast<size_t>(p.n_ops) * kTile * super + 16 * static_cast<size_t>(p.n_ops) + 16 +
-           (threads / 32) * warp_resource_scratch_bytes(p) + (permuted ? (threads + 32) * 4 : 0);
+           (threads / 32) * warp_resource_scratch_bytes(p) + (permuted ? (candidates + candidates / 32) * 4 : 0);
 }
 
 // The verification of one launch (tiles of kTile candidates, one thread per candidate).
@@ -162,8 +165,10 @@ __device__ __forceinline__ void tma_verify_body(const DevProblem& p, const DevFr
                                                 const DevPeriodic& b, const DevResults& out, int n_tiles,
                                                 const CUtensorMap* map_p, const CUtensorMap* map_o, int spec_frame) {
     extern __shared__ __align__(128) unsigned char smem[];
-    constexpr int kSuper = Spec::kSuper;      // tiles per CTA iteration
-    constexpr int kThreads = kTile * kSuper;  // threads per CTA = candidates per iteration
+    constexpr int kSuper = Spec::kSuper;            // tiles per CTA iteration
+    constexpr int kPasses = Spec::kPasses;          // candidates per thread and iteration
+    constexpr int kCands = kTile * kSuper;          // candidates per iteration
+    constexpr int kThreads = kCands / kPasses;      // threads per CTA
     const int N = p.n_ops;
     const int I = p.iterations;
     const int t = threadIdx.x;
@@ -179,7 +184,7 @@ __device__ __forceinline__ void tma_verify_body(const DevProblem& p, const DevFr
     int4* scratch = reinterpret_cast<int4*>(bar + 2) + (t >> 5) * records;
     // tile permutation of the specialised kernel, after every warp's records
     int* perm = reinterpret_cast<int*>(reinterpret_cast<int4*>(bar + 2) + (kThreads / 32) * records);
-    int* warp_count = perm + kThreads;
+    int* warp_count = perm + kCands;  // [kPasses][kThreads / 32]
     const int n_ii = kSweep ? b.n_ii : 1;
 
     bool base_ok = true;
@@ -208,163 +213,177 @@ __device__ __forceinline__ void tma_verify_body(const DevProblem& p, const DevFr
                 tma_load_2d(tile_p(j) + N * kTile, map_o, (sup * kSuper + j) * kTile, 0, bar);
             }
         }
-        const long long c_own = static_cast<long long>(sup) * kThreads + t;
-        const bool live_own = c_own < b.n;
-        const int f_own = live_own ? b.frame[c_own] : 0;
-        const int ii_own = live_own ? b.ii[c_own] : 0;
+        const long long first = static_cast<long long>(sup) * kCands;  // the iteration's first candidate
         const bool landed = __syncthreads_and(mbar_wait_bounded(bar, phase));
         if (!landed) {  // report, drain the copy (bounded) and leave
-            if (live_own)
+            for (int q = 0; q < kPasses; ++q) {
+                const long long c_own = first + q * kThreads + t;
+                if (c_own >= b.n) continue;
                 for (int k = 0; k < n_ii; ++k) {
                     const long long o = k * b.ii_stride + c_own;
                     out.verdict[o] = TFV_CLASS_DEVICE_TIMEOUT;
                     out.makespan[o] = 0;
                     out.ii[o] = 0;
                 }
+            }
             mbar_wait_bounded(bar, phase);
             return;
         }
         phase ^= 1;
-        // The tile column this thread verifies: its own, or with a specialised frame the
-        // column the permutation gives it (that frame's candidates first, in order).
-        int col = t;
-        bool spec = false;
+        // Positions in the iteration's candidate order: thread t owns positions q * kThreads + t.
+        // With a specialised frame the permutation sorts that frame's candidates first; whole
+        // warps of them (positions below `cut`) run the generated code. A warp's passes cover
+        // positions 32 apart by kThreads, so the frame-table passes (at the end of the order)
+        // fall to different warps than most generated-code passes.
+        int cut = 0;
         if constexpr (Spec::kEnabled) {
-            const bool mine = live_own && f_own == spec_frame;
-            const unsigned m = __ballot_sync(0xFFFFFFFFu, mine);
-            if (lane == 0) warp_count[t >> 5] = __popc(m);
-            __syncthreads();
-            int before = 0, total = 0;
-            for (int w = 0; w < kThreads / 32; ++w) {
-                const int cw = warp_count[w];
-                before += w < (t >> 5) ? cw : 0;
-                total += cw;
+            constexpr int kWarps = kThreads / 32;
+            unsigned masks[kPasses];
+#pragma unroll
+            for (int q = 0; q < kPasses; ++q) {
+                const long long c_own = first + q * kThreads + t;
+                const bool mine = c_own < b.n && b.frame[c_own] == spec_frame;
+                masks[q] = __ballot_sync(0xFFFFFFFFu, mine);
+                if (lane == 0) warp_count[q * kWarps + (t >> 5)] = __popc(masks[q]);
             }
-            const int lower = before + __popc(m & ((1u << lane) - 1));
-            perm[mine ? lower : total + t - lower] = t;
             __syncthreads();
-            col = perm[t];
-            spec = t < (total & ~31);  // whole warps of the frame's candidates
+            int total = 0;
+            for (int i = 0; i < kPasses * kWarps; ++i) total += warp_count[i];
+#pragma unroll
+            for (int q = 0; q < kPasses; ++q) {
+                int before = 0;
+                for (int i = 0; i < q * kWarps + (t >> 5); ++i) before += warp_count[i];
+                const int pos = q * kThreads + t;
+                const int lower = before + __popc(masks[q] & ((1u << lane) - 1));
+                const bool mine = (masks[q] >> lane) & 1u;
+                perm[mine ? lower : total + pos - lower] = pos;
+            }
+            __syncthreads();
+            cut = total & ~31;
         }
-        // the candidate's tile and its column there
-        int16_t* const tp = tile_p(col / kTile);
-        int16_t* const to = tp + N * kTile;
-        const int tc = col % kTile;
-        const long long c = static_cast<long long>(sup) * kThreads + col;
-        const bool live = c < b.n;
-        const int f_in = Spec::kEnabled ? (live ? b.frame[c] : 0) : f_own;
-        const int ii_first = Spec::kEnabled ? (live ? b.ii[c] : 0) : ii_own;
-        for (int k = 0; k < n_ii; ++k) {  // each II of the sweep reuses the staged tile
-            const long long o = k * b.ii_stride + c;
-            const int ii = k == 0 ? ii_first : (live ? b.ii[o] : 0);
-            int cls = 0, ms = 0;  // this thread's verdict and makespan
-            if (live && fr.n_frames > 0) {
-                const int16_t* mp = tp + tc;
-                const int16_t* mo = to + tc;
-                const bool frame_ok = static_cast<unsigned>(f_in) < static_cast<unsigned>(fr.n_frames);
-                const int f = frame_ok ? f_in : 0;
-                const int fclass = frame_ok ? ft.frame_class[f] : TFV_CLASS_BAD_PACKING;
-                Extremes x{INT_MAX, INT_MAX, INT_MIN, INT_MIN};
-                const char* row_p = reinterpret_cast<const char*>(mp);
-                const int to_bytes = N * kTmaRowBytes;
-                int lane_min = INT_MAX, sync_min = INT_MAX;
-                if (spec)
-                    Spec::eval(row_p, ii, x, lane_min, sync_min);
-                else
-                    lane_min = walk_lanes<kBodyRows>(ft.order + static_cast<size_t>(f) * N,
-                                                     ft.lane_len + static_cast<size_t>(f) * 16, opc, row_p, to_bytes,
-                                                     N, ii, x);
-                const int set = fr.sync_set[f];
-                const int2 meta = (static_cast<unsigned>(set) < static_cast<unsigned>(fr.n_sync_sets))
-                                      ? ft.set_meta[set] : make_int2(0, TFV_CLASS_BAD_PACKING);
-                if (!spec) {
-                    // Sync edges before the set's first static failure, base starts folded in.
-                    const int4* prog = ft.set_prog + (meta.x > 0 ? fr.sync_offsets[set] : 0);
-#pragma unroll 4
-                    for (int j = 0; j < meta.x; ++j) {
-                        const int4 e = prog[j];
-                        const int a_row = e.x & 0xFFFF, b_row = static_cast<unsigned>(e.x) >> 16;
-                        const int x_row = e.y & 0x1FFFF, d = static_cast<unsigned>(e.y) >> 17;
-                        const int dpa = *reinterpret_cast<const int16_t*>(row_p + a_row);
-                        const int doa = *reinterpret_cast<const int16_t*>(row_p + to_bytes + a_row);
-                        const int dob = *reinterpret_cast<const int16_t*>(row_p + to_bytes + b_row);
-                        const int xb = *reinterpret_cast<const int16_t*>(row_p + x_row);
-                        const int shift = d * ii;
-                        sync_min = __viaddmin_s32(e.z + xb - dpa, shift, sync_min);  // instance 0
-                        sync_min = __viaddmin_s32(e.w + dob - doa, shift, sync_min);  // instances >= 1
+#pragma unroll 1
+        for (int q = 0; q < kPasses; ++q) {
+            const int pos = q * kThreads + t;
+            const int col = Spec::kEnabled ? perm[pos] : pos;  // the candidate's column in the iteration
+            const bool spec = Spec::kEnabled && pos < cut;
+            int16_t* const tp = tile_p(col / kTile);
+            int16_t* const to = tp + N * kTile;
+            const int tc = col % kTile;
+            const long long c = first + col;
+            const bool live = c < b.n;
+            const int f_in = live ? b.frame[c] : 0;
+            const int ii_first = live ? b.ii[c] : 0;
+            for (int k = 0; k < n_ii; ++k) {  // each II of the sweep reuses the staged tile
+                const long long o = k * b.ii_stride + c;
+                const int ii = k == 0 ? ii_first : (live ? b.ii[o] : 0);
+                int cls = 0, ms = 0;  // this thread's verdict and makespan
+                if (live && fr.n_frames > 0) {
+                    const int16_t* mp = tp + tc;
+                    const int16_t* mo = to + tc;
+                    const bool frame_ok = static_cast<unsigned>(f_in) < static_cast<unsigned>(fr.n_frames);
+                    const int f = frame_ok ? f_in : 0;
+                    const int fclass = frame_ok ? ft.frame_class[f] : TFV_CLASS_BAD_PACKING;
+                    Extremes x{INT_MAX, INT_MAX, INT_MIN, INT_MIN};
+                    const char* row_p = reinterpret_cast<const char*>(mp);
+                    const int to_bytes = N * kTmaRowBytes;
+                    int lane_min = INT_MAX, sync_min = INT_MAX;
+                    if (spec)
+                        Spec::eval(row_p, ii, x, lane_min, sync_min);
+                    else
+                        lane_min = walk_lanes<kBodyRows>(ft.order + static_cast<size_t>(f) * N,
+                                                         ft.lane_len + static_cast<size_t>(f) * 16, opc, row_p, to_bytes,
+                                                         N, ii, x);
+                    const int set = fr.sync_set[f];
+                    const int2 meta = (static_cast<unsigned>(set) < static_cast<unsigned>(fr.n_sync_sets))
+                                          ? ft.set_meta[set] : make_int2(0, TFV_CLASS_BAD_PACKING);
+                    if (!spec) {
+                        // Sync edges before the set's first static failure, base starts folded in.
+                        const int4* prog = ft.set_prog + (meta.x > 0 ? fr.sync_offsets[set] : 0);
+    #pragma unroll 4
+                        for (int j = 0; j < meta.x; ++j) {
+                            const int4 e = prog[j];
+                            const int a_row = e.x & 0xFFFF, b_row = static_cast<unsigned>(e.x) >> 16;
+                            const int x_row = e.y & 0x1FFFF, d = static_cast<unsigned>(e.y) >> 17;
+                            const int dpa = *reinterpret_cast<const int16_t*>(row_p + a_row);
+                            const int doa = *reinterpret_cast<const int16_t*>(row_p + to_bytes + a_row);
+                            const int dob = *reinterpret_cast<const int16_t*>(row_p + to_bytes + b_row);
+                            const int xb = *reinterpret_cast<const int16_t*>(row_p + x_row);
+                            const int shift = d * ii;
+                            sync_min = __viaddmin_s32(e.z + xb - dpa, shift, sync_min);  // instance 0
+                            sync_min = __viaddmin_s32(e.w + dob - doa, shift, sync_min);  // instances >= 1
+                        }
+                    }
+                    // First relation without a lane/sync path: timing at instance 0 decides 17 vs 18.
+                    int rel_cls = 0;
+                    const int r = ft.first_unreached[f];
+                    if (r >= 0) {
+                        const int packed = p.relation[r];
+                        const int a = packed & 0xFFF, bb = (packed >> 12) & 0xFFF, d = packed >> 24;
+                        const int ready = opc[a].z + mp[a * kTile] + opc[a].y;
+                        const int target = d == 0 ? opc[bb].z + mp[bb * kTile] : opc[bb].w + mo[bb * kTile] + ii;
+                        rel_cls = ready > target ? TFV_CLASS_RELATION_TIMING : TFV_CLASS_RELATION_NO_PATH;
+                    }
+                    bool carried_bad = false;
+                    if (kBodyRows >= 1) {
+                        for (int k = 0; k < p.n_carried; ++k) {
+                            const int packed = p.carried[k];
+                            const int u = packed & 0xFFFF, df = packed >> 16;
+                            carried_bad |= opc[u].w + mo[u * kTile] + opc[u].y > opc[df].w + mo[df * kTile];
+                        }
+                    }
+                    long long makespan = x.max_pl;
+                    bool negative = x.min_p < 0;
+                    bool out_of_range = !base_ok;
+                    if (kBodyRows >= 1) {
+                        const long long k1 = ii, kl = static_cast<long long>(I - 1) * ii;
+                        const long long lo = k1 < kl ? k1 : kl, hi = k1 < kl ? kl : k1;
+                        negative |= static_cast<long long>(x.min_o) + lo < 0;
+                        const long long body = static_cast<long long>(x.max_ol) + hi;
+                        makespan = makespan > body ? makespan : body;
+                        out_of_range |= hi >= TFV_TIME_LIMIT || lo <= -static_cast<long long>(TFV_TIME_LIMIT);
+                    }
+                    out_of_range |= makespan >= TFV_TIME_LIMIT;
+                    if (fclass == TFV_CLASS_BAD_PACKING) cls = TFV_CLASS_BAD_PACKING;
+                    else if (fclass == TFV_CLASS_SCHEDULE_MALFORMED || negative) cls = TFV_CLASS_SCHEDULE_MALFORMED;
+                    else if (out_of_range) cls = TFV_CLASS_OUT_OF_RANGE;
+                    else if (fclass != 0) cls = fclass;
+                    else if (kBodyRows >= 2 && ii <= 0) cls = TFV_CLASS_II_NONPOSITIVE;
+                    else if (lane_min < 0) cls = TFV_CLASS_LANE_ORDER;
+                    else if (sync_min < 0) cls = TFV_CLASS_SYNC_INEQUALITY;
+                    else if (meta.y != 0) cls = meta.y;
+                    else if (ft.frame_flags[f] & kFrameRegisterCross) cls = TFV_CLASS_REGISTER_CROSSES_LANES;
+                    else if (rel_cls) cls = rel_cls;
+                    else if (carried_bad) cls = TFV_CLASS_CARRIED_SHARED_LIFETIME;
+                    else if (p.n_resources == 0) cls = TFV_CLASS_PASS;
+                    else if (warp_path) cls = kResourcesPending;
+                    else cls = thread_resources_exceed(p, TileView{opc, mp, mo}, ii) ? TFV_CLASS_RESOURCE_CAPACITY
+                                                                                       : TFV_CLASS_PASS;
+                    ms = makespan > INT_MAX ? INT_MAX : (makespan < INT_MIN ? INT_MIN : static_cast<int>(makespan));
+                } else if (live) {  // no frames at all: the candidate cannot name one
+                    cls = TFV_CLASS_BAD_PACKING;
+                }
+                if (warp_path) {  // capacity (class 20): the warp checks its pending candidates one by one
+                    unsigned pending = __ballot_sync(0xFFFFFFFFu, cls == kResourcesPending);
+                    while (pending) {
+                        const int src = __ffs(pending) - 1;
+                        pending &= pending - 1;
+                        const int src_ii = __shfl_sync(0xFFFFFFFFu, ii, src);
+                        const int src_col = __shfl_sync(0xFFFFFFFFu, col, src);
+                        int16_t* const sp = tile_p(src_col / kTile);
+                        const bool exceed = warp_resources_exceed(
+                            p, TileView{opc, sp + src_col % kTile, sp + N * kTile + src_col % kTile}, src_ii, scratch, lane);
+                        if (lane == src) cls = exceed ? TFV_CLASS_RESOURCE_CAPACITY : TFV_CLASS_PASS;
                     }
                 }
-                // First relation without a lane/sync path: timing at instance 0 decides 17 vs 18.
-                int rel_cls = 0;
-                const int r = ft.first_unreached[f];
-                if (r >= 0) {
-                    const int packed = p.relation[r];
-                    const int a = packed & 0xFFF, bb = (packed >> 12) & 0xFFF, d = packed >> 24;
-                    const int ready = opc[a].z + mp[a * kTile] + opc[a].y;
-                    const int target = d == 0 ? opc[bb].z + mp[bb * kTile] : opc[bb].w + mo[bb * kTile] + ii;
-                    rel_cls = ready > target ? TFV_CLASS_RELATION_TIMING : TFV_CLASS_RELATION_NO_PATH;
+                if (live) {
+                    out.verdict[o] = cls;
+                    out.makespan[o] = ms;
+                    out.ii[o] = kBodyRows >= 2 ? ii : 0;
                 }
-                bool carried_bad = false;
-                if (kBodyRows >= 1) {
-                    for (int k = 0; k < p.n_carried; ++k) {
-                        const int packed = p.carried[k];
-                        const int u = packed & 0xFFFF, df = packed >> 16;
-                        carried_bad |= opc[u].w + mo[u * kTile] + opc[u].y > opc[df].w + mo[df * kTile];
-                    }
-                }
-                long long makespan = x.max_pl;
-                bool negative = x.min_p < 0;
-                bool out_of_range = !base_ok;
-                if (kBodyRows >= 1) {
-                    const long long k1 = ii, kl = static_cast<long long>(I - 1) * ii;
-                    const long long lo = k1 < kl ? k1 : kl, hi = k1 < kl ? kl : k1;
-                    negative |= static_cast<long long>(x.min_o) + lo < 0;
-                    const long long body = static_cast<long long>(x.max_ol) + hi;
-                    makespan = makespan > body ? makespan : body;
-                    out_of_range |= hi >= TFV_TIME_LIMIT || lo <= -static_cast<long long>(TFV_TIME_LIMIT);
-                }
-                out_of_range |= makespan >= TFV_TIME_LIMIT;
-                if (fclass == TFV_CLASS_BAD_PACKING) cls = TFV_CLASS_BAD_PACKING;
-                else if (fclass == TFV_CLASS_SCHEDULE_MALFORMED || negative) cls = TFV_CLASS_SCHEDULE_MALFORMED;
-                else if (out_of_range) cls = TFV_CLASS_OUT_OF_RANGE;
-                else if (fclass != 0) cls = fclass;
-                else if (kBodyRows >= 2 && ii <= 0) cls = TFV_CLASS_II_NONPOSITIVE;
-                else if (lane_min < 0) cls = TFV_CLASS_LANE_ORDER;
-                else if (sync_min < 0) cls = TFV_CLASS_SYNC_INEQUALITY;
-                else if (meta.y != 0) cls = meta.y;
-                else if (ft.frame_flags[f] & kFrameRegisterCross) cls = TFV_CLASS_REGISTER_CROSSES_LANES;
-                else if (rel_cls) cls = rel_cls;
-                else if (carried_bad) cls = TFV_CLASS_CARRIED_SHARED_LIFETIME;
-                else if (p.n_resources == 0) cls = TFV_CLASS_PASS;
-                else if (warp_path) cls = kResourcesPending;
-                else cls = thread_resources_exceed(p, TileView{opc, mp, mo}, ii) ? TFV_CLASS_RESOURCE_CAPACITY
-                                                                                   : TFV_CLASS_PASS;
-                ms = makespan > INT_MAX ? INT_MAX : (makespan < INT_MIN ? INT_MIN : static_cast<int>(makespan));
-            } else if (live) {  // no frames at all: the candidate cannot name one
-                cls = TFV_CLASS_BAD_PACKING;
-            }
-            if (warp_path) {  // capacity (class 20): the warp checks its pending candidates one by one
-                unsigned pending = __ballot_sync(0xFFFFFFFFu, cls == kResourcesPending);
-                while (pending) {
-                    const int src = __ffs(pending) - 1;
-                    pending &= pending - 1;
-                    const int src_ii = __shfl_sync(0xFFFFFFFFu, ii, src);
-                    const int src_col = __shfl_sync(0xFFFFFFFFu, col, src);
-                    int16_t* const sp = tile_p(src_col / kTile);
-                    const bool exceed = warp_resources_exceed(
-                        p, TileView{opc, sp + src_col % kTile, sp + N * kTile + src_col % kTile}, src_ii, scratch, lane);
-                    if (lane == src) cls = exceed ? TFV_CLASS_RESOURCE_CAPACITY : TFV_CLASS_PASS;
-                }
-            }
-            if (live) {
-                out.verdict[o] = cls;
-                out.makespan[o] = ms;
-                out.ii[o] = kBodyRows >= 2 ? ii : 0;
             }
         }
-        __syncthreads();  // every thread is done with the tile before the next copy lands
+        __syncthreads();  // every thread is done with the tiles before the next copies land
     }
 }
-
 
 }  // namespace tfv

@@ -348,15 +348,22 @@ def run_ours(args) -> None:
         key: torch.from_numpy(np.ascontiguousarray(getattr(batch, key))).to(dev)
         for key in ("base_prologue", "base_offset", "prologue_delta", "offset_delta", "ii", "frame")
     }
-    # Results live in [3, n_ii, n] tensors (verdict, makespan, ii), double-buffered so that
-    # the gather of one step's results to rank 0 overlaps the next step's verification.
-    # With n_ii > 1 every candidate is verified at n_ii IIs spread over [II_lb, 2 II_lb].
+    # Results, double-buffered so that the gather of one step's results to rank 0 overlaps
+    # the next step's verification: int32 verdict and II [n_ii, n], and the gathered
+    # payload (shard.pack_results: int32 makespans, written there by the verifier, then
+    # int8 verdicts; 5 bytes per schedule). With n_ii > 1 every candidate is verified at
+    # n_ii IIs spread over [II_lb, 2 II_lb].
+    from tilefoundry_b200.shard import pack_results
     from tilefoundry_b200.workloads import ii_lower_bound, ii_sweep
 
     sweep = np.repeat(ii_sweep(ii_lower_bound(packed), n_ii)[:, None], n, axis=1).astype(np.int32) if n_ii > 1 else None
     ii_values = torch.from_numpy(sweep).to(dev) if sweep is not None else None
-    results = [torch.empty((3, n_ii, n), dtype=torch.int32, device=dev) for _ in range(2)]
-    gathered = [[torch.empty((3, n_ii, n), dtype=torch.int32, device=dev) for _ in range(world)] if rank == 0 else None
+    m = n_ii * n
+    verdicts = [torch.empty((n_ii, n), dtype=torch.int32, device=dev) for _ in range(2)]
+    iis = [torch.empty((n_ii, n), dtype=torch.int32, device=dev) for _ in range(2)]
+    payload = [torch.empty(5 * m, dtype=torch.uint8, device=dev) for _ in range(2)]
+    makespans = [buf[: 4 * m].view(torch.int32).view(n_ii, n) for buf in payload]
+    gathered = [[torch.empty(5 * m, dtype=torch.uint8, device=dev) for _ in range(world)] if rank == 0 else None
                 for _ in range(2)] if world > 1 else None
     pending = [None, None]
     table = verifier.analyze(dframes)
@@ -386,16 +393,18 @@ def run_ours(args) -> None:
         verifier.analyze(dframes, table=table)
         if events is not None:
             events[1].record(stream)
-        out = results[buf]
+        out = (verdicts[buf], makespans[buf], iis[buf])
         if ii_values is None:
-            verifier.verify_periodic_device(dframes, table, tensors, out=(out[0, 0], out[1, 0], out[2, 0]), plan=plan,
+            verifier.verify_periodic_device(dframes, table, tensors, out=tuple(t[0] for t in out), plan=plan,
                                             spec_frame=spec_frame)
         else:
-            verifier.verify_periodic_sweep_device(dframes, table, tensors, ii_values, out=(out[0], out[1], out[2]))
+            verifier.verify_periodic_sweep_device(dframes, table, tensors, ii_values, out=out)
         if events is not None:
             events[2].record(stream)
         if dist is not None:
-            pending[buf] = dist.gather(out, gather_list=gathered[buf] if rank == 0 else None, dst=0, async_op=True)
+            pack_results(verdicts[buf], makespans[buf], out=payload[buf])
+            pending[buf] = dist.gather(payload[buf], gather_list=gathered[buf] if rank == 0 else None, dst=0,
+                                       async_op=True)
 
     def drain():
         for k in range(2):
@@ -463,8 +472,8 @@ def run_ours(args) -> None:
         dist.all_reduce(t, op=dist.ReduceOp.MAX)
         e2e_s = float(t.item())
     e2e_value = n * n_ii * world * e2e_steps / e2e_s
-    last = results[(args.steps - 1) % 2]
-    assert np.array_equal(np.asarray(e2e_out[0]).reshape(n_ii, n), last[0].cpu().numpy()), \
+    last = verdicts[(args.steps - 1) % 2]
+    assert np.array_equal(np.asarray(e2e_out[0]).reshape(n_ii, n), last.cpu().numpy()), \
         "host-buffer and device entries disagree"
     h2d = sum(int(np.asarray(v).nbytes) for v in arrays.values()) + sum(
         int(getattr(batch, k).nbytes) for k in ("base_prologue", "base_offset", "prologue_delta", "offset_delta", "frame"))
@@ -493,7 +502,7 @@ def run_ours(args) -> None:
                 "kind": "port",
                 "sample": f"{sample} candidates of this batch through oracle/verify_port.py in {workers} processes ({secs:.1f} s)",
             }
-        verdicts = np.bincount(last[0].cpu().numpy().ravel() + 3, minlength=25)
+        histogram = np.bincount(last.cpu().numpy().ravel() + 4, minlength=26)
         line = {
             "metric": METRIC,
             "value": value,
@@ -520,8 +529,8 @@ def run_ours(args) -> None:
                 "format": "periodic: int16 prologue/offset deltas + int32 ii + int32 frame per candidate",
                 "bytes_per_candidate": algorithmic_bytes_per_candidate(packed.n_ops),
                 "l2": f"inputs {per_launch / 1e9:.2f} GB per GPU per step, larger than the 126 MB L2",
-                "parallelism": f"dp{world} (contiguous candidate shards, gather to rank 0)",
-                "valid_fraction": float(verdicts[3] / (n * n_ii)),
+                "parallelism": f"dp{world} (contiguous candidate shards; int8 verdict + int32 makespan gathered to rank 0)",
+                "valid_fraction": float(histogram[4] / (n * n_ii)),
             },
             "roofline": {
                 "bound": "hbm",

@@ -227,3 +227,46 @@ def test_closed_problem_is_built_once_per_document_pair():
     assert closed_problem(program, hardware, build) is first
     assert closed_problem(program, other, build) is not first
     assert len(calls) == 2
+
+
+def _packed_worker(rank, world, port, queue):
+    import os
+
+    import torch
+    import torch.distributed as dist
+
+    from tilefoundry_b200.shard import gather_packed, pack_results, shard_bounds, unpack_results
+
+    os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port))
+    dist.init_process_group("gloo", rank=rank, world_size=world)
+    lo, hi = shard_bounds(13, rank, world)
+    idx = torch.arange(lo, hi, dtype=torch.int32)
+    verdict = (idx % 26) - 4                     # every class, -4 .. 21
+    makespan = idx * 1000003 + 7
+    packed = pack_results(verdict, makespan)
+    v, m = unpack_results(packed, hi - lo)
+    assert torch.equal(v, verdict) and torch.equal(m, makespan)
+    full = gather_packed(packed, 13)
+    if rank == 0:
+        queue.put((full[0].tolist(), full[1].tolist()))
+    dist.destroy_process_group()
+
+
+def test_gather_packed_two_gloo_ranks():
+    import multiprocessing as mp
+    import socket
+
+    with socket.socket() as sock:
+        sock.bind(("127.0.0.1", 0))
+        port = sock.getsockname()[1]
+    ctx = mp.get_context("spawn")
+    queue = ctx.Queue()
+    procs = [ctx.Process(target=_packed_worker, args=(r, 2, port, queue)) for r in range(2)]
+    for proc in procs:
+        proc.start()
+    verdict, makespan = queue.get(timeout=120)
+    for proc in procs:
+        proc.join(timeout=60)
+        assert proc.exitcode == 0
+    assert verdict == [(i % 26) - 4 for i in range(13)]
+    assert makespan == [i * 1000003 + 7 for i in range(13)]

@@ -130,7 +130,9 @@ const Driver& driver() {
 // iteration and candidates per thread. Two tiles give the frame's candidates more whole
 // warps than one; bodies too large for two tiles take one. (Four tiles with two passes per
 // thread balance the warps of a CTA better but halve the resident warps; measured slower
-// on the MLA batch: 1.106 ms against 0.962 ms for two tiles.)
+// on the MLA batch: 1.106 ms against 0.962 ms for two tiles. So did giving each frame-table
+// candidate two threads, one for the lanes and one for the sync program: 384-thread CTAs
+// spill and fewer fit, 1.37 ms.)
 struct Shape {
     int super, passes;
 };

@@ -250,7 +250,7 @@ TFV_API int tfv_verify_periodic_sweep(const tfv_problem* problem, const tfv_fram
  * (16-byte aligned deltas, op_stride % 8 == 0). tfv_verify_periodic_planned takes the
  * device frames and frame table like tfv_verify_periodic; `spec_frame` must index a frame
  * identical to the plan's (same lanes and sync set); a plan serves one stream at a time
- * (its constants live in the module). */
+ * (its constants live in the module) and must be destroyed before its problem. */
 typedef struct tfv_plan tfv_plan;
 TFV_API int tfv_plan_create(const tfv_problem* problem, const tfv_frames* host_frames, int frame, tfv_plan** out);
 TFV_API int tfv_plan_destroy(tfv_plan* plan);

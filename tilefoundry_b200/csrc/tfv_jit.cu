@@ -122,6 +122,21 @@ const Driver& driver() {
     return d;
 }
 
+// Makes `device` current for the scope and restores the caller's current device after it.
+class CurrentDevice {
+  public:
+    explicit CurrentDevice(int device) {
+        cudaGetDevice(&previous_);
+        status_ = cudaSetDevice(device);
+    }
+    ~CurrentDevice() { cudaSetDevice(previous_); }
+    cudaError_t status() const { return status_; }
+
+  private:
+    int previous_ = 0;
+    cudaError_t status_ = cudaSuccess;
+};
+
 // ---------------------------------------------------------------------------------------
 // Code generation
 // ---------------------------------------------------------------------------------------
@@ -404,7 +419,8 @@ int tfv_plan_create(const tfv_problem* p, const tfv_frames* host_frames, int fra
     nv.destroy(&prog);
 
     const Driver& drv = driver();
-    cudaError_t e = cudaSetDevice(plan->device);
+    CurrentDevice current(plan->device);
+    cudaError_t e = current.status();
     if (e == cudaSuccess) e = cudaFree(nullptr);  // the primary context is current from here on
     if (e != cudaSuccess) {
         delete plan;
@@ -441,7 +457,7 @@ int tfv_plan_create(const tfv_problem* p, const tfv_frames* host_frames, int fra
 
 int tfv_plan_destroy(tfv_plan* plan) {
     if (!plan) return TFV_OK;
-    cudaSetDevice(plan->device);
+    CurrentDevice current(plan->device);
     if (plan->consts_scratch) cudaFree(plan->consts_scratch);
     if (plan->module) driver().unload(plan->module);
     delete plan;
@@ -468,9 +484,8 @@ int tfv_verify_periodic_planned(const tfv_plan* plan, const tfv_frames* frames, 
         return tfv_internal_fail(TFV_ERR_INVALID_ARGUMENT, "frame table missing or too small");
     if (!b->base_prologue || !b->base_offset || !b->prologue_delta || !b->offset_delta || !b->ii || !b->frame)
         return tfv_internal_fail(TFV_ERR_INVALID_ARGUMENT, "batch arrays must not be NULL");
-    int previous = 0;
-    cudaGetDevice(&previous);
-    cudaError_t e = cudaSetDevice(plan->device);
+    CurrentDevice current(plan->device);
+    cudaError_t e = current.status();
     if (e != cudaSuccess) return tfv_internal_cuda_fail(e, "tfv_verify_periodic_planned");
     const tfv::DevProblem& d = *tfv_internal_dev(p);
     tfv::DevPeriodic db{b->n_candidates, b->op_stride, b->base_prologue, b->base_offset,
@@ -486,7 +501,6 @@ int tfv_verify_periodic_planned(const tfv_plan* plan, const tfv_frames* frames, 
                              !tfv::make_map(&map_o, db.offset_delta, db.n, db.stride, d.n_ops)))
         e = cudaErrorInvalidValue;
     if (e != cudaSuccess) {
-        cudaSetDevice(previous);
         return e == cudaErrorInvalidValue
                    ? tfv_internal_fail(TFV_ERR_UNSUPPORTED, "the batch layout does not allow the TMA-fed kernel")
                    : tfv_internal_cuda_fail(e, "tfv_verify_periodic_planned");
@@ -511,7 +525,6 @@ int tfv_verify_periodic_planned(const tfv_plan* plan, const tfv_frames* frames, 
     if (cr == CUDA_SUCCESS)
         cr = drv.launch(plan->kernel, grid, 1, 1, plan->threads, 1, 1, static_cast<unsigned>(plan->smem),
                         reinterpret_cast<CUstream>(s), args, nullptr);
-    cudaSetDevice(previous);
     if (cr != CUDA_SUCCESS) return tfv_internal_fail(TFV_ERR_CUDA, "launching the frame-specialised kernel failed");
     return TFV_OK;
 }

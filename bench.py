@@ -60,6 +60,12 @@ def parse_args():
                    help="order the batch by frame (as a search loop emits neighbours variant by variant)")
     p.add_argument("--no-plan", action="store_true",
                    help="skip the kernel generated for the batch's most frequent frame (tfv_plan_create)")
+    p.add_argument("--plan-kernel", choices=["auto", "ring", "tiles"], default="auto",
+                   help="kernel of the generated plan: ring (producer warp + consumer warps per SM), "
+                        "tiles (CTAs in lock step) or auto (the ring when it fits)")
+    p.add_argument("--ring-warps", type=int, default=0, help="consumer warps of the ring kernel (0: default)")
+    p.add_argument("--no-delta", action="store_true",
+                   help="only the plan frame's candidates run the generated code (no delta verification)")
     p.add_argument("--cpu-sample", type=int, default=None, help="oracle sample size per step")
     return p.parse_args()
 
@@ -374,7 +380,8 @@ def run_ours(args) -> None:
     if not args.no_plan and n_ii == 1 and packed.n_ops <= 256:
         spec_frame = int(np.argmax(np.bincount(batch.frame, minlength=len(frames))))
         try:
-            plan = verifier.plan(frames, spec_frame)
+            plan = verifier.plan(frames, spec_frame, kernel=args.plan_kernel, ring_warps=args.ring_warps,
+                                 delta=not args.no_delta)
         except VerifierRuntimeError as error:  # no run-time compiler here: the frame-table kernel serves all
             print(f"# frame-specialised kernel unavailable ({error}); frame-table kernel only", file=sys.stderr)
             plan, spec_frame = None, -1
@@ -541,7 +548,8 @@ def run_ours(args) -> None:
                 "traffic": MEASURED_DRAM_BYTES_PER_CANDIDATE * n if args.workload == "mla" else None,
                 "traffic_source": "ncu dram__bytes_read+write on 2097152 candidates, scaled per candidate",
                 "peak_source": peak_src,
-                "kernel": ("tfv_spec_kernel (generated for the most frequent frame, "
+                "kernel": (("tfv_spec_ring" if plan.kernel == "ring" else "tfv_spec_kernel") +
+                           " (generated for the most frequent frame, "
                            f"{float(np.mean(batch.frame == spec_frame)):.2f} of the batch)" if plan is not None else
                            "tfv::verify_periodic_tma_kernel" if packed.n_ops <= 256 else "tfv::verify_periodic_global_kernel"),
                 "kernel_ms": statistics.mean(verify_ms),
@@ -550,8 +558,9 @@ def run_ours(args) -> None:
             "cpu_baseline": cpu,
             "e2e": {"value": e2e_value, "unit": UNIT, "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h,
                     "steps": e2e_steps, "entry": e2e_entry},
-            # frame analysis, sync-program compile, verification (+ the plan's constants kernel)
-            "gpu_launches": (4 if plan is not None else 3) * args.steps,
+            # frame analysis, sync-program compile, verification (+ the plan's constants kernel
+            # and, with delta verification, its frame comparison)
+            "gpu_launches": (3 + (0 if plan is None else 2 if plan.delta else 1)) * args.steps,
             "clocks": clocks.summary(),
         }
         print(json.dumps(line), flush=True)

@@ -37,7 +37,7 @@
 extern "C" {
 #endif
 
-#define TFV_ABI_VERSION 3
+#define TFV_ABI_VERSION 4
 
 #if defined(__GNUC__)
 #define TFV_API __attribute__((visibility("default")))
@@ -253,10 +253,38 @@ TFV_API int tfv_verify_periodic_sweep(const tfv_problem* problem, const tfv_fram
  * (its constants live in the module) and must be destroyed before its problem. */
 typedef struct tfv_plan tfv_plan;
 TFV_API int tfv_plan_create(const tfv_problem* problem, const tfv_frames* host_frames, int frame, tfv_plan** out);
+/* Kernels a plan can be built with. TFV_PLAN_RING: one CTA per SM, a producer warp
+ * streaming tiles into a ring of shared-memory slots and consumer warps verifying them 32
+ * candidates at a time, each warp at its own pace. TFV_PLAN_TILES: CTAs verifying whole
+ * tiles in lock step. TFV_PLAN_AUTO (what tfv_plan_create uses): the ring kernel when at
+ * least three slots fit in shared memory, else the tiles kernel. */
+#define TFV_PLAN_AUTO 0
+#define TFV_PLAN_TILES 1
+#define TFV_PLAN_RING 2
+typedef struct tfv_plan_options {
+    int kernel;      /* TFV_PLAN_AUTO, TFV_PLAN_TILES or TFV_PLAN_RING */
+    int ring_warps;  /* consumer warps of the ring kernel, 1..31; 0 picks the default */
+    int no_delta;    /* nonzero: only the plan's own frame runs the generated code (below) */
+} tfv_plan_options;
+/* tfv_plan_create with options (NULL: the defaults); TFV_ERR_UNSUPPORTED when the
+ * requested kernel does not fit the problem. */
+TFV_API int tfv_plan_create_with(const tfv_problem* problem, const tfv_frames* host_frames, int frame,
+                                 const tfv_plan_options* options, tfv_plan** out);
+/* The kernel a plan was built with (TFV_PLAN_TILES or TFV_PLAN_RING), or -1 for NULL. */
+TFV_API int tfv_plan_kernel(const tfv_plan* plan);
+/* Delta verification (1) or not (0); -1 for NULL. With delta verification the generated
+ * code records which of the plan frame's lane and sync edges each candidate violates, and
+ * every other frame that shares all but at most 8 added lane edges and 8 added sync edges
+ * with it runs the same code: per call, a kernel compares each frame with `spec_frame`
+ * (kept edges as a bit mask, added edges as program entries). Plans of bodies with more
+ * than 128 operations or sync program edges, or built with no_delta, serve the plan
+ * frame's candidates only. A delta plan grows a device buffer to the largest frame count
+ * it has seen, inside tfv_verify_periodic_planned. */
+TFV_API int tfv_plan_delta(const tfv_plan* plan);
 TFV_API int tfv_plan_destroy(tfv_plan* plan);
 /* The generated CUDA source of a plan (truncated to size - 1 bytes). */
 TFV_API int tfv_plan_source(const tfv_plan* plan, char* buffer, size_t size);
-TFV_API int tfv_verify_periodic_planned(const tfv_plan* plan, const tfv_frames* frames, void* frame_table,
+TFV_API int tfv_verify_periodic_planned(tfv_plan* plan, const tfv_frames* frames, void* frame_table,
                                         size_t frame_table_bytes, const tfv_periodic_batch* batch, int spec_frame,
                                         const tfv_results* results, void* stream);
 

@@ -22,7 +22,9 @@ from tilefoundry_b200.workloads import (
 pytestmark = pytest.mark.gpu
 
 
-def _both(verifier, frames, batch):
+def _both(verifier, frames, batch, kernel="auto", ring_warps=0, misalign=False):
+    """Frame-table kernel and plan on the same batch. misalign: the frame and II arrays
+    start 4 bytes past a 16-byte boundary (the ring then stages them with plain loads)."""
     import torch
 
     dev = torch.device("cuda", verifier.device)
@@ -30,24 +32,34 @@ def _both(verifier, frames, batch):
     table = verifier.analyze(dframes)
     tensors = {k: torch.from_numpy(np.ascontiguousarray(getattr(batch, k))).to(dev)
                for k in ("base_prologue", "base_offset", "prologue_delta", "offset_delta", "ii", "frame")}
+    if misalign:
+        for k in ("ii", "frame"):
+            shifted = torch.empty(tensors[k].numel() + 1, dtype=tensors[k].dtype, device=dev)[1:]
+            shifted.copy_(tensors[k])
+            assert shifted.data_ptr() % 16 == 4
+            tensors[k] = shifted
     counts = np.bincount(batch.frame, minlength=len(frames))
     top = int(np.argmax(counts))
-    plan = verifier.plan(frames, top)
+    plan = verifier.plan(frames, top, kernel=kernel, ring_warps=ring_warps)
+    if kernel != "auto":
+        assert plan.kernel == kernel
     generic = [t.cpu().numpy() for t in verifier.verify_periodic_device(dframes, table, tensors)]
     planned = [t.cpu().numpy() for t in verifier.verify_periodic_device(dframes, table, tensors, plan=plan,
                                                                          spec_frame=top)]
     return generic, planned, top
 
 
+@pytest.mark.parametrize("kernel", ["ring", "tiles"])
 @pytest.mark.parametrize("n", [65536, 1000, 8])
-def test_plan_matches_frame_table_kernel_and_oracle_mla(n):
+def test_plan_matches_frame_table_kernel_and_oracle_mla(n, kernel):
     problem = problem_from_json(problem_text("mla"))
     packed = pack_problem(problem)
     witness = witness_from_rows(packed, *raw_cases("mla")[0][0])
     frames, batch, _ = mla_perturbations(packed, witness, n, seed=n + 11, producers=shared_producers(problem))
     with WarpgroupVerifier(packed) as verifier:
-        generic, planned, top = _both(verifier, frames, batch)
-        assert "tfv_spec_kernel" in verifier.plan(frames, top).source()
+        generic, planned, top = _both(verifier, frames, batch, kernel=kernel)
+        name = "tfv_spec_ring" if kernel == "ring" else "tfv_spec_kernel"
+        assert name in verifier.plan(frames, top, kernel=kernel).source()
     for g, p in zip(generic, planned):
         assert np.array_equal(g, p)
     oracle = OracleProblem(load_problem(problem_to_json(problem)))
@@ -59,14 +71,45 @@ def test_plan_matches_frame_table_kernel_and_oracle_mla(n):
     assert np.array_equal(planned[2][sample], oi)
 
 
+@pytest.mark.parametrize("kernel", ["auto", "tiles"])
 @pytest.mark.parametrize("seed", range(16))
-def test_plan_matches_frame_table_kernel_random(seed):
+def test_plan_matches_frame_table_kernel_random(seed, kernel):
     problem, packed, witness = random_problem(seed)
     frames, batch = neighbourhood(packed, witness, 4096, seed=seed + 3, jitter=48)
     with WarpgroupVerifier(packed) as verifier:
-        generic, planned, _top = _both(verifier, frames, batch)
+        generic, planned, _top = _both(verifier, frames, batch, kernel=kernel)
     for g, p in zip(generic, planned):
         assert np.array_equal(g, p)
+
+
+@pytest.mark.parametrize("ring_warps,misalign", [(1, False), (7, True), (31, True), (16, False)])
+def test_ring_plan_warps_and_unaligned_frames(ring_warps, misalign):
+    """Any consumer-warp count, and frame/II arrays off a 16-byte boundary, give the same results."""
+    problem = problem_from_json(problem_text("mla"))
+    packed = pack_problem(problem)
+    witness = witness_from_rows(packed, *raw_cases("mla")[0][0])
+    frames, batch, _ = mla_perturbations(packed, witness, 20000 + 8 * ring_warps, seed=ring_warps,
+                                         producers=shared_producers(problem))
+    with WarpgroupVerifier(packed) as verifier:
+        generic, planned, _top = _both(verifier, frames, batch, kernel="ring", ring_warps=ring_warps,
+                                       misalign=misalign)
+    for g, p in zip(generic, planned):
+        assert np.array_equal(g, p)
+
+
+def test_ring_plan_unsupported_when_slots_do_not_fit():
+    """A 256-operation body leaves no room for three ring slots: the ring is refused and
+    the automatic choice falls back to the tiles kernel."""
+    from tilefoundry_b200 import workloads
+    from tilefoundry_b200.errors import VerifierRuntimeError
+
+    packed = pack_problem(workloads.dag_problem())
+    witness = workloads.list_schedule_witness(packed, seed=1)
+    frames, _batch = neighbourhood(packed, witness, 16, seed=2, jitter=8)
+    with WarpgroupVerifier(packed) as verifier:
+        with pytest.raises(VerifierRuntimeError):
+            verifier.plan(frames, 0, kernel="ring")
+        assert verifier.plan(frames, 0).kernel == "tiles"
 
 
 @pytest.mark.parametrize("name", ["gemm", "fa", "dag"])

@@ -26,7 +26,10 @@ TFV_MAX_LANES = 15
 TFV_MAX_OPS = 4095
 TFV_TIME_LIMIT = 1 << 30
 TFV_BASE_LIMIT = 1 << 28
-ABI_VERSION = 3
+ABI_VERSION = 4
+PLAN_AUTO = 0
+PLAN_TILES = 1
+PLAN_RING = 2
 CLASS_OUT_OF_RANGE = -1
 CLASS_BAD_PACKING = -2
 CLASS_DEVICE_TIMEOUT = -3
@@ -74,6 +77,10 @@ class Frames(ctypes.Structure):
         ("sync_offsets", _p),
         ("sync_edges", _p),
     ]
+
+
+class PlanOptions(ctypes.Structure):
+    _fields_ = [("kernel", ctypes.c_int32), ("ring_warps", ctypes.c_int32), ("no_delta", ctypes.c_int32)]
 
 
 class PeriodicBatch(ctypes.Structure):
@@ -138,6 +145,11 @@ EXPORTS = {
         [_p, ctypes.c_int64, ctypes.POINTER(ctypes.c_char_p), ctypes.POINTER(ctypes.c_size_t)] + [_p] * 8 + [ctypes.c_int],
     ),
     "tfv_plan_create": (ctypes.c_int, [_p, ctypes.POINTER(Frames), ctypes.c_int, ctypes.POINTER(_p)]),
+    "tfv_plan_create_with": (
+        ctypes.c_int, [_p, ctypes.POINTER(Frames), ctypes.c_int, ctypes.POINTER(PlanOptions), ctypes.POINTER(_p)]
+    ),
+    "tfv_plan_kernel": (ctypes.c_int, [_p]),
+    "tfv_plan_delta": (ctypes.c_int, [_p]),
     "tfv_plan_destroy": (ctypes.c_int, [_p]),
     "tfv_plan_source": (ctypes.c_int, [_p, ctypes.c_char_p, ctypes.c_size_t]),
     "tfv_verify_periodic_planned": (

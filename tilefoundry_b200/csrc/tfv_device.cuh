@@ -75,8 +75,10 @@ struct DevFrames {
 //   int32  first_unreached[F]   first relation (sorted order, with instances) whose
 //                               completion -> start path is absent, or -1
 //   int16  succ[F][N]           lane successor (see kWrap)
-//   uint16 order[F][N]          the operations lane by lane in program order; operations in
-//                               no lane follow as pseudo-lane 15
+//   uint16 order[N][F]          position-major: order[j * F + f] is frame f's j-th operation,
+//                               lane by lane in program order; operations in no lane follow
+//                               as pseudo-lane 15 (a warp whose candidates name different
+//                               frames reads a few cache lines per position, not one per frame)
 //   uint16 lane_len[F][16]      length of each lane's run in order[]
 //   int2   set_meta[S]          {program length, class of the first statically failing edge}
 //   int4   set_prog[E]          per sync edge, base starts folded in (written per batch), in
@@ -138,6 +140,50 @@ inline FrameTable frame_table_view(void* base, FrameTableShape s) {
     return t;
 }
 
+// Frames relative to the frame of a frame-specialised kernel (delta verification). The
+// lane inequalities of a frame are one edge per placed operation a, from a to its lane
+// successor (succ), and its sync inequalities are its set's program; the generated code
+// records, per candidate, which of the specialised frame's edges are violated (one bit per
+// operation, one per program edge). For another frame f the lane (sync) check fails iff a
+// violated edge is among those f shares with that frame (keep) or one of f's own edges is
+// violated (prog, at most kDeltaMax of each kind, in the set_prog format: a lane edge a -> b
+// is {a_row | b_row << 16, x_row | d << 17, w0, w1} with x_row b's prologue row and d = 0,
+// or for the wrap to the lane's first operation b's offset row and d = 1).
+//   int4     header[F]                    {kind, added lane edges, added sync edges, 0}
+//   uint32   keep[F][lane_words + sync_words]
+//   int4     prog[F][2 * kDeltaMax]       added lane edges, then added sync edges
+constexpr int kDeltaMax = 8;
+constexpr int kDeltaSame = 0;     // the specialised frame itself
+constexpr int kDeltaEdges = 1;    // keep masks and added edges describe the frame
+constexpr int kDeltaGeneric = 2;  // too different: the frame-table path verifies it
+
+struct DeltaTable {
+    int4* header;
+    unsigned* keep;
+    int4* prog;
+    int lane_words, sync_words;
+};
+
+inline size_t delta_table_bytes(int frames, int lane_words, int sync_words) {
+    const size_t F = static_cast<size_t>(frames);
+    return round16(sizeof(int4) * F) + round16(sizeof(unsigned) * F * (lane_words + sync_words)) +
+           sizeof(int4) * F * 2 * kDeltaMax;
+}
+
+inline DeltaTable delta_table_view(void* base, int frames, int lane_words, int sync_words) {
+    const size_t F = static_cast<size_t>(frames);
+    DeltaTable t;
+    char* p = static_cast<char*>(base);
+    t.header = reinterpret_cast<int4*>(p);
+    p += round16(sizeof(int4) * F);
+    t.keep = reinterpret_cast<unsigned*>(p);
+    p += round16(sizeof(unsigned) * F * (lane_words + sync_words));
+    t.prog = reinterpret_cast<int4*>(p);
+    t.lane_words = lane_words;
+    t.sync_words = sync_words;
+    return t;
+}
+
 struct DevPeriodic {
     long long n;
     long long stride;
@@ -190,6 +236,10 @@ cudaError_t launch_verify_rows(const DevProblem& p, const DevFrames& f, FrameTab
                                cudaStream_t stream);
 
 // Shared-memory footprint checks used by the host before launching.
+cudaError_t launch_delta_frames(const DevProblem& p, const DevFrames& f, FrameTable t, int spec_frame,
+                                const int* base_prologue, const int* base_offset, DeltaTable d, int sm_count,
+                                cudaStream_t stream);
+
 size_t analyze_smem_bytes(int n_ops, int lanes);
 int periodic_tile(int n_ops);
 size_t periodic_smem_bytes(const DevProblem& p, int tile);

@@ -153,6 +153,10 @@ struct Shape {
 };
 constexpr Shape kShapes[] = {{2, 1}, {1, 1}};
 
+// Ring kernel: consumer warps per CTA (one CTA per SM) and the fewest slots it runs with.
+constexpr int kRingWarpsDefault = 31;
+constexpr int kRingMinSlots = 3;
+
 struct FrameInput {
     int N = 0, I = 0;
     std::vector<std::vector<int>> lanes;  // operations of each lane in program order
@@ -174,9 +178,26 @@ class Gen {
 
 std::string I2S(long long v) { return std::to_string(v); }
 
-std::string generate(const FrameInput& in, const int* issue, const int* lat, int body_rows, Shape shape) {
+// Words of the violation masks of delta verification: one bit per operation (its lane
+// edge) and one per sync program edge; larger bodies keep the minimum form.
+constexpr int kDeltaMaxWords = 4;
+int mask_words(int bits) { return std::max(1, (bits + 31) / 32); }
+
+// ring_warps > 0: the ring kernel (tfv_spec_ring) with that many consumer warps; else the
+// tiles kernel (tfv_spec_kernel) of `shape`. delta: the generated code records which of the
+// frame's lane and sync edges are violated (bit masks, eval_masks), so that every frame a
+// DeltaTable describes by edges runs it; otherwise it computes the smallest slacks (eval)
+// and only the frame's own candidates run it.
+std::string generate(const FrameInput& in, const int* issue, const int* lat, int body_rows, Shape shape,
+                     int ring_warps, bool delta) {
     const int N = in.N;
+    const int lane_words = mask_words(N), sync_words = mask_words(static_cast<int>(in.ea.size()));
     Gen g;
+    // delta: OR the sign of slack `t` (an expression) into bit k of mask `m`
+    const auto flag = [&](const std::string& m, int k, const std::string& t) {
+        g.line("{ const int t = " + t + "; " + m + I2S(k / 32) + " |= static_cast<unsigned>(t >> 31) & " +
+               I2S(1u << (k % 32)) + "u; }");
+    };
     const auto bp = [](int k) { return "bp[" + I2S(k) + "]"; };
     const auto bo = [](int k) { return "bo[" + I2S(k) + "]"; };
     const auto P = [](int k) { return "p" + I2S(k); };
@@ -186,7 +207,12 @@ std::string generate(const FrameInput& in, const int* issue, const int* lat, int
     // feed the start/completion extremes and the lane inequalities with its predecessor;
     // the inequalities without II go to l0, the wraps (+ ii) to l1.
     g.line("int mnp = INT_MAX, mno = INT_MAX, mxp = INT_MIN, mxo = INT_MIN;");
-    g.line("int l0 = INT_MAX, l1 = INT_MAX;");
+    if (delta) {
+        for (int w = 0; w < lane_words; ++w) g.line("unsigned lm" + I2S(w) + " = 0;");
+        for (int w = 0; w < sync_words; ++w) g.line("unsigned sm" + I2S(w) + " = 0;");
+    } else {
+        g.line("int l0 = INT_MAX, l1 = INT_MAX;");
+    }
     std::vector<char> seen(N, 0);
     auto load = [&](int k) {
         g.line("const int " + P(k) + " = P[" + I2S(k * tfv::kTmaTile) + "];");
@@ -206,26 +232,38 @@ std::string generate(const FrameInput& in, const int* issue, const int* lat, int
             load(b);
             if (q == 0) continue;
             const int a = lane[q - 1];
-            g.line("l0 = min(l0, " + P(b) + " - " + P(a) + " + " +
-                   C(g.constant(bp(b) + " - " + bp(a) + " - " + I2S(issue[a]))) + ");");
-            if (body_rows >= 1)
-                g.line("l0 = min(l0, " + O(b) + " - " + O(a) + " + " +
-                       C(g.constant(bo(b) + " - " + bo(a) + " - " + I2S(issue[a]))) + ");");
+            const std::string t0 = P(b) + " - " + P(a) + " + " +
+                                   C(g.constant(bp(b) + " - " + bp(a) + " - " + I2S(issue[a])));
+            const std::string t1 = body_rows >= 1 ? O(b) + " - " + O(a) + " + " +
+                                                        C(g.constant(bo(b) + " - " + bo(a) + " - " + I2S(issue[a])))
+                                                  : std::string();
+            if (delta) {  // the edge keyed by a: a -> b in the same iteration
+                flag("lm", a, body_rows >= 1 ? "min(" + t0 + ", " + t1 + ")" : t0);
+            } else {
+                g.line("l0 = min(l0, " + t0 + ");");
+                if (body_rows >= 1) g.line("l0 = min(l0, " + t1 + ");");
+            }
         }
         if (!lane.empty() && body_rows >= 1) {
             const int f = lane.front(), l = lane.back();
-            g.line("l1 = min(l1, " + O(f) + " - " + P(l) + " + " +
-                   C(g.constant(bo(f) + " - " + bp(l) + " - " + I2S(issue[l]))) + ");");
-            if (body_rows >= 2)
-                g.line("l1 = min(l1, " + O(f) + " - " + O(l) + " + " +
-                       C(g.constant(bo(f) + " - " + bo(l) + " - " + I2S(issue[l]))) + ");");
+            const std::string t0 = O(f) + " - " + P(l) + " + " +
+                                   C(g.constant(bo(f) + " - " + bp(l) + " - " + I2S(issue[l])));
+            const std::string t1 = body_rows >= 2 ? O(f) + " - " + O(l) + " + " +
+                                                        C(g.constant(bo(f) + " - " + bo(l) + " - " + I2S(issue[l])))
+                                                  : std::string();
+            if (delta) {  // the edge keyed by l: the wrap to the lane's first operation, + ii
+                flag("lm", l, (body_rows >= 2 ? "min(" + t0 + ", " + t1 + ")" : t0) + " + ii");
+            } else {
+                g.line("l1 = min(l1, " + t0 + ");");
+                if (body_rows >= 2) g.line("l1 = min(l1, " + t1 + ");");
+            }
             wraps = true;
         }
     }
     for (int k = 0; k < N; ++k)
         if (!seen[k]) load(k);  // operations in no lane still count for the extremes
     g.line("x.min_p = mnp; x.max_pl = mxp; x.min_o = mno; x.max_ol = mxo;");
-    g.line(wraps ? "lane_min = min(l0, l1 + ii);" : "lane_min = l0;");
+    if (!delta) g.line(wraps ? "lane_min = min(l0, l1 + ii);" : "lane_min = l0;");
     // Sync inequalities (verify.py:284-292), grouped by distance d and shifted by d * ii at
     // the end. Values are read again here through volatile loads, so that the walk's
     // registers need not live until their last use (the edges run in source order, one
@@ -233,7 +271,9 @@ std::string generate(const FrameInput& in, const int* issue, const int* lat, int
     std::vector<int> dists;
     for (int d : in.ed)
         if (std::find(dists.begin(), dists.end(), d) == dists.end()) dists.push_back(d);
-    for (int d : dists) g.line("int s" + I2S(d) + " = INT_MAX;");
+    for (int d : dists)
+        g.line(delta ? (d ? "const int dii" + I2S(d) + " = " + I2S(d) + " * ii;" : std::string())
+                     : "int s" + I2S(d) + " = INT_MAX;");
     const auto VP = [](int k) { return "VP[" + I2S(k * tfv::kTmaTile) + "]"; };
     const auto VO = [](int k) { return "VO[" + I2S(k * tfv::kTmaTile) + "]"; };
     int run = -1, run_id = 0;
@@ -250,16 +290,28 @@ std::string generate(const FrameInput& in, const int* issue, const int* lat, int
         g.line("{");
         if (d == 0) g.line("    const int xb = " + VP(b) + ";");
         if (d != 0 || body) g.line("    const int ob = " + VO(b) + ";");
-        g.line("    " + s + " = min(" + s + ", " + (d == 0 ? "xb" : "ob") + " - " + pa + " + " +
-               C(g.constant((d == 0 ? bp(b) : bo(b)) + " - " + bp(a) + " - " + I2S(lat[a]))) + ");");
-        if (body)
-            g.line("    " + s + " = min(" + s + ", ob - " + oa + " + " +
-                   C(g.constant(bo(b) + " - " + bo(a) + " - " + I2S(lat[a]))) + ");");
+        const std::string t0 = std::string(d == 0 ? "xb" : "ob") + " - " + pa + " + " +
+                               C(g.constant((d == 0 ? bp(b) : bo(b)) + " - " + bp(a) + " - " + I2S(lat[a])));
+        const std::string t1 =
+            body ? "ob - " + oa + " + " + C(g.constant(bo(b) + " - " + bo(a) + " - " + I2S(lat[a]))) : std::string();
+        if (delta) {  // program edge e: its bit
+            const std::string t = body ? "min(" + t0 + ", " + t1 + ")" : t0;
+            flag("sm", static_cast<int>(e), d ? t + " + dii" + I2S(d) : t);
+        } else {
+            g.line("    " + s + " = min(" + s + ", " + t0 + ");");
+            if (body) g.line("    " + s + " = min(" + s + ", " + t1 + ");");
+        }
         g.line("}");
     }
-    std::string sync = "INT_MAX";
-    for (int d : dists) sync = "min(" + sync + ", s" + I2S(d) + (d ? " + " + I2S(d) + " * ii" : std::string()) + ")";
-    g.line("sync_min = " + sync + ";");
+    if (delta) {
+        for (int w = 0; w < lane_words; ++w) g.line("lm[" + I2S(w) + "] = lm" + I2S(w) + ";");
+        for (int w = 0; w < sync_words; ++w) g.line("sm[" + I2S(w) + "] = sm" + I2S(w) + ";");
+    } else {
+        std::string sync = "INT_MAX";
+        for (int d : dists)
+            sync = "min(" + sync + ", s" + I2S(d) + (d ? " + " + I2S(d) + " * ii" : std::string()) + ")";
+        g.line("sync_min = " + sync + ";");
+    }
 
     std::string src;
     src += "// Generated by tfv_jit.cu for one frame.\n";
@@ -273,10 +325,21 @@ std::string generate(const FrameInput& in, const int* issue, const int* lat, int
     src += "#include \"tfv_periodic_tma.cuh\"\n";
     src += "__constant__ int tfv_spec_c[" + I2S(std::max(1, g.n_consts)) + "];\n";
     src += "struct Spec {\n    static constexpr bool kEnabled = true;\n";
+    src += std::string("    static constexpr bool kDelta = ") + (delta ? "true" : "false") + ";\n";
+    src += "    static constexpr int kLaneWords = " + I2S(lane_words) + ";\n";
+    src += "    static constexpr int kSyncWords = " + I2S(sync_words) + ";\n";
     src += "    static constexpr int kSuper = " + I2S(shape.super) + ";\n";
     src += "    static constexpr int kPasses = " + I2S(shape.passes) + ";\n";
-    src += "    __device__ __forceinline__ static void eval(const char* rp, int ii, tfv::Extremes& x, int& lane_min,\n";
-    src += "                                                int& sync_min) {\n";
+    if (delta) {
+        src += "    __device__ __forceinline__ static void eval(const char*, int, tfv::Extremes&, int&, int&) {}\n";
+        src += "    __device__ __forceinline__ static void eval_masks(const char* rp, int ii, tfv::Extremes& x,\n";
+        src += "                                                      unsigned* lm, unsigned* sm) {\n";
+    } else {
+        src += "    __device__ __forceinline__ static void eval_masks(const char*, int, tfv::Extremes&, unsigned*,\n";
+        src += "                                                      unsigned*) {}\n";
+        src += "    __device__ __forceinline__ static void eval(const char* rp, int ii, tfv::Extremes& x, int& lane_min,\n";
+        src += "                                                int& sync_min) {\n";
+    }
     src += "        const int16_t* P = reinterpret_cast<const int16_t*>(rp);\n";
     src += "        const int16_t* O = reinterpret_cast<const int16_t*>(rp + " + I2S(static_cast<long long>(N) * tfv::kTmaRowBytes) + ");\n";
     src += "        const volatile int16_t* VP = P;\n";
@@ -288,11 +351,23 @@ std::string generate(const FrameInput& in, const int* issue, const int* lat, int
     src += "    if (threadIdx.x != 0 || blockIdx.x != 0) return;\n";
     src += g.consts;
     src += "}\n";
+    if (ring_warps > 0) {
+        src += "extern \"C\" __global__ void __launch_bounds__(" + I2S(32 * (ring_warps + 1)) + ", 1) tfv_spec_ring(\n";
+        src += "    tfv::DevProblem p, tfv::DevFrames fr, tfv::FrameTable ft, tfv::DevPeriodic b, tfv::DevResults out, int n_tiles,\n";
+        src += "    const __grid_constant__ CUtensorMap map_p, const __grid_constant__ CUtensorMap map_o, int spec_frame,\n";
+        src += "    tfv::DeltaTable dt, int slots) {\n";
+        src += "    tfv::tma_ring_body<" + I2S(body_rows) + ", Spec, " + I2S(ring_warps) +
+               ">(p, fr, ft, b, out, n_tiles, &map_p, &map_o, spec_frame, dt, slots);\n";
+        src += "}\n";
+        return src;
+    }
     src += "extern \"C\" __global__ void __launch_bounds__(" + I2S(tfv::kTmaTile * shape.super / shape.passes) +
            ") tfv_spec_kernel(\n";
     src += "    tfv::DevProblem p, tfv::DevFrames fr, tfv::FrameTable ft, tfv::DevPeriodic b, tfv::DevResults out, int n_tiles,\n";
-    src += "    const __grid_constant__ CUtensorMap map_p, const __grid_constant__ CUtensorMap map_o, int spec_frame) {\n";
-    src += "    tfv::tma_verify_body<" + I2S(body_rows) + ", false, Spec>(p, fr, ft, b, out, n_tiles, &map_p, &map_o, spec_frame);\n";
+    src += "    const __grid_constant__ CUtensorMap map_p, const __grid_constant__ CUtensorMap map_o, int spec_frame,\n";
+    src += "    tfv::DeltaTable dt) {\n";
+    src += "    tfv::tma_verify_body<" + I2S(body_rows) +
+           ", false, Spec>(p, fr, ft, b, out, n_tiles, &map_p, &map_o, spec_frame, dt);\n";
     src += "}\n";
     return src;
 }
@@ -307,12 +382,18 @@ struct tfv_plan {
     const tfv_problem* problem = nullptr;
     int device = 0;
     int body_rows = 0;
-    int super = 1;   // tiles per CTA iteration
-    int passes = 1;  // candidates per thread and iteration
+    int kernel = TFV_PLAN_TILES;
+    int super = 1;   // tiles per CTA iteration (tiles kernel)
+    int passes = 1;  // candidates per thread and iteration (tiles kernel)
+    int slots = 0;   // ring slots (ring kernel)
+    bool delta = false;  // the generated code serves every frame a DeltaTable describes by edges
+    int lane_words = 0, sync_words = 0;
+    void* delta_buf = nullptr;  // device DeltaTable, grown to the frames of the largest call
+    size_t delta_bytes = 0;
     int threads = 0;
     int n_consts = 0;
     CUmodule module = nullptr;
-    CUfunction kernel = nullptr, consts_kernel = nullptr;
+    CUfunction function = nullptr, consts_kernel = nullptr;
     CUdeviceptr consts_symbol = 0;
     void* consts_scratch = nullptr;  // device buffer the constants kernel writes
     size_t smem = 0;
@@ -365,7 +446,20 @@ int build_input(const tfv_problem* p, const tfv_frames* f, int frame, FrameInput
 extern "C" {
 
 int tfv_plan_create(const tfv_problem* p, const tfv_frames* host_frames, int frame, tfv_plan** out) {
+    return tfv_plan_create_with(p, host_frames, frame, nullptr, out);
+}
+
+int tfv_plan_kernel(const tfv_plan* plan) { return plan ? plan->kernel : -1; }
+
+int tfv_plan_create_with(const tfv_problem* p, const tfv_frames* host_frames, int frame,
+                         const tfv_plan_options* options, tfv_plan** out) {
     if (!p || !out) return tfv_internal_fail(TFV_ERR_INVALID_ARGUMENT, "problem and out must not be NULL");
+    const int want = options ? options->kernel : TFV_PLAN_AUTO;
+    const int ring_warps = options && options->ring_warps ? options->ring_warps : kRingWarpsDefault;
+    if (want != TFV_PLAN_AUTO && want != TFV_PLAN_TILES && want != TFV_PLAN_RING)
+        return tfv_internal_fail(TFV_ERR_INVALID_ARGUMENT, "unknown plan kernel");
+    if (ring_warps < 1 || ring_warps > 31)
+        return tfv_internal_fail(TFV_ERR_INVALID_ARGUMENT, "ring_warps must be 1..31");
     int rc = tfv_internal_check_frames(host_frames);
     if (rc) return rc;
     const tfv::DevProblem& d = *tfv_internal_dev(p);
@@ -389,10 +483,32 @@ int tfv_plan_create(const tfv_problem* p, const tfv_frames* host_frames, int fra
             shape = candidate;
             break;
         }
-    plan->super = shape.super;
-    plan->passes = shape.passes;
-    plan->threads = tfv::kTmaTile * shape.super / shape.passes;
-    plan->source = generate(in, tfv_internal_issue_host(p), tfv_internal_latency_host(p), body_rows, shape);
+    // ring slots that fit beside the fixed part of the ring's shared memory
+    const size_t ring_fixed = tfv::ring_smem_bytes(d, 0, ring_warps);
+    const int slots = ring_fixed >= static_cast<size_t>(optin)
+                          ? 0
+                          : static_cast<int>(std::min<size_t>(tfv::kRingMaxSlots,
+                                                              (static_cast<size_t>(optin) - ring_fixed) /
+                                                                  tfv::ring_slot_bytes(d)));
+    if (want == TFV_PLAN_RING && slots < kRingMinSlots) {
+        delete plan;
+        return tfv_internal_fail(TFV_ERR_UNSUPPORTED, "the ring kernel needs three tile slots in shared memory");
+    }
+    plan->kernel = want == TFV_PLAN_TILES || slots < kRingMinSlots ? TFV_PLAN_TILES : TFV_PLAN_RING;
+    if (plan->kernel == TFV_PLAN_RING) {
+        plan->slots = slots;
+        plan->threads = 32 * (ring_warps + 1);
+    } else {
+        plan->super = shape.super;
+        plan->passes = shape.passes;
+        plan->threads = tfv::kTmaTile * shape.super / shape.passes;
+    }
+    plan->lane_words = mask_words(in.N);
+    plan->sync_words = mask_words(static_cast<int>(in.ea.size()));
+    plan->delta = !(options && options->no_delta) && plan->lane_words <= kDeltaMaxWords &&
+                  plan->sync_words <= kDeltaMaxWords;
+    plan->source = generate(in, tfv_internal_issue_host(p), tfv_internal_latency_host(p), body_rows, shape,
+                            plan->kernel == TFV_PLAN_RING ? ring_warps : 0, plan->delta);
 
     const Nvrtc& nv = nvrtc();
     void* prog = nullptr;
@@ -400,8 +516,8 @@ int tfv_plan_create(const tfv_problem* p, const tfv_frames* host_frames, int fra
         delete plan;
         return tfv_internal_fail(TFV_ERR_UNSUPPORTED, "nvrtcCreateProgram failed");
     }
-    const char* options[] = {"--gpu-architecture=sm_100a", "-default-device", "--std=c++17", "-lineinfo"};
-    const int compiled = nv.compile(prog, 4, options);
+    const char* flags[] = {"--gpu-architecture=sm_100a", "-default-device", "--std=c++17", "-lineinfo"};
+    const int compiled = nv.compile(prog, 4, flags);
     if (compiled != 0) {
         size_t n = 0;
         nv.log_size(prog, &n);
@@ -428,17 +544,19 @@ int tfv_plan_create(const tfv_problem* p, const tfv_frames* host_frames, int fra
     }
     size_t sym_bytes = 0;
     if (drv.load(&plan->module, cubin.data()) != CUDA_SUCCESS ||
-        drv.function(&plan->kernel, plan->module, "tfv_spec_kernel") != CUDA_SUCCESS ||
+        drv.function(&plan->function, plan->module,
+                     plan->kernel == TFV_PLAN_RING ? "tfv_spec_ring" : "tfv_spec_kernel") != CUDA_SUCCESS ||
         drv.function(&plan->consts_kernel, plan->module, "tfv_spec_consts") != CUDA_SUCCESS ||
         drv.global(&plan->consts_symbol, &sym_bytes, plan->module, "tfv_spec_c") != CUDA_SUCCESS) {
         if (plan->module) drv.unload(plan->module);
         delete plan;
         return tfv_internal_fail(TFV_ERR_CUDA, "loading the frame-specialised module failed");
     }
-    plan->smem = tfv::tma_body_smem_bytes(d, plan->super, plan->passes, true);
-    if (drv.set_attribute(plan->kernel, CU_FUNC_ATTRIBUTE_MAX_DYNAMIC_SHARED_SIZE_BYTES, static_cast<int>(plan->smem)) !=
-            CUDA_SUCCESS ||
-        drv.occupancy(&plan->per_sm, plan->kernel, plan->threads, plan->smem) != CUDA_SUCCESS ||
+    plan->smem = plan->kernel == TFV_PLAN_RING ? tfv::ring_smem_bytes(d, plan->slots, ring_warps)
+                                               : tfv::tma_body_smem_bytes(d, plan->super, plan->passes, true);
+    if (drv.set_attribute(plan->function, CU_FUNC_ATTRIBUTE_MAX_DYNAMIC_SHARED_SIZE_BYTES,
+                          static_cast<int>(plan->smem)) != CUDA_SUCCESS ||
+        drv.occupancy(&plan->per_sm, plan->function, plan->threads, plan->smem) != CUDA_SUCCESS ||
         plan->per_sm < 1) {
         drv.unload(plan->module);
         delete plan;
@@ -459,6 +577,7 @@ int tfv_plan_destroy(tfv_plan* plan) {
     if (!plan) return TFV_OK;
     CurrentDevice current(plan->device);
     if (plan->consts_scratch) cudaFree(plan->consts_scratch);
+    if (plan->delta_buf) cudaFree(plan->delta_buf);
     if (plan->module) driver().unload(plan->module);
     delete plan;
     return TFV_OK;
@@ -470,7 +589,9 @@ int tfv_plan_source(const tfv_plan* plan, char* buffer, size_t size) {
     return TFV_OK;
 }
 
-int tfv_verify_periodic_planned(const tfv_plan* plan, const tfv_frames* frames, void* table, size_t table_bytes,
+int tfv_plan_delta(const tfv_plan* plan) { return plan ? (plan->delta ? 1 : 0) : -1; }
+
+int tfv_verify_periodic_planned(tfv_plan* plan, const tfv_frames* frames, void* table, size_t table_bytes,
                                 const tfv_periodic_batch* b, int spec_frame, const tfv_results* r, void* stream) {
     if (!plan || !b || !r) return tfv_internal_fail(TFV_ERR_INVALID_ARGUMENT, "plan, batch and results must not be NULL");
     const tfv_problem* p = plan->problem;
@@ -505,6 +626,23 @@ int tfv_verify_periodic_planned(const tfv_plan* plan, const tfv_frames* frames, 
                    ? tfv_internal_fail(TFV_ERR_UNSUPPORTED, "the batch layout does not allow the TMA-fed kernel")
                    : tfv_internal_cuda_fail(e, "tfv_verify_periodic_planned");
     }
+    // delta verification: every frame relative to spec_frame, after the sync programs
+    tfv::DeltaTable dt{};
+    if (plan->delta) {
+        const size_t need = tfv::delta_table_bytes(frames->n_frames, plan->lane_words, plan->sync_words);
+        if (need > plan->delta_bytes) {
+            if (plan->delta_buf) cudaFree(plan->delta_buf);
+            plan->delta_buf = nullptr;
+            plan->delta_bytes = 0;
+            e = cudaMalloc(&plan->delta_buf, need);
+            if (e != cudaSuccess) return tfv_internal_cuda_fail(e, "tfv_verify_periodic_planned");
+            plan->delta_bytes = need;
+        }
+        dt = tfv::delta_table_view(plan->delta_buf, frames->n_frames, plan->lane_words, plan->sync_words);
+        e = tfv::launch_delta_frames(d, df, view, spec_frame, b->base_prologue, b->base_offset, dt,
+                                     tfv_internal_sm_count(p), s);
+        if (e != cudaSuccess) return tfv_internal_cuda_fail(e, "tfv_verify_periodic_planned");
+    }
     const Driver& drv = driver();
     // constants of this batch's base starts -> the module's constant bank
     const int* bp = b->base_prologue;
@@ -516,14 +654,15 @@ int tfv_verify_periodic_planned(const tfv_plan* plan, const tfv_frames* frames, 
         cr = drv.copy(plan->consts_symbol, reinterpret_cast<CUdeviceptr>(plan->consts_scratch),
                       sizeof(int) * static_cast<size_t>(plan->n_consts), reinterpret_cast<CUstream>(s));
     const long long tiles = (db.n + tfv::kTmaTile - 1) / tfv::kTmaTile;
-    const long long supers = (tiles + plan->super - 1) / plan->super;
+    const long long supers = (tiles + plan->super - 1) / plan->super;  // the ring takes one tile at a time
     const long long cap = static_cast<long long>(tfv_internal_sm_count(p)) * plan->per_sm;
     const int grid = static_cast<int>(supers < cap ? supers : cap);
     int n_tiles = static_cast<int>(tiles);
+    int slots = plan->slots;
     tfv::DevProblem dp = d;
-    void* args[] = {&dp, &df, &view, &db, &dr, &n_tiles, &map_p, &map_o, &spec_frame};
+    void* args[] = {&dp, &df, &view, &db, &dr, &n_tiles, &map_p, &map_o, &spec_frame, &dt, &slots};
     if (cr == CUDA_SUCCESS)
-        cr = drv.launch(plan->kernel, grid, 1, 1, plan->threads, 1, 1, static_cast<unsigned>(plan->smem),
+        cr = drv.launch(plan->function, grid, 1, 1, plan->threads, 1, 1, static_cast<unsigned>(plan->smem),
                         reinterpret_cast<CUstream>(s), args, nullptr);
     if (cr != CUDA_SUCCESS) return tfv_internal_fail(TFV_ERR_CUDA, "launching the frame-specialised kernel failed");
     return TFV_OK;

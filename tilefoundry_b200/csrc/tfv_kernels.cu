@@ -194,14 +194,15 @@ __global__ void __launch_bounds__(32) analyze_frames_kernel(DevProblem p, DevFra
         // Lane-major walk order: slot[] lists the placed operations lane by lane; the
         // operations in no lane follow as pseudo-lane 15. Bad frames walk in index order.
         const int placed = bad ? 0 : first[15];
-        uint16_t* order = ft.order + static_cast<size_t>(f) * N;
-        for (int j = lane; j < placed; j += 32) order[j] = static_cast<uint16_t>(slot[j]);
+        uint16_t* order = ft.order + f;  // stride F: position-major
+        const size_t F = static_cast<size_t>(fr.n_frames);
+        for (int j = lane; j < placed; j += 32) order[j * F] = static_cast<uint16_t>(slot[j]);
         int tail = placed;
         for (int a0 = 0; a0 < N; a0 += 32) {
             const int a = a0 + lane;
             const bool loose = a < N && (bad || lane_of(lp[a]) == TFV_LANE_ABSENT);
             const unsigned m = __ballot_sync(kFull, loose);
-            if (loose) order[tail + __popc(m & ((1u << lane) - 1))] = static_cast<uint16_t>(a);
+            if (loose) order[(tail + __popc(m & ((1u << lane) - 1))) * F] = static_cast<uint16_t>(a);
             tail += __popc(m);
         }
         if (lane < 16) {
@@ -491,6 +492,126 @@ __global__ void __launch_bounds__(32) compile_sync_programs_kernel(DevProblem p,
         }
         if (lane == 0) ft.set_meta[s] = make_int2(stop - e0, tail);
     }
+}
+
+// ---------------------------------------------------------------------------------------
+// Frames relative to the specialised frame m (delta verification, see DeltaTable)
+// ---------------------------------------------------------------------------------------
+
+// One warp per frame f, after the analysis and the per-batch sync programs. Lane edges are
+// compared by successor: f keeps m's edge from a iff succ[f][a] == succ[m][a] (the same
+// target and the same wrap flag); every other successor of f is an added edge, with the
+// batch's base starts and a's issue duration folded in (verify.py:99-112, 278-282; for
+// I == 1 the wraps have no instance and are left out). Sync edges are compared as (a, b, d)
+// triples of the two programs (edges before each set's first static failure); f's edges
+// absent from m's program are added as their set_prog entries. Frames with a structural
+// class need no lane or sync answer; frames with more than kDeltaMax added edges of a kind
+// are left to the frame-table path.
+__global__ void __launch_bounds__(128) delta_frames_kernel(DevProblem p, DevFrames fr, FrameTable ft, int m,
+                                                           const int* base_prologue, const int* base_offset,
+                                                           DeltaTable dt) {
+    const int N = p.n_ops, I = p.iterations;
+    const int lane = threadIdx.x & 31;
+    const int warps = blockDim.x >> 5;
+    const int KW = dt.lane_words + dt.sync_words;
+    // m must be a well-formed frame whose edges fit the masks; otherwise every frame takes
+    // the frame-table path
+    const bool m_frame = m >= 0 && m < fr.n_frames;
+    const int s_m = m_frame ? fr.sync_set[m] : -1;
+    const bool m_ok = m_frame && ft.frame_class[m] == 0 && s_m >= 0 && s_m < fr.n_sync_sets &&
+                      ft.set_meta[s_m].x <= 32 * dt.sync_words && N <= 32 * dt.lane_words;
+    const int len_m = m_ok ? ft.set_meta[s_m].x : 0;
+    const int off_m = m_ok ? fr.sync_offsets[s_m] : 0;
+    for (int f = blockIdx.x * warps + (threadIdx.x >> 5); f < fr.n_frames; f += gridDim.x * warps) {
+        unsigned* keep = dt.keep + static_cast<size_t>(f) * KW;
+        int4* prog = dt.prog + static_cast<size_t>(f) * 2 * kDeltaMax;
+        if (!m_ok) {
+            if (lane == 0) dt.header[f] = make_int4(kDeltaGeneric, 0, 0, 0);
+            continue;
+        }
+        if (f == m || ft.frame_class[f] != 0) {  // itself, or no lane/sync answer needed
+            for (int w = lane; w < KW; w += 32) keep[w] = 0xFFFFFFFFu;
+            if (lane == 0) dt.header[f] = make_int4(f == m ? kDeltaSame : kDeltaEdges, 0, 0, 0);
+            continue;
+        }
+        // lane edges
+        int n_lane = 0;
+        for (int w = 0; w < dt.lane_words; ++w) {
+            const int a = w * 32 + lane;
+            const int sf = a < N ? ft.succ[static_cast<size_t>(f) * N + a] : 0;
+            const int sm = a < N ? ft.succ[static_cast<size_t>(m) * N + a] : 0;
+            const bool kept = a < N && sf == sm;
+            const bool wrap = (sf & kWrap) != 0;
+            const bool add = a < N && !kept && sf >= 0 && !(wrap && I < 2);
+            const unsigned kept_bits = __ballot_sync(kFull, kept);
+            const unsigned add_bits = __ballot_sync(kFull, add);
+            if (lane == 0) keep[w] = kept_bits;
+            const int pos = n_lane + __popc(add_bits & ((1u << lane) - 1));
+            if (add && pos < kDeltaMax) {
+                const int b = sf & kSuccMask;
+                const int a_row = a * kTmaRowBytes, b_row = b * kTmaRowBytes;
+                const int issue = p.issue[a];
+                int4 e;
+                if (!wrap)
+                    e = make_int4(a_row | (b_row << 16), b_row, base_prologue[b] - base_prologue[a] - issue,
+                                  I >= 2 ? base_offset[b] - base_offset[a] - issue : kNoBodyWeight);
+                else
+                    e = make_int4(a_row | (b_row << 16), (N * kTmaRowBytes + b_row) | (1 << 17),
+                                  base_offset[b] - base_prologue[a] - issue,
+                                  I >= 3 ? base_offset[b] - base_offset[a] - issue : kNoBodyWeight);
+                prog[pos] = e;
+            }
+            n_lane += __popc(add_bits);
+        }
+        // sync edges
+        int n_sync = 0;
+        const int s_f = fr.sync_set[f];
+        unsigned* skeep = keep + dt.lane_words;
+        if (s_f == s_m) {
+            for (int w = lane; w < dt.sync_words; w += 32) skeep[w] = 0xFFFFFFFFu;
+        } else {
+            const int len_f = ft.set_meta[s_f].x;
+            const int off_f = fr.sync_offsets[s_f];
+            const int* E = fr.sync_edges;
+            for (int w = 0; w < dt.sync_words; ++w) {  // m's edges that f's program has too
+                const int e = w * 32 + lane;
+                bool kept = false;
+                if (e < len_m) {
+                    const int a = E[3 * (off_m + e)], b = E[3 * (off_m + e) + 1], d = E[3 * (off_m + e) + 2];
+                    for (int j = 0; j < len_f && !kept; ++j)
+                        kept = E[3 * (off_f + j)] == a && E[3 * (off_f + j) + 1] == b && E[3 * (off_f + j) + 2] == d;
+                }
+                const unsigned bits = __ballot_sync(kFull, kept);
+                if (lane == 0) skeep[w] = bits;
+            }
+            for (int j0 = 0; j0 < len_f; j0 += 32) {  // f's edges that m's program lacks
+                const int j = j0 + lane;
+                bool add = false;
+                if (j < len_f) {
+                    const int a = E[3 * (off_f + j)], b = E[3 * (off_f + j) + 1], d = E[3 * (off_f + j) + 2];
+                    add = true;
+                    for (int e = 0; e < len_m && add; ++e)
+                        add = !(E[3 * (off_m + e)] == a && E[3 * (off_m + e) + 1] == b && E[3 * (off_m + e) + 2] == d);
+                }
+                const unsigned bits = __ballot_sync(kFull, add);
+                const int pos = n_sync + __popc(bits & ((1u << lane) - 1));
+                if (add && pos < kDeltaMax) prog[kDeltaMax + pos] = ft.set_prog[off_f + j];
+                n_sync += __popc(bits);
+            }
+        }
+        if (lane == 0)
+            dt.header[f] = make_int4(n_lane > kDeltaMax || n_sync > kDeltaMax ? kDeltaGeneric : kDeltaEdges,
+                                     min(n_lane, kDeltaMax), min(n_sync, kDeltaMax), 0);
+    }
+}
+
+cudaError_t launch_delta_frames(const DevProblem& p, const DevFrames& f, FrameTable t, int spec_frame,
+                                const int* base_prologue, const int* base_offset, DeltaTable d, int sm_count,
+                                cudaStream_t stream) {
+    if (f.n_frames <= 0) return cudaSuccess;
+    const int grid = min((f.n_frames + 3) / 4, sm_count * 8);
+    delta_frames_kernel<<<grid, 128, 0, stream>>>(p, f, t, spec_frame, base_prologue, base_offset, d);
+    return cudaGetLastError();
 }
 
 cudaError_t launch_compile_sync_programs(const DevProblem& p, const DevFrames& f, FrameTable t, const int* base_prologue,

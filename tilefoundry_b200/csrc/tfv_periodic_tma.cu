@@ -19,7 +19,7 @@ __global__ void __launch_bounds__(kTile) verify_periodic_tma_kernel(DevProblem p
                                                                      DevPeriodic b, DevResults out, int n_tiles,
                                                                      const __grid_constant__ CUtensorMap map_p,
                                                                      const __grid_constant__ CUtensorMap map_o) {
-    tma_verify_body<kBodyRows, kSweep, NoSpec>(p, fr, ft, b, out, n_tiles, &map_p, &map_o, -1);
+    tma_verify_body<kBodyRows, kSweep, NoSpec>(p, fr, ft, b, out, n_tiles, &map_p, &map_o, -1, DeltaTable{});
 }
 
 }  // namespace

@@ -117,6 +117,16 @@ class FramePlan:
         self.handle = handle
         self.key = key
 
+    @property
+    def kernel(self) -> str:
+        """The kernel the plan was built with: ``"ring"`` or ``"tiles"``."""
+        return "ring" if self._lib.tfv_plan_kernel(self.handle) == _lib.PLAN_RING else "tiles"
+
+    @property
+    def delta(self) -> bool:
+        """Whether frames other than the plan's run its generated code (delta verification)."""
+        return self._lib.tfv_plan_delta(self.handle) == 1
+
     def source(self) -> str:
         """The generated CUDA source."""
         buf = ctypes.create_string_buffer(1 << 22)
@@ -218,16 +228,29 @@ class WarpgroupVerifier:
         verdict, makespan, ii = out
         return out, _lib.Results(verdict.data_ptr(), makespan.data_ptr(), ii.data_ptr())
 
-    def plan(self, frames: FrameSet, frame: int) -> "FramePlan":
-        """A frame-specialised kernel for ``frames``' frame ``frame`` (compiled once per frame content)."""
-        key = frames.frames[frame]
+    def plan(self, frames: FrameSet, frame: int, kernel: str = "auto", ring_warps: int = 0,
+             delta: bool = True) -> "FramePlan":
+        """A frame-specialised kernel for ``frames``' frame ``frame`` (compiled once per frame content).
+
+        ``kernel``: ``"ring"`` (a producer warp and consumer warps over a ring of tile slots),
+        ``"tiles"`` (CTAs verifying whole tiles in lock step) or ``"auto"`` (the ring when it
+        fits in shared memory); ``ring_warps``: the ring's consumer warps (0: the default);
+        ``delta``: let frames that differ from this one by a few edges run the generated code
+        too (where the body is small enough, see ``tfv_plan_delta``).
+        """
+        kinds = {"auto": _lib.PLAN_AUTO, "tiles": _lib.PLAN_TILES, "ring": _lib.PLAN_RING}
+        if kernel not in kinds:
+            raise ValueError(f"unknown plan kernel {kernel!r}")
+        key = (frames.frames[frame], kernel, int(ring_warps), bool(delta))
         found = self._plans.get(key)
         if found is None:
             arrays = frames.arrays()
             struct = _lib.frames_struct(arrays, len(frames))
             handle = ctypes.c_void_p()
-            _lib.check(self._lib.tfv_plan_create(self._handle, ctypes.byref(struct), int(frame), ctypes.byref(handle)),
-                       "tfv_plan_create")
+            options = _lib.PlanOptions(kinds[kernel], int(ring_warps), 0 if delta else 1)
+            _lib.check(self._lib.tfv_plan_create_with(self._handle, ctypes.byref(struct), int(frame),
+                                                      ctypes.byref(options), ctypes.byref(handle)),
+                       "tfv_plan_create_with")
             found = FramePlan(self._lib, handle, key)
             self._plans[key] = found
         return found

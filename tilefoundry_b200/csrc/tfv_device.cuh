@@ -143,13 +143,18 @@ inline FrameTable frame_table_view(void* base, FrameTableShape s) {
 // Frames relative to the frame of a frame-specialised kernel (delta verification). The
 // lane inequalities of a frame are one edge per placed operation a, from a to its lane
 // successor (succ), and its sync inequalities are its set's program; the generated code
-// records, per candidate, which of the specialised frame's edges are violated (one bit per
-// operation, one per program edge). For another frame f the lane (sync) check fails iff a
+// records, per candidate, which of the specialised frame's edges are violated: one bit per
+// operation in the frame's walk order (order[]) and one per program edge, 32 edges a word,
+// edge k of a word with n edges at bit n - 1 - k. For another frame f the lane (sync) check fails iff a
 // violated edge is among those f shares with that frame (keep) or one of f's own edges is
 // violated (prog, at most kDeltaMax of each kind, in the set_prog format: a lane edge a -> b
 // is {a_row | b_row << 16, x_row | d << 17, w0, w1} with x_row b's prologue row and d = 0,
 // or for the wrap to the lane's first operation b's offset row and d = 1).
 //   int4     header[F]                    {kind, added lane edges, added sync edges, 0}
+//   int4     record[F]                    {frame_class, class of the set's first static
+//                                          failure (set_meta.y), register crossing (0/1),
+//                                          first_unreached}: a candidate's frame facts in
+//                                          one load
 //   uint32   keep[F][lane_words + sync_words]
 //   int4     prog[F][2 * kDeltaMax]       added lane edges, then added sync edges
 constexpr int kDeltaMax = 8;
@@ -159,6 +164,7 @@ constexpr int kDeltaGeneric = 2;  // too different: the frame-table path verifie
 
 struct DeltaTable {
     int4* header;
+    int4* record;
     unsigned* keep;
     int4* prog;
     int lane_words, sync_words;
@@ -166,7 +172,7 @@ struct DeltaTable {
 
 inline size_t delta_table_bytes(int frames, int lane_words, int sync_words) {
     const size_t F = static_cast<size_t>(frames);
-    return round16(sizeof(int4) * F) + round16(sizeof(unsigned) * F * (lane_words + sync_words)) +
+    return 2 * round16(sizeof(int4) * F) + round16(sizeof(unsigned) * F * (lane_words + sync_words)) +
            sizeof(int4) * F * 2 * kDeltaMax;
 }
 
@@ -175,6 +181,8 @@ inline DeltaTable delta_table_view(void* base, int frames, int lane_words, int s
     DeltaTable t;
     char* p = static_cast<char*>(base);
     t.header = reinterpret_cast<int4*>(p);
+    p += round16(sizeof(int4) * F);
+    t.record = reinterpret_cast<int4*>(p);
     p += round16(sizeof(int4) * F);
     t.keep = reinterpret_cast<unsigned*>(p);
     p += round16(sizeof(unsigned) * F * (lane_words + sync_words));

@@ -154,7 +154,10 @@ struct Shape {
 constexpr Shape kShapes[] = {{2, 1}, {1, 1}};
 
 // Ring kernel: consumer warps per CTA (one CTA per SM) and the fewest slots it runs with.
-constexpr int kRingWarpsDefault = 31;
+// Measured on the MLA batch (8.4M candidates, random order, delta verification), verify
+// kernel ms for 15/19/21/23/25/27/31 consumer warps: 0.740/0.669/0.665/0.653/0.693/0.709/0.727;
+// 23 warps leave room for registers (up to 80 a thread) and for tiles in flight.
+constexpr int kRingWarpsDefault = 23;
 constexpr int kRingMinSlots = 3;
 
 struct FrameInput {
@@ -193,11 +196,13 @@ std::string generate(const FrameInput& in, const int* issue, const int* lat, int
     const int N = in.N;
     const int lane_words = mask_words(N), sync_words = mask_words(static_cast<int>(in.ea.size()));
     Gen g;
-    // delta: OR the sign of slack `t` (an expression) into bit k of mask `m`
+    // delta: shift the sign of slack `t` (an expression) into mask word k / 32 of `m` (one
+    // SHF); the k-th edge of a word ends at bit n - 1 - k % 32 of the word's n edges
     const auto flag = [&](const std::string& m, int k, const std::string& t) {
-        g.line("{ const int t = " + t + "; " + m + I2S(k / 32) + " |= static_cast<unsigned>(t >> 31) & " +
-               I2S(1u << (k % 32)) + "u; }");
+        const std::string w = m + I2S(k / 32);
+        g.line("{ const int t = " + t + "; " + w + " = __funnelshift_l(static_cast<unsigned>(t), " + w + ", 1); }");
     };
+    int lane_edges = 0;  // lane edges flagged so far: the walk position of the edge's source
     const auto bp = [](int k) { return "bp[" + I2S(k) + "]"; };
     const auto bo = [](int k) { return "bo[" + I2S(k) + "]"; };
     const auto P = [](int k) { return "p" + I2S(k); };
@@ -237,8 +242,8 @@ std::string generate(const FrameInput& in, const int* issue, const int* lat, int
             const std::string t1 = body_rows >= 1 ? O(b) + " - " + O(a) + " + " +
                                                         C(g.constant(bo(b) + " - " + bo(a) + " - " + I2S(issue[a])))
                                                   : std::string();
-            if (delta) {  // the edge keyed by a: a -> b in the same iteration
-                flag("lm", a, body_rows >= 1 ? "min(" + t0 + ", " + t1 + ")" : t0);
+            if (delta) {  // the edge of a (walk position lane_edges): a -> b in the same iteration
+                flag("lm", lane_edges++, body_rows >= 1 ? "min(" + t0 + ", " + t1 + ")" : t0);
             } else {
                 g.line("l0 = min(l0, " + t0 + ");");
                 if (body_rows >= 1) g.line("l0 = min(l0, " + t1 + ");");
@@ -251,13 +256,15 @@ std::string generate(const FrameInput& in, const int* issue, const int* lat, int
             const std::string t1 = body_rows >= 2 ? O(f) + " - " + O(l) + " + " +
                                                         C(g.constant(bo(f) + " - " + bo(l) + " - " + I2S(issue[l])))
                                                   : std::string();
-            if (delta) {  // the edge keyed by l: the wrap to the lane's first operation, + ii
-                flag("lm", l, (body_rows >= 2 ? "min(" + t0 + ", " + t1 + ")" : t0) + " + ii");
+            if (delta) {  // the edge of l: the wrap to the lane's first operation, + ii
+                flag("lm", lane_edges++, (body_rows >= 2 ? "min(" + t0 + ", " + t1 + ")" : t0) + " + ii");
             } else {
                 g.line("l1 = min(l1, " + t0 + ");");
                 if (body_rows >= 2) g.line("l1 = min(l1, " + t1 + ");");
             }
             wraps = true;
+        } else if (!lane.empty() && delta) {  // I == 1: no wrap, the position holds a clear bit
+            flag("lm", lane_edges++, "0");
         }
     }
     for (int k = 0; k < N; ++k)

@@ -507,6 +507,12 @@ __global__ void __launch_bounds__(32) compile_sync_programs_kernel(DevProblem p,
 // absent from m's program are added as their set_prog entries. Frames with a structural
 // class need no lane or sync answer; frames with more than kDeltaMax added edges of a kind
 // are left to the frame-table path.
+// Bit k of `bits` (edge k of a mask word with n edges) moved to bit n - 1 - k: the
+// generated code shifts each edge's flag in from the bottom, so its first edge ends on top.
+__device__ __forceinline__ unsigned shifted_order(unsigned bits, int n) {
+    return n <= 0 ? 0u : __brev(bits) >> (32 - n);
+}
+
 __global__ void __launch_bounds__(128) delta_frames_kernel(DevProblem p, DevFrames fr, FrameTable ft, int m,
                                                            const int* base_prologue, const int* base_offset,
                                                            DeltaTable dt) {
@@ -525,6 +531,12 @@ __global__ void __launch_bounds__(128) delta_frames_kernel(DevProblem p, DevFram
     for (int f = blockIdx.x * warps + (threadIdx.x >> 5); f < fr.n_frames; f += gridDim.x * warps) {
         unsigned* keep = dt.keep + static_cast<size_t>(f) * KW;
         int4* prog = dt.prog + static_cast<size_t>(f) * 2 * kDeltaMax;
+        if (lane == 0) {  // the facts the verification reads per candidate
+            const int set = fr.sync_set[f];
+            const int tail = set >= 0 && set < fr.n_sync_sets ? ft.set_meta[set].y : TFV_CLASS_BAD_PACKING;
+            dt.record[f] = make_int4(ft.frame_class[f], tail, (ft.frame_flags[f] & kFrameRegisterCross) ? 1 : 0,
+                                     ft.first_unreached[f]);
+        }
         if (!m_ok) {
             if (lane == 0) dt.header[f] = make_int4(kDeltaGeneric, 0, 0, 0);
             continue;
@@ -534,18 +546,19 @@ __global__ void __launch_bounds__(128) delta_frames_kernel(DevProblem p, DevFram
             if (lane == 0) dt.header[f] = make_int4(f == m ? kDeltaSame : kDeltaEdges, 0, 0, 0);
             continue;
         }
-        // lane edges
+        // lane edges, by m's walk position j of their source a (the generated code's bit order)
         int n_lane = 0;
         for (int w = 0; w < dt.lane_words; ++w) {
-            const int a = w * 32 + lane;
-            const int sf = a < N ? ft.succ[static_cast<size_t>(f) * N + a] : 0;
-            const int sm = a < N ? ft.succ[static_cast<size_t>(m) * N + a] : 0;
-            const bool kept = a < N && sf == sm;
+            const int j = w * 32 + lane;
+            const int a = j < N ? min(static_cast<int>(ft.order[static_cast<size_t>(j) * fr.n_frames + m]), N - 1) : 0;
+            const int sf = j < N ? ft.succ[static_cast<size_t>(f) * N + a] : 0;
+            const int sm = j < N ? ft.succ[static_cast<size_t>(m) * N + a] : 0;
+            const bool kept = j < N && sf == sm;
             const bool wrap = (sf & kWrap) != 0;
-            const bool add = a < N && !kept && sf >= 0 && !(wrap && I < 2);
+            const bool add = j < N && !kept && sf >= 0 && !(wrap && I < 2);
             const unsigned kept_bits = __ballot_sync(kFull, kept);
             const unsigned add_bits = __ballot_sync(kFull, add);
-            if (lane == 0) keep[w] = kept_bits;
+            if (lane == 0) keep[w] = shifted_order(kept_bits, min(32, N - w * 32));
             const int pos = n_lane + __popc(add_bits & ((1u << lane) - 1));
             if (add && pos < kDeltaMax) {
                 const int b = sf & kSuccMask;
@@ -582,7 +595,7 @@ __global__ void __launch_bounds__(128) delta_frames_kernel(DevProblem p, DevFram
                         kept = E[3 * (off_f + j)] == a && E[3 * (off_f + j) + 1] == b && E[3 * (off_f + j) + 2] == d;
                 }
                 const unsigned bits = __ballot_sync(kFull, kept);
-                if (lane == 0) skeep[w] = bits;
+                if (lane == 0) skeep[w] = shifted_order(bits, min(32, len_m - w * 32));
             }
             for (int j0 = 0; j0 < len_f; j0 += 32) {  // f's edges that m's program lacks
                 const int j = j0 + lane;

@@ -235,7 +235,11 @@ __device__ __forceinline__ void column_verdict(const DevProblem& p, const DevFra
         const int16_t* mo = mp + N * kTile;
         const bool frame_ok = static_cast<unsigned>(f_in) < static_cast<unsigned>(fr.n_frames);
         const int f = frame_ok ? f_in : 0;
-        const int fclass = frame_ok ? ft.frame_class[f] : TFV_CLASS_BAD_PACKING;
+        // the frame's facts: {structural class, static sync class, register crossing, first
+        // unreached relation}, one record with delta verification, else the frame table
+        const bool from_record = Spec::kDelta && spec;
+        const int4 rec = from_record ? dt.record[f] : make_int4(0, 0, 0, 0);
+        const int fclass = from_record ? rec.x : (frame_ok ? ft.frame_class[f] : TFV_CLASS_BAD_PACKING);
         Extremes x{INT_MAX, INT_MAX, INT_MIN, INT_MIN};
         const char* row_p = reinterpret_cast<const char*>(mp);
         const int to_bytes = N * kTmaRowBytes;
@@ -269,9 +273,13 @@ __device__ __forceinline__ void column_verdict(const DevProblem& p, const DevFra
         } else
             lane_min = walk_lanes<kBodyRows>(ft.order + f, fr.n_frames, ft.lane_len + static_cast<size_t>(f) * 16, opc,
                                              row_p, to_bytes, N, ii, x);
-        const int set = fr.sync_set[f];
-        const int2 meta = (static_cast<unsigned>(set) < static_cast<unsigned>(fr.n_sync_sets))
-                              ? ft.set_meta[set] : make_int2(0, TFV_CLASS_BAD_PACKING);
+        int set = 0;
+        int2 meta = make_int2(0, rec.y);
+        if (!from_record) {
+            set = fr.sync_set[f];
+            meta = (static_cast<unsigned>(set) < static_cast<unsigned>(fr.n_sync_sets)) ? ft.set_meta[set]
+                                                                                      : make_int2(0, TFV_CLASS_BAD_PACKING);
+        }
         if (!spec) {
             // Sync edges before the set's first static failure, base starts folded in.
             const int4* prog = ft.set_prog + (meta.x > 0 ? fr.sync_offsets[set] : 0);
@@ -280,7 +288,7 @@ __device__ __forceinline__ void column_verdict(const DevProblem& p, const DevFra
         }
         // First relation without a lane/sync path: timing at instance 0 decides 17 vs 18.
         int rel_cls = 0;
-        const int r = ft.first_unreached[f];
+        const int r = from_record ? rec.w : ft.first_unreached[f];
         if (r >= 0) {
             const int packed = p.relation[r];
             const int a = packed & 0xFFF, bb = (packed >> 12) & 0xFFF, d = packed >> 24;
@@ -316,7 +324,8 @@ __device__ __forceinline__ void column_verdict(const DevProblem& p, const DevFra
         else if (lane_min < 0) cls = TFV_CLASS_LANE_ORDER;
         else if (sync_min < 0) cls = TFV_CLASS_SYNC_INEQUALITY;
         else if (meta.y != 0) cls = meta.y;
-        else if (ft.frame_flags[f] & kFrameRegisterCross) cls = TFV_CLASS_REGISTER_CROSSES_LANES;
+        else if (from_record ? rec.z != 0 : (ft.frame_flags[f] & kFrameRegisterCross) != 0)
+            cls = TFV_CLASS_REGISTER_CROSSES_LANES;
         else if (rel_cls) cls = rel_cls;
         else if (carried_bad) cls = TFV_CLASS_CARRIED_SHARED_LIFETIME;
         else if (p.n_resources == 0) cls = TFV_CLASS_PASS;

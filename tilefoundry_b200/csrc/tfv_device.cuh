@@ -158,6 +158,7 @@ inline FrameTable frame_table_view(void* base, FrameTableShape s) {
 //   uint32   keep[F][lane_words + sync_words]
 //   int4     prog[F][2 * kDeltaMax]       added lane edges, then added sync edges
 constexpr int kDeltaMax = 8;
+constexpr int kDeltaMaxWords = 4;  // mask words of each kind: bodies up to 128 operations / program edges
 constexpr int kDeltaSame = 0;     // the specialised frame itself
 constexpr int kDeltaEdges = 1;    // keep masks and added edges describe the frame
 constexpr int kDeltaGeneric = 2;  // too different: the frame-table path verifies it

@@ -171,9 +171,10 @@ class Gen {
     std::string eval, consts;
     int n_consts = 0;
 
-    // A new constant computed by the constants kernel from bp[], bo[] and immediates.
+    // A new constant computed by the constants kernel from bp[], bo[] and immediates; the
+    // kernel's 32 threads take every 32nd constant each.
     int constant(const std::string& expr) {
-        consts += "    c[" + std::to_string(n_consts) + "] = " + expr + ";\n";
+        consts += "    if (t == " + std::to_string(n_consts % 32) + ") c[" + std::to_string(n_consts) + "] = " + expr + ";\n";
         return n_consts++;
     }
     void line(const std::string& s) { eval += "        " + s + "\n"; }
@@ -183,7 +184,7 @@ std::string I2S(long long v) { return std::to_string(v); }
 
 // Words of the violation masks of delta verification: one bit per operation (its lane
 // edge) and one per sync program edge; larger bodies keep the minimum form.
-constexpr int kDeltaMaxWords = 4;
+using tfv::kDeltaMaxWords;
 int mask_words(int bits) { return std::max(1, (bits + 31) / 32); }
 
 // ring_warps > 0: the ring kernel (tfv_spec_ring) with that many consumer warps; else the
@@ -354,8 +355,13 @@ std::string generate(const FrameInput& in, const int* issue, const int* lat, int
     src += "        (void)O; (void)VP; (void)VO;\n";
     src += g.eval;
     src += "    }\n};\n";
-    src += "extern \"C\" __global__ void tfv_spec_consts(const int* bp, const int* bo, int* c) {\n";
-    src += "    if (threadIdx.x != 0 || blockIdx.x != 0) return;\n";
+    // one warp: the base starts staged in shared memory, then every 32nd constant per thread
+    src += "extern \"C\" __global__ void __launch_bounds__(32) tfv_spec_consts(const int* bp_in, const int* bo_in, int* c) {\n";
+    src += "    __shared__ int bp[" + I2S(N) + "], bo[" + I2S(N) + "];\n";
+    src += "    const int t = threadIdx.x;\n";
+    src += "    if (blockIdx.x != 0) return;\n";
+    src += "    for (int k = t; k < " + I2S(N) + "; k += 32) { bp[k] = bp_in[k]; bo[k] = bo_in[k]; }\n";
+    src += "    __syncwarp();\n";
     src += g.consts;
     src += "}\n";
     if (ring_warps > 0) {

@@ -525,9 +525,20 @@ __global__ void __launch_bounds__(128) delta_frames_kernel(DevProblem p, DevFram
     const bool m_frame = m >= 0 && m < fr.n_frames;
     const int s_m = m_frame ? fr.sync_set[m] : -1;
     const bool m_ok = m_frame && ft.frame_class[m] == 0 && s_m >= 0 && s_m < fr.n_sync_sets &&
-                      ft.set_meta[s_m].x <= 32 * dt.sync_words && N <= 32 * dt.lane_words;
+                      ft.set_meta[s_m].x <= 32 * min(dt.sync_words, kDeltaMaxWords) && N <= 32 * dt.lane_words;
     const int len_m = m_ok ? ft.set_meta[s_m].x : 0;
     const int off_m = m_ok ? fr.sync_offsets[s_m] : 0;
+    // m's program edges as (a, b, d) keys, staged once per block (at most 32 * sync_words)
+    __shared__ unsigned long long mkeys[32 * kDeltaMaxWords];
+    __shared__ unsigned kept_sync[4][kDeltaMaxWords];  // per warp: m's edges found in f's program
+    const auto key = [&](int k) {
+        return static_cast<unsigned long long>(static_cast<unsigned>(fr.sync_edges[3 * k]) & 0xFFFFu) |
+               static_cast<unsigned long long>(static_cast<unsigned>(fr.sync_edges[3 * k + 1]) & 0xFFFFu) << 16 |
+               static_cast<unsigned long long>(static_cast<unsigned>(fr.sync_edges[3 * k + 2])) << 32;
+    };
+    for (int e = threadIdx.x; e < len_m; e += blockDim.x) mkeys[e] = key(off_m + e);
+    __syncthreads();
+    unsigned* kept_w = kept_sync[threadIdx.x >> 5];
     for (int f = blockIdx.x * warps + (threadIdx.x >> 5); f < fr.n_frames; f += gridDim.x * warps) {
         unsigned* keep = dt.keep + static_cast<size_t>(f) * KW;
         int4* prog = dt.prog + static_cast<size_t>(f) * 2 * kDeltaMax;
@@ -585,32 +596,26 @@ __global__ void __launch_bounds__(128) delta_frames_kernel(DevProblem p, DevFram
         } else {
             const int len_f = ft.set_meta[s_f].x;
             const int off_f = fr.sync_offsets[s_f];
-            const int* E = fr.sync_edges;
-            for (int w = 0; w < dt.sync_words; ++w) {  // m's edges that f's program has too
-                const int e = w * 32 + lane;
-                bool kept = false;
-                if (e < len_m) {
-                    const int a = E[3 * (off_m + e)], b = E[3 * (off_m + e) + 1], d = E[3 * (off_m + e) + 2];
-                    for (int j = 0; j < len_f && !kept; ++j)
-                        kept = E[3 * (off_f + j)] == a && E[3 * (off_f + j) + 1] == b && E[3 * (off_f + j) + 2] == d;
-                }
-                const unsigned bits = __ballot_sync(kFull, kept);
-                if (lane == 0) skeep[w] = shifted_order(bits, min(32, len_m - w * 32));
-            }
-            for (int j0 = 0; j0 < len_f; j0 += 32) {  // f's edges that m's program lacks
+            if (lane < kDeltaMaxWords) kept_w[lane] = 0;
+            __syncwarp();
+            // each of f's program edges: the same edge of m's program is kept, none is added
+            for (int j0 = 0; j0 < len_f; j0 += 32) {
                 const int j = j0 + lane;
                 bool add = false;
                 if (j < len_f) {
-                    const int a = E[3 * (off_f + j)], b = E[3 * (off_f + j) + 1], d = E[3 * (off_f + j) + 2];
-                    add = true;
-                    for (int e = 0; e < len_m && add; ++e)
-                        add = !(E[3 * (off_m + e)] == a && E[3 * (off_m + e) + 1] == b && E[3 * (off_m + e) + 2] == d);
+                    const unsigned long long kf = key(off_f + j);
+                    int e = 0;
+                    while (e < len_m && mkeys[e] != kf) ++e;
+                    if (e < len_m) atomicOr(&kept_w[e >> 5], 1u << (e & 31));
+                    add = e == len_m;
                 }
                 const unsigned bits = __ballot_sync(kFull, add);
                 const int pos = n_sync + __popc(bits & ((1u << lane) - 1));
                 if (add && pos < kDeltaMax) prog[kDeltaMax + pos] = ft.set_prog[off_f + j];
                 n_sync += __popc(bits);
             }
+            __syncwarp();
+            for (int w = lane; w < dt.sync_words; w += 32) skeep[w] = shifted_order(kept_w[w], min(32, len_m - w * 32));
         }
         if (lane == 0)
             dt.header[f] = make_int4(n_lane > kDeltaMax || n_sync > kDeltaMax ? kDeltaGeneric : kDeltaEdges,

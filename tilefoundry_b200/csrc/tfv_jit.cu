@@ -7,10 +7,14 @@
 // operations' rows are compile-time offsets into the candidate's tile column, and the
 // batch's base starts, issue durations and latencies are folded into constants held in the
 // module's constant bank, so that each inequality is an add and a minimum. NVRTC compiles
-// the generated code together with the generic kernel body (tfv_periodic_tma.cuh), whose
-// tile permutation hands that frame's candidates to whole warps; the remaining candidates
-// of each tile take the frame-table path. Verdicts are identical: the generated code
-// computes the same extremes and the same signs of every lane and sync slack.
+// the generated code together with a generic kernel body (tfv_periodic_tma.cuh): the ring
+// kernel (a producer warp and consumer warps per SM) or the tiles kernel (CTAs in lock
+// step). With delta verification the generated code records one violation bit per lane and
+// sync edge instead of the smallest slack, and every frame that a per-call comparison
+// (delta_frames_kernel) describes by kept edges and a few added edges runs it as well; the
+// body's tile permutation hands those candidates to whole warps and the rest take the
+// frame-table path. Verdicts are identical: the generated code computes the same extremes
+// and the same signs of every lane and sync slack.
 #include <dlfcn.h>
 
 #include <algorithm>

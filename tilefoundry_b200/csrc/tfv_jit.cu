@@ -413,6 +413,10 @@ struct tfv_plan {
     CUfunction function = nullptr, consts_kernel = nullptr;
     CUdeviceptr consts_symbol = 0;
     void* consts_scratch = nullptr;  // device buffer the constants kernel writes
+    // the constants kernel and its copy run on a side stream, forked from and joined to the
+    // caller's stream, beside the sync-program and frame-comparison kernels
+    cudaStream_t side = nullptr;
+    cudaEvent_t fork = nullptr, join = nullptr;
     size_t smem = 0;
     int per_sm = 0;
     std::string source;
@@ -586,6 +590,13 @@ int tfv_plan_create_with(const tfv_problem* p, const tfv_frames* host_frames, in
         return tfv_internal_cuda_fail(e, "tfv_plan_create");
     }
     plan->n_consts = static_cast<int>(sym_bytes / sizeof(int));
+    e = cudaStreamCreateWithFlags(&plan->side, cudaStreamNonBlocking);
+    if (e == cudaSuccess) e = cudaEventCreateWithFlags(&plan->fork, cudaEventDisableTiming);
+    if (e == cudaSuccess) e = cudaEventCreateWithFlags(&plan->join, cudaEventDisableTiming);
+    if (e != cudaSuccess) {
+        tfv_plan_destroy(plan);
+        return tfv_internal_cuda_fail(e, "tfv_plan_create");
+    }
     *out = plan;
     return TFV_OK;
 }
@@ -593,8 +604,12 @@ int tfv_plan_create_with(const tfv_problem* p, const tfv_frames* host_frames, in
 int tfv_plan_destroy(tfv_plan* plan) {
     if (!plan) return TFV_OK;
     CurrentDevice current(plan->device);
+    if (plan->side) cudaStreamSynchronize(plan->side);
     if (plan->consts_scratch) cudaFree(plan->consts_scratch);
     if (plan->delta_buf) cudaFree(plan->delta_buf);
+    if (plan->fork) cudaEventDestroy(plan->fork);
+    if (plan->join) cudaEventDestroy(plan->join);
+    if (plan->side) cudaStreamDestroy(plan->side);
     if (plan->module) driver().unload(plan->module);
     delete plan;
     return TFV_OK;
@@ -632,17 +647,30 @@ int tfv_verify_periodic_planned(tfv_plan* plan, const tfv_frames* frames, void* 
     tfv::DevFrames df = tfv_internal_to_dev(*frames);
     tfv::FrameTable view = tfv::frame_table_view(table, tfv_internal_shape(p, frames));
     const cudaStream_t s = static_cast<cudaStream_t>(stream);
-    e = tfv::launch_compile_sync_programs(d, df, view, b->base_prologue, b->base_offset, tfv_internal_sm_count(p), s);
     CUtensorMap map_p, map_o;
-    if (e == cudaSuccess && !tfv::periodic_tma_supported(d, db)) e = cudaErrorInvalidValue;
-    if (e == cudaSuccess && (!tfv::make_map(&map_p, db.prologue_delta, db.n, db.stride, d.n_ops) ||
-                             !tfv::make_map(&map_o, db.offset_delta, db.n, db.stride, d.n_ops)))
-        e = cudaErrorInvalidValue;
-    if (e != cudaSuccess) {
-        return e == cudaErrorInvalidValue
-                   ? tfv_internal_fail(TFV_ERR_UNSUPPORTED, "the batch layout does not allow the TMA-fed kernel")
-                   : tfv_internal_cuda_fail(e, "tfv_verify_periodic_planned");
-    }
+    if (!tfv::periodic_tma_supported(d, db) || !tfv::make_map(&map_p, db.prologue_delta, db.n, db.stride, d.n_ops) ||
+        !tfv::make_map(&map_o, db.offset_delta, db.n, db.stride, d.n_ops))
+        return tfv_internal_fail(TFV_ERR_UNSUPPORTED, "the batch layout does not allow the TMA-fed kernel");
+    const Driver& drv = driver();
+    // constants of this batch's base starts -> the module's constant bank, on the side stream
+    // after everything the caller's stream holds so far (an earlier call's kernel included)
+    e = cudaEventRecord(plan->fork, s);
+    if (e == cudaSuccess) e = cudaStreamWaitEvent(plan->side, plan->fork, 0);
+    if (e != cudaSuccess) return tfv_internal_cuda_fail(e, "tfv_verify_periodic_planned");
+    const int* bp = b->base_prologue;
+    const int* bo = b->base_offset;
+    void* cptr = plan->consts_scratch;
+    void* cargs[] = {&bp, &bo, &cptr};
+    CUresult cr =
+        drv.launch(plan->consts_kernel, 1, 1, 1, 32, 1, 1, 0, reinterpret_cast<CUstream>(plan->side), cargs, nullptr);
+    if (cr == CUDA_SUCCESS)
+        cr = drv.copy(plan->consts_symbol, reinterpret_cast<CUdeviceptr>(plan->consts_scratch),
+                      sizeof(int) * static_cast<size_t>(plan->n_consts), reinterpret_cast<CUstream>(plan->side));
+    if (cr != CUDA_SUCCESS) return tfv_internal_fail(TFV_ERR_CUDA, "launching the plan's constants kernel failed");
+    e = cudaEventRecord(plan->join, plan->side);
+    if (e == cudaSuccess)
+        e = tfv::launch_compile_sync_programs(d, df, view, b->base_prologue, b->base_offset, tfv_internal_sm_count(p), s);
+    if (e != cudaSuccess) return tfv_internal_cuda_fail(e, "tfv_verify_periodic_planned");
     // delta verification: every frame relative to spec_frame, after the sync programs
     tfv::DeltaTable dt{};
     if (plan->delta) {
@@ -660,16 +688,8 @@ int tfv_verify_periodic_planned(tfv_plan* plan, const tfv_frames* frames, void* 
                                      tfv_internal_sm_count(p), s);
         if (e != cudaSuccess) return tfv_internal_cuda_fail(e, "tfv_verify_periodic_planned");
     }
-    const Driver& drv = driver();
-    // constants of this batch's base starts -> the module's constant bank
-    const int* bp = b->base_prologue;
-    const int* bo = b->base_offset;
-    void* cptr = plan->consts_scratch;
-    void* cargs[] = {&bp, &bo, &cptr};
-    CUresult cr = drv.launch(plan->consts_kernel, 1, 1, 1, 32, 1, 1, 0, reinterpret_cast<CUstream>(s), cargs, nullptr);
-    if (cr == CUDA_SUCCESS)
-        cr = drv.copy(plan->consts_symbol, reinterpret_cast<CUdeviceptr>(plan->consts_scratch),
-                      sizeof(int) * static_cast<size_t>(plan->n_consts), reinterpret_cast<CUstream>(s));
+    e = cudaStreamWaitEvent(s, plan->join, 0);  // the constants are in place
+    if (e != cudaSuccess) return tfv_internal_cuda_fail(e, "tfv_verify_periodic_planned");
     const long long tiles = (db.n + tfv::kTmaTile - 1) / tfv::kTmaTile;
     const long long supers = (tiles + plan->super - 1) / plan->super;  // the ring takes one tile at a time
     const long long cap = static_cast<long long>(tfv_internal_sm_count(p)) * plan->per_sm;
@@ -678,9 +698,8 @@ int tfv_verify_periodic_planned(tfv_plan* plan, const tfv_frames* frames, void* 
     int slots = plan->slots;
     tfv::DevProblem dp = d;
     void* args[] = {&dp, &df, &view, &db, &dr, &n_tiles, &map_p, &map_o, &spec_frame, &dt, &slots};
-    if (cr == CUDA_SUCCESS)
-        cr = drv.launch(plan->function, grid, 1, 1, plan->threads, 1, 1, static_cast<unsigned>(plan->smem),
-                        reinterpret_cast<CUstream>(s), args, nullptr);
+    cr = drv.launch(plan->function, grid, 1, 1, plan->threads, 1, 1, static_cast<unsigned>(plan->smem),
+                    reinterpret_cast<CUstream>(s), args, nullptr);
     if (cr != CUDA_SUCCESS) return tfv_internal_fail(TFV_ERR_CUDA, "launching the frame-specialised kernel failed");
     return TFV_OK;
 }

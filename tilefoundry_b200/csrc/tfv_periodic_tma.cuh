@@ -703,7 +703,11 @@ __device__ __forceinline__ void tma_ring_body(const DevProblem& p, const DevFram
             int col = q * 32 + lane;
             bool spec = false;
             if constexpr (Spec::kEnabled) {
-                // the tile's columns in position order: the specialised frame's candidates first
+                // The tile's columns in position order: the candidates that run the generated
+                // code first (the specialised frame's and, with delta verification, the frames
+                // described by edges, in column order), then the rest. The delta frames stay
+                // spread over the units: a unit of delta frames alone would take longer than
+                // the others and hold the slot.
                 unsigned m[kRingUnits];
                 int total = 0;
 #pragma unroll
@@ -714,17 +718,21 @@ __device__ __forceinline__ void tma_ring_body(const DevProblem& p, const DevFram
                     total += __popc(m[w]);
                 }
                 const int pos = q * 32 + lane;
-                const bool in_spec = pos < total;
-                int r = in_spec ? pos : pos - total;
-                col = 0;
+                if (total == kTile) {
+                    col = pos;  // every column runs the generated code
+                } else {
+                    const bool in_spec = pos < total;
+                    int r = in_spec ? pos : pos - total;
+                    col = 0;
 #pragma unroll
-                for (int w = 0; w < kRingUnits; ++w) {
-                    const unsigned mw = in_spec ? m[w] : ~m[w];
-                    const int cnt = __popc(mw);
-                    if (r >= 0 && r < cnt) col = w * 32 + select_bit(mw, r);
-                    r -= cnt;
+                    for (int w = 0; w < kRingUnits; ++w) {
+                        const unsigned mw = in_spec ? m[w] : ~m[w];
+                        const int cnt = __popc(mw);
+                        if (r >= 0 && r < cnt) col = w * 32 + select_bit(mw, r);
+                        r -= cnt;
+                    }
                 }
-                spec = q * 32 < (total & ~31);  // whole units of the frame run the generated code
+                spec = q * 32 < (total & ~31);  // whole units run the generated code
             }
             const long long c = first + col;
             const bool live = c < b.n;

@@ -139,3 +139,34 @@ def test_delta_random_problems_plan_of_a_minor_frame(seed):
         generic, planned = _generic_and_planned(verifier, frames, batch, plan, minor)
     for g, p in zip(generic, planned):
         assert np.array_equal(g, p)
+
+
+def test_back_to_back_calls_with_different_bases():
+    """Two planned verifications enqueued on one stream before either result is read, with
+    different base starts: the second call's constants (computed on the plan's side stream)
+    must not reach the constant bank while the first call's kernel runs."""
+    import torch
+
+    problem, packed, witness = _mla()
+    frames, batch, _ = mla_perturbations(packed, witness, 65536, seed=21, producers=shared_producers(problem))
+    top = int(np.argmax(np.bincount(batch.frame, minlength=len(frames))))
+    # the same candidates against bases shifted by 7: every delta moves by -7
+    shifted = PeriodicBatch(batch.base_prologue + 7, batch.base_offset + 7,
+                            (batch.prologue_delta.astype(np.int32) - 7).astype(np.int16),
+                            (batch.offset_delta.astype(np.int32) - 7).astype(np.int16), batch.ii, batch.frame)
+    with WarpgroupVerifier(packed) as verifier:
+        plan = verifier.plan(frames, top)
+        dframes = verifier.frames_to_device(frames)
+        table = verifier.analyze(dframes)
+        first = _device_batch(verifier, batch)
+        second = _device_batch(verifier, shifted)
+        dev = torch.device("cuda", verifier.device)
+        outs = [tuple(torch.empty(batch.n, dtype=torch.int32, device=dev) for _ in range(3)) for _ in range(2)]
+        for _ in range(3):  # both calls in flight together, several times
+            verifier.verify_periodic_device(dframes, table, first, out=outs[0], plan=plan, spec_frame=top)
+            verifier.verify_periodic_device(dframes, table, second, out=outs[1], plan=plan, spec_frame=top)
+        torch.cuda.synchronize(dev)
+        generic = [t.cpu().numpy() for t in verifier.verify_periodic_device(dframes, table, first)]
+    for out in outs:
+        for g, p in zip(generic, (t.cpu().numpy() for t in out)):
+            assert np.array_equal(g, p)

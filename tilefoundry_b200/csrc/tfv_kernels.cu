@@ -524,8 +524,9 @@ __global__ void __launch_bounds__(128) delta_frames_kernel(DevProblem p, DevFram
     // the frame-table path
     const bool m_frame = m >= 0 && m < fr.n_frames;
     const int s_m = m_frame ? fr.sync_set[m] : -1;
-    const bool m_ok = m_frame && ft.frame_class[m] == 0 && s_m >= 0 && s_m < fr.n_sync_sets &&
-                      ft.set_meta[s_m].x <= 32 * min(dt.sync_words, kDeltaMaxWords) && N <= 32 * dt.lane_words;
+    const bool m_ok = m_frame && dt.sync_words <= kDeltaMaxWords && dt.lane_words <= kDeltaMaxWords &&
+                      ft.frame_class[m] == 0 && s_m >= 0 && s_m < fr.n_sync_sets &&
+                      ft.set_meta[s_m].x <= 32 * dt.sync_words && N <= 32 * dt.lane_words;
     const int len_m = m_ok ? ft.set_meta[s_m].x : 0;
     const int off_m = m_ok ? fr.sync_offsets[s_m] : 0;
     // m's program edges as (a, b, d) keys, staged once per block (at most 32 * sync_words)
@@ -628,6 +629,7 @@ cudaError_t launch_delta_frames(const DevProblem& p, const DevFrames& f, FrameTa
                                 cudaStream_t stream) {
     if (f.n_frames <= 0) return cudaSuccess;
     const int grid = min((f.n_frames + 3) / 4, sm_count * 8);
+    // four warps a block: the kernel keeps one row of kept_sync per warp
     delta_frames_kernel<<<grid, 128, 0, stream>>>(p, f, t, spec_frame, base_prologue, base_offset, d);
     return cudaGetLastError();
 }

@@ -580,6 +580,7 @@ __device__ __forceinline__ void tma_ring_body(const DevProblem& p, const DevFram
                                               const DevPeriodic& b, const DevResults& out, int n_tiles,
                                               const CUtensorMap* map_p, const CUtensorMap* map_o, int spec_frame,
                                               const DeltaTable& dt, int slots) {
+    static_assert(kWarps >= 1 && kWarps <= 31, "a producer warp and 1..31 consumer warps per CTA");
     extern __shared__ __align__(128) unsigned char smem[];
     const int N = p.n_ops;
     const int t = threadIdx.x, warp = t >> 5, lane = t & 31;

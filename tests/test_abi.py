@@ -62,6 +62,22 @@ def test_invalid_arguments_are_rejected_before_cuda():
     assert lib.tfv_verify_periodic_host(None, None, None, None) == -1
 
 
+def test_plan_entry_points_reject_null_before_cuda():
+    """The frame-specialised plan entries validate their handles before any CUDA or NVRTC call."""
+    lib = _lib.load()
+    handle = ctypes.c_void_p()
+    options = _lib.PlanOptions(_lib.PLAN_RING, 23, 0)
+    assert lib.tfv_plan_create_with(None, None, 0, ctypes.byref(options), ctypes.byref(handle)) == -1
+    assert lib.tfv_plan_create(None, None, 0, ctypes.byref(handle)) == -1
+    assert lib.tfv_plan_kernel(None) == -1
+    assert lib.tfv_plan_delta(None) == -1
+    assert lib.tfv_plan_destroy(None) == 0
+    buf = ctypes.create_string_buffer(16)
+    assert lib.tfv_plan_source(None, buf, len(buf)) == -1
+    assert lib.tfv_verify_periodic_planned(None, None, None, 0, None, 0, None, None) == -1
+    assert (_lib.PLAN_AUTO, _lib.PLAN_TILES, _lib.PLAN_RING) == (0, 1, 2)
+
+
 @pytest.mark.parametrize(
     "struct,cname",
     [
@@ -70,6 +86,7 @@ def test_invalid_arguments_are_rejected_before_cuda():
         (_lib.PeriodicBatch, "tfv_periodic_batch"),
         (_lib.RowsBatch, "tfv_rows_batch"),
         (_lib.Results, "tfv_results"),
+        (_lib.PlanOptions, "tfv_plan_options"),
     ],
 )
 def test_ctypes_layout_matches_header(tmp_path, struct, cname):

@@ -64,7 +64,7 @@ def _load():
         lib.oracle_classify_batch.restype = None
         lib.oracle_classify_batch.argtypes = [
             ctypes.POINTER(_Problem), ctypes.c_int, _i32p, _i32p, _i32p, _i32p, _i32p, _i32p, _i32p,
-            ctypes.c_longlong, _i32p, _i32p, _i64p, _i64p, _i64p, _i32p,
+            ctypes.c_longlong, _i32p, _i32p, _i64p, _i64p, _i64p, _i32p, ctypes.c_void_p, ctypes.c_void_p,
         ]
         _lib = lib
     return _lib
@@ -154,13 +154,19 @@ class OracleProblem:
         return (as32(lane_count), as32(lane_base), as32(lane_off), as32(lane_ops),
                 as32(sync_base), as32(sync_count), as32(sync_all), np.array(malformed, dtype=bool))
 
-    def _run(self, frame_arrays, frame_idx, pre, start, issue_end, completion, threads):
+    def new_memo(self, n_frames: int):
+        """Per-frame answers of the reachability and acyclicity checks (-1: not asked yet)."""
+        reach = np.full(max(1, n_frames) * max(1, len(self.rel) * self.iterations), -1, dtype=np.int8)
+        return reach, np.full(max(1, n_frames), -1, dtype=np.int8)
+
+    def _run(self, frame_arrays, frame_idx, pre, start, issue_end, completion, threads, memo=None):
         lib = _load()
         n = len(frame_idx)
         verdict = np.zeros(n, dtype=np.int32)
         if n == 0:
             return verdict
         lc, lb, lo, lops, sb, sc, sa, _ = frame_arrays
+        memo_reach, memo_cycle = memo if memo is not None else self.new_memo(len(lc))
         M = self.n * self.iterations
         frame_idx = np.ascontiguousarray(frame_idx, dtype=np.int32)
         pre = np.ascontiguousarray(pre, dtype=np.int32)
@@ -178,7 +184,7 @@ class OracleProblem:
                 ctypes.byref(self._struct), 0, _ptr(lc), _ptr(lb), _ptr(lo), _ptr(lops), _ptr(sb), _ptr(sc), _ptr(sa),
                 e - s, _ptr(frame_idx[s:e]), _ptr(pre[s:e]),
                 _ptr(start[s:e], _i64p), _ptr(issue_end[s:e], _i64p), _ptr(completion[s:e], _i64p),
-                _ptr(verdict[s:e]),
+                _ptr(verdict[s:e]), memo_reach.ctypes.data, memo_cycle.ctypes.data,
             )
 
         with ThreadPoolExecutor(max_workers=threads) as pool:
@@ -229,15 +235,38 @@ class OracleProblem:
         completion = start + self.latency.astype(np.int64)[None, None, :]
         return start, issue_end, completion
 
-    def classify_periodic(self, prologue, offset, ii, frames, frame_idx, threads: int | None = None):
-        """Classify periodic candidates; ``prologue``/``offset`` are [n, N] absolute starts."""
-        start, issue_end, completion = self.materialize(prologue, offset, ii)
-        n = start.shape[0]
-        makespan = completion.reshape(n, -1).max(axis=1)
-        iiv = (start[:, 2, 0] - start[:, 1, 0]) if self.iterations >= 3 else np.zeros(n, dtype=np.int64)
-        frame_arrays = self._frames(frames)
-        malformed_frame = frame_arrays[-1]
+    def classify_periodic(self, prologue, offset, ii, frames, frame_idx, threads: int | None = None,
+                          frame_arrays=None, memo=None):
+        """Classify periodic candidates; ``prologue``/``offset`` are [n, N] absolute starts.
+
+        Candidates are materialised in chunks of about 2^24 rows. ``frame_arrays`` and
+        ``memo`` (see :meth:`prepare_frames`) may be passed to share the frames' answers
+        between calls over the same frames.
+        """
+        prologue = np.asarray(prologue, dtype=np.int64)
+        offset = np.asarray(offset, dtype=np.int64)
+        ii = np.asarray(ii, dtype=np.int64)
         frame_idx = np.asarray(frame_idx, dtype=np.int32)
-        pre = np.where((start.reshape(n, -1) < 0).any(axis=1) | malformed_frame[frame_idx], 1, 0).astype(np.int32)
-        verdict = self._run(frame_arrays, frame_idx, pre, start, issue_end, completion, threads)
+        if frame_arrays is None:
+            frame_arrays, memo = self.prepare_frames(frames)
+        n = prologue.shape[0]
+        verdict = np.zeros(n, dtype=np.int32)
+        makespan = np.zeros(n, dtype=np.int64)
+        iiv = np.zeros(n, dtype=np.int64)
+        chunk = max(1, (1 << 24) // max(1, self.n * self.iterations))
+        for c0 in range(0, n, chunk):
+            sl = slice(c0, min(n, c0 + chunk))
+            start, issue_end, completion = self.materialize(prologue[sl], offset[sl], ii[sl])
+            m = start.shape[0]
+            makespan[sl] = completion.reshape(m, -1).max(axis=1)
+            if self.iterations >= 3:
+                iiv[sl] = start[:, 2, 0] - start[:, 1, 0]
+            pre = np.where((start.reshape(m, -1) < 0).any(axis=1) | frame_arrays[-1][frame_idx[sl]], 1, 0)
+            verdict[sl] = self._run(frame_arrays, frame_idx[sl], pre.astype(np.int32), start, issue_end, completion,
+                                    threads, memo)
         return verdict, makespan, iiv
+
+    def prepare_frames(self, frames):
+        """Flattened frames and a fresh answer memo for :meth:`classify_periodic`."""
+        arrays = self._frames(frames)
+        return arrays, self.new_memo(len(frames))

@@ -15,6 +15,15 @@
  * (verify.py:105-111 and 139-140 add edges from iteration i to i or i + distance >= i).
  * Times are int64, so the oracle has no 2^30 domain limit.
  *
+ * Memoisation. _completion_event_edges (verify.py:122-141) reads the problem and the
+ * schedule's lanes and sync edges, never its times, so every answer of _event_reachable
+ * and of _require_acyclic (verify.py:163-180, whose graph is built from lanes, sync and the
+ * problem's relations) is a function of the candidate's frame (lanes + sync). The batch
+ * driver therefore keeps, per frame, the reachability answer of every (relation, instance)
+ * pair it has asked and the acyclicity result. A missing answer is filled by one search
+ * from completion(i, a) that answers every relation leaving a at instance i (the same
+ * reachable set the reference explores once per query).
+ *
  * Parity pin: tests/test_oracle.py checks this file against oracle/verify_port.py and
  * against the reference verdicts committed under tests/golden/.
  */
@@ -114,29 +123,6 @@ static void free_event_graph(event_graph *g) {
     free(g->off); free(g->dst); free(g->stamp); free(g->stack);
 }
 
-/* _event_reachable (verify.py:144-160): completion(i, a) -> start(j, b). */
-static int event_reachable(const event_graph *g0, int N, int i, int a, int j, int b) {
-    event_graph *g = (event_graph *)g0;
-    const int source = (i * N + a) * 3 + 2, target = (j * N + b) * 3;
-    const int limit = (j + 1) * N * 3; /* events of iterations <= j */
-    int top = 0;
-    g->epoch++;
-    g->stack[top++] = source;
-    g->stamp[source] = g->epoch;
-    while (top) {
-        int v = g->stack[--top];
-        if (v == target) return 1;
-        for (int e = g->off[v]; e < g->off[v + 1]; ++e) {
-            int w = g->dst[e];
-            if (w < limit && g->stamp[w] != g->epoch) {
-                g->stamp[w] = g->epoch;
-                g->stack[top++] = w;
-            }
-        }
-    }
-    return 0;
-}
-
 /* _require_acyclic (verify.py:163-180) over lane, sync and semantic instance edges. */
 static int has_cycle(const oracle_problem *p, const oracle_candidate *c) {
     const int N = p->n, I = p->iters, V = N * I;
@@ -216,7 +202,52 @@ static int resources_fail(const oracle_problem *p, const oracle_candidate *c) {
     return fail;
 }
 
-int oracle_classify(const oracle_problem *p, const oracle_candidate *c) {
+/* Answers of one frame (see the memoisation note at the top): reach[r * I + i] for relation r
+ * at instance i, -1 while unknown; cycle likewise. Threads that share a memo may fill the same
+ * entry concurrently; they write the same value. */
+typedef struct {
+    signed char *reach;
+    signed char *cycle;
+} oracle_memo;
+
+static signed char memo_get(const signed char *at) { return __atomic_load_n(at, __ATOMIC_RELAXED); }
+static void memo_set(signed char *at, signed char v) { __atomic_store_n(at, v, __ATOMIC_RELAXED); }
+
+/* One search from completion(i, a) of relation r's source a, restricted to the iterations up
+ * to the furthest target of a's relations at instance i; records the answer of every relation
+ * leaving a (relations are sorted, so they are one run) at instance i. */
+static void answer_source(const oracle_problem *p, event_graph *g, oracle_memo *memo, int r, int i) {
+    const int N = p->n, I = p->iters, a = p->rel[3 * r];
+    int r0 = r, r1 = r + 1, dmax = 0;
+    while (r0 > 0 && p->rel[3 * (r0 - 1)] == a) --r0;
+    while (r1 < p->n_rel && p->rel[3 * r1] == a) ++r1;
+    for (int k = r0; k < r1; ++k)
+        if (i + p->rel[3 * k + 2] < I && p->rel[3 * k + 2] > dmax) dmax = p->rel[3 * k + 2];
+    const int source = (i * N + a) * 3 + 2;
+    const int limit = (i + dmax + 1) * N * 3; /* events of iterations <= i + dmax */
+    int top = 0;
+    g->epoch++;
+    g->stack[top++] = source;
+    g->stamp[source] = g->epoch;
+    while (top) {
+        int v = g->stack[--top];
+        for (int e = g->off[v]; e < g->off[v + 1]; ++e) {
+            int w = g->dst[e];
+            if (w < limit && g->stamp[w] != g->epoch) {
+                g->stamp[w] = g->epoch;
+                g->stack[top++] = w;
+            }
+        }
+    }
+    for (int k = r0; k < r1; ++k) {
+        const int b = p->rel[3 * k + 1], d = p->rel[3 * k + 2];
+        if (i + d >= I) continue;
+        const int target = ((i + d) * N + b) * 3;
+        memo_set(&memo->reach[(size_t)k * I + i], (signed char)(g->stamp[target] == g->epoch));
+    }
+}
+
+int oracle_classify(const oracle_problem *p, const oracle_candidate *c, oracle_memo *memo) {
     const int N = p->n, I = p->iters;
     if (c->pre_class == 1) return 1;
     if (c->n_lanes != p->lanes) return 2;                                     /* verify.py:211 */
@@ -271,35 +302,52 @@ int oracle_classify(const oracle_problem *p, const oracle_candidate *c) {
     }
     {
         event_graph g;
-        build_event_graph(p, c, lane_of, &g);
+        int built = 0;
         for (int r = 0; r < p->n_rel && !result; ++r) {                       /* verify.py:308-314 */
             int a = p->rel[3 * r], b = p->rel[3 * r + 1], d = p->rel[3 * r + 2];
             for (int i = 0; i + d < I; ++i) {
                 if (c->completion[i * N + a] > c->start[(i + d) * N + b]) { result = 17; break; }
-                if (!event_reachable(&g, N, i, a, i + d, b)) { result = 18; break; }
+                signed char known = memo_get(&memo->reach[(size_t)r * I + i]);
+                if (known < 0) {
+                    if (!built) { build_event_graph(p, c, lane_of, &g); built = 1; }
+                    answer_source(p, &g, memo, r, i);
+                    known = memo_get(&memo->reach[(size_t)r * I + i]);
+                }
+                if (!known) { result = 18; break; }
             }
         }
-        free_event_graph(&g);
+        if (built) free_event_graph(&g);
         if (result) goto done;
     }
     for (int k = 0; k < p->n_car; ++k)                                        /* verify.py:315-318 */
         for (int i = 1; i < I; ++i)
             if (c->completion[i * N + p->car[2 * k]] > c->start[i * N + p->car[2 * k + 1]]) { result = 19; goto done; }
     if (resources_fail(p, c)) { result = 20; goto done; }                    /* verify.py:320 */
-    if (has_cycle(p, c)) { result = 21; goto done; }                         /* verify.py:321-322 */
+    {                                                                         /* verify.py:321-322 */
+        signed char cyclic = memo_get(memo->cycle);
+        if (cyclic < 0) {
+            cyclic = (signed char)has_cycle(p, c);
+            memo_set(memo->cycle, cyclic);
+        }
+        if (cyclic) { result = 21; goto done; }
+    }
 done:
     free(lane_of);
     return result;
 }
 
 /* Batch over candidates sharing one problem. Candidate k uses structure frame[k]
- * (lanes and sync from the frame arrays) and rows at start + k * I * N. */
+ * (lanes and sync from the frame arrays) and rows at start + k * I * N. memo_reach
+ * ([n_frames][R][I]) and memo_cycle ([n_frames]) hold each frame's answers, -1 where unknown;
+ * they may be shared by concurrent calls over the same frames. */
 void oracle_classify_batch(const oracle_problem *p, int n_frames, const int *frame_lane_count,
                            const int *frame_lane_off_base, const int *lane_off_all, const int *lane_ops_all,
                            const int *frame_sync_base, const int *frame_sync_count, const int *sync_all,
                            long long n, const int *frame, const int *pre_class, const i64 *start,
-                           const i64 *issue_end, const i64 *completion, int *verdict) {
+                           const i64 *issue_end, const i64 *completion, int *verdict, signed char *memo_reach,
+                           signed char *memo_cycle) {
     const long long M = (long long)p->n * p->iters;
+    const size_t per_frame = (size_t)p->n_rel * p->iters;
     (void)n_frames;
     for (long long k = 0; k < n; ++k) {
         int f = frame[k];
@@ -313,6 +361,7 @@ void oracle_classify_batch(const oracle_problem *p, int n_frames, const int *fra
         c.start = start + k * M;
         c.issue_end = issue_end + k * M;
         c.completion = completion + k * M;
-        verdict[k] = oracle_classify(p, &c);
+        oracle_memo memo = {memo_reach + (size_t)f * per_frame, memo_cycle + f};
+        verdict[k] = oracle_classify(p, &c, &memo);
     }
 }

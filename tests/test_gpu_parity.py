@@ -286,25 +286,36 @@ def test_resource_capacity_many_windows_match_oracle(seed, n_ops, n_resources, i
     assert 20 in classes or iterations == 1
 
 
-@pytest.mark.parametrize("name,count", [("gemm", 4000), ("fa", 4000), ("dag", 300), ("stress", 3)])
-def test_kernel_body_configs_match_oracle(name, count):
-    """The GEMM mainloop, FlashAttention, 256-op DAG and 1024-op stress bodies (global-read kernel)."""
+# (body, candidates, calibrated capacities, classes the oracle must report). The nominal GEMM and
+# FlashAttention capacities cannot be exceeded by a candidate that keeps its lane, sync and
+# relation inequalities, so their capacity checks run on the calibrated variants.
+BODY_CASES = [
+    ("gemm", 4000, True, {0, 12, 15, 18, 20}),
+    ("fa", 4000, True, {0, 12, 15, 18, 20}),
+    ("gemm", 4000, False, {0, 5, 12, 15, 18}),
+    ("fa", 4000, False, {0, 1, 5, 12, 15, 18}),
+    ("dag", 1500, False, {0, 1, 5, 12, 15, 20}),
+    ("stress", 256, False, {0, 5, 12, 20}),
+]
+
+
+@pytest.mark.parametrize("name,count,calibrated,required", BODY_CASES,
+                         ids=[f"{c[0]}{'-calibrated' if c[2] else ''}" for c in BODY_CASES])
+def test_kernel_body_configs_match_oracle(name, count, calibrated, required):
+    """The GEMM mainloop, FlashAttention, 256-op DAG and 1024-op stress bodies.
+
+    Software-pipelined candidates (half of them corrupted) whose verdicts cover the capacity
+    check (class 20) as well as the lane, sync and relation classes.
+    """
     from tilefoundry_b200 import workloads
 
-    problem = {
-        "gemm": workloads.gemm_mainloop_problem,
-        "fa": workloads.flash_attention_problem,
-        "dag": workloads.dag_problem,
-        "stress": workloads.stress_problem,
-    }[name]()
-    packed = pack_problem(problem)
-    witness = workloads.list_schedule_witness(packed, seed=1)
-    frames, batch = neighbourhood(packed, witness, count, seed=3, jitter=64)
+    problem, packed, _witness, frames, batch, _kind = workloads.body_batch(name, count, seed=3, calibrated=calibrated)
     with WarpgroupVerifier(packed) as verifier:
         verdict, makespan, ii = verifier.verify_periodic(frames, batch)
     oracle = OracleProblem(load_problem(problem_to_json(problem)))
     p, o = absolute_starts(batch)
     ov, om, oi = oracle.classify_periodic(p, o, batch.ii, frames.frames, batch.frame)
+    assert required <= set(np.unique(ov).tolist())
     assert np.array_equal(verdict, ov)
     assert np.array_equal(makespan, om)
     assert np.array_equal(ii, oi)
@@ -313,7 +324,9 @@ def test_kernel_body_configs_match_oracle(name, count):
 def _oracle_rows(problem, frames, batch, ii_values):
     oracle = OracleProblem(load_problem(problem_to_json(problem)))
     p, o = absolute_starts(batch)
-    return [oracle.classify_periodic(p, o, row, frames.frames, batch.frame) for row in ii_values]
+    arrays, memo = oracle.prepare_frames(frames.frames)  # the frames' answers serve every II row
+    return [oracle.classify_periodic(p, o, row, frames.frames, batch.frame, frame_arrays=arrays, memo=memo)
+            for row in ii_values]
 
 
 def _assert_sweep(got, want):
@@ -356,18 +369,16 @@ def test_ii_sweep_matches_oracle_resources():
 
 
 def test_ii_sweep_stress_body_matches_oracle():
-    """The 1024-op stress body at four IIs over [II_lb, 2 II_lb] (global-read kernel)."""
+    """The 1024-op stress body: 256 candidates, each at the 16 IIs spread over [II_lb, 2 II_lb]."""
     from tilefoundry_b200 import workloads
 
-    problem = workloads.stress_problem()
-    packed = pack_problem(problem)
-    witness = workloads.list_schedule_witness(packed, seed=1)
-    frames, batch = neighbourhood(packed, witness, 2, seed=5, jitter=64)
-    ii_values = np.repeat(workloads.ii_sweep(workloads.ii_lower_bound(packed), 4)[:, None], 2, axis=1)
-    ii_values[-1] = witness.ii  # one row at the witness II
+    problem, packed, _witness, frames, batch, _kind = workloads.body_batch("stress", 256, seed=11)
+    ii_values = np.repeat(workloads.ii_sweep(workloads.ii_lower_bound(packed), 16)[:, None], 256, axis=1)
     with WarpgroupVerifier(packed) as verifier:
         got = verifier.verify_periodic_sweep(frames, batch, ii_values.astype(np.int32))
-    _assert_sweep(got, _oracle_rows(problem, frames, batch, ii_values))
+    want = _oracle_rows(problem, frames, batch, ii_values)
+    assert {0, 12, 15, 20} <= set(np.unique(np.concatenate([w[0] for w in want])).tolist())
+    _assert_sweep(got, want)
 
 
 @pytest.mark.parametrize("name", ["mla", "resource_c4_w5", "shared_init_i4", "tiny_free"])

@@ -154,7 +154,10 @@ def absolute_starts(batch: PeriodicBatch) -> tuple[np.ndarray, np.ndarray]:
     return prologue, offset
 
 
-__all__ = ["MIX", "Witness", "absolute_starts", "mla_perturbations", "shared_producers", "witness_from_rows"]
+__all__ = [
+    "BODIES", "MIX", "Witness", "absolute_starts", "body_batch", "mla_perturbations", "peak_demands", "pipelined_batch",
+    "pipelined_starts", "shared_producers", "witness_from_rows", "with_capacities",
+]
 
 
 # ---------------------------------------------------------------------------------------
@@ -457,7 +460,7 @@ def _body_problem(ops_spec, lanes: int, iterations: int, capacities: dict, iter_
         WarpgroupProblem,
     )
 
-    kinds = {"register": "reg", "shared": "smem"}
+    kinds = {"register": "reg", "shared": "smem", "global": "gmem"}
     ops = tuple(
         ProblemOperation(
             op_id,
@@ -483,12 +486,17 @@ def gemm_mainloop_problem(iterations: int = 8):
     """GEMM mainloop body: TMA loads of A (128x64 bf16, 16 KB) and B (256x64 bf16, 32 KB)
     by the producer warpgroup, a 128x256x64 tcgen05 MMA (latency 512) and a barrier
     arrive by the consumer, and an epilogue store of the 128x256 fp32 accumulator.
-    Resources: shared memory in KB (227), TMEM columns (512), mbarriers, TMA slots; a
-    4-stage ring bounds the loads in flight through the TMA-slot capacity."""
+    Resources: shared memory in KB (227), TMEM columns (512), mbarriers (8) and the slots
+    of the 4-stage A/B ring (8: a stage holds one A and one B tile). The tiles live in ring
+    buffers, not in one shared allocation per value, so the loads of later iterations may
+    run ahead of the MMA: the ring's slot capacity and the shared-memory capacity bound the
+    loads in flight. The accumulator belongs to the MMA warpgroup (a register-space value
+    carried from one iteration's MMA to the next)."""
     spec = [
-        ("load_a", 0, 24, 700, [("smem_kb", 16, 700), ("tma_slots", 1, 700)], "%a", "shared", ["%gmem"]),
-        ("load_b", 0, 24, 900, [("smem_kb", 32, 900), ("tma_slots", 1, 900)], "%b", "shared", ["%gmem"]),
-        ("mma", 1, 64, 512, [("tmem_cols", 256, 512)], "%acc", "shared", ["%a", "%b", "%acc_prev"]),
+        ("load_a", 0, 24, 700, [("smem_kb", 16, 700), ("tma_slots", 1, 700)], "%a", "global", ["%gmem"]),
+        ("load_b", 0, 24, 900, [("smem_kb", 32, 900), ("tma_slots", 1, 900)], "%b", "global", ["%gmem"]),
+        ("mma", 1, 64, 512, [("tmem_cols", 256, 512), ("mbarrier", 1, 512)], "%acc", "register",
+         ["%a", "%b", "%acc_prev"]),
         ("arrive", 1, 4, 4, [("mbarrier", 1, 4)], "%bar", "register", ["%acc"]),
         ("store", 1, 160, 420, [("smem_kb", 96, 420)], "%out", "register", ["%acc", "%bar"]),
     ]
@@ -499,13 +507,15 @@ def gemm_mainloop_problem(iterations: int = 8):
 def flash_attention_problem(iterations: int = 16):
     """FlashAttention-forward body (Q 128x128, K/V 128x128 bf16 tiles): loads of K and V
     (load warpgroup), S = QK^T and P.V MMAs (MMA warpgroup), rowmax, exp2, rowsum and the O
-    rescale (softmax warpgroup). Shared memory 227 KB, TMEM 512 columns."""
+    rescale (softmax warpgroup). Shared memory 227 KB, TMEM 512 columns. K and V tiles, the
+    S tile (TMEM) and the P tile (shared memory) live in ping-pong buffers bounded by those
+    capacities, so the loads and the S MMA of later iterations may overlap the current one."""
     spec = [
-        ("load_k", 0, 24, 800, [("smem_kb", 32, 800)], "%k", "shared", ["%gmem"]),
-        ("load_v", 0, 24, 800, [("smem_kb", 32, 800)], "%v", "shared", ["%gmem"]),
-        ("qk", 1, 48, 384, [("tmem_cols", 128, 384)], "%s", "shared", ["%gmem", "%k"]),
+        ("load_k", 0, 24, 800, [("smem_kb", 32, 800)], "%k", "global", ["%gmem"]),
+        ("load_v", 0, 24, 800, [("smem_kb", 32, 800)], "%v", "global", ["%gmem"]),
+        ("qk", 1, 48, 384, [("tmem_cols", 128, 384)], "%s", "global", ["%gmem", "%k"]),
         ("rowmax", 2, 90, 110, [], "%m", "register", ["%s", "%m_prev"]),
-        ("exp2", 2, 220, 240, [("smem_kb", 32, 240)], "%p", "shared", ["%s", "%m"]),
+        ("exp2", 2, 220, 240, [("smem_kb", 32, 240)], "%p", "global", ["%s", "%m"]),
         ("rowsum", 2, 80, 96, [], "%l", "register", ["%p", "%l_prev"]),
         ("rescale", 2, 140, 160, [("tmem_cols", 128, 160)], "%o_scaled", "shared", ["%o_prev", "%m", "%m_prev"]),
         ("pv", 1, 48, 384, [("tmem_cols", 128, 384)], "%o", "shared", ["%p", "%v", "%o_scaled"]),
@@ -549,3 +559,280 @@ def ii_sweep(ii_lb: int, n_ii: int = 16) -> np.ndarray:
     if n_ii == 1:
         return np.array([ii_lb], dtype=np.int64)
     return ii_lb + (np.arange(n_ii, dtype=np.int64) * ii_lb) // (n_ii - 1)
+
+
+# ---------------------------------------------------------------------------------------
+# Software-pipelined candidates: overlapping iterations decided by the resource capacities
+# ---------------------------------------------------------------------------------------
+
+
+def _constraint_lists(packed: PackedProblem, lanes: list[list[str]]):
+    """Difference constraints of a periodic schedule with fixed lanes (verify.py:278-318).
+
+    Returns the same-iteration topological order and, per operation b, its same-iteration
+    predecessors ``(a, weight)`` (lane predecessor with a's issue duration, distance-0
+    relations with a's latency), its body-only predecessors (carried shared lifetimes, which
+    hold in iterations 1..I-1) and its next-iteration predecessors (distance-1 relations
+    and the lane wrap from a lane's last operation to its first).
+    """
+    N = packed.n_ops
+    same: list[list[tuple[int, int]]] = [[] for _ in range(N)]
+    body: list[list[tuple[int, int]]] = [[] for _ in range(N)]
+    nxt: list[list[tuple[int, int]]] = [[] for _ in range(N)]
+    for lane in lanes:
+        ks = [packed.index[op] for op in lane]
+        for a, b in zip(ks, ks[1:]):
+            same[b].append((a, int(packed.issue[a])))
+        if ks:
+            nxt[ks[0]].append((ks[-1], int(packed.issue[ks[-1]])))
+    for a, b, d in packed.relations:
+        (same if d == 0 else nxt)[int(b)].append((int(a), int(packed.latency[a])))
+    for u, df in packed.carried:
+        body[int(df)].append((int(u), int(packed.latency[u])))
+    indeg = [0] * N
+    succs: list[list[int]] = [[] for _ in range(N)]
+    for b in range(N):
+        for a, _ in same[b] + body[b]:
+            succs[a].append(b)
+            indeg[b] += 1
+    order = [k for k in range(N) if indeg[k] == 0]
+    for k in order:
+        for b in succs[k]:
+            indeg[b] -= 1
+            if indeg[b] == 0:
+                order.append(b)
+    if len(order) != N:
+        raise ValueError("the lanes and same-iteration relations are cyclic")
+    return order, same, body, nxt
+
+
+def pipelined_starts(packed: PackedProblem, lanes, ii: np.ndarray, delay_p: np.ndarray, delay_o: np.ndarray,
+                     rounds: int | None = None, floor_p: np.ndarray | None = None, floor_o: np.ndarray | None = None):
+    """Earliest prologue and body-offset starts of periodic schedules at the given IIs.
+
+    ``ii`` is [n]; ``delay_p``/``delay_o`` [n, N] non-negative extra delays; ``floor_p`` /
+    ``floor_o`` ([n, N] or [N]) optional earliest starts of each operation. The prologue
+    (iteration 0, solve.py:215-217) is scheduled as soon as its same-iteration constraints
+    allow; the body offsets (iterations >= 1 start at offset + i * II, solve.py:218-221) are
+    the least solution of every constraint at that II, including those from iteration 0 to
+    iteration 1, by Bellman-Ford rounds. Returns ``(prologue, offset, feasible)``: a
+    candidate is feasible when the rounds converged (no positive cycle at its II); feasible
+    candidates satisfy every lane, sync, relation and carried-lifetime inequality with the
+    full relation set as sync, so the resource capacities decide their verdict.
+    """
+    order, same, body, nxt = _constraint_lists(packed, lanes)
+    n, N = delay_p.shape
+    ii = np.asarray(ii, dtype=np.int64)
+    fp = np.broadcast_to(np.zeros(N, dtype=np.int64) if floor_p is None else np.asarray(floor_p, np.int64), (n, N))
+    fo = np.broadcast_to(np.zeros(N, dtype=np.int64) if floor_o is None else np.asarray(floor_o, np.int64), (n, N))
+    p = np.zeros((n, N), dtype=np.int64)
+    for b in order:
+        t = fp[:, b].copy()
+        for a, w in same[b]:
+            t = np.maximum(t, p[:, a] + w)
+        p[:, b] = t + delay_p[:, b]
+    o = fo + delay_o.astype(np.int64)  # body rows start no earlier than cycle ii
+    live = np.ones(n, dtype=bool)
+    limit = rounds if rounds is not None else N + 2
+    for _ in range(limit):
+        before = o.copy()
+        for b in order:
+            t = o[:, b]
+            for a, w in same[b]:
+                t = np.maximum(t, o[:, a] + w)
+            for a, w in body[b]:
+                t = np.maximum(t, o[:, a] + w)
+            for a, w in nxt[b]:
+                t = np.maximum(t, np.maximum(p[:, a], o[:, a]) + w - ii)
+            o[:, b] = t
+        changed = (o != before).any(axis=1)
+        if not changed.any():
+            break
+    else:
+        changed = (o != before).any(axis=1)
+        live &= ~changed
+    return p, o, live
+
+
+def pipelined_batch(
+    packed: PackedProblem,
+    witness: Witness,
+    n: int,
+    *,
+    seed: int = 0,
+    ii_range: tuple[int, int] | None = None,
+    delay: float = 0.1,
+    delay_scale: int = 200,
+    start_range: int | None = None,
+    corrupt: float = 0.5,
+    jitter: int = 64,
+    pool: int = 2048,
+    pool_size: int = 32,
+) -> tuple[FrameSet, PeriodicBatch, np.ndarray]:
+    """``n`` seeded software-pipelined candidates around the witness's lanes.
+
+    A pool of ``pool`` templates is drawn first, each with sparse random delays
+    (probability ``delay`` per operation, exponential with mean ``delay_scale`` cycles) and
+    the earliest starts that satisfy every lane, sync, relation and carried constraint at
+    its II (:func:`pipelined_starts`). Half the templates are pipelined: an II uniform in
+    ``ii_range`` (default [II_lb, witness II]) and no other floor, so iterations overlap
+    whenever the II is below the span. The other half keep every start at or after the
+    witness's (its resource-feasible single iteration), without delays, at an II uniform in
+    [0.9, 1.3] times the witness II. Either way the resource capacities decide between
+    verdicts 0 and 20.
+    Every candidate takes a template
+    and moves all its starts later by a common shift (up to ``start_range`` minus the
+    template's largest start, so starts stay in [0, ``start_range``] when given). A fraction
+    ``corrupt`` of the candidates is then broken in one of four ways: 1-3 operations
+    jittered by U[-jitter, jitter] (lane order, sync and relation timing), the II cut by up
+    to a third (wrap edges and distance-1 relations, more overlap), a structural variant
+    (an operation moved to another lane, two lane neighbours swapped or a sync edge dropped)
+    or one resource-holding operation moved onto another's start (capacity). Returns the
+    frames, the batch and each candidate's kind (0 = uncorrupted, 1-4 as listed).
+    """
+    rng = np.random.default_rng(seed)
+    N = packed.n_ops
+    lo, hi = ii_range if ii_range is not None else (ii_lower_bound(packed), max(ii_lower_bound(packed), witness.ii))
+    m = max(2, min(pool, n))
+    floored = np.arange(m) % 2 == 1
+    t_ii = np.where(floored, rng.integers(int(0.9 * witness.ii), int(1.3 * witness.ii) + 2, size=m),
+                    rng.integers(lo, hi + 1, size=m))
+    sparse = (rng.random((2, m, N)) < delay) & ~floored[None, :, None]
+    dp = np.where(sparse[0], rng.exponential(delay_scale, size=(m, N)), 0).astype(np.int64)
+    dq = np.where(sparse[1], rng.exponential(delay_scale, size=(m, N)), 0).astype(np.int64)
+    floor = np.where(floored[:, None], witness.prologue.astype(np.int64)[None, :], 0)
+    tp, to, ok = pipelined_starts(packed, witness.lanes, t_ii, dp, dq, floor_p=floor, floor_o=floor)
+    keep = np.flatnonzero(ok)
+    if keep.size == 0:
+        raise ValueError("no template converged: the II range is below every recurrence bound")
+    tp, to, t_ii = tp[keep], to[keep], t_ii[keep]
+    pick = rng.integers(0, keep.size, size=n)
+    top = np.maximum(tp.max(axis=1), to.max(axis=1) + t_ii)[pick]
+    room = np.maximum(0, (start_range - top) if start_range is not None else np.full(n, 64))
+    shift = (rng.random(n) * (room + 1)).astype(np.int64)
+    prologue = tp[pick] + shift[:, None]
+    offset = to[pick] + shift[:, None]
+    ii = t_ii[pick].copy()
+
+    frames = FrameSet(packed)
+    base = frames.add(witness.lanes, witness.sync)
+    frame = np.full(n, base, dtype=np.int32)
+    kind = np.where(rng.random(n) < corrupt, rng.integers(1, 5, size=n), 0).astype(np.int8)
+    sel = np.flatnonzero(kind == 1)
+    for _ in range(3):
+        rows = sel[rng.random(sel.size) < 0.7]
+        ops = rng.integers(0, N, size=rows.size)
+        prologue[rows, ops] += rng.integers(-jitter, jitter + 1, size=rows.size)
+        offset[rows, ops] += rng.integers(-jitter, jitter + 1, size=rows.size)
+    sel = np.flatnonzero(kind == 2)
+    ii[sel] -= (rng.random(sel.size) * ii[sel] / 3).astype(np.int64)
+    sel = np.flatnonzero(kind == 3)
+    if sel.size:
+        variants = []
+        for _ in range(pool_size):
+            lanes = [list(l) for l in witness.lanes]
+            sync = list(witness.sync)
+            roll = rng.random()
+            if roll < 0.34:
+                op = packed.op_ids[int(rng.integers(N))]
+                for lane in lanes:
+                    if op in lane:
+                        lane.remove(op)
+                target = lanes[int(rng.integers(len(lanes)))]
+                target.insert(int(rng.integers(len(target) + 1)), op)
+            elif roll < 0.67:
+                nonempty = [l for l in lanes if len(l) >= 2] or lanes
+                lane = nonempty[int(rng.integers(len(nonempty)))]
+                if len(lane) >= 2:
+                    x = int(rng.integers(len(lane) - 1))
+                    lane[x], lane[x + 1] = lane[x + 1], lane[x]
+            elif sync:
+                sync.pop(int(rng.integers(len(sync))))
+            variants.append(frames.add(lanes, sync))
+        frame[sel] = np.array(variants, dtype=np.int32)[rng.integers(0, len(variants), size=sel.size)]
+    sel = np.flatnonzero(kind == 4)
+    holders = np.flatnonzero(np.diff(packed.window_offsets) > 0)
+    if sel.size and holders.size >= 2:
+        a = holders[rng.integers(0, holders.size, size=sel.size)]
+        b = holders[rng.integers(0, holders.size, size=sel.size)]
+        offset[sel, a] = offset[sel, b]
+        prologue[sel, a] = prologue[sel, b]
+    batch = PeriodicBatch.from_starts(prologue, offset, ii, frame)
+    return frames, batch, kind
+
+
+def peak_demands(packed: PackedProblem, prologue: np.ndarray, offset: np.ndarray, ii: np.ndarray) -> np.ndarray:
+    """[n, Q] largest demand of every resource over each periodic candidate's timeline.
+
+    The netted sweep of verify.py:183-200 on every candidate at once (numpy; meant for
+    bodies with a few hundred windows at most): +amount at each window copy's start,
+    -amount at its end, summed in time order with ends before starts at equal times.
+    """
+    n = prologue.shape[0]
+    I, Q = packed.iterations, len(packed.resource_ids)
+    out = np.zeros((n, Q), dtype=np.int64)
+    i = np.arange(I, dtype=np.int64)
+    starts = offset[:, None, :] + i[None, :, None] * np.asarray(ii, dtype=np.int64)[:, None, None]
+    starts[:, 0, :] = prologue
+    ops = np.repeat(np.arange(packed.n_ops), np.diff(packed.window_offsets))
+    for q in range(Q):
+        w = np.flatnonzero(packed.window_resource == q)
+        if w.size == 0:
+            continue
+        s = starts[:, :, ops[w]].reshape(n, -1)
+        e = s + np.tile(packed.window_duration[w].astype(np.int64), I)
+        a = np.tile(packed.window_amount[w].astype(np.int64), I)
+        t = np.concatenate([s, e], axis=1)
+        d = np.concatenate([np.broadcast_to(a, s.shape), -np.broadcast_to(a, s.shape)], axis=1)
+        order = np.argsort(t * 2 + (d > 0), axis=1, kind="stable")  # ends before starts at equal times
+        out[:, q] = np.cumsum(np.take_along_axis(d, order, axis=1), axis=1).max(axis=1)
+    return out
+
+
+def with_capacities(problem: object, capacities: dict[str, int]) -> object:
+    """``problem`` (mirror records) with the named resources' capacities replaced."""
+    import dataclasses
+
+    resources = tuple(dataclasses.replace(r, capacity=int(capacities.get(r.id, r.capacity)))
+                      for r in problem.resources)  # type: ignore[attr-defined]
+    return dataclasses.replace(problem, resources=resources)
+
+
+BODIES = {
+    "gemm": gemm_mainloop_problem,
+    "fa": flash_attention_problem,
+    "dag": dag_problem,
+    "stress": stress_problem,
+}
+
+
+def body_batch(name: str, n: int, *, seed: int = 0, calibrated: bool = False, pool: int = 2048):
+    """A seeded batch of ``n`` candidates for one of the kernel-body problems.
+
+    ``name`` is ``gemm`` (starts in [0, 8000]), ``fa``, ``dag`` or ``stress``; candidates
+    come from :func:`pipelined_batch` with half of them corrupted. With ``calibrated`` the
+    problem's capacities are set to the 75th percentile of the uncorrupted candidates' peak
+    demands (:func:`peak_demands`), so that each resource is exceeded by part of the batch:
+    with the nominal capacities of the GEMM and FlashAttention bodies no candidate that
+    keeps the lane, sync and relation inequalities can exceed them (their recurrences bound
+    the work in flight). Returns ``(problem, packed, witness, frames, batch, kind)``.
+    """
+    from .problem import pack_problem
+
+    problem = BODIES[name]()
+    packed = pack_problem(problem)
+    witness = list_schedule_witness(packed, seed=1)
+    frames, batch, kind = pipelined_batch(packed, witness, n, seed=seed, pool=min(pool, max(2, n)),
+                                          start_range=8000 if name == "gemm" else None)
+    if calibrated:
+        p, o = absolute_starts(batch)
+        clean = np.flatnonzero(kind == 0)[:4096]
+        peaks = peak_demands(packed, p[clean], o[clean], batch.ii[clean])
+        caps = {rid: max(1, int(np.quantile(peaks[:, q], 0.75))) for q, rid in enumerate(packed.resource_ids)}
+        problem = with_capacities(problem, caps)
+        packed = pack_problem(problem)
+        frames_new = FrameSet(packed)  # the same frames, indexed against the new problem tables
+        for lanes, sync in frames.frames:
+            frames_new.add(lanes, sync)
+        frames = frames_new
+    return problem, packed, witness, frames, batch, kind

@@ -37,10 +37,10 @@ sys.path[:0] = [str(ROOT), str(ROOT / "tests")]
 METRIC = "candidate schedules verified/sec (bit-exact verdict+makespan) at 1/2/4/8 B200"
 UNIT = "candidates/s"
 FALLBACK_HBM_GBS = 6650.0
-# DRAM bytes per candidate of verify_periodic_tma_kernel measured by ncu on a 2 097 152-
-# candidate launch (dram__bytes_read.sum + dram__bytes_write.sum = 467.7 MB; see
-# profiles/verify_periodic_tma_mla.md). Traffic grows in proportion to the candidates.
-MEASURED_DRAM_BYTES_PER_CANDIDATE = 467.7e6 / 2097152
+# DRAM bytes per candidate of the MLA batch's default kernel, tfv_spec_ring, measured by ncu
+# on a 2 097 152-candidate launch (dram__bytes_read.sum + dram__bytes_write.sum = 444.7 MB +
+# 23.5 MB; see profiles/tfv_spec_ring_mla.md). Traffic grows in proportion to the candidates.
+MEASURED_DRAM_BYTES_PER_CANDIDATE = (444.7e6 + 23.5e6) / 2097152
 
 
 def parse_args():
@@ -67,6 +67,9 @@ def parse_args():
     p.add_argument("--no-delta", action="store_true",
                    help="only the plan frame's candidates run the generated code (no delta verification)")
     p.add_argument("--cpu-sample", type=int, default=None, help="oracle sample size per step")
+    p.add_argument("--gather", choices=["peer", "nccl"], default="peer",
+                   help="N > 1: how each step's packed results reach rank 0: copy engines writing into rank 0's "
+                        "memory (peer, shard.PeerGather) or an NCCL gather")
     return p.parse_args()
 
 
@@ -85,37 +88,28 @@ def mla_workload(n: int, seed: int):
     return problem, packed, frames, batch
 
 
-def body_workload(builder):
+def body_workload(name: str):
     def make(n: int, seed: int):
-        from tilefoundry_b200 import pack_problem
-        from tilefoundry_b200.workloads import list_schedule_witness, neighbourhood
+        from tilefoundry_b200.workloads import body_batch
 
-        problem = builder()
-        packed = pack_problem(problem)
-        witness = list_schedule_witness(packed, seed=1)
-        frames, batch = neighbourhood(packed, witness, n, seed=seed, jitter=64)
+        problem, packed, _witness, frames, batch, _kind = body_batch(name, n, seed=seed)
         return problem, packed, frames, batch
 
     return make
 
 
-def _builder(name):
-    def build():
-        from tilefoundry_b200 import workloads
-
-        return getattr(workloads, name)()
-
-    return build
-
-
-# name: (generator, default candidates per GPU, description)
+# name: (generator, default candidates per GPU, description). The kernel bodies' candidates
+# are software-pipelined schedules of the body, half of them corrupted (workloads.body_batch).
 WORKLOADS = {
     "mla": (mla_workload, 1 << 23, "mla-decode-perturbations"),
-    "gemm": (body_workload(_builder("gemm_mainloop_problem")), 1 << 24, "gemm-mainloop-neighbourhood"),
-    "fa": (body_workload(_builder("flash_attention_problem")), 1 << 23, "flash-attention-fwd-neighbourhood"),
-    "dag": (body_workload(_builder("dag_problem")), 1 << 21, "layered-dag-256-neighbourhood"),
-    "stress": (body_workload(_builder("stress_problem")), 1 << 16, "stress-dag-1024-neighbourhood"),
+    "gemm": (body_workload("gemm"), 1 << 22, "gemm-mainloop-pipelined"),
+    "fa": (body_workload("fa"), 1 << 22, "flash-attention-fwd-pipelined"),
+    "dag": (body_workload("dag"), 1 << 21, "layered-dag-256-pipelined"),
+    "stress": (body_workload("stress"), 1 << 16, "stress-dag-1024-pipelined"),
 }
+# Bodies of this many operations or more run the large-body kernel (one warp per candidate);
+# smaller ones the kernel generated for the batch's most frequent frame.
+LARGE_MIN_OPS = 128
 
 
 def workload(name: str, n: int, seed: int):
@@ -125,6 +119,43 @@ def workload(name: str, n: int, seed: int):
 def algorithmic_bytes_per_candidate(n_ops: int) -> int:
     """Inputs: int16 prologue and offset deltas per op, int32 II and frame; outputs: 3 x int32."""
     return 2 * 2 * n_ops + 4 + 4 + 12
+
+
+def workload_config(args, packed, frames, n: int, n_ii: int, world: int) -> dict:
+    """The workload description both arms print (the same dict for the same arguments)."""
+    per_launch = (algorithmic_bytes_per_candidate(packed.n_ops) + 16 * (n_ii - 1)) * n
+    return {
+        "workload": WORKLOADS[args.workload][2],
+        "candidates_per_gpu": n,
+        "iis_per_candidate": n_ii,
+        "ops": packed.n_ops,
+        "iterations": packed.iterations,
+        "warpgroups": packed.warp_groups,
+        "relations": int(packed.relations.shape[0]),
+        "frames": len(frames),
+        "format": "periodic: int16 prologue/offset deltas + int32 ii + int32 frame per candidate",
+        "bytes_per_candidate": algorithmic_bytes_per_candidate(packed.n_ops),
+        "l2": f"inputs {per_launch / 1e9:.2f} GB per GPU per step, larger than the 126 MB L2",
+        "parallelism": f"dp{world} (contiguous candidate shards; int8 verdict + int32 makespan gathered to rank 0"
+                       + (f", {args.gather})" if world > 1 else ")"),
+    }
+
+
+def cpu_model() -> str:
+    """The host CPU's model name (/proc/cpuinfo), or the platform's processor string."""
+    try:
+        for line in Path("/proc/cpuinfo").read_text().splitlines():
+            if line.startswith("model name"):
+                return line.split(":", 1)[1].strip()
+    except OSError:
+        pass
+    import platform
+
+    return platform.processor() or "unknown"
+
+
+def default_iis(args) -> int:
+    return args.iis or (16 if args.workload == "stress" else 1)
 
 
 # --------------------------------------------------------------------------- oracle timing
@@ -185,7 +216,7 @@ def run_reference(args) -> None:
         return
     pool, workers = make_pool()
     global ORACLE_PROBLEM
-    n = max(4096, args.steps * 64)
+    n = args.candidates or WORKLOADS[args.workload][1]  # the GPU arm's batch (rank 0's seed)
     problem, packed, frames, batch = workload(args.workload, n, args.seed)
     from tilefoundry_b200 import problem_to_json
 
@@ -213,14 +244,15 @@ def run_reference(args) -> None:
         "vs_baseline": None,
         "dtype": "int64",
         "data": "synthetic: seeded candidates of the workload (same generator and seed as the GPU arm)",
-        "config": {"workload": WORKLOADS[args.workload][2], "ops": packed.n_ops, "iterations": packed.iterations,
-                   "warpgroups": packed.warp_groups},
+        "config": workload_config(args, packed, frames, n, default_iis(args), int(os.environ.get("WORLD_SIZE", "1"))),
         "cpu_baseline": {
             "value": value,
             "unit": UNIT,
             "cores": workers,
+            "cpu_model": cpu_model(),
             "kind": "port",
-            "sample": f"{sample} candidates per step, {args.steps} steps, oracle/verify_port.py in {workers} processes",
+            "sample": f"{sample} candidates per step of this batch (each at its own II), {args.steps} steps, "
+                      f"oracle/verify_port.py in {workers} processes",
         },
         "e2e": {"value": value, "unit": UNIT, "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
     }
@@ -311,6 +343,35 @@ class ClockSampler:
 # --------------------------------------------------------------------------- GPU arm
 
 
+def link_bandwidth(device: int, nbytes: int = 1 << 29) -> dict:
+    """Pinned host <-> device copy bandwidth of this GPU (CUDA events, best of 3) and the
+    NUMA node its PCI device sits on; they bound the host-buffer entry."""
+    import torch
+
+    host = torch.empty(nbytes, dtype=torch.uint8).pin_memory()
+    dev = torch.empty(nbytes, dtype=torch.uint8, device=torch.device("cuda", device))
+    stream = torch.cuda.current_stream(device)
+    rates = {}
+    for name, (dst, src) in {"h2d_gbs": (dev, host), "d2h_gbs": (host, dev)}.items():
+        best = float("inf")
+        for _ in range(3):
+            a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            a.record(stream)
+            dst.copy_(src, non_blocking=True)
+            b.record(stream)
+            b.synchronize()
+            best = min(best, a.elapsed_time(b))
+        rates[name] = nbytes / (best / 1e3) / 1e9
+    props = torch.cuda.get_device_properties(device)
+    bus = f"{props.pci_domain_id:04x}:{props.pci_bus_id:02x}:{props.pci_device_id:02x}.0"
+    try:
+        numa = int(Path(f"/sys/bus/pci/devices/{bus}/numa_node").read_text().strip())
+    except (OSError, ValueError):
+        numa = None
+    del host, dev
+    return {**rates, "gpu_pci": bus, "gpu_numa_node": numa, "host_cpus": len(os.sched_getaffinity(0))}
+
+
 def run_ours(args) -> None:
     world = int(os.environ.get("WORLD_SIZE", "1"))
     rank = int(os.environ.get("RANK", "0"))
@@ -336,7 +397,7 @@ def run_ours(args) -> None:
 
     global ORACLE_PROBLEM
     n = args.candidates or WORKLOADS[args.workload][1]
-    n_ii = args.iis or (16 if args.workload == "stress" else 1)
+    n_ii = default_iis(args)
     problem, packed, frames, batch = workload(args.workload, n, args.seed + rank)
     if args.grouped:  # same candidates, frame by frame
         from tilefoundry_b200.batch import PeriodicBatch
@@ -369,19 +430,26 @@ def run_ours(args) -> None:
     iis = [torch.empty((n_ii, n), dtype=torch.int32, device=dev) for _ in range(2)]
     payload = [torch.empty(5 * m, dtype=torch.uint8, device=dev) for _ in range(2)]
     makespans = [buf[: 4 * m].view(torch.int32).view(n_ii, n) for buf in payload]
+    peer = None
+    if world > 1 and args.gather == "peer":
+        from tilefoundry_b200.shard import PeerGather
+
+        peer = PeerGather(5 * m)
     gathered = [[torch.empty(5 * m, dtype=torch.uint8, device=dev) for _ in range(world)] if rank == 0 else None
-                for _ in range(2)] if world > 1 else None
+                for _ in range(2)] if world > 1 and peer is None else None
     pending = [None, None]
     table = verifier.analyze(dframes)
     stream = torch.cuda.current_stream(dev)
     # The batch's most frequent frame gets a kernel generated and compiled for it (before
     # any timing); its candidates run that code, the others the frame-table path.
-    plan, spec_frame = None, -1
-    if not args.no_plan and n_ii == 1 and packed.n_ops <= 256:
+    plan, spec_frame, plan_compile_ms = None, -1, None
+    if not args.no_plan and n_ii == 1 and packed.n_ops < LARGE_MIN_OPS:
         spec_frame = int(np.argmax(np.bincount(batch.frame, minlength=len(frames))))
+        t0 = time.perf_counter()
         try:
             plan = verifier.plan(frames, spec_frame, kernel=args.plan_kernel, ring_warps=args.ring_warps,
                                  delta=not args.no_delta)
+            plan_compile_ms = 1000.0 * (time.perf_counter() - t0)  # NVRTC compile + module load, once per frame
         except VerifierRuntimeError as error:  # no run-time compiler here: the frame-table kernel serves all
             print(f"# frame-specialised kernel unavailable ({error}); frame-table kernel only", file=sys.stderr)
             plan, spec_frame = None, -1
@@ -392,6 +460,8 @@ def run_ours(args) -> None:
 
     def step(s, events=None):
         buf = s % 2
+        if peer is not None:
+            peer.wait(buf, stream)  # the stream waits until that copy has read the buffer
         if pending[buf] is not None:
             pending[buf].wait()  # the stream waits until that gather has read the buffer
             pending[buf] = None
@@ -410,10 +480,15 @@ def run_ours(args) -> None:
             events[2].record(stream)
         if dist is not None:
             pack_results(verdicts[buf], makespans[buf], out=payload[buf])
-            pending[buf] = dist.gather(payload[buf], gather_list=gathered[buf] if rank == 0 else None, dst=0,
-                                       async_op=True)
+            if peer is not None:
+                peer.send(buf, payload[buf], stream)
+            else:
+                pending[buf] = dist.gather(payload[buf], gather_list=gathered[buf] if rank == 0 else None, dst=0,
+                                           async_op=True)
 
     def drain():
+        if peer is not None:
+            stream.wait_stream(peer.stream)  # the copies are part of the step
         for k in range(2):
             if pending[k] is not None:
                 pending[k].wait()
@@ -438,6 +513,14 @@ def run_ours(args) -> None:
         torch.cuda.synchronize(dev)
         barrier()
     elapsed_ms = begin.elapsed_time(end)
+    if peer is not None:  # every rank's last payload arrived intact in rank 0's memory
+        last_buf = (args.steps - 1) % 2
+        mine = int(payload[last_buf].to(torch.int64).sum().item())
+        sums = [None] * world
+        dist.all_gather_object(sums, mine)
+        if rank == 0:
+            rows = peer.received(last_buf).to(torch.int64).sum(dim=1).tolist()
+            assert rows == sums, "peer gather rows differ from the ranks' payloads"
     analyze_ms = [e[0].elapsed_time(e[1]) for e in events]
     verify_ms = [e[1].elapsed_time(e[2]) for e in events]
     if dist is not None:
@@ -482,6 +565,7 @@ def run_ours(args) -> None:
     last = verdicts[(args.steps - 1) % 2]
     assert np.array_equal(np.asarray(e2e_out[0]).reshape(n_ii, n), last.cpu().numpy()), \
         "host-buffer and device entries disagree"
+    link = link_bandwidth(local)
     h2d = sum(int(np.asarray(v).nbytes) for v in arrays.values()) + sum(
         int(getattr(batch, k).nbytes) for k in ("base_prologue", "base_offset", "prologue_delta", "offset_delta", "frame"))
     h2d += int(sweep.nbytes) if sweep is not None else int(batch.ii.nbytes)
@@ -506,6 +590,7 @@ def run_ours(args) -> None:
                 "value": sample / secs,
                 "unit": UNIT,
                 "cores": workers,
+                "cpu_model": cpu_model(),
                 "kind": "port",
                 "sample": f"{sample} candidates of this batch through oracle/verify_port.py in {workers} processes ({secs:.1f} s)",
             }
@@ -523,21 +608,14 @@ def run_ours(args) -> None:
             "vs_baseline": None,
             "dtype": "int32",
             "data": ("synthetic: seeded perturbations of the MLA example's verified witness (per-rank seed)"
-                     if args.workload == "mla" else "synthetic: seeded neighbourhood of a list-scheduled witness (per-rank seed)"),
-            "config": {
-                "workload": WORKLOADS[args.workload][2],
-                "candidates_per_gpu": n,
-                "iis_per_candidate": n_ii,
-                "ops": packed.n_ops,
-                "iterations": packed.iterations,
-                "warpgroups": packed.warp_groups,
-                "relations": int(packed.relations.shape[0]),
-                "frames": len(frames),
-                "format": "periodic: int16 prologue/offset deltas + int32 ii + int32 frame per candidate",
-                "bytes_per_candidate": algorithmic_bytes_per_candidate(packed.n_ops),
-                "l2": f"inputs {per_launch / 1e9:.2f} GB per GPU per step, larger than the 126 MB L2",
-                "parallelism": f"dp{world} (contiguous candidate shards; int8 verdict + int32 makespan gathered to rank 0)",
-                "valid_fraction": float(histogram[4] / (n * n_ii)),
+                     if args.workload == "mla" else
+                     "synthetic: seeded software-pipelined schedules of the body, half corrupted (per-rank seed)"),
+            "config": workload_config(args, packed, frames, n, n_ii, world),
+            "valid_fraction": float(histogram[4] / (n * n_ii)),
+            "plan": None if plan is None else {
+                "kernel": plan.kernel, "delta": plan.delta, "compile_ms": plan_compile_ms,
+                "note": "compiled once per frame content before timing; a share of "
+                        f"{plan_compile_ms / (plan_compile_ms + elapsed_ms):.3f} of compile + timed region",
             },
             "roofline": {
                 "bound": "hbm",
@@ -546,18 +624,24 @@ def run_ours(args) -> None:
                 "unit": "GB/s",
                 "frac": achieved / peak,
                 "traffic": MEASURED_DRAM_BYTES_PER_CANDIDATE * n if args.workload == "mla" else None,
-                "traffic_source": "ncu dram__bytes_read+write on 2097152 candidates, scaled per candidate",
+                "traffic_source": "ncu dram__bytes_read+write of tfv_spec_ring on 2097152 MLA candidates, "
+                                  "scaled per candidate" if args.workload == "mla" else None,
                 "peak_source": peak_src,
                 "kernel": (("tfv_spec_ring" if plan.kernel == "ring" else "tfv_spec_kernel") +
                            " (generated for the most frequent frame, "
                            f"{float(np.mean(batch.frame == spec_frame)):.2f} of the batch)" if plan is not None else
-                           "tfv::verify_periodic_tma_kernel" if packed.n_ops <= 256 else "tfv::verify_periodic_global_kernel"),
+                           "tfv::verify_periodic_large_kernel" if packed.n_ops >= LARGE_MIN_OPS else
+                           "tfv::verify_periodic_tma_kernel"),
                 "kernel_ms": statistics.mean(verify_ms),
                 "analyze_ms": statistics.mean(analyze_ms),
             },
             "cpu_baseline": cpu,
             "e2e": {"value": e2e_value, "unit": UNIT, "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h,
-                    "steps": e2e_steps, "entry": e2e_entry},
+                    "steps": e2e_steps, "entry": e2e_entry, **link,
+                    # the copies bound the entry: one step needs h2d / h2d_gbs + d2h / d2h_gbs
+                    "link_bound": n * n_ii / (h2d / (link["h2d_gbs"] * 1e9) + d2h / (link["d2h_gbs"] * 1e9)),
+                    "frac_of_link_bound": e2e_value / (n * n_ii / (h2d / (link["h2d_gbs"] * 1e9) +
+                                                                   d2h / (link["d2h_gbs"] * 1e9)))},
             # frame analysis, sync-program compile, verification (+ the plan's constants kernel
             # and, with delta verification, its frame comparison)
             "gpu_launches": (3 + (0 if plan is None else 2 if plan.delta else 1)) * args.steps,
@@ -567,6 +651,12 @@ def run_ours(args) -> None:
     verifier.close()
     if dist is not None:
         dist.barrier()
+        if peer is not None:  # the other ranks unmap rank 0's buffers before rank 0 frees them
+            if rank != 0:
+                peer.close()
+            dist.barrier()
+            if rank == 0:
+                peer.close()
         dist.destroy_process_group()
 
 

@@ -187,6 +187,16 @@ typedef struct tfv_results {
 TFV_API int tfv_abi_version(void);
 TFV_API int tfv_last_error(char* buffer, size_t size);
 
+/* Failure detection. Every wait between the warps of the ring kernel (the generated plans)
+ * and of the large-body kernel is bounded in time: a wait that has not ended after `ns`
+ * nanoseconds (default 1e9) gives up, the CTA stops, its unverified candidates report
+ * TFV_CLASS_DEVICE_TIMEOUT and the kernel returns; copies already issued are still waited
+ * for before a CTA exits. Sets the limit for launches made after the call, process-wide, and
+ * stores the previous one in *previous (may be NULL). A short limit makes a run report
+ * timeouts on purpose (a test of the failure path without a fault); no reference
+ * counterpart. */
+TFV_API int tfv_set_device_wait_limit(uint64_t ns, uint64_t* previous);
+
 /* Create/destroy the device-resident problem tables on `device`
  * (the closure `build_warpgroup_problem`, build.py:169-220, hands to the verifier). */
 TFV_API int tfv_problem_create(const tfv_problem_desc* desc, int device, tfv_problem** out);
@@ -248,9 +258,12 @@ TFV_API int tfv_verify_periodic_sweep(const tfv_problem* problem, const tfv_fram
  * frame take the generated code, the others the frame-table path. `host_frames` are host
  * pointers; `frame` indexes them. Needs N <= 256 and the TMA layout of the batch
  * (16-byte aligned deltas, op_stride % 8 == 0). tfv_verify_periodic_planned takes the
- * device frames and frame table like tfv_verify_periodic; `spec_frame` must index a frame
- * identical to the plan's (same lanes and sync set); a plan serves one stream at a time
- * (its constants live in the module) and must be destroyed before its problem. */
+ * device frames and frame table like tfv_verify_periodic; `spec_frame` names the frame of
+ * these frames that has the plan frame's lanes and sync set (TFV_ERR_INVALID_ARGUMENT when
+ * it indexes no frame). Each call checks that frame against the plan's on the device: if it
+ * differs, every candidate takes the frame-table path (same results, none faster). A plan
+ * serves one stream at a time (its constants live in the module) and must be destroyed
+ * before its problem. */
 typedef struct tfv_plan tfv_plan;
 TFV_API int tfv_plan_create(const tfv_problem* problem, const tfv_frames* host_frames, int frame, tfv_plan** out);
 /* Kernels a plan can be built with. TFV_PLAN_RING: one CTA per SM, a producer warp
@@ -297,7 +310,9 @@ TFV_API int tfv_verify_rows(const tfv_problem* problem, const tfv_frames* frames
  * device in chunks (pinned host memory gives full PCIe bandwidth), analyses the frames,
  * verifies every candidate with copies overlapped with compute, and writes host results.
  * Synchronous. All pointers in `frames`, `batch` (op_stride counts host elements) and
- * `results` are host pointers. */
+ * `results` are host pointers. The problem handle keeps the device workspace (grown to the
+ * largest call), two streams and an event from the first call until it is destroyed, so
+ * later calls of that size allocate nothing; calls on one problem handle run one at a time. */
 TFV_API int tfv_verify_periodic_host(const tfv_problem* problem, const tfv_frames* frames,
                              const tfv_periodic_batch* batch, const tfv_results* results);
 
@@ -309,8 +324,10 @@ TFV_API int tfv_verify_periodic_host(const tfv_problem* problem, const tfv_frame
  * array of TFV_STATIC_TABLE_BYTES (8 MiB, held by every GPU that loads the library until
  * exit). Frames needing a larger table are rejected with TFV_ERR_RANGE. Allocates
  * nothing. The first call on a device looks up the array's device address with that
- * device current; make it before any stream capture. All calls share the array: calls
- * whose work overlaps on the GPU race. Device pointers, stream-ordered like
+ * device current; make it before any stream capture. Later calls check the cached address
+ * and look it up again after a reset of the device's context (cudaDeviceReset), so the
+ * first call after such a reset must also come before any capture. All calls share the
+ * array: calls whose work overlaps on the GPU race. Device pointers, stream-ordered like
  * tfv_verify_periodic. */
 TFV_API int tfv_verify_periodic_static(const tfv_problem* problem, const tfv_frames* frames,
                                        const tfv_periodic_batch* batch, const tfv_results* results, void* stream);

@@ -114,3 +114,53 @@ def test_native_decode_frames_accumulate_across_calls():
     both = np.concatenate([first.rows.frame, second.rows.frame])
     assert np.array_equal(both[np.concatenate([first.status, second.status]) == 0], rows_py.frame)
     assert len(native) == len(frames_py)
+
+
+def test_decoders_match_the_reference_decoder():
+    """Both decoders accept exactly the documents the reference's warpgroup_schedule_from_json
+    accepts (serialization.py:679-727) and decode them to the records it decoded. The fixture
+    holds the reference's own outcomes for golden documents and seeded mutations of them
+    (tests/golden/make_decode_golden.py ran the reference decoder)."""
+    import gzip
+
+    from golden_data import GOLDEN
+    from tilefoundry_b200.batch import schedule_parts
+
+    with gzip.open(GOLDEN / "decode_cases.json.gz", "rt", encoding="utf-8") as handle:
+        payload = json.load(handle)
+    names = sorted(set(payload["problem"]))
+    assert names == sorted(PROBLEMS)
+    for name in names:
+        pick = [k for k, p in enumerate(payload["problem"]) if p == name]
+        docs = [payload["document"][k] for k in pick]
+        accepted = np.array([payload["outcome"][k] == "accepted" for k in pick])
+        decoded = [payload["decoded"][k] for k in pick]
+        assert set(payload["outcome"][k] for k in pick) <= {"accepted", "WarpgroupSerializationError"}
+        # the Python decoder: same accept/reject, same records
+        for doc, ok, want in zip(docs, accepted, decoded):
+            try:
+                lanes, sync, rows = schedule_parts(schedule_from_json(doc))
+            except WarpgroupSerializationError:
+                assert not ok
+                continue
+            assert ok
+            assert [list(l) for l in lanes] == want[0]
+            assert [list(e) for e in sync] == want[1]
+            assert [list(r) for r in rows] == want[2]
+        # the native decoder: same accept/reject, and rows and frames equal to packing the
+        # reference's decoded records
+        packed = pack_problem(problem_from_json(problem_text(name)))
+        native = NativeFrameSet(packed)
+        got = decode_schedule_documents(native, docs, threads=4)
+        assert np.array_equal(got.status == 0, accepted)
+        frames = FrameSet(packed)
+        ref_rows = pack_rows(packed, frames, [(d[0], [tuple(e) for e in d[1]], [tuple(r) for r in d[2]])
+                                              for d, ok in zip(decoded, accepted) if ok])
+        ok = np.flatnonzero(accepted)
+        for key in ("start", "issue_end", "completion", "frame", "row_flags", "override", "override_makespan",
+                    "override_ii"):
+            assert np.array_equal(getattr(got.rows, key)[ok], getattr(ref_rows, key)), (name, key)
+        ours, theirs = native.arrays(), frames.arrays()
+        for key in ours:
+            assert np.array_equal(ours[key], theirs[key]), (name, key)
+        native.close()

@@ -409,3 +409,32 @@ def test_verify_documents_matches_record_path(name):
     assert np.array_equal(makespan[index], rm)
     assert np.array_equal(ii[index], ri)
     assert len(index) < len(docs)
+
+
+def test_outlier_candidates_get_verdicts(verifiers):
+    """1% of the candidates lie 10^5 cycles or more from the rest, outside the int16 delta range
+    of the batch's base: they are verified in batches of their own (verify_periodic_starts)
+    and every candidate matches the oracle."""
+    problem = problem_from_json(problem_text("mla"))
+    verifier = verifier_for(verifiers, "mla")
+    witness = witness_from_rows(verifier.packed, *raw_cases("mla")[0][0])
+    n = 20000
+    frames, batch, _ = mla_perturbations(verifier.packed, witness, n, seed=31, producers=shared_producers(problem))
+    p, o = absolute_starts(batch)
+    rng = np.random.default_rng(31)
+    out = np.flatnonzero(rng.random(n) < 0.01)
+    whole = out[: out.size // 2]  # every start later by 1e5-3e5 cycles (verdicts kept, makespans move)
+    shift = rng.integers(1, 4, size=whole.size) * 100000
+    p[whole] += shift[:, None]
+    o[whole] += shift[:, None]
+    one = out[out.size // 2:]  # one operation's starts moved by 1e5 cycles
+    ops = rng.integers(0, p.shape[1], size=one.size)
+    p[one, ops] += 100000
+    o[one, ops] += 100000
+    verdict, makespan, ii = verifier.verify_periodic_starts(frames, p, o, batch.ii, batch.frame)
+    oracle = OracleProblem(load_problem(problem_text("mla")))
+    ov, om, oi = oracle.classify_periodic(p, o, batch.ii, frames.frames, batch.frame)
+    assert np.array_equal(verdict, ov)
+    assert np.array_equal(makespan, om)
+    assert np.array_equal(ii, oi)
+    assert (verdict[whole] == 0).any()

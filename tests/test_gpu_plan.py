@@ -126,3 +126,36 @@ def test_plan_matches_frame_table_kernel_bodies(name):
         assert (plan.kernel, plan.delta) == (("tiles", False) if name == "dag" else ("ring", True))
     for g, p in zip(generic, planned):
         assert np.array_equal(g, p)
+
+
+def test_plan_with_another_frames_index_takes_the_frame_table_path():
+    """A spec_frame that names a frame other than the plan's is detected on the device: every
+    candidate then takes the frame-table path and the results stay exact. An index outside
+    the frames is refused."""
+    import torch
+
+    from tilefoundry_b200.errors import VerifierRuntimeError
+
+    problem = problem_from_json(problem_text("mla"))
+    packed = pack_problem(problem)
+    witness = witness_from_rows(packed, *raw_cases("mla")[0][0])
+    frames, batch, _ = mla_perturbations(packed, witness, 20000, seed=77, producers=shared_producers(problem))
+    with WarpgroupVerifier(packed) as verifier:
+        dev = torch.device("cuda", verifier.device)
+        dframes = verifier.frames_to_device(frames)
+        table = verifier.analyze(dframes)
+        tensors = {k: torch.from_numpy(np.ascontiguousarray(getattr(batch, k))).to(dev)
+                   for k in ("base_prologue", "base_offset", "prologue_delta", "offset_delta", "ii", "frame")}
+        counts = np.bincount(batch.frame, minlength=len(frames))
+        top = int(np.argmax(counts))
+        other = int(np.argsort(counts)[-2])
+        assert frames.frames[other] != frames.frames[top]
+        generic = [t.cpu().numpy() for t in verifier.verify_periodic_device(dframes, table, tensors)]
+        for delta in (True, False):
+            plan = verifier.plan(frames, top, delta=delta)
+            wrong = [t.cpu().numpy() for t in verifier.verify_periodic_device(dframes, table, tensors, plan=plan,
+                                                                               spec_frame=other)]
+            for g, w in zip(generic, wrong):
+                assert np.array_equal(g, w)
+            with pytest.raises(VerifierRuntimeError):
+                verifier.verify_periodic_device(dframes, table, tensors, plan=plan, spec_frame=len(frames))

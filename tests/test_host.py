@@ -222,11 +222,46 @@ def test_closed_problem_is_built_once_per_document_pair():
         calls.append((program, hardware))
         return ("problem", len(calls))
 
-    program, hardware, other = object(), object(), object()
+    from dataclasses import dataclass
+
+    @dataclass(frozen=True)
+    class Document:
+        name: str
+
+    program, hardware, other = Document("program"), Document("hardware"), Document("other")
     first = closed_problem(program, hardware, build)
     assert closed_problem(program, hardware, build) is first
     assert closed_problem(program, other, build) is not first
     assert len(calls) == 2
+
+
+def test_closed_problem_rebuilds_for_mutable_cost_libraries():
+    """A cost library that is not an immutable record may change between calls (the
+    reference accepts any object with lookup() and resources, cost.py:166-175): it is closed
+    again on every call, as the reference does (verify.py:325-331)."""
+    from dataclasses import dataclass
+
+    from tilefoundry_b200.verify import closed_problem
+
+    @dataclass(frozen=True)
+    class Program:
+        name: str
+
+    class Library:  # a stateful provider
+        resources = ()
+
+        def lookup(self, signature):
+            return None
+
+    calls = []
+
+    def build(program, hardware):
+        calls.append(1)
+        return ("problem", len(calls))
+
+    program, library = Program("p"), Library()
+    assert closed_problem(program, library, build) == ("problem", 1)
+    assert closed_problem(program, library, build) == ("problem", 2)
 
 
 def _packed_worker(rank, world, port, queue):
@@ -270,3 +305,27 @@ def test_gather_packed_two_gloo_ranks():
         assert proc.exitcode == 0
     assert verdict == [(i % 26) - 4 for i in range(13)]
     assert makespan == [i * 1000003 + 7 for i in range(13)]
+
+
+def test_periodic_groups_cover_outliers_exactly():
+    """Candidates whose starts leave the int16 range of the batch base are split off into
+    batches of their own; every candidate lands in one batch and its starts are exact."""
+    from tilefoundry_b200.batch import periodic_groups
+
+    rng = np.random.default_rng(4)
+    n, N = 5000, 7
+    prologue = rng.integers(0, 3000, size=(n, N)).astype(np.int64)
+    offset = prologue + rng.integers(0, 500, size=(n, N))
+    out = rng.random(n) < 0.01
+    prologue[out, rng.integers(0, N, size=int(out.sum()))] += rng.choice([-1, 1], size=int(out.sum())) * 100000
+    offset[out] += 150000
+    ii = rng.integers(1, 9000, size=n)
+    frame = rng.integers(0, 3, size=n)
+    groups = periodic_groups(prologue, offset, ii, frame)
+    seen = np.concatenate([take for take, _ in groups])
+    assert sorted(seen.tolist()) == list(range(n))
+    assert len(groups) >= 2 and groups[0][0].size > 0.95 * n
+    for take, batch in groups:
+        assert np.array_equal(batch.base_prologue[None, :] + batch.prologue_delta.T.astype(np.int64), prologue[take])
+        assert np.array_equal(batch.base_offset[None, :] + batch.offset_delta.T.astype(np.int64), offset[take])
+        assert np.array_equal(batch.ii, ii[take]) and np.array_equal(batch.frame, frame[take])

@@ -129,6 +129,7 @@ def frames_struct(arrays: dict, n_frames: int, pointer=lambda a: a.ctypes.data) 
 EXPORTS = {
     "tfv_abi_version": (ctypes.c_int, []),
     "tfv_last_error": (ctypes.c_int, [ctypes.c_char_p, ctypes.c_size_t]),
+    "tfv_set_device_wait_limit": (ctypes.c_int, [ctypes.c_uint64, ctypes.POINTER(ctypes.c_uint64)]),
     "tfv_problem_create": (ctypes.c_int, [ctypes.POINTER(ProblemDesc), ctypes.c_int, ctypes.POINTER(_p)]),
     "tfv_problem_destroy": (ctypes.c_int, [_p]),
     "tfv_frame_table_bytes": (ctypes.c_int, [_p, ctypes.POINTER(Frames), ctypes.POINTER(ctypes.c_size_t)]),

@@ -192,6 +192,53 @@ class PeriodicBatch:
         )
 
 
+def periodic_groups(prologue, offset, ii, frame) -> list[tuple[np.ndarray, PeriodicBatch]]:
+    """Split candidates given by absolute starts into batches whose deltas fit int16.
+
+    ``prologue``/``offset`` are [n, N] starts (any integers), ``ii`` and ``frame`` [n]. The
+    first batch takes every candidate within the int16 range of the per-operation midpoint
+    of all candidates (the base :meth:`PeriodicBatch.from_starts` picks); each further batch
+    is based on the starts of the first candidate left and takes every remaining candidate
+    within range of that base. So a batch with a few outliers becomes one main batch plus a
+    batch per cluster of outliers, and every candidate gets a verdict. A base outside
+    (-2^28, 2^28) makes its batch's candidates report TFV_CLASS_OUT_OF_RANGE, as the kernels
+    do for any base out of that domain. Returns ``(candidate indices, batch)`` pairs that
+    cover every candidate once, in increasing index order within each batch.
+    """
+    prologue = np.asarray(prologue, dtype=np.int64)
+    offset = np.asarray(offset, dtype=np.int64)
+    ii = np.asarray(ii, dtype=np.int64)
+    frame = np.asarray(frame, dtype=np.int64)
+    n = prologue.shape[0]
+    left = np.arange(n)
+    groups: list[tuple[np.ndarray, PeriodicBatch]] = []
+    first = True
+    while left.size:
+        p, o = prologue[left], offset[left]
+        if first:
+            bp = (p.min(axis=0) + p.max(axis=0)) // 2
+            bo = (o.min(axis=0) + o.max(axis=0)) // 2
+        else:  # the first remaining candidate fits its own base
+            bp, bo = p[0].copy(), o[0].copy()
+        fits = ((np.abs(p - bp[None, :]) <= 32767).all(axis=1) & (np.abs(o - bo[None, :]) <= 32767).all(axis=1))
+        first = False
+        if not fits.any():
+            continue
+        take = left[fits]
+        clip = lambda base: np.clip(base, -(2**31), 2**31 - 1)  # noqa: E731 (int32 storage of any base)
+        dp = (prologue[take] - bp[None, :]).T
+        dq = (offset[take] - bo[None, :]).T
+        groups.append((take, PeriodicBatch(
+            base_prologue=clip(bp).astype(np.int32), base_offset=clip(bo).astype(np.int32),
+            prologue_delta=np.ascontiguousarray(dp.astype(np.int16)),
+            offset_delta=np.ascontiguousarray(dq.astype(np.int16)),
+            ii=np.ascontiguousarray(np.clip(ii[take], -(2**31), 2**31 - 1).astype(np.int32)),
+            frame=np.ascontiguousarray(frame[take].astype(np.int32)),
+        )))
+        left = left[~fits]
+    return groups
+
+
 @dataclass
 class RowsBatch:
     """Explicit timing rows [n, I, N] plus the host-side facts the dense layout cannot hold."""
@@ -288,4 +335,4 @@ def pack_rows(packed: PackedProblem, frames: FrameSet, schedules) -> RowsBatch:
     return RowsBatch(start, issue_end, completion, frame, row_flags, override, override_makespan, override_ii)
 
 
-__all__ = ["FrameSet", "PeriodicBatch", "RowsBatch", "pack_rows", "schedule_parts"]
+__all__ = ["FrameSet", "PeriodicBatch", "RowsBatch", "pack_rows", "periodic_groups", "schedule_parts"]

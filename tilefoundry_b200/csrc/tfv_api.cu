@@ -4,6 +4,7 @@
 #include <cstdarg>
 #include <cstdio>
 #include <cstring>
+#include <mutex>
 #include <string>
 #include <vector>
 
@@ -16,6 +17,15 @@ struct tfv_problem {
     void* buffer = nullptr;  // one device allocation holding every table
     tfv::DevProblem dev{};
     std::vector<int> issue_h, latency_h;  // host copies for generated code
+    // tfv_verify_periodic_host keeps its device workspace, two streams and an event here
+    // from its first call on (the workspace grows to the largest call), so that a call
+    // allocates and creates nothing once the problem has served one of its size; calls on
+    // one problem are serialised by host_mutex
+    std::mutex host_mutex;
+    char* host_ws = nullptr;
+    size_t host_ws_bytes = 0;
+    cudaStream_t host_streams[2] = {nullptr, nullptr};
+    cudaEvent_t host_ready = nullptr;
 };
 
 namespace {
@@ -95,11 +105,22 @@ int check_results(const tfv_results* r) {
     return TFV_OK;
 }
 
-// The TMA-fed kernel when its layout preconditions hold, else the plain-load kernel.
+// The large-body kernel (one warp per candidate) for bodies of kLargeMinOps operations or
+// more, the TMA-fed kernel when its layout preconditions hold, else the plain-load kernel.
+// The batch's sync programs must be compiled in the form the chosen kernel reads
+// (compile_sync_programs below).
 cudaError_t launch_periodic(const tfv_problem* p, const tfv::DevFrames& f, tfv::FrameTable t, const tfv::DevPeriodic& b,
                             tfv::DevResults r, cudaStream_t s) {
+    if (tfv::periodic_large_supported(p->dev, b)) return tfv::launch_verify_periodic_large(p->dev, f, t, b, r, p->sm_count, s);
     if (tfv::periodic_tma_supported(p->dev, b)) return tfv::launch_verify_periodic_tma(p->dev, f, t, b, r, p->sm_count, s);
     return tfv::launch_verify_periodic(p->dev, f, t, b, r, p->sm_count, s);
+}
+
+// Sync programs of a batch in the form launch_periodic's kernel for it reads.
+cudaError_t compile_sync_programs(const tfv_problem* p, const tfv::DevFrames& f, tfv::FrameTable t,
+                                  const tfv::DevPeriodic& b, cudaStream_t s) {
+    return tfv::launch_compile_sync_programs(p->dev, f, t, b.base_prologue, b.base_offset, p->sm_count, s,
+                                             tfv::periodic_large_supported(p->dev, b));
 }
 
 tfv::FrameTableShape shape_of(const tfv_problem* p, const tfv_frames* f) {
@@ -132,7 +153,7 @@ int verify_periodic_sweep(const tfv_problem* p, const tfv_frames* frames, void* 
     const tfv::DevFrames df = to_dev(*frames);
     const tfv::FrameTable view = tfv::frame_table_view(table, shape_of(p, frames));
     const cudaStream_t s = static_cast<cudaStream_t>(stream);
-    cudaError_t e = tfv::launch_compile_sync_programs(p->dev, df, view, b->base_prologue, b->base_offset, p->sm_count, s);
+    cudaError_t e = compile_sync_programs(p, df, view, db, s);
     if (e == cudaSuccess) e = launch_periodic(p, df, view, db, dr, s);
     if (e != cudaSuccess) return cuda_fail(e, "verify_periodic launch");
     return TFV_OK;
@@ -149,6 +170,12 @@ int tfv_last_error(char* buffer, size_t size) {
     const size_t n = std::min(size - 1, g_last_error.size());
     memcpy(buffer, g_last_error.data(), n);
     buffer[n] = '\0';
+    return TFV_OK;
+}
+
+int tfv_set_device_wait_limit(uint64_t ns, uint64_t* previous) {
+    if (previous) *previous = tfv::device_wait_ns();
+    tfv::set_device_wait_ns(ns);
     return TFV_OK;
 }
 
@@ -317,6 +344,14 @@ int tfv_problem_create(const tfv_problem_desc* d, int device, tfv_problem** out)
 int tfv_problem_destroy(tfv_problem* p) {
     if (!p) return TFV_OK;
     DeviceGuard guard(p->device);
+    for (auto& hs : p->host_streams)
+        if (hs) {
+            cudaStreamSynchronize(hs);
+            cudaStreamDestroy(hs);
+        }
+    if (p->host_ready) cudaEventDestroy(p->host_ready);
+    if (p->host_ws) cudaFree(p->host_ws);
+    cudaGetLastError();  // a teardown call's error must not surface at a later launch check
     cudaError_t e = cudaFree(p->buffer);
     delete p;
     if (e != cudaSuccess) return cuda_fail(e, "tfv_problem_destroy");
@@ -413,30 +448,27 @@ int tfv_verify_periodic_host(const tfv_problem* p, const tfv_frames* hf, const t
 
     DeviceGuard guard(p->device);
     if (!guard.ok()) return fail(TFV_ERR_CUDA, "cannot select device %d", p->device);
+    std::lock_guard<std::mutex> lock(*const_cast<std::mutex*>(&p->host_mutex));
+    tfv_problem* mp = const_cast<tfv_problem*>(p);  // the host-entry workspace is the handle's
 
     const long long chunk = std::min<long long>(n, 1LL << 21);
     const long long pitch = (chunk + 7) & ~7LL;  // device rows keep 16-byte strides for TMA
     const tfv::FrameTableShape shape{F, N, S, E};
     const size_t table_bytes = tfv::frame_table_bytes(shape);
-    cudaStream_t streams[2] = {nullptr, nullptr};
-    cudaEvent_t ready = nullptr;
-    char* ws = nullptr;
     cudaError_t e = cudaSuccess;
     auto bail = [&](cudaError_t err, const char* where) {
-        for (auto& s : streams)
+        for (auto& s : mp->host_streams)
             if (s) cudaStreamSynchronize(s);
-        if (ws) cudaFree(ws);
-        for (auto& s : streams)
-            if (s) cudaStreamDestroy(s);
-        if (ready) cudaEventDestroy(ready);
         return cuda_fail(err, where);
     };
-    for (auto& s : streams) {
-        e = cudaStreamCreateWithFlags(&s, cudaStreamNonBlocking);
+    for (auto& s : mp->host_streams) {
+        if (!s) e = cudaStreamCreateWithFlags(&s, cudaStreamNonBlocking);
         if (e != cudaSuccess) return bail(e, "stream create");
     }
-    e = cudaEventCreateWithFlags(&ready, cudaEventDisableTiming);
+    if (!mp->host_ready) e = cudaEventCreateWithFlags(&mp->host_ready, cudaEventDisableTiming);
     if (e != cudaSuccess) return bail(e, "event create");
+    cudaStream_t* streams = mp->host_streams;
+    cudaEvent_t ready = mp->host_ready;
 
     // Workspace: frames, sync sets, frame table, base times, then two chunk slots.
     auto up = [](size_t x) { return (x + 255) & ~static_cast<size_t>(255); };
@@ -446,8 +478,15 @@ int tfv_verify_periodic_host(const tfv_problem* p, const tfv_frames* hf, const t
     const size_t sz_d = up(sizeof(int16_t) * N * pitch), sz_c = up(sizeof(int) * chunk);
     const size_t fixed = sz_lp + 3 * sz_f + sz_so + sz_se + sz_tab + 2 * sz_base;
     const size_t slot = 2 * sz_d + 2 * sz_c + 3 * sz_c;
-    e = cudaMalloc(&ws, fixed + 2 * slot);
-    if (e != cudaSuccess) return bail(e, "workspace alloc");
+    if (mp->host_ws_bytes < fixed + 2 * slot) {  // grow (the previous call's work is complete)
+        if (mp->host_ws) cudaFree(mp->host_ws);
+        mp->host_ws = nullptr;
+        mp->host_ws_bytes = 0;
+        e = cudaMalloc(&mp->host_ws, fixed + 2 * slot);
+        if (e != cudaSuccess) return bail(e, "workspace alloc");
+        mp->host_ws_bytes = fixed + 2 * slot;
+    }
+    char* ws = mp->host_ws;
     char* cur = ws;
     auto take = [&](size_t bytes) {
         char* at = cur;
@@ -478,8 +517,11 @@ int tfv_verify_periodic_host(const tfv_problem* p, const tfv_frames* hf, const t
     if (e != cudaSuccess) return bail(e, "frame upload");
     tfv::DevFrames df{F, d_lp, d_lc, d_fl, d_ss, S, E, d_so, d_se};
     tfv::FrameTable tab = tfv::frame_table_view(d_tab, shape);
+    // every chunk has the same layout (pitch, 256-byte aligned slots): one program form serves all
+    const tfv::DevPeriodic layout{chunk, pitch, d_bp, d_bo, reinterpret_cast<const int16_t*>(ws + fixed),
+                                  reinterpret_cast<const int16_t*>(ws + fixed), nullptr, nullptr, 1, chunk};
     e = tfv::launch_analyze_frames(p->dev, df, tab, p->sm_count, s0);
-    if (e == cudaSuccess) e = tfv::launch_compile_sync_programs(p->dev, df, tab, d_bp, d_bo, p->sm_count, s0);
+    if (e == cudaSuccess) e = compile_sync_programs(p, df, tab, layout, s0);
     if (e != cudaSuccess) return bail(e, "analyze_frames launch");
     e = cudaEventRecord(ready, s0);
     if (e == cudaSuccess) e = cudaStreamWaitEvent(streams[1], ready, 0);
@@ -529,13 +571,10 @@ int tfv_verify_periodic_host(const tfv_problem* p, const tfv_frames* hf, const t
         if (e == cudaSuccess) e = cudaMemcpyAsync(hr->ii + c0, sl.iio, sizeof(int) * len, cudaMemcpyDeviceToHost, s);
         if (e != cudaSuccess) return bail(e, "result download");
     }
-    for (auto& s : streams) {
-        e = cudaStreamSynchronize(s);
+    for (int k = 0; k < 2; ++k) {
+        e = cudaStreamSynchronize(streams[k]);
         if (e != cudaSuccess) return bail(e, "synchronize");
     }
-    cudaFree(ws);
-    for (auto& s : streams) cudaStreamDestroy(s);
-    cudaEventDestroy(ready);
     return TFV_OK;
 }
 
@@ -592,7 +631,7 @@ int tfv_internal_periodic_with_table(const tfv_problem* p, const tfv_frames* fra
     const cudaStream_t s = static_cast<cudaStream_t>(stream);
     cudaError_t e = cudaSuccess;
     if (analyze) e = tfv::launch_analyze_frames(p->dev, df, view, p->sm_count, s);
-    if (e == cudaSuccess) e = tfv::launch_compile_sync_programs(p->dev, df, view, b->base_prologue, b->base_offset, p->sm_count, s);
+    if (e == cudaSuccess) e = compile_sync_programs(p, df, view, db, s);
     if (e == cudaSuccess) e = launch_periodic(p, df, view, db, dr, s);
     if (e != cudaSuccess) return cuda_fail(e, "verify_periodic_static launch");
     return TFV_OK;

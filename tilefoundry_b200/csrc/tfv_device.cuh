@@ -81,8 +81,10 @@ struct DevFrames {
 //                               frames reads a few cache lines per position, not one per frame)
 //   uint16 lane_len[F][16]      length of each lane's run in order[]
 //   int2   set_meta[S]          {program length, class of the first statically failing edge}
-//   int4   set_prog[E]          per sync edge, base starts folded in (written per batch), in
-//                               the TMA tile's byte offsets (rows of kTmaTile int16 values):
+//   int4   set_prog[E]          per sync edge, base starts folded in (written per batch). The
+//                               large-body kernel reads the index form {a | b << 16, distance,
+//                               w0, w1}; the tile kernels read byte offsets into the TMA tile
+//                               (rows of kTmaTile int16 values):
 //                               {a_row | b_row << 16, x_row | distance << 17, w0, w1}
 //                               a_row/b_row: offsets of a's and b's prologue rows; x_row: the
 //                               row instance 0 reads for b (prologue row for distance 0, offset
@@ -221,6 +223,21 @@ struct DevResults {
     int* ii;
 };
 
+// Large-body kernel (tfv_large.cu): one warp per candidate for bodies of kLargeMinOps
+// operations or more. A CTA has `producers` warps streaming tiles of 8 * halves candidates
+// into `groups` groups of per-candidate buffers (nstride words each) and `consumers` warps
+// verifying one candidate at a time.
+constexpr int kLargeMinOps = 128;
+constexpr int kLargeProducers = 4;  // one warp's 128-bit loads in flight cannot feed 16 consumer warps
+constexpr int kLargeMaxThreads = 32 * (kLargeProducers + 16);
+struct LargeShape {
+    int halves, groups, producers, consumers, nstride, n_tiles;
+    unsigned long long wait_ns;  // a bounded wait gives up after this long (device_wait_ns)
+};
+// Words of a candidate buffer: the operations rounded up to 4, plus 2, so that the
+// transposed stores of two half-tiles fall into disjoint banks.
+__host__ __device__ inline int large_nstride(int n_ops) { return ((n_ops + 3) & ~3) + 2; }
+
 #ifndef __CUDACC_RTC__
 // Launchers (tfv_kernels.cu). Each returns the cudaError_t of its launch.
 // With keep != nullptr the analysis also exports each frame's sync set (sync.py:21-62):
@@ -232,9 +249,18 @@ cudaError_t launch_analyze_frames(const DevProblem& p, const DevFrames& f, Frame
 cudaError_t launch_verify_periodic(const DevProblem& p, const DevFrames& f, FrameTable t,
                                    const DevPeriodic& b, DevResults r, int sm_count,
                                    cudaStream_t stream);
-// Per-batch sync programs: the base starts folded into every edge of every set.
+// Per-batch sync programs: the base starts folded into every edge of every set, in the
+// index form (index_form, read by the large-body kernel) or the TMA-tile form.
 cudaError_t launch_compile_sync_programs(const DevProblem& p, const DevFrames& f, FrameTable t, const int* base_prologue,
-                                         const int* base_offset, int sm_count, cudaStream_t stream);
+                                         const int* base_offset, int sm_count, cudaStream_t stream,
+                                         bool index_form = false);
+// Large-body kernel: needs N >= kLargeMinOps, 16-byte aligned delta arrays, op_stride % 8 == 0
+// and at most kWarpWindowCap windows per resource; its sync programs are in the index form.
+bool periodic_large_supported(const DevProblem& p, const DevPeriodic& b);
+size_t large_smem_bytes(const DevProblem& p, int halves, int groups, int consumers);
+bool large_shape(const DevProblem& p, int optin, LargeShape& shape);
+cudaError_t launch_verify_periodic_large(const DevProblem& p, const DevFrames& f, FrameTable t, const DevPeriodic& b,
+                                         DevResults r, int sm_count, cudaStream_t stream);
 // TMA variant: needs 16-byte aligned delta arrays, op_stride % 8 == 0 and N <= 256.
 bool periodic_tma_supported(const DevProblem& p, const DevPeriodic& b);
 cudaError_t launch_verify_periodic_tma(const DevProblem& p, const DevFrames& f, FrameTable t,
@@ -245,9 +271,18 @@ cudaError_t launch_verify_rows(const DevProblem& p, const DevFrames& f, FrameTab
                                cudaStream_t stream);
 
 // Shared-memory footprint checks used by the host before launching.
-cudaError_t launch_delta_frames(const DevProblem& p, const DevFrames& f, FrameTable t, int spec_frame,
+cudaError_t launch_delta_frames(const DevProblem& p, const DevFrames& f, FrameTable t, const int* spec_frame,
                                 const int* base_prologue, const int* base_offset, DeltaTable d, int sm_count,
                                 cudaStream_t stream);
+// Writes spec to *out when frame spec has the lanes (sig_lane_pos [N]) and sync program
+// (sig_edges [sig_len][3]) a plan was generated for, else -1.
+cudaError_t launch_check_spec_frame(const DevProblem& p, const DevFrames& f, int spec, const uint16_t* sig_lane_pos,
+                                    const int* sig_edges, int sig_len, int* out, cudaStream_t stream);
+
+// Time after which a bounded wait of the ring and large-body kernels gives up (1 s unless a
+// caller changed it with tfv_set_device_wait_limit).
+unsigned long long device_wait_ns();
+void set_device_wait_ns(unsigned long long ns);
 
 size_t analyze_smem_bytes(int n_ops, int lanes);
 int periodic_tile(int n_ops);

@@ -371,20 +371,20 @@ std::string generate(const FrameInput& in, const int* issue, const int* lat, int
     if (ring_warps > 0) {
         src += "extern \"C\" __global__ void __launch_bounds__(" + I2S(32 * (ring_warps + 1)) + ", 1) tfv_spec_ring(\n";
         src += "    tfv::DevProblem p, tfv::DevFrames fr, tfv::FrameTable ft, tfv::DevPeriodic b, tfv::DevResults out, int n_tiles,\n";
-        src += "    const __grid_constant__ CUtensorMap map_p, const __grid_constant__ CUtensorMap map_o, int spec_frame,\n";
-        src += "    tfv::DeltaTable dt, int slots) {\n";
+        src += "    const __grid_constant__ CUtensorMap map_p, const __grid_constant__ CUtensorMap map_o,\n";
+        src += "    const int* spec_frame, tfv::DeltaTable dt, int slots, unsigned long long wait_ns) {\n";
         src += "    tfv::tma_ring_body<" + I2S(body_rows) + ", Spec, " + I2S(ring_warps) +
-               ">(p, fr, ft, b, out, n_tiles, &map_p, &map_o, spec_frame, dt, slots);\n";
+               ">(p, fr, ft, b, out, n_tiles, &map_p, &map_o, *spec_frame, dt, slots, wait_ns);\n";
         src += "}\n";
         return src;
     }
     src += "extern \"C\" __global__ void __launch_bounds__(" + I2S(tfv::kTmaTile * shape.super / shape.passes) +
            ") tfv_spec_kernel(\n";
     src += "    tfv::DevProblem p, tfv::DevFrames fr, tfv::FrameTable ft, tfv::DevPeriodic b, tfv::DevResults out, int n_tiles,\n";
-    src += "    const __grid_constant__ CUtensorMap map_p, const __grid_constant__ CUtensorMap map_o, int spec_frame,\n";
-    src += "    tfv::DeltaTable dt) {\n";
+    src += "    const __grid_constant__ CUtensorMap map_p, const __grid_constant__ CUtensorMap map_o,\n";
+    src += "    const int* spec_frame, tfv::DeltaTable dt) {\n";
     src += "    tfv::tma_verify_body<" + I2S(body_rows) +
-           ", false, Spec>(p, fr, ft, b, out, n_tiles, &map_p, &map_o, spec_frame, dt);\n";
+           ", false, Spec>(p, fr, ft, b, out, n_tiles, &map_p, &map_o, *spec_frame, dt);\n";
     src += "}\n";
     return src;
 }
@@ -420,6 +420,10 @@ struct tfv_plan {
     size_t smem = 0;
     int per_sm = 0;
     std::string source;
+    // the plan frame's signature on the device: [spec frame checked per call (int)] [lane_pos
+    // row N x u16, padded to 4 bytes] [sync program edges sig_len x 3 int]
+    void* sig = nullptr;
+    int sig_len = 0;
 };
 
 namespace {
@@ -590,6 +594,26 @@ int tfv_plan_create_with(const tfv_problem* p, const tfv_frames* host_frames, in
         return tfv_internal_cuda_fail(e, "tfv_plan_create");
     }
     plan->n_consts = static_cast<int>(sym_bytes / sizeof(int));
+    {  // the plan frame's signature, checked against the caller's frame on every call
+        const size_t lp_bytes = (sizeof(uint16_t) * d.n_ops + 3) & ~static_cast<size_t>(3);
+        std::vector<int> edges;
+        for (size_t k = 0; k < in.ea.size(); ++k) {
+            const int e = host_frames->sync_offsets[host_frames->sync_set[frame]] + static_cast<int>(k);
+            for (int c = 0; c < 3; ++c) edges.push_back(host_frames->sync_edges[3 * e + c]);
+        }
+        plan->sig_len = static_cast<int>(in.ea.size());
+        const size_t bytes = sizeof(int) + lp_bytes + sizeof(int) * edges.size();
+        std::vector<char> image(bytes, 0);
+        std::memcpy(image.data() + sizeof(int), host_frames->lane_pos + static_cast<size_t>(frame) * d.n_ops,
+                    sizeof(uint16_t) * d.n_ops);
+        if (!edges.empty()) std::memcpy(image.data() + sizeof(int) + lp_bytes, edges.data(), sizeof(int) * edges.size());
+        e = cudaMalloc(&plan->sig, bytes);
+        if (e == cudaSuccess) e = cudaMemcpy(plan->sig, image.data(), bytes, cudaMemcpyHostToDevice);
+        if (e != cudaSuccess) {
+            tfv_plan_destroy(plan);
+            return tfv_internal_cuda_fail(e, "tfv_plan_create");
+        }
+    }
     e = cudaStreamCreateWithFlags(&plan->side, cudaStreamNonBlocking);
     if (e == cudaSuccess) e = cudaEventCreateWithFlags(&plan->fork, cudaEventDisableTiming);
     if (e == cudaSuccess) e = cudaEventCreateWithFlags(&plan->join, cudaEventDisableTiming);
@@ -607,11 +631,13 @@ int tfv_plan_destroy(tfv_plan* plan) {
     if (plan->side) cudaStreamSynchronize(plan->side);
     if (plan->consts_scratch) cudaFree(plan->consts_scratch);
     if (plan->delta_buf) cudaFree(plan->delta_buf);
+    if (plan->sig) cudaFree(plan->sig);
     if (plan->fork) cudaEventDestroy(plan->fork);
     if (plan->join) cudaEventDestroy(plan->join);
     if (plan->side) cudaStreamDestroy(plan->side);
     if (plan->module) driver().unload(plan->module);
     delete plan;
+    cudaGetLastError();  // a teardown call's error must not surface at a later launch check
     return TFV_OK;
 }
 
@@ -637,6 +663,8 @@ int tfv_verify_periodic_planned(tfv_plan* plan, const tfv_frames* frames, void* 
         return tfv_internal_fail(TFV_ERR_INVALID_ARGUMENT, "frame table missing or too small");
     if (!b->base_prologue || !b->base_offset || !b->prologue_delta || !b->offset_delta || !b->ii || !b->frame)
         return tfv_internal_fail(TFV_ERR_INVALID_ARGUMENT, "batch arrays must not be NULL");
+    if (spec_frame < 0 || spec_frame >= frames->n_frames)
+        return tfv_internal_fail(TFV_ERR_INVALID_ARGUMENT, "spec_frame must index one of the frames");
     CurrentDevice current(plan->device);
     cudaError_t e = current.status();
     if (e != cudaSuccess) return tfv_internal_cuda_fail(e, "tfv_verify_periodic_planned");
@@ -670,6 +698,13 @@ int tfv_verify_periodic_planned(tfv_plan* plan, const tfv_frames* frames, void* 
     e = cudaEventRecord(plan->join, plan->side);
     if (e == cudaSuccess)
         e = tfv::launch_compile_sync_programs(d, df, view, b->base_prologue, b->base_offset, tfv_internal_sm_count(p), s);
+    // the frame the generated code serves: spec_frame if it has the plan frame's lanes and
+    // sync program, else -1 (every candidate then takes the frame-table path)
+    int* spec_dev = static_cast<int*>(plan->sig);
+    const size_t lp_bytes = (sizeof(uint16_t) * d.n_ops + 3) & ~static_cast<size_t>(3);
+    const uint16_t* sig_lp = reinterpret_cast<const uint16_t*>(static_cast<char*>(plan->sig) + sizeof(int));
+    const int* sig_edges = reinterpret_cast<const int*>(static_cast<char*>(plan->sig) + sizeof(int) + lp_bytes);
+    if (e == cudaSuccess) e = tfv::launch_check_spec_frame(d, df, spec_frame, sig_lp, sig_edges, plan->sig_len, spec_dev, s);
     if (e != cudaSuccess) return tfv_internal_cuda_fail(e, "tfv_verify_periodic_planned");
     // delta verification: every frame relative to spec_frame, after the sync programs
     tfv::DeltaTable dt{};
@@ -684,7 +719,7 @@ int tfv_verify_periodic_planned(tfv_plan* plan, const tfv_frames* frames, void* 
             plan->delta_bytes = need;
         }
         dt = tfv::delta_table_view(plan->delta_buf, frames->n_frames, plan->lane_words, plan->sync_words);
-        e = tfv::launch_delta_frames(d, df, view, spec_frame, b->base_prologue, b->base_offset, dt,
+        e = tfv::launch_delta_frames(d, df, view, spec_dev, b->base_prologue, b->base_offset, dt,
                                      tfv_internal_sm_count(p), s);
         if (e != cudaSuccess) return tfv_internal_cuda_fail(e, "tfv_verify_periodic_planned");
     }
@@ -697,7 +732,8 @@ int tfv_verify_periodic_planned(tfv_plan* plan, const tfv_frames* frames, void* 
     int n_tiles = static_cast<int>(tiles);
     int slots = plan->slots;
     tfv::DevProblem dp = d;
-    void* args[] = {&dp, &df, &view, &db, &dr, &n_tiles, &map_p, &map_o, &spec_frame, &dt, &slots};
+    unsigned long long wait_ns = tfv::device_wait_ns();
+    void* args[] = {&dp, &df, &view, &db, &dr, &n_tiles, &map_p, &map_o, &spec_dev, &dt, &slots, &wait_ns};
     cr = drv.launch(plan->function, grid, 1, 1, plan->threads, 1, 1, static_cast<unsigned>(plan->smem),
                     reinterpret_cast<CUstream>(s), args, nullptr);
     if (cr != CUDA_SUCCESS) return tfv_internal_fail(TFV_ERR_CUDA, "launching the frame-specialised kernel failed");

@@ -25,6 +25,7 @@
 //       the first relation whose path is absent; its class is 17 if its timing fails at
 //       instance 0 (checked first, verify.py:311) and 18 otherwise.
 #include <algorithm>
+#include <atomic>
 #include <climits>
 #include <cstdint>
 
@@ -47,6 +48,13 @@ __device__ __forceinline__ int pos_of(uint16_t v) { return v & TFV_POS_MASK; }
 // ---------------------------------------------------------------------------------------
 // Frame analysis
 // ---------------------------------------------------------------------------------------
+
+namespace {
+std::atomic<unsigned long long> g_device_wait_ns{1000000000ULL};
+}  // namespace
+
+unsigned long long device_wait_ns() { return g_device_wait_ns.load(std::memory_order_relaxed); }
+void set_device_wait_ns(unsigned long long ns) { g_device_wait_ns.store(ns, std::memory_order_relaxed); }
 
 size_t analyze_smem_bytes(int n, int lanes) {
     size_t b = 0;
@@ -445,10 +453,12 @@ cudaError_t launch_analyze_frames(const DevProblem& p, const DevFrames& f, Frame
 //   instance 0:      start(d, b) - completion(0, a) = w0 + delta(b) - delta_prologue(a) + d * ii
 //   instances >= 1:  start(i+d, b) - completion(i, a) = w1 + delta_offset(b) - delta_offset(a) + d * ii
 // where delta(b) is b's prologue delta for d == 0 and its offset delta otherwise. Entries
-// address the TMA tile directly (see set_prog in tfv_device.cuh); they are only consumed by
-// the TMA kernel, which requires N <= 256 and iterations <= kMaxProgDistance.
+// address the TMA tile directly (see set_prog in tfv_device.cuh), for the TMA kernels
+// (N <= 256, iterations <= kMaxProgDistance), or name the operations (index_form), for the
+// large-body kernel.
 __global__ void __launch_bounds__(32) compile_sync_programs_kernel(DevProblem p, DevFrames fr, FrameTable ft,
-                                                                     const int* base_prologue, const int* base_offset) {
+                                                                     const int* base_prologue, const int* base_offset,
+                                                                     bool index_form) {
     const int N = p.n_ops, I = p.iterations;
     const int lane = threadIdx.x;
     const int total = min(fr.sync_offsets[fr.n_sync_sets], fr.n_sync_edges);
@@ -486,6 +496,10 @@ __global__ void __launch_bounds__(32) compile_sync_programs_kernel(DevProblem p,
             const int lat = p.latency[a];
             const int w0 = (d == 0 ? base_prologue[b] : base_offset[b]) - base_prologue[a] - lat;
             const int w1 = I - d >= 2 ? base_offset[b] - base_offset[a] - lat : kNoBodyWeight;
+            if (index_form) {
+                ft.set_prog[k] = make_int4(a | (b << 16), d, w0, w1);
+                continue;
+            }
             const int a_row = a * kTmaRowBytes, b_row = b * kTmaRowBytes;
             const int x_row = d == 0 ? b_row : to_rows + b_row;
             ft.set_prog[k] = make_int4(a_row | (b_row << 16), x_row | (min(d, kMaxProgDistance) << 17), w0, w1);
@@ -513,10 +527,11 @@ __device__ __forceinline__ unsigned shifted_order(unsigned bits, int n) {
     return n <= 0 ? 0u : __brev(bits) >> (32 - n);
 }
 
-__global__ void __launch_bounds__(128) delta_frames_kernel(DevProblem p, DevFrames fr, FrameTable ft, int m,
+__global__ void __launch_bounds__(128) delta_frames_kernel(DevProblem p, DevFrames fr, FrameTable ft, const int* m_ptr,
                                                            const int* base_prologue, const int* base_offset,
                                                            DeltaTable dt) {
     const int N = p.n_ops, I = p.iterations;
+    const int m = *m_ptr;  // the checked specialised frame, -1 when the caller's did not match
     const int lane = threadIdx.x & 31;
     const int warps = blockDim.x >> 5;
     const int KW = dt.lane_words + dt.sync_words;
@@ -624,7 +639,7 @@ __global__ void __launch_bounds__(128) delta_frames_kernel(DevProblem p, DevFram
     }
 }
 
-cudaError_t launch_delta_frames(const DevProblem& p, const DevFrames& f, FrameTable t, int spec_frame,
+cudaError_t launch_delta_frames(const DevProblem& p, const DevFrames& f, FrameTable t, const int* spec_frame,
                                 const int* base_prologue, const int* base_offset, DeltaTable d, int sm_count,
                                 cudaStream_t stream) {
     if (f.n_frames <= 0) return cudaSuccess;
@@ -634,11 +649,52 @@ cudaError_t launch_delta_frames(const DevProblem& p, const DevFrames& f, FrameTa
     return cudaGetLastError();
 }
 
+// One warp: whether the caller's frame `spec` has the lanes and the sync program a plan's
+// code was generated for (sig_lane_pos [N]; sig_edges [sig_len][3], the set's edges before its
+// first static failure). Writes spec to *out when it has, else -1, so that a frame index that
+// names another frame makes every candidate take the frame-table path.
+__global__ void __launch_bounds__(32) check_spec_frame_kernel(DevProblem p, DevFrames fr, int spec,
+                                                               const uint16_t* sig_lane_pos, const int* sig_edges,
+                                                               int sig_len, int* out) {
+    const int N = p.n_ops, I = p.iterations;
+    const int lane = threadIdx.x;
+    bool ok = spec >= 0 && spec < fr.n_frames;
+    int e0 = 0, e1 = 0;
+    if (ok) {
+        const int set = fr.sync_set[spec];
+        ok = set >= 0 && set < fr.n_sync_sets;
+        if (ok) {
+            e0 = fr.sync_offsets[set];
+            e1 = fr.sync_offsets[set + 1];
+            ok = e0 >= 0 && e1 >= e0 && e1 <= fr.n_sync_edges && e1 - e0 >= sig_len;
+        }
+    }
+    if (ok) {
+        bool same = true;
+        for (int a = lane; a < N; a += 32) same &= fr.lane_pos[static_cast<size_t>(spec) * N + a] == sig_lane_pos[a];
+        for (int k = lane; k < sig_len; k += 32)
+            for (int c = 0; c < 3; ++c) same &= fr.sync_edges[3 * (e0 + k) + c] == sig_edges[3 * k + c];
+        if (lane == 0 && e0 + sig_len < e1) {  // the program must end where the signature's does
+            const int a = fr.sync_edges[3 * (e0 + sig_len)], b = fr.sync_edges[3 * (e0 + sig_len) + 1];
+            const int d = fr.sync_edges[3 * (e0 + sig_len) + 2];
+            same &= a < 0 || b < 0 || d >= I;
+        }
+        ok = __all_sync(kFull, same);
+    }
+    if (lane == 0) *out = ok ? spec : -1;
+}
+
+cudaError_t launch_check_spec_frame(const DevProblem& p, const DevFrames& f, int spec, const uint16_t* sig_lane_pos,
+                                    const int* sig_edges, int sig_len, int* out, cudaStream_t stream) {
+    check_spec_frame_kernel<<<1, 32, 0, stream>>>(p, f, spec, sig_lane_pos, sig_edges, sig_len, out);
+    return cudaGetLastError();
+}
+
 cudaError_t launch_compile_sync_programs(const DevProblem& p, const DevFrames& f, FrameTable t, const int* base_prologue,
-                                         const int* base_offset, int sm_count, cudaStream_t stream) {
+                                         const int* base_offset, int sm_count, cudaStream_t stream, bool index_form) {
     if (f.n_sync_sets <= 0) return cudaSuccess;
     const int grid = min(f.n_sync_sets, sm_count * 16);
-    compile_sync_programs_kernel<<<grid, 32, 0, stream>>>(p, f, t, base_prologue, base_offset);
+    compile_sync_programs_kernel<<<grid, 32, 0, stream>>>(p, f, t, base_prologue, base_offset, index_form);
     return cudaGetLastError();
 }
 
@@ -814,7 +870,7 @@ __global__ void verify_periodic_kernel(DevProblem p, DevFrames fr, FrameTable ft
     int* bo_s = psm + 3 * N;
     int* Ps = psm + 4 * N;
     int* Os = Ps + static_cast<size_t>(N) * T;
-    int4* scratch = reinterpret_cast<int4*>(Os + static_cast<size_t>(N) * T) + (t >> 5) * 2 * p.res_max_windows;
+    int4* scratch = reinterpret_cast<int4*>(Os + static_cast<size_t>(N) * T) + (t >> 5) * warp_scratch_records(p);
     const bool warp_path = warp_resources_used(p);
     for (int a = t; a < N; a += T) {
         issue_s[a] = p.issue[a];
@@ -873,7 +929,7 @@ __global__ void __launch_bounds__(128) verify_periodic_global_kernel(DevProblem 
     int* lat_s = gsm + N;
     int* bp_s = gsm + 2 * N;
     int* bo_s = gsm + 3 * N;
-    int4* scratch = reinterpret_cast<int4*>(gsm + 4 * N) + (threadIdx.x >> 5) * 2 * p.res_max_windows;
+    int4* scratch = reinterpret_cast<int4*>(gsm + 4 * N) + (threadIdx.x >> 5) * warp_scratch_records(p);
     const bool warp_path = warp_resources_used(p);
     for (int a = threadIdx.x; a < N; a += blockDim.x) {
         issue_s[a] = p.issue[a];

@@ -390,7 +390,7 @@ __device__ __forceinline__ void tma_verify_body(const DevProblem& p, const DevFr
     // capacity-check records of this warp (warp path only)
     const bool warp_path = warp_resources_used(p);
     // per-warp records exist only on the warp path (the same size tma_smem_bytes counts)
-    const int records = warp_path ? 2 * p.res_max_windows : 0;
+    const int records = warp_path ? warp_scratch_records(p) : 0;
     int4* scratch = reinterpret_cast<int4*>(bar + 2) + (t >> 5) * records;
     // tile permutation of the specialised kernel, after every warp's records
     int* perm = reinterpret_cast<int*>(reinterpret_cast<int4*>(bar + 2) + (kThreads / 32) * records);
@@ -538,7 +538,8 @@ __host__ __device__ inline size_t ring_slot_bytes(const DevProblem& p) {
 }
 
 constexpr unsigned kRingSuspendNs = 20000;                 // longest single suspension of a waiting warp
-constexpr unsigned long long kRingWaitNs = 1000000000ULL;  // a wait gives up after one second
+// A wait gives up after wait_ns (a kernel parameter, one second unless the caller set another
+// limit with tfv_set_device_wait_limit); the final drain of issued copies keeps kWaitSpins.
 
 // Shared-memory bytes of the ring body with `slots` buffers and `warps` consumer warps:
 // the slots, per-op constants, two mbarriers and a tag per slot (rounded to 16 bytes),
@@ -564,13 +565,14 @@ __device__ __forceinline__ int select_bit(unsigned m, int r) {
     return pos;
 }
 
-// Wait for a phase of `bar`, suspended in the barrier; gives up after kRingWaitNs or once
-// the CTA aborts.
-__device__ __forceinline__ bool ring_wait(uint64_t* bar, unsigned parity, const int* abort) {
+// Wait for a phase of `bar`, suspended in the barrier; gives up after wait_ns or once the
+// CTA aborts.
+__device__ __forceinline__ bool ring_wait(uint64_t* bar, unsigned parity, const int* abort,
+                                          unsigned long long wait_ns) {
     const unsigned long long start = global_ns();
     for (long long spin = 0; spin < kWaitSpins; ++spin) {
         if (mbar_try_wait_suspend(bar, parity, kRingSuspendNs)) return true;
-        if (*reinterpret_cast<const volatile int*>(abort) || global_ns() - start > kRingWaitNs) return false;
+        if (*reinterpret_cast<const volatile int*>(abort) || global_ns() - start > wait_ns) return false;
     }
     return false;
 }
@@ -579,7 +581,7 @@ template <int kBodyRows, class Spec, int kWarps>
 __device__ __forceinline__ void tma_ring_body(const DevProblem& p, const DevFrames& fr, const FrameTable& ft,
                                               const DevPeriodic& b, const DevResults& out, int n_tiles,
                                               const CUtensorMap* map_p, const CUtensorMap* map_o, int spec_frame,
-                                              const DeltaTable& dt, int slots) {
+                                              const DeltaTable& dt, int slots, unsigned long long wait_ns) {
     static_assert(kWarps >= 1 && kWarps <= 31, "a producer warp and 1..31 consumer warps per CTA");
     extern __shared__ __align__(128) unsigned char smem[];
     const int N = p.n_ops;
@@ -596,7 +598,7 @@ __device__ __forceinline__ void tma_ring_body(const DevProblem& p, const DevFram
     int* next_unit = counters;
     int* abort = counters + 1;
     const bool warp_path = warp_resources_used(p);
-    const int records = warp_path ? 2 * p.res_max_windows : 0;
+    const int records = warp_path ? warp_scratch_records(p) : 0;
     int4* scratch = reinterpret_cast<int4*>(counters + 4) + (warp > 0 ? warp - 1 : 0) * records;
 
     bool base_ok = true;
@@ -626,7 +628,7 @@ __device__ __forceinline__ void tma_ring_body(const DevProblem& p, const DevFram
         // ---- producer ----
         for (int i = 0; i < n_local; ++i) {
             const int slot = i % slots, round = i / slots;
-            bool ok = round == 0 || ring_wait(&empty[slot], (round - 1) & 1, abort);  // every lane writes the slot
+            bool ok = round == 0 || ring_wait(&empty[slot], (round - 1) & 1, abort, wait_ns);  // every lane writes the slot
             ok = __all_sync(0xFFFFFFFFu, ok && !*reinterpret_cast<volatile int*>(abort));
             if (!ok) {
                 if (lane == 0) atomicExch(abort, 1);
@@ -682,13 +684,13 @@ __device__ __forceinline__ void tma_ring_body(const DevProblem& p, const DevFram
                         ok = true;
                         break;
                     }
-                    if (tag >= 0 && !ring_wait(&empty[slot], (tag / slots) & 1, abort)) break;  // tile tag's units
-                    if (*reinterpret_cast<volatile int*>(abort) || global_ns() - start > kRingWaitNs) break;
+                    if (tag >= 0 && !ring_wait(&empty[slot], (tag / slots) & 1, abort, wait_ns)) break;  // tile tag's units
+                    if (*reinterpret_cast<volatile int*>(abort) || global_ns() - start > wait_ns) break;
                     __nanosleep(128);  // the producer refills the slot next
                 }
             }
             ok = __shfl_sync(0xFFFFFFFFu, ok, 0);
-            if (ok) ok = ring_wait(&full[slot], round & 1, abort);
+            if (ok) ok = ring_wait(&full[slot], round & 1, abort, wait_ns);
             ok = __all_sync(0xFFFFFFFFu, ok);
             if (!ok) {  // report the unit's candidates and stop the CTA; the slot is not released
                 if (lane == 0) atomicExch(abort, 1);

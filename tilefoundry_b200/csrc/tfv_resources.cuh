@@ -22,7 +22,11 @@
 //   * thread_resources_exceed: one thread per candidate, window values recomputed where
 //     they are used (cheapest for a few windows per resource);
 //   * warp_resources_exceed: one warp per candidate, the window values staged once in
-//     shared memory and the starts split across the lanes.
+//     shared memory and the starts split across the lanes. With three or more iterations it
+//     decides the steady state first (F at every window's phase, kept per window), then the
+//     prologue starts, then the body starts before E. F bounds the clipped body demand at any
+//     time of its phase, so a body start whose prologue demand plus F stays within the
+//     capacity cannot exceed it; only the other body starts are evaluated exactly.
 #pragma once
 
 #ifndef __CUDACC_RTC__
@@ -43,9 +47,14 @@ constexpr int kResourcesPending = 0x7FFF;
 __host__ __device__ inline bool warp_resources_used(const DevProblem& p) {
     return p.n_resources > 0 && p.res_max_windows > kThreadWindowMax && p.res_max_windows <= kWarpWindowCap;
 }
-// Shared-memory records one warp needs for the warp path.
-inline size_t warp_resource_scratch_bytes(const DevProblem& p) {
-    return warp_resources_used(p) ? 2 * sizeof(int4) * static_cast<size_t>(p.res_max_windows) : 0;
+// int4 records of one warp's capacity-check scratch: two per window ({P, P + D, a, rs} and
+// {e, m, qs, S}) and each window's steady-state demand (one int per window).
+__host__ __device__ inline int warp_scratch_records(const DevProblem& p) {
+    return 2 * p.res_max_windows + (p.res_max_windows + 3) / 4;
+}
+// Shared-memory bytes one warp needs for the warp path.
+__host__ __device__ inline size_t warp_resource_scratch_bytes(const DevProblem& p) {
+    return warp_resources_used(p) ? sizeof(int4) * static_cast<size_t>(warp_scratch_records(p)) : 0;
 }
 
 // floor(x / d) for x in [0, 2^30) and d in [1, 2^30) by one multiply and a shift:
@@ -108,13 +117,13 @@ struct LiveWindows {
     }
 };
 
-// Window values staged in shared memory as {rs, e, a, m}, {P, D, qs, S} (warp driver).
+// Window values staged in shared memory as {P, P + D, a, rs}, {e, m, qs, S} (warp driver).
 struct StagedWindows {
     const int4* rec;
     const int4* rec2;
     __device__ __forceinline__ Win operator()(int w) const {
         const int4 r = rec[w], r2 = rec2[w];
-        return Win{r2.x, r2.y, r.z, r2.w, r2.z, r.x, r.w, r.y};
+        return Win{r.x, r.y - r.x, r.z, r2.w, r2.z, r.w, r2.y, r2.x};
     }
 };
 
@@ -242,15 +251,94 @@ __device__ bool thread_resources_exceed(const DevProblem& p, const Vals& V, int 
     return false;
 }
 
+// Prologue demand at t from the staged {P, P + D, a, rs} records.
+__device__ __forceinline__ int staged_prologue_demand(const int4* rec, int W, int t) {
+    int demand = 0;
+    for (int w = 0; w < W; ++w) {
+        const int4 r = rec[w];
+        demand += (t >= r.x && t < r.y) ? r.z : 0;
+    }
+    return demand;
+}
+
+// F at phase rv from the staged records (rs and a in rec, e in rec2).
+__device__ __forceinline__ int staged_periodic_demand(const int4* rec, const int4* rec2, int W, int rv, int C0, int T) {
+    int F = C0;
+    for (int w = 0; w < W; ++w) {
+        const int4 r = rec[w];
+        const int d = rv - r.w;
+        const unsigned u = min(static_cast<unsigned>(d), static_cast<unsigned>(d + T));  // (rv - rs) mod T
+        F += u < static_cast<unsigned>(rec2[w].x) ? r.z : 0;
+    }
+    return F;
+}
+
+// Warp driver for I >= 3 (see the file comment); lanes split the windows, every lane calls it.
+// Fv holds each window's F (or sumF when the steady state needs no check). Returns this
+// lane's finding; the caller combines the lanes.
+__device__ inline bool warp_periodic_exceed(const int4* rec, const int4* rec2, int* Fv, int W, int lane,
+                                            const ResourceSums& s, int cap, int T, int I, const Divider& div) {
+    const unsigned full = 0xFFFFFFFFu;
+    const int n = I - 1;
+    const StagedWindows src{rec, rec2};
+    const bool middle = s.Smin + n * T >= s.Lend;  // the unclipped range spans a full period
+    const bool phase = middle && s.sumF > cap;
+    bool ex = false;
+    // 1. the steady state: F at every window's phase; F > cap is exceeded at a real start
+    for (int v = lane; v < W; v += 32) {
+        int F = s.sumF;
+        if (phase) {
+            F = staged_periodic_demand(rec, rec2, W, rec[v].w, s.C0, T);
+            ex |= F > cap;
+        }
+        Fv[v] = F;
+    }
+    if (__any_sync(full, ex)) return true;
+    __syncwarp();  // every lane's Fv is written
+    // 2. prologue starts: before the first body start only the prologue copies count
+    for (int v = lane; v < W; v += 32) {
+        const int P = rec[v].x;
+        if (P < s.Smin) {
+            if (s.sumA > cap) ex |= staged_prologue_demand(rec, W, P) > cap;
+        } else {
+            const int qp = div.quot(P);
+            ex |= clipped_demand(src, W, P, qp, P - qp * T, T, n) > cap;
+        }
+    }
+    if (__any_sync(full, ex)) return true;
+    // 3. body starts S_v + j * T before the horizon (E with a full period, else all of them);
+    //    the flattened index j * W + v keeps the lanes evenly loaded
+    const int horizon = middle ? s.E : INT_MAX;
+    int kmax = 0;
+    for (int v = lane; v < W; v += 32) {
+        const int S = rec2[v].w;
+        const int k = S >= horizon ? 0 : (horizon == INT_MAX ? n : min(n, div.quot(horizon - S - 1) + 1));
+        kmax = max(kmax, k);
+    }
+    kmax = __reduce_max_sync(full, kmax);
+    const Divider divW(W > 0 ? W : 1);
+    const int tasks = kmax * W;
+    for (int idx = lane; idx < tasks; idx += 32) {
+        const int j = divW.quot(idx), v = idx - j * W;
+        const int4 r2 = rec2[v];
+        const int t = r2.w + j * T;
+        if (t >= horizon) continue;
+        if (staged_prologue_demand(rec, W, t) + Fv[v] <= cap) continue;  // demand(t) <= prologue(t) + F
+        ex |= clipped_demand(src, W, t, r2.z + j, rec[v].w, T, n) > cap;
+    }
+    return ex;
+}
+
 // One warp per candidate: every lane passes the same V and T. Same requirements as the
-// thread driver, plus warp_resources_used and scratch for 2 * res_max_windows int4
-// records private to the warp.
+// thread driver, plus at most kWarpWindowCap windows per resource and scratch for
+// warp_scratch_records(p) int4 records private to the warp.
 template <class Vals>
 __device__ bool warp_resources_exceed(const DevProblem& p, const Vals& V, int T, int4* scratch, int lane) {
     const unsigned full = 0xFFFFFFFFu;
     const int I = p.iterations;
     int4* rec = scratch;
     int4* rec2 = scratch + p.res_max_windows;
+    int* Fv = reinterpret_cast<int*>(scratch + 2 * p.res_max_windows);
     const Divider div(I >= 3 ? T : 1);
     for (int q = 0; q < p.n_resources; ++q) {
         const int w0 = p.res_offsets[q], W = p.res_offsets[q + 1] - w0;
@@ -258,8 +346,8 @@ __device__ bool warp_resources_exceed(const DevProblem& p, const Vals& V, int T,
         ResourceSums s{INT_MIN, INT_MAX, INT_MIN, 0, 0, 0};
         for (int w = lane; w < W; w += 32) {
             const Win x = live(w);
-            rec[w] = make_int4(x.rs, x.e, x.a, x.m);
-            rec2[w] = make_int4(x.P, x.D, x.qs, x.S);
+            rec[w] = make_int4(x.P, x.P + x.D, x.a, x.rs);
+            rec2[w] = make_int4(x.e, x.m, x.qs, x.S);
             add_window(s, x, I - 1);
         }
         s.E = __reduce_max_sync(full, s.E);
@@ -269,7 +357,8 @@ __device__ bool warp_resources_exceed(const DevProblem& p, const Vals& V, int T,
         s.sumF = __reduce_add_sync(full, s.sumF);
         s.C0 = __reduce_add_sync(full, s.C0);
         __syncwarp();
-        const bool exceed = starts_exceed(StagedWindows{rec, rec2}, W, lane, 32, s, p.capacity[q], T, I, div);
+        const bool exceed = I >= 3 ? warp_periodic_exceed(rec, rec2, Fv, W, lane, s, p.capacity[q], T, I, div)
+                                   : starts_exceed(StagedWindows{rec, rec2}, W, lane, 32, s, p.capacity[q], T, I, div);
         if (__any_sync(full, exceed)) return true;
         __syncwarp();  // every lane is done with this resource's records
     }

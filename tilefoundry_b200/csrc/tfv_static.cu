@@ -11,9 +11,13 @@
 // The array is TFV_STATIC_TABLE_BYTES long and every GPU that loads the library holds it
 // until the process exits. Its device address is looked up once per device, on the first
 // call for that device, with the device current; make that first call before any stream
-// capture. Every call shares the one array and leaves its contents behind, so calls whose
-// work overlaps on the GPU (different streams, or different host threads) race; the
-// kernels overwrite every entry they later read, so nothing needs clearing between calls.
+// capture. Each later call checks that the cached address is still device memory of that
+// device (cudaPointerGetAttributes, a host-side query) and looks it up again when it is not,
+// which happens only after the device's context was reset (cudaDeviceReset): the module is
+// then loaded anew and the array may sit elsewhere. Every call shares the one array and
+// leaves its contents behind, so calls whose work overlaps on the GPU (different streams, or
+// different host threads) race; the kernels overwrite every entry they later read, so
+// nothing needs clearing between calls.
 #include <mutex>
 
 #include "tfv_device.cuh"
@@ -42,6 +46,15 @@ extern "C" int tfv_verify_periodic_static(const tfv_problem* problem, const tfv_
     void* table = nullptr;
     {
         std::lock_guard<std::mutex> lock(g_setup_mutex);
+        if (g_table_address[device]) {  // still this device's memory? (not after a context reset)
+            cudaPointerAttributes attr{};
+            const bool valid = cudaPointerGetAttributes(&attr, g_table_address[device]) == cudaSuccess &&
+                               attr.type == cudaMemoryTypeDevice && attr.device == device;
+            if (!valid) {
+                cudaGetLastError();  // clear a lookup error of the stale address
+                g_table_address[device] = nullptr;
+            }
+        }
         if (!g_table_address[device]) {
             int previous = 0;
             if (cudaGetDevice(&previous) != cudaSuccess) return tfv_internal_fail(TFV_ERR_CUDA, "cudaGetDevice failed");

@@ -2,9 +2,11 @@
 
 Candidates are independent, so a batch is split into contiguous ranges, one per rank
 (one process per GPU), with the problem and frame tables replicated on every device.
-The only exchange is the final gather of each candidate's results to one rank over
-``torch.distributed`` (NCCL between GPUs, gloo for CPU processes): ``(verdict, makespan,
-ii)`` as 12 bytes per candidate, or packed as an int8 verdict and an int32 makespan in 5.
+The only exchange is the final gather of each candidate's results to one rank: over
+``torch.distributed`` (NCCL between GPUs, gloo for CPU processes) as ``(verdict, makespan,
+ii)`` in 12 bytes per candidate or packed as an int8 verdict and an int32 makespan in 5, or
+(:class:`PeerGather`) by copy engines writing the packed results straight into rank 0's
+memory, which leaves rank 0's SMs to the verifier.
 """
 
 from __future__ import annotations
@@ -103,4 +105,118 @@ def gather_packed(packed, n_total: int, *, dst: int = 0, group=None):
     return torch.cat(verdicts), torch.cat(makespans)
 
 
-__all__ = ["gather_packed", "gather_results", "pack_results", "shard_bounds", "unpack_results"]
+__all__ = ["PeerGather", "gather_packed", "gather_results", "pack_results", "shard_bounds", "unpack_results"]
+
+
+class PeerGather:
+    """Every rank's packed results pushed into rank 0's memory by copy engines.
+
+    The NCCL gather runs kernels on rank 0 that need SMs the verifier's persistent kernels
+    occupy, so rank 0 verifies slower while it receives. Here rank 0 allocates ``slots``
+    receive buffers of ``world x nbytes`` once (cudaMalloc) and exports them as CUDA IPC
+    handles; every other rank maps them from its own device (peer access over NVLink) and
+    copies its payload with cudaMemcpyAsync on a side stream, ordered after an event of the
+    producing stream. No kernel reads another GPU's memory. One process per GPU of one node;
+    the handles are exchanged once through ``torch.distributed``.
+
+    ``send(slot, payload, stream)`` queues the copy of this rank's ``payload`` (uint8 CUDA
+    tensor of at most ``nbytes``) into row ``rank`` of receive buffer ``slot`` after the work
+    queued so far on ``stream``, and makes the next use of ``payload`` wait for it through
+    ``wait(slot, stream)``. ``finish()`` waits for every copy of this rank; after a barrier
+    rank 0 reads the rows with ``received(slot)``.
+    """
+
+    def __init__(self, nbytes: int, slots: int = 2, group=None) -> None:
+        import torch
+        import torch.distributed as dist
+        from cuda.bindings import runtime as rt
+
+        self._rt = rt
+        self.world = dist.get_world_size(group)
+        self.rank = dist.get_rank(group)
+        self.nbytes = int(nbytes)
+        self.slots = int(slots)
+        self.device = torch.cuda.current_device()
+        self.stream = torch.cuda.Stream(self.device)
+        self._done = [torch.cuda.Event() for _ in range(self.slots)]
+        self._sent = [False] * self.slots
+        self._buffers: list[int] = []
+        self._mapped: list[int] = []
+        handles = None
+        if self.rank == 0:
+            handles = []
+            for _ in range(self.slots):
+                err, ptr = rt.cudaMalloc(self.world * self.nbytes)
+                self._check(err, "cudaMalloc")
+                self._buffers.append(int(ptr))
+                err, handle = rt.cudaIpcGetMemHandle(ptr)
+                self._check(err, "cudaIpcGetMemHandle")
+                handles.append(bytes(handle.reserved))
+        box = [handles]
+        dist.broadcast_object_list(box, src=0, group=group)
+        if self.rank != 0:
+            for raw in box[0]:
+                handle = rt.cudaIpcMemHandle_t()
+                handle.reserved = raw
+                err, ptr = rt.cudaIpcOpenMemHandle(handle, rt.cudaIpcMemLazyEnablePeerAccess)
+                self._check(err, "cudaIpcOpenMemHandle")
+                self._mapped.append(int(ptr))
+
+    @staticmethod
+    def _check(err, what: str) -> None:
+        from cuda.bindings import runtime as rt
+
+        if err != rt.cudaError_t.cudaSuccess:
+            raise RuntimeError(f"{what} failed: {err}")
+
+    def wait(self, slot: int, stream) -> None:
+        """Make ``stream`` wait until this rank's last copy from ``slot`` has read its payload."""
+        if self._sent[slot]:
+            stream.wait_event(self._done[slot])
+
+    def send(self, slot: int, payload, stream) -> None:
+        """Queue this rank's payload for row ``rank`` of receive buffer ``slot``."""
+        import torch
+
+        nbytes = int(payload.numel())
+        if nbytes > self.nbytes:
+            raise ValueError("payload larger than the receive rows")
+        ready = torch.cuda.Event()
+        ready.record(stream)
+        self.stream.wait_event(ready)
+        if self.rank == 0:
+            dst = self._buffers[slot]
+        else:
+            dst = self._mapped[slot]
+        err, = self._rt.cudaMemcpyAsync(dst + self.rank * self.nbytes, payload.data_ptr(), nbytes,
+                                        self._rt.cudaMemcpyKind.cudaMemcpyDefault,
+                                        self._rt.cudaStream_t(self.stream.cuda_stream))
+        self._check(err, "cudaMemcpyAsync")
+        self._done[slot].record(self.stream)
+        self._sent[slot] = True
+
+    def finish(self) -> None:
+        """Wait for every copy this rank queued."""
+        self.stream.synchronize()
+
+    def received(self, slot: int):
+        """Rank 0: a uint8 tensor [world, nbytes] copy of receive buffer ``slot``."""
+        import torch
+
+        if self.rank != 0:
+            raise RuntimeError("only rank 0 holds the receive buffers")
+        out = torch.empty((self.world, self.nbytes), dtype=torch.uint8, device=torch.device("cuda", self.device))
+        err, = self._rt.cudaMemcpy(out.data_ptr(), self._buffers[slot], self.world * self.nbytes,
+                                   self._rt.cudaMemcpyKind.cudaMemcpyDeviceToDevice)
+        self._check(err, "cudaMemcpy")
+        return out
+
+    def close(self) -> None:
+        """Unmap (other ranks) and free (rank 0) the receive buffers; every rank calls it after a barrier."""
+        self.stream.synchronize()
+        for ptr in self._mapped:
+            self._rt.cudaIpcCloseMemHandle(ptr)
+        self._mapped = []
+        for ptr in self._buffers:
+            self._rt.cudaFree(ptr)
+        self._buffers = []

@@ -110,12 +110,25 @@ class DeviceFrames:
 
 
 class FramePlan:
-    """A frame-specialised kernel (``tfv_plan``) of one verifier and one frame content."""
+    """A frame-specialised kernel (``tfv_plan``) of one verifier and one frame content.
+
+    A plan keeps its batch constants in its module, so it serves one CUDA stream: the
+    first verification through it binds it to that stream, and a call on another stream
+    raises (make a second plan with :meth:`WarpgroupVerifier.plan` and ``stream=`` for it).
+    """
 
     def __init__(self, lib: ctypes.CDLL, handle: ctypes.c_void_p, key: tuple) -> None:
         self._lib = lib
         self.handle = handle
         self.key = key
+        self.stream: int | None = None
+
+    def bind(self, stream: int | None) -> None:
+        """Bind the plan to ``stream`` (a raw cudaStream_t) or check that it is bound to it."""
+        if self.stream is None:
+            self.stream = stream
+        elif self.stream != stream:
+            raise VerifierRuntimeError("a frame plan serves one stream at a time; it is bound to another stream")
 
     @property
     def kernel(self) -> str:
@@ -229,19 +242,20 @@ class WarpgroupVerifier:
         return out, _lib.Results(verdict.data_ptr(), makespan.data_ptr(), ii.data_ptr())
 
     def plan(self, frames: FrameSet, frame: int, kernel: str = "auto", ring_warps: int = 0,
-             delta: bool = True) -> "FramePlan":
+             delta: bool = True, stream: Any = None) -> "FramePlan":
         """A frame-specialised kernel for ``frames``' frame ``frame`` (compiled once per frame content).
 
         ``kernel``: ``"ring"`` (a producer warp and consumer warps over a ring of tile slots),
         ``"tiles"`` (CTAs verifying whole tiles in lock step) or ``"auto"`` (the ring when it
         fits in shared memory); ``ring_warps``: the ring's consumer warps (0: the default);
         ``delta``: let frames that differ from this one by a few edges run the generated code
-        too (where the body is small enough, see ``tfv_plan_delta``).
+        too (where the body is small enough, see ``tfv_plan_delta``); ``stream``: the stream
+        the plan will serve (default: the device's current stream), part of the cache key.
         """
         kinds = {"auto": _lib.PLAN_AUTO, "tiles": _lib.PLAN_TILES, "ring": _lib.PLAN_RING}
         if kernel not in kinds:
             raise ValueError(f"unknown plan kernel {kernel!r}")
-        key = (frames.frames[frame], kernel, int(ring_warps), bool(delta))
+        key = (frames.frames[frame], kernel, int(ring_warps), bool(delta), self._stream(stream))
         found = self._plans.get(key)
         if found is None:
             arrays = frames.arrays()
@@ -278,6 +292,7 @@ class WarpgroupVerifier:
         )
         out, results = self._results(n, out)
         if plan is not None:
+            plan.bind(self._stream(stream))
             _lib.check(
                 self._lib.tfv_verify_periodic_planned(
                     plan.handle, ctypes.byref(frames.struct), table.data_ptr(), int(table.numel()), ctypes.byref(struct),
@@ -390,6 +405,25 @@ class WarpgroupVerifier:
         makespan = np.empty(n, dtype=np.int32)
         ii = np.empty(n, dtype=np.int32)
         return self.verify_periodic_host_arrays(fstruct, batch, (verdict, makespan, ii))
+
+    def verify_periodic_starts(self, frames: FrameSet, prologue, offset, ii, frame):
+        """Verify periodic candidates given by absolute starts ([n, N] prologue and offset
+        starts, [n] IIs and frame indices), whatever their spread.
+
+        The candidates are split into batches whose deltas fit int16 (:func:`periodic_groups`:
+        one main batch, plus one per cluster of outliers), each verified through the host
+        entry, and the results are returned in candidate order.
+        """
+        from .batch import periodic_groups
+
+        n = int(np.asarray(ii).shape[0])
+        verdict = np.empty(n, dtype=np.int32)
+        makespan = np.empty(n, dtype=np.int32)
+        ii_out = np.empty(n, dtype=np.int32)
+        for take, batch in periodic_groups(prologue, offset, ii, frame):
+            v, m, i = self.verify_periodic(frames, batch)
+            verdict[take], makespan[take], ii_out[take] = v, m, i
+        return verdict, makespan, ii_out
 
     def verify_periodic_host_arrays(self, frames_struct: _lib.Frames, batch: PeriodicBatch, out):
         """Host-buffer entry with caller-owned (e.g. pinned) result arrays."""
@@ -523,6 +557,12 @@ def _verify_warpgroup_schedule(problem: object, schedule: object, *, device: int
 _CLOSED: "OrderedDict[tuple, tuple]" = OrderedDict()
 
 
+def _frozen(value: object) -> bool:
+    """Whether ``value`` is an instance of a frozen dataclass (an immutable record)."""
+    params = getattr(type(value), "__dataclass_params__", None)
+    return bool(params is not None and params.frozen)
+
+
 def closed_problem(program: object, hardware: object, build) -> object:
     """``build(program, hardware)``, cached for the last 8 (program, hardware, build) triples.
 
@@ -530,8 +570,14 @@ def closed_problem(program: object, hardware: object, build) -> object:
     build.py:169-220); the closure depends only on the two documents, so repeated calls
     with the same objects reuse it (and with it the device tables of the problem). The
     cache keys on object identity and keeps the objects alive while they are cached,
-    so a key cannot be reused by another object; the records are immutable.
+    so a key cannot be reused by another object. Only immutable records are cached: both
+    must be frozen dataclasses (the reference's WarpgroupProgram and WarpgroupHardware, or
+    this package's mirrors). Any other cost library — the reference accepts any object with
+    ``lookup()`` and ``resources`` (cost.py:166-175), which may change between calls — is
+    closed again on every call, as the reference does.
     """
+    if not (_frozen(program) and _frozen(hardware)):
+        return build(program, hardware)
     key = (id(program), id(hardware), id(build))
     found = _CLOSED.get(key)
     if found is not None and found[0] is program and found[1] is hardware and found[2] is build:

@@ -460,7 +460,7 @@ def _body_problem(ops_spec, lanes: int, iterations: int, capacities: dict, iter_
         WarpgroupProblem,
     )
 
-    kinds = {"register": "reg", "shared": "smem", "global": "gmem"}
+    kinds = {"register": "reg", "shared": "smem"}
     ops = tuple(
         ProblemOperation(
             op_id,
@@ -478,7 +478,7 @@ def _body_problem(ops_spec, lanes: int, iterations: int, capacities: dict, iter_
         tuple(ResourceCapacity(r, c) for r, c in capacities.items()),
         (TensorType("gmem", "global"), TensorType("reg", "register"), TensorType("smem", "shared")),
         tuple(ProgramInput(i, "gmem") for i in inputs),
-        ProblemLoop("%k", iterations, tuple(LoopIterArg(a, ValueRef(y)) for a, y in iter_args), ops),
+        ProblemLoop("%iter", iterations, tuple(LoopIterArg(a, ValueRef(y)) for a, y in iter_args), ops),
     )
 
 
@@ -487,14 +487,16 @@ def gemm_mainloop_problem(iterations: int = 8):
     by the producer warpgroup, a 128x256x64 tcgen05 MMA (latency 512) and a barrier
     arrive by the consumer, and an epilogue store of the 128x256 fp32 accumulator.
     Resources: shared memory in KB (227), TMEM columns (512), mbarriers (8) and the slots
-    of the 4-stage A/B ring (8: a stage holds one A and one B tile). The tiles live in ring
-    buffers, not in one shared allocation per value, so the loads of later iterations may
-    run ahead of the MMA: the ring's slot capacity and the shared-memory capacity bound the
-    loads in flight. The accumulator belongs to the MMA warpgroup (a register-space value
-    carried from one iteration's MMA to the next)."""
+    of the 4-stage A/B ring (8: a stage holds one A and one B tile). As in the reference's
+    model each loaded tile is one shared allocation, reused by the next iteration's load
+    once this iteration's MMA has completed; the accumulator belongs to the MMA warpgroup (a
+    register value carried from one iteration's MMA to the next). The MMA's recurrence bounds
+    the work in flight, so these capacities are never exceeded by a candidate that keeps its
+    lane, sync and relation inequalities (the calibrated variant of body_batch tightens
+    them)."""
     spec = [
-        ("load_a", 0, 24, 700, [("smem_kb", 16, 700), ("tma_slots", 1, 700)], "%a", "global", ["%gmem"]),
-        ("load_b", 0, 24, 900, [("smem_kb", 32, 900), ("tma_slots", 1, 900)], "%b", "global", ["%gmem"]),
+        ("load_a", 0, 24, 700, [("smem_kb", 16, 700), ("tma_slots", 1, 700)], "%a", "shared", ["%gmem"]),
+        ("load_b", 0, 24, 900, [("smem_kb", 32, 900), ("tma_slots", 1, 900)], "%b", "shared", ["%gmem"]),
         ("mma", 1, 64, 512, [("tmem_cols", 256, 512), ("mbarrier", 1, 512)], "%acc", "register",
          ["%a", "%b", "%acc_prev"]),
         ("arrive", 1, 4, 4, [("mbarrier", 1, 4)], "%bar", "register", ["%acc"]),
@@ -507,15 +509,14 @@ def gemm_mainloop_problem(iterations: int = 8):
 def flash_attention_problem(iterations: int = 16):
     """FlashAttention-forward body (Q 128x128, K/V 128x128 bf16 tiles): loads of K and V
     (load warpgroup), S = QK^T and P.V MMAs (MMA warpgroup), rowmax, exp2, rowsum and the O
-    rescale (softmax warpgroup). Shared memory 227 KB, TMEM 512 columns. K and V tiles, the
-    S tile (TMEM) and the P tile (shared memory) live in ping-pong buffers bounded by those
-    capacities, so the loads and the S MMA of later iterations may overlap the current one."""
+    rescale (softmax warpgroup). Shared memory 227 KB, TMEM 512 columns. As for the GEMM
+    body, the recurrences bound the work in flight below the nominal capacities."""
     spec = [
-        ("load_k", 0, 24, 800, [("smem_kb", 32, 800)], "%k", "global", ["%gmem"]),
-        ("load_v", 0, 24, 800, [("smem_kb", 32, 800)], "%v", "global", ["%gmem"]),
-        ("qk", 1, 48, 384, [("tmem_cols", 128, 384)], "%s", "global", ["%gmem", "%k"]),
+        ("load_k", 0, 24, 800, [("smem_kb", 32, 800)], "%k", "shared", ["%gmem"]),
+        ("load_v", 0, 24, 800, [("smem_kb", 32, 800)], "%v", "shared", ["%gmem"]),
+        ("qk", 1, 48, 384, [("tmem_cols", 128, 384)], "%s", "shared", ["%gmem", "%k"]),
         ("rowmax", 2, 90, 110, [], "%m", "register", ["%s", "%m_prev"]),
-        ("exp2", 2, 220, 240, [("smem_kb", 32, 240)], "%p", "global", ["%s", "%m"]),
+        ("exp2", 2, 220, 240, [("smem_kb", 32, 240)], "%p", "shared", ["%s", "%m"]),
         ("rowsum", 2, 80, 96, [], "%l", "register", ["%p", "%l_prev"]),
         ("rescale", 2, 140, 160, [("tmem_cols", 128, 160)], "%o_scaled", "shared", ["%o_prev", "%m", "%m_prev"]),
         ("pv", 1, 48, 384, [("tmem_cols", 128, 384)], "%o", "shared", ["%p", "%v", "%o_scaled"]),
@@ -675,8 +676,9 @@ def pipelined_batch(
     (probability ``delay`` per operation, exponential with mean ``delay_scale`` cycles) and
     the earliest starts that satisfy every lane, sync, relation and carried constraint at
     its II (:func:`pipelined_starts`). Half the templates are pipelined: an II uniform in
-    ``ii_range`` (default [II_lb, witness II]) and no other floor, so iterations overlap
-    whenever the II is below the span. The other half keep every start at or after the
+    ``ii_range`` (default [II_lb, witness II]) and every start at most 30% of the witness II
+    before the witness's, so iterations overlap whenever the II is below the span and every
+    template's starts stay within one int16 delta range. The other half keep every start at or after the
     witness's (its resource-feasible single iteration), without delays, at an II uniform in
     [0.9, 1.3] times the witness II. Either way the resource capacities decide between
     verdicts 0 and 20.
@@ -687,7 +689,8 @@ def pipelined_batch(
     jittered by U[-jitter, jitter] (lane order, sync and relation timing), the II cut by up
     to a third (wrap edges and distance-1 relations, more overlap), a structural variant
     (an operation moved to another lane, two lane neighbours swapped or a sync edge dropped)
-    or one resource-holding operation moved onto another's start (capacity). Returns the
+    or one resource-holding operation moved onto another's start, at most 12000 cycles away
+    (capacity). Returns the
     frames, the batch and each candidate's kind (0 = uncorrupted, 1-4 as listed).
     """
     rng = np.random.default_rng(seed)
@@ -700,7 +703,10 @@ def pipelined_batch(
     sparse = (rng.random((2, m, N)) < delay) & ~floored[None, :, None]
     dp = np.where(sparse[0], rng.exponential(delay_scale, size=(m, N)), 0).astype(np.int64)
     dq = np.where(sparse[1], rng.exponential(delay_scale, size=(m, N)), 0).astype(np.int64)
-    floor = np.where(floored[:, None], witness.prologue.astype(np.int64)[None, :], 0)
+    # pipelined templates may move each operation up to 30% of the witness II earlier than the
+    # witness (its lanes compress, so IIs below the span become feasible); floored ones none
+    wp = witness.prologue.astype(np.int64)[None, :]
+    floor = np.where(floored[:, None], wp, np.maximum(0, wp - int(0.3 * witness.ii)))
     tp, to, ok = pipelined_starts(packed, witness.lanes, t_ii, dp, dq, floor_p=floor, floor_o=floor)
     keep = np.flatnonzero(ok)
     if keep.size == 0:
@@ -710,20 +716,18 @@ def pipelined_batch(
     top = np.maximum(tp.max(axis=1), to.max(axis=1) + t_ii)[pick]
     room = np.maximum(0, (start_range - top) if start_range is not None else np.full(n, 64))
     shift = (rng.random(n) * (room + 1)).astype(np.int64)
-    prologue = tp[pick] + shift[:, None]
-    offset = to[pick] + shift[:, None]
     ii = t_ii[pick].copy()
 
     frames = FrameSet(packed)
     base = frames.add(witness.lanes, witness.sync)
     frame = np.full(n, base, dtype=np.int32)
     kind = np.where(rng.random(n) < corrupt, rng.integers(1, 5, size=n), 0).astype(np.int8)
-    sel = np.flatnonzero(kind == 1)
-    for _ in range(3):
-        rows = sel[rng.random(sel.size) < 0.7]
-        ops = rng.integers(0, N, size=rows.size)
-        prologue[rows, ops] += rng.integers(-jitter, jitter + 1, size=rows.size)
-        offset[rows, ops] += rng.integers(-jitter, jitter + 1, size=rows.size)
+    # kind 1: up to three (operation, prologue shift, offset shift) triples per candidate
+    jit = np.flatnonzero(kind == 1)
+    jit_use = rng.random((3, jit.size)) < 0.7
+    jit_op = rng.integers(0, N, size=(3, jit.size))
+    jit_dp = rng.integers(-jitter, jitter + 1, size=(3, jit.size))
+    jit_dq = rng.integers(-jitter, jitter + 1, size=(3, jit.size))
     sel = np.flatnonzero(kind == 2)
     ii[sel] -= (rng.random(sel.size) * ii[sel] / 3).astype(np.int64)
     sel = np.flatnonzero(kind == 3)
@@ -750,14 +754,43 @@ def pipelined_batch(
                 sync.pop(int(rng.integers(len(sync))))
             variants.append(frames.add(lanes, sync))
         frame[sel] = np.array(variants, dtype=np.int32)[rng.integers(0, len(variants), size=sel.size)]
-    sel = np.flatnonzero(kind == 4)
+    # kind 4: one resource-holding operation moved onto another's starts
+    sq = np.flatnonzero(kind == 4)
     holders = np.flatnonzero(np.diff(packed.window_offsets) > 0)
-    if sel.size and holders.size >= 2:
-        a = holders[rng.integers(0, holders.size, size=sel.size)]
-        b = holders[rng.integers(0, holders.size, size=sel.size)]
-        offset[sel, a] = offset[sel, b]
-        prologue[sel, a] = prologue[sel, b]
-    batch = PeriodicBatch.from_starts(prologue, offset, ii, frame)
+    if holders.size < 2:
+        sq = sq[:0]
+    sq_a = holders[rng.integers(0, max(1, holders.size), size=sq.size)] if sq.size else sq
+    sq_b = holders[rng.integers(0, max(1, holders.size), size=sq.size)] if sq.size else sq
+
+    # Materialise int16 deltas chunk by chunk against per-operation bases at the middle of the
+    # templates' range (shifts, jitter and squeezes stay well inside the int16 range).
+    base_p = (tp.min(axis=0) + tp.max(axis=0) + 2 * (int(shift.max()) // 2 if n else 0)) // 2
+    base_o = (to.min(axis=0) + to.max(axis=0) + 2 * (int(shift.max()) // 2 if n else 0)) // 2
+    dp_all = np.empty((N, n), dtype=np.int16)
+    dq_all = np.empty((N, n), dtype=np.int16)
+    chunk = max(1, (1 << 22) // max(1, N))
+    for c0 in range(0, n, chunk):
+        c1 = min(n, c0 + chunk)
+        prologue = tp[pick[c0:c1]] + shift[c0:c1, None]
+        offset = to[pick[c0:c1]] + shift[c0:c1, None]
+        lo_j, hi_j = np.searchsorted(jit, [c0, c1])
+        for r in range(3):
+            rows = jit[lo_j:hi_j][jit_use[r, lo_j:hi_j]]
+            ops = jit_op[r, lo_j:hi_j][jit_use[r, lo_j:hi_j]]
+            prologue[rows - c0, ops] += jit_dp[r, lo_j:hi_j][jit_use[r, lo_j:hi_j]]
+            offset[rows - c0, ops] += jit_dq[r, lo_j:hi_j][jit_use[r, lo_j:hi_j]]
+        lo_s, hi_s = np.searchsorted(sq, [c0, c1])
+        rows = sq[lo_s:hi_s] - c0
+        for arr in (offset, prologue):  # at most 12000 cycles, to stay inside the delta range
+            a_now = arr[rows, sq_a[lo_s:hi_s]]
+            arr[rows, sq_a[lo_s:hi_s]] = np.clip(arr[rows, sq_b[lo_s:hi_s]], a_now - 12000, a_now + 12000)
+        d1 = prologue - base_p[None, :]
+        d2 = offset - base_o[None, :]
+        if min(d1.min(), d2.min()) < -32768 or max(d1.max(), d2.max()) > 32767:
+            raise ValueError("candidate starts leave the int16 range around their bases")
+        dp_all[:, c0:c1] = d1.T
+        dq_all[:, c0:c1] = d2.T
+    batch = PeriodicBatch(base_p.astype(np.int32), base_o.astype(np.int32), dp_all, dq_all, ii.astype(np.int32), frame)
     return frames, batch, kind
 
 
@@ -811,8 +844,9 @@ def body_batch(name: str, n: int, *, seed: int = 0, calibrated: bool = False, po
 
     ``name`` is ``gemm`` (starts in [0, 8000]), ``fa``, ``dag`` or ``stress``; candidates
     come from :func:`pipelined_batch` with half of them corrupted. With ``calibrated`` the
-    problem's capacities are set to the 75th percentile of the uncorrupted candidates' peak
-    demands (:func:`peak_demands`), so that each resource is exceeded by part of the batch:
+    problem's capacities are set to the median of the uncorrupted candidates' peak demands
+    (:func:`peak_demands`), so that each resource whose peak varies is exceeded by part of
+    the batch:
     with the nominal capacities of the GEMM and FlashAttention bodies no candidate that
     keeps the lane, sync and relation inequalities can exceed them (their recurrences bound
     the work in flight). Returns ``(problem, packed, witness, frames, batch, kind)``.
@@ -828,7 +862,7 @@ def body_batch(name: str, n: int, *, seed: int = 0, calibrated: bool = False, po
         p, o = absolute_starts(batch)
         clean = np.flatnonzero(kind == 0)[:4096]
         peaks = peak_demands(packed, p[clean], o[clean], batch.ii[clean])
-        caps = {rid: max(1, int(np.quantile(peaks[:, q], 0.75))) for q, rid in enumerate(packed.resource_ids)}
+        caps = {rid: max(1, int(np.quantile(peaks[:, q], 0.5, method="lower"))) for q, rid in enumerate(packed.resource_ids)}
         problem = with_capacities(problem, caps)
         packed = pack_problem(problem)
         frames_new = FrameSet(packed)  # the same frames, indexed against the new problem tables

@@ -294,6 +294,17 @@ TFV_API int tfv_plan_kernel(const tfv_plan* plan);
  * frame's candidates only. A delta plan grows a device buffer to the largest frame count
  * it has seen, inside tfv_verify_periodic_planned. */
 TFV_API int tfv_plan_delta(const tfv_plan* plan);
+/* Consumer warps of a ring plan's kernel (0 for the tiles kernel, -1 for NULL). Unless the
+ * options name a count, tfv_plan_create_with compiles with 19 and, while the compiled kernel
+ * still uses local memory (register spills), again with 15 and then 11. */
+TFV_API int tfv_plan_ring_warps(const tfv_plan* plan);
+/* Kernel timing. With `enable` nonzero every later tfv_verify_periodic_planned call records
+ * a pair of CUDA events on its stream right before and right after its verification kernel
+ * (not around the small per-call kernels before it). tfv_plan_kernel_times writes the
+ * milliseconds of up to `capacity` recorded launches, oldest first, sets *count to the number
+ * recorded, and clears the record; call it once those launches have completed. */
+TFV_API int tfv_plan_set_timing(tfv_plan* plan, int enable);
+TFV_API int tfv_plan_kernel_times(tfv_plan* plan, float* ms, int capacity, int* count);
 TFV_API int tfv_plan_destroy(tfv_plan* plan);
 /* The generated CUDA source of a plan (truncated to size - 1 bytes). */
 TFV_API int tfv_plan_source(const tfv_plan* plan, char* buffer, size_t size);

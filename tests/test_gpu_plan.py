@@ -159,3 +159,43 @@ def test_plan_with_another_frames_index_takes_the_frame_table_path():
                 assert np.array_equal(g, w)
             with pytest.raises(VerifierRuntimeError):
                 verifier.verify_periodic_device(dframes, table, tensors, plan=plan, spec_frame=len(frames))
+
+
+def test_ring_plan_warp_count_and_kernel_timing():
+    """The default ring plan keeps its values in registers at one of the warp counts the
+    library tries, and with timing on records one event pair per call around the generated
+    kernel (positive, shorter than the whole call)."""
+    import torch
+
+    problem = problem_from_json(problem_text("mla"))
+    packed = pack_problem(problem)
+    witness = witness_from_rows(packed, *raw_cases("mla")[0][0])
+    frames, batch, _ = mla_perturbations(packed, witness, 1 << 20, seed=5, producers=shared_producers(problem))
+    with WarpgroupVerifier(packed) as verifier:
+        dev = torch.device("cuda", verifier.device)
+        dframes = verifier.frames_to_device(frames)
+        table = verifier.analyze(dframes)
+        tensors = {k: torch.from_numpy(np.ascontiguousarray(getattr(batch, k))).to(dev)
+                   for k in ("base_prologue", "base_offset", "prologue_delta", "offset_delta", "ii", "frame")}
+        top = int(np.argmax(np.bincount(batch.frame, minlength=len(frames))))
+        plan = verifier.plan(frames, top)
+        assert plan.kernel == "ring" and plan.ring_warps in (19, 15, 11)
+        assert verifier.plan(frames, top, ring_warps=7).ring_warps == 7
+        assert plan.kernel_times() == []
+        plan.set_timing(True)
+        begin, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        begin.record()
+        results = [verifier.verify_periodic_device(dframes, table, tensors, plan=plan, spec_frame=top)
+                   for _ in range(3)]
+        end.record()
+        torch.cuda.synchronize(dev)
+        plan.set_timing(False)
+        times = plan.kernel_times()
+        assert len(times) == 3 and all(0 < t for t in times)
+        assert sum(times) < begin.elapsed_time(end)
+        assert plan.kernel_times() == []  # read once
+        verifier.verify_periodic_device(dframes, table, tensors, plan=plan, spec_frame=top)
+        torch.cuda.synchronize(dev)
+        assert plan.kernel_times() == []  # timing off: nothing recorded
+        for r in results[1:]:
+            assert all(torch.equal(a, b) for a, b in zip(results[0], r))

@@ -151,6 +151,9 @@ EXPORTS = {
     ),
     "tfv_plan_kernel": (ctypes.c_int, [_p]),
     "tfv_plan_delta": (ctypes.c_int, [_p]),
+    "tfv_plan_ring_warps": (ctypes.c_int, [_p]),
+    "tfv_plan_set_timing": (ctypes.c_int, [_p, ctypes.c_int]),
+    "tfv_plan_kernel_times": (ctypes.c_int, [_p, ctypes.POINTER(ctypes.c_float), ctypes.c_int, ctypes.POINTER(ctypes.c_int)]),
     "tfv_plan_destroy": (ctypes.c_int, [_p]),
     "tfv_plan_source": (ctypes.c_int, [_p, ctypes.c_char_p, ctypes.c_size_t]),
     "tfv_verify_periodic_planned": (

@@ -146,8 +146,9 @@ inline FrameTable frame_table_view(void* base, FrameTableShape s) {
 // lane inequalities of a frame are one edge per placed operation a, from a to its lane
 // successor (succ), and its sync inequalities are its set's program; the generated code
 // records, per candidate, which of the specialised frame's edges are violated: one bit per
-// operation in the frame's walk order (order[]) and one per program edge, 32 edges a word,
-// edge k of a word with n edges at bit n - 1 - k. For another frame f the lane (sync) check fails iff a
+// lane edge (named by its source's position in the frame's walk order, order[]) and one per
+// program edge, at the positions the plan's generator chose (lane_bit / sync_bit: word *
+// 32 + bit). For another frame f the lane (sync) check fails iff a
 // violated edge is among those f shares with that frame (keep) or one of f's own edges is
 // violated (prog, at most kDeltaMax of each kind, in the set_prog format: a lane edge a -> b
 // is {a_row | b_row << 16, x_row | d << 17, w0, w1} with x_row b's prologue row and d = 0,
@@ -272,8 +273,8 @@ cudaError_t launch_verify_rows(const DevProblem& p, const DevFrames& f, FrameTab
 
 // Shared-memory footprint checks used by the host before launching.
 cudaError_t launch_delta_frames(const DevProblem& p, const DevFrames& f, FrameTable t, const int* spec_frame,
-                                const int* base_prologue, const int* base_offset, DeltaTable d, int sm_count,
-                                cudaStream_t stream);
+                                const int* base_prologue, const int* base_offset, const int* lane_bit,
+                                const int* sync_bit, DeltaTable d, int sm_count, cudaStream_t stream);
 // Writes spec to *out when frame spec has the lanes (sig_lane_pos [N]) and sync program
 // (sig_edges [sig_len][3]) a plan was generated for, else -1.
 cudaError_t launch_check_spec_frame(const DevProblem& p, const DevFrames& f, int spec, const uint16_t* sig_lane_pos,

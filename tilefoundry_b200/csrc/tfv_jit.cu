@@ -18,8 +18,11 @@
 #include <dlfcn.h>
 
 #include <algorithm>
+#include <climits>
 #include <cstdio>
 #include <cstring>
+#include <functional>
+#include <map>
 #include <mutex>
 #include <string>
 #include <vector>
@@ -98,6 +101,7 @@ struct Driver {
     PFN_cuFuncSetAttribute_v9000 set_attribute = nullptr;
     PFN_cuOccupancyMaxActiveBlocksPerMultiprocessor_v6050 occupancy = nullptr;
     PFN_cuMemcpyDtoDAsync_v3020 copy = nullptr;
+    PFN_cuFuncGetAttribute_v2020 get_attribute = nullptr;
     bool ok = false;
 };
 
@@ -119,6 +123,7 @@ const Driver& driver() {
         entry("cuModuleGetGlobal", d.global);
         entry("cuLaunchKernel", d.launch);
         entry("cuFuncSetAttribute", d.set_attribute);
+        entry("cuFuncGetAttribute", d.get_attribute);
         entry("cuOccupancyMaxActiveBlocksPerMultiprocessor", d.occupancy);
         entry("cuMemcpyDtoDAsync", d.copy);
         d.ok = d.load && d.unload && d.function && d.global && d.launch && d.set_attribute && d.occupancy && d.copy;
@@ -158,10 +163,13 @@ struct Shape {
 constexpr Shape kShapes[] = {{2, 1}, {1, 1}};
 
 // Ring kernel: consumer warps per CTA (one CTA per SM) and the fewest slots it runs with.
-// Measured on the MLA batch (8.4M candidates, random order, delta verification), verify
-// kernel ms for 15/19/21/23/25/27/31 consumer warps: 0.740/0.669/0.665/0.653/0.693/0.709/0.727;
-// 23 warps leave room for registers (up to 80 a thread) and for tiles in flight.
-constexpr int kRingWarpsDefault = 23;
+// Measured on the MLA batch (8.4M candidates, random order, delta verification, one call
+// including its small kernels): 0.545 / 0.503 / 0.588 ms for 15 / 19 / 23 consumer warps.
+// With 20 warps a CTA (five per scheduler) a thread may hold up to 96 registers; at 24
+// warps ptxas caps the generated kernel at 80 and spills. A kernel that still spills is
+// compiled again with the next count of kRingWarpSteps.
+constexpr int kRingWarpsDefault = 19;
+constexpr int kRingWarpSteps[] = {kRingWarpsDefault, 15, 11};
 constexpr int kRingMinSlots = 3;
 
 struct FrameInput {
@@ -175,13 +183,20 @@ class Gen {
     std::string eval, consts;
     int n_consts = 0;
 
-    // A new constant computed by the constants kernel from bp[], bo[] and immediates; the
-    // kernel's 32 threads take every 32nd constant each.
+    // The constant of `expr`, computed by the constants kernel from bp[], bo[] and
+    // immediates (the kernel's 32 threads take every 32nd constant each); an expression
+    // already asked for gets its earlier constant.
     int constant(const std::string& expr) {
+        const auto it = ids.find(expr);
+        if (it != ids.end()) return it->second;
         consts += "    if (t == " + std::to_string(n_consts % 32) + ") c[" + std::to_string(n_consts) + "] = " + expr + ";\n";
+        ids.emplace(expr, n_consts);
         return n_consts++;
     }
     void line(const std::string& s) { eval += "        " + s + "\n"; }
+
+  private:
+    std::map<std::string, int> ids;
 };
 
 std::string I2S(long long v) { return std::to_string(v); }
@@ -191,139 +206,201 @@ std::string I2S(long long v) { return std::to_string(v); }
 using tfv::kDeltaMaxWords;
 int mask_words(int bits) { return std::max(1, (bits + 31) / 32); }
 
-// ring_warps > 0: the ring kernel (tfv_spec_ring) with that many consumer warps; else the
-// tiles kernel (tfv_spec_kernel) of `shape`. delta: the generated code records which of the
-// frame's lane and sync edges are violated (bit masks, eval_masks), so that every frame a
-// DeltaTable describes by edges runs it; otherwise it computes the smallest slacks (eval)
-// and only the frame's own candidates run it.
-std::string generate(const FrameInput& in, const int* issue, const int* lat, int body_rows, Shape shape,
-                     int ring_warps, bool delta) {
-    const int N = in.N;
-    const int lane_words = mask_words(N), sync_words = mask_words(static_cast<int>(in.ea.size()));
-    Gen g;
-    // delta: shift the sign of slack `t` (an expression) into mask word k / 32 of `m` (one
-    // SHF); the k-th edge of a word ends at bit n - 1 - k % 32 of the word's n edges
-    const auto flag = [&](const std::string& m, int k, const std::string& t) {
-        const std::string w = m + I2S(k / 32);
-        g.line("{ const int t = " + t + "; " + w + " = __funnelshift_l(static_cast<unsigned>(t), " + w + ", 1); }");
+// The frame's inequalities as edges and the order the generated code loads operations in:
+// a topological order of the lane edges and distance-0 sync edges (ties: the earlier lane
+// position, then the lower index), each edge due once both its endpoints are loaded, so
+// that an operation's registers live only until its last edge. Operations in a cycle of
+// those edges (a frame no candidate satisfies) follow in index order.
+struct Walk {
+    struct Edge {
+        int a, b, kind, d;  // kind 0: lane edge a -> b; 1: a lane's wrap (last a to first b, + ii); 2: sync
+        int id;             // lane kinds: the walk position of a; sync: the program index
     };
-    int lane_edges = 0;  // lane edges flagged so far: the walk position of the edge's source
+    std::vector<Edge> edges;
+    std::vector<int> order;
+    std::vector<std::vector<int>> due;  // per operation: the edges evaluated once it is loaded
+};
+
+Walk frame_walk(const FrameInput& in, int body_rows) {
+    const int N = in.N;
+    Walk w;
+    std::vector<std::pair<int, int>> lane_pos(N, {INT_MAX, INT_MAX});
+    int j = 0;  // walk position: the lanes one after another
+    for (size_t l = 0; l < in.lanes.size(); ++l) {
+        const auto& lane = in.lanes[l];
+        for (size_t q = 0; q < lane.size(); ++q, ++j) {
+            lane_pos[lane[q]] = {static_cast<int>(q), static_cast<int>(l)};
+            if (q + 1 < lane.size()) w.edges.push_back({lane[q], lane[q + 1], 0, 0, j});
+            else if (body_rows >= 1) w.edges.push_back({lane[q], lane.front(), 1, 0, j});
+        }
+    }
+    for (size_t e = 0; e < in.ea.size(); ++e) w.edges.push_back({in.ea[e], in.eb[e], 2, in.ed[e], static_cast<int>(e)});
+    std::vector<std::vector<int>> succ(N);
+    std::vector<int> indeg(N, 0);
+    for (const auto& e : w.edges)
+        if (e.kind == 0 || (e.kind == 2 && e.d == 0)) {
+            succ[e.a].push_back(e.b);
+            ++indeg[e.b];
+        }
+    using Key = std::pair<std::pair<int, int>, int>;
+    std::vector<Key> ready;
+    const auto push = [&](int k) {
+        ready.push_back({lane_pos[k], k});
+        std::push_heap(ready.begin(), ready.end(), std::greater<Key>());
+    };
+    for (int k = 0; k < N; ++k)
+        if (indeg[k] == 0) push(k);
+    std::vector<char> placed(N, 0);
+    while (!ready.empty()) {
+        std::pop_heap(ready.begin(), ready.end(), std::greater<Key>());
+        const int k = ready.back().second;
+        ready.pop_back();
+        w.order.push_back(k);
+        placed[k] = 1;
+        for (int t : succ[k])
+            if (--indeg[t] == 0) push(t);
+    }
+    for (int k = 0; k < N; ++k)
+        if (!placed[k]) w.order.push_back(k);
+    std::vector<int> rank(N);
+    for (int i = 0; i < N; ++i) rank[w.order[i]] = i;
+    w.due.assign(N, {});
+    for (size_t e = 0; e < w.edges.size(); ++e)
+        w.due[w.order[std::max(rank[w.edges[e].a], rank[w.edges[e].b])]].push_back(static_cast<int>(e));
+    return w;
+}
+
+// One operation's loads and its contribution to the start/completion extremes.
+void emit_load(Gen& g, int k, const int* lat, int body_rows) {
+    const std::string p = "p" + I2S(k), o = "o" + I2S(k), bp = "bp[" + I2S(k) + "]", bo = "bo[" + I2S(k) + "]";
+    const auto C = [](int i) { return "tfv_spec_c[" + I2S(i) + "]"; };
+    g.line("const int " + p + " = P[" + I2S(k * tfv::kTmaTile) + "];");
+    if (body_rows >= 1) g.line("const int " + o + " = O[" + I2S(k * tfv::kTmaTile) + "];");
+    g.line("mnp = __viaddmin_s32(" + p + ", " + C(g.constant(bp)) + ", mnp);");
+    g.line("mxp = __viaddmax_s32(" + p + ", " + C(g.constant(bp + " + " + I2S(lat[k]))) + ", mxp);");
+    if (body_rows >= 1) {
+        g.line("mno = __viaddmin_s32(" + o + ", " + C(g.constant(bo)) + ", mno);");
+        g.line("mxo = __viaddmax_s32(" + o + ", " + C(g.constant(bo + " + " + I2S(lat[k]))) + ", mxo);");
+    }
+}
+
+// The two instance-class slacks of an edge (t1 empty where the edge has one class): a lane
+// edge (verify.py:270-282; a wrap adds ii later), a sync edge (verify.py:284-292; d * ii
+// is added later).
+std::pair<std::string, std::string> edge_slacks(Gen& g, const Walk::Edge& e, const FrameInput& in,
+                                                const int* issue, const int* lat, int body_rows) {
     const auto bp = [](int k) { return "bp[" + I2S(k) + "]"; };
     const auto bo = [](int k) { return "bo[" + I2S(k) + "]"; };
     const auto P = [](int k) { return "p" + I2S(k); };
     const auto O = [](int k) { return "o" + I2S(k); };
     const auto C = [](int i) { return "tfv_spec_c[" + I2S(i) + "]"; };
-    // Lane walk: each operation's values are loaded once, when its lane reaches it, and
-    // feed the start/completion extremes and the lane inequalities with its predecessor;
-    // the inequalities without II go to l0, the wraps (+ ii) to l1.
+    const int a = e.a, b = e.b, d = e.d;
+    if (e.kind == 0)
+        return {P(b) + " - " + P(a) + " + " + C(g.constant(bp(b) + " - " + bp(a) + " - " + I2S(issue[a]))),
+                body_rows >= 1 ? O(b) + " - " + O(a) + " + " + C(g.constant(bo(b) + " - " + bo(a) + " - " + I2S(issue[a])))
+                               : std::string()};
+    if (e.kind == 1)
+        return {O(b) + " - " + P(a) + " + " + C(g.constant(bo(b) + " - " + bp(a) + " - " + I2S(issue[a]))),
+                body_rows >= 2 ? O(b) + " - " + O(a) + " + " + C(g.constant(bo(b) + " - " + bo(a) + " - " + I2S(issue[a])))
+                               : std::string()};
+    const bool body = in.I - d >= 2;
+    return {(d == 0 ? P(b) : O(b)) + " - " + P(a) + " + " +
+                C(g.constant((d == 0 ? bp(b) : bo(b)) + " - " + bp(a) + " - " + I2S(lat[a]))),
+            body ? O(b) + " - " + O(a) + " + " + C(g.constant(bo(b) + " - " + bo(a) + " - " + I2S(lat[a])))
+                 : std::string()};
+}
+
+// The min form of the frame's inequalities: the statements of Spec::eval, which leave the
+// start/completion extremes in x, the smallest lane slack in lane_min and the smallest sync
+// slack in sync_min, in the load order of frame_walk.
+void emit_min_form(Gen& g, const FrameInput& in, const int* issue, const int* lat, int body_rows) {
+    const Walk w = frame_walk(in, body_rows);
+    std::vector<int> dists;
+    bool wraps = false, lanes = false;
+    for (const auto& e : w.edges) {
+        wraps |= e.kind == 1;
+        lanes |= e.kind == 0;
+        if (e.kind == 2 && std::find(dists.begin(), dists.end(), e.d) == dists.end()) dists.push_back(e.d);
+    }
     g.line("int mnp = INT_MAX, mno = INT_MAX, mxp = INT_MIN, mxo = INT_MIN;");
-    if (delta) {
-        for (int w = 0; w < lane_words; ++w) g.line("unsigned lm" + I2S(w) + " = 0;");
-        for (int w = 0; w < sync_words; ++w) g.line("unsigned sm" + I2S(w) + " = 0;");
-    } else {
-        g.line("int l0 = INT_MAX, l1 = INT_MAX;");
-    }
-    std::vector<char> seen(N, 0);
-    auto load = [&](int k) {
-        g.line("const int " + P(k) + " = P[" + I2S(k * tfv::kTmaTile) + "];");
-        if (body_rows >= 1) g.line("const int " + O(k) + " = O[" + I2S(k * tfv::kTmaTile) + "];");
-        g.line("mnp = __viaddmin_s32(" + P(k) + ", " + C(g.constant(bp(k))) + ", mnp);");
-        g.line("mxp = __viaddmax_s32(" + P(k) + ", " + C(g.constant(bp(k) + " + " + I2S(lat[k]))) + ", mxp);");
-        if (body_rows >= 1) {
-            g.line("mno = __viaddmin_s32(" + O(k) + ", " + C(g.constant(bo(k))) + ", mno);");
-            g.line("mxo = __viaddmax_s32(" + O(k) + ", " + C(g.constant(bo(k) + " + " + I2S(lat[k]))) + ", mxo);");
-        }
-        seen[k] = 1;
-    };
-    bool wraps = false;
-    for (const auto& lane : in.lanes) {
-        for (size_t q = 0; q < lane.size(); ++q) {
-            const int b = lane[q];
-            load(b);
-            if (q == 0) continue;
-            const int a = lane[q - 1];
-            const std::string t0 = P(b) + " - " + P(a) + " + " +
-                                   C(g.constant(bp(b) + " - " + bp(a) + " - " + I2S(issue[a])));
-            const std::string t1 = body_rows >= 1 ? O(b) + " - " + O(a) + " + " +
-                                                        C(g.constant(bo(b) + " - " + bo(a) + " - " + I2S(issue[a])))
-                                                  : std::string();
-            if (delta) {  // the edge of a (walk position lane_edges): a -> b in the same iteration
-                flag("lm", lane_edges++, body_rows >= 1 ? "min(" + t0 + ", " + t1 + ")" : t0);
-            } else {
-                g.line("l0 = min(l0, " + t0 + ");");
-                if (body_rows >= 1) g.line("l0 = min(l0, " + t1 + ");");
-            }
-        }
-        if (!lane.empty() && body_rows >= 1) {
-            const int f = lane.front(), l = lane.back();
-            const std::string t0 = O(f) + " - " + P(l) + " + " +
-                                   C(g.constant(bo(f) + " - " + bp(l) + " - " + I2S(issue[l])));
-            const std::string t1 = body_rows >= 2 ? O(f) + " - " + O(l) + " + " +
-                                                        C(g.constant(bo(f) + " - " + bo(l) + " - " + I2S(issue[l])))
-                                                  : std::string();
-            if (delta) {  // the edge of l: the wrap to the lane's first operation, + ii
-                flag("lm", lane_edges++, (body_rows >= 2 ? "min(" + t0 + ", " + t1 + ")" : t0) + " + ii");
-            } else {
-                g.line("l1 = min(l1, " + t0 + ");");
-                if (body_rows >= 2) g.line("l1 = min(l1, " + t1 + ");");
-            }
-            wraps = true;
-        } else if (!lane.empty() && delta) {  // I == 1: no wrap, the position holds a clear bit
-            flag("lm", lane_edges++, "0");
+    g.line("int l0 = INT_MAX, l1 = INT_MAX;");
+    for (int d : dists) g.line("int s" + I2S(d) + " = INT_MAX;");
+    for (int k : w.order) {
+        emit_load(g, k, lat, body_rows);
+        for (int id : w.due[k]) {
+            const auto& e = w.edges[id];
+            const auto t = edge_slacks(g, e, in, issue, lat, body_rows);
+            const std::string acc = e.kind == 0 ? "l0" : (e.kind == 1 ? "l1" : "s" + I2S(e.d));
+            g.line(acc + " = min(" + acc + ", " + (t.second.empty() ? t.first : "min(" + t.first + ", " + t.second + ")") + ");");
         }
     }
-    for (int k = 0; k < N; ++k)
-        if (!seen[k]) load(k);  // operations in no lane still count for the extremes
     g.line("x.min_p = mnp; x.max_pl = mxp; x.min_o = mno; x.max_ol = mxo;");
-    if (!delta) g.line(wraps ? "lane_min = min(l0, l1 + ii);" : "lane_min = l0;");
-    // Sync inequalities (verify.py:284-292), grouped by distance d and shifted by d * ii at
-    // the end. Values are read again here through volatile loads, so that the walk's
-    // registers need not live until their last use (the edges run in source order, one
-    // reload of the source's values per run).
+    g.line(wraps ? "lane_min = min(l0, l1 + ii);" : (lanes ? "lane_min = l0;" : "lane_min = INT_MAX;"));
+    std::string sync = "INT_MAX";
+    for (int d : dists) sync = "min(" + sync + ", s" + I2S(d) + (d ? " + " + I2S(d) + " * ii" : std::string()) + ")";
+    g.line("sync_min = " + sync + ";");
+}
+
+// The mask form of the frame's inequalities (delta verification): the statements of
+// Spec::eval_masks, which leave the extremes in x and one violation bit per lane edge (lm)
+// and per sync program edge (sm), in the load order of frame_walk, so that the edges a
+// frame shares with the plan frame can be kept by mask. Each edge's flag is shifted in
+// from the bottom of its kind's current word, so the i-th edge of a kind ends at bit
+// n - 1 - i % 32 of word i / 32 (n: that word's edge count); lane_bit[j] receives that
+// position (word * 32 + bit) for the lane edge of walk position j (-1: no edge, a lane's
+// last operation when I == 1) and sync_bit[e] for program edge e.
+void emit_mask_form(Gen& g, const FrameInput& in, const int* issue, const int* lat, int body_rows,
+                    std::vector<int>& lane_bit, std::vector<int>& sync_bit) {
+    const Walk w = frame_walk(in, body_rows);
+    int n_kind[2] = {0, 0};
+    for (const auto& e : w.edges) ++n_kind[e.kind == 2 ? 1 : 0];
+    const int lane_words = mask_words(in.N), sync_words = mask_words(static_cast<int>(in.ea.size()));
+    lane_bit.assign(in.N, -1);
+    sync_bit.assign(in.ea.size(), -1);
+    g.line("int mnp = INT_MAX, mno = INT_MAX, mxp = INT_MIN, mxo = INT_MIN;");
+    for (int i = 0; i < lane_words; ++i) g.line("unsigned lm" + I2S(i) + " = 0;");
+    for (int i = 0; i < sync_words; ++i) g.line("unsigned sm" + I2S(i) + " = 0;");
     std::vector<int> dists;
     for (int d : in.ed)
-        if (std::find(dists.begin(), dists.end(), d) == dists.end()) dists.push_back(d);
-    for (int d : dists)
-        g.line(delta ? (d ? "const int dii" + I2S(d) + " = " + I2S(d) + " * ii;" : std::string())
-                     : "int s" + I2S(d) + " = INT_MAX;");
-    const auto VP = [](int k) { return "VP[" + I2S(k * tfv::kTmaTile) + "]"; };
-    const auto VO = [](int k) { return "VO[" + I2S(k * tfv::kTmaTile) + "]"; };
-    int run = -1, run_id = 0;
-    for (size_t e = 0; e < in.ea.size(); ++e) {
-        const int a = in.ea[e], b = in.eb[e], d = in.ed[e];
-        if (a != run) {
-            run = a;
-            ++run_id;
-            g.line("const int sa" + I2S(run_id) + " = " + VP(a) + ";");
-            if (body_rows >= 1) g.line("const int soa" + I2S(run_id) + " = " + VO(a) + ";");
+        if (d && std::find(dists.begin(), dists.end(), d) == dists.end()) dists.push_back(d);
+    for (int d : dists) g.line("const int dii" + I2S(d) + " = " + I2S(d) + " * ii;");
+    int done[2] = {0, 0};
+    for (int k : w.order) {
+        emit_load(g, k, lat, body_rows);
+        for (int id : w.due[k]) {
+            const auto& e = w.edges[id];
+            const int kind = e.kind == 2 ? 1 : 0;
+            const int i = done[kind]++;
+            const int word = i / 32, n = std::min(32, n_kind[kind] - 32 * word);
+            (kind ? sync_bit[e.id] : lane_bit[e.id]) = 32 * word + n - 1 - i % 32;
+            const auto t = edge_slacks(g, e, in, issue, lat, body_rows);
+            std::string v = t.second.empty() ? t.first : "min(" + t.first + ", " + t.second + ")";
+            if (e.kind == 1) v += " + ii";
+            if (e.kind == 2 && e.d) v += " + dii" + I2S(e.d);
+            const std::string m = (kind ? "sm" : "lm") + I2S(word);
+            g.line("{ const int t = " + v + "; " + m + " = __funnelshift_l(static_cast<unsigned>(t), " + m + ", 1); }");
         }
-        const std::string s = "s" + I2S(d), pa = "sa" + I2S(run_id), oa = "soa" + I2S(run_id);
-        const bool body = in.I - d >= 2;
-        g.line("{");
-        if (d == 0) g.line("    const int xb = " + VP(b) + ";");
-        if (d != 0 || body) g.line("    const int ob = " + VO(b) + ";");
-        const std::string t0 = std::string(d == 0 ? "xb" : "ob") + " - " + pa + " + " +
-                               C(g.constant((d == 0 ? bp(b) : bo(b)) + " - " + bp(a) + " - " + I2S(lat[a])));
-        const std::string t1 =
-            body ? "ob - " + oa + " + " + C(g.constant(bo(b) + " - " + bo(a) + " - " + I2S(lat[a]))) : std::string();
-        if (delta) {  // program edge e: its bit
-            const std::string t = body ? "min(" + t0 + ", " + t1 + ")" : t0;
-            flag("sm", static_cast<int>(e), d ? t + " + dii" + I2S(d) : t);
-        } else {
-            g.line("    " + s + " = min(" + s + ", " + t0 + ");");
-            if (body) g.line("    " + s + " = min(" + s + ", " + t1 + ");");
-        }
-        g.line("}");
     }
-    if (delta) {
-        for (int w = 0; w < lane_words; ++w) g.line("lm[" + I2S(w) + "] = lm" + I2S(w) + ";");
-        for (int w = 0; w < sync_words; ++w) g.line("sm[" + I2S(w) + "] = sm" + I2S(w) + ";");
-    } else {
-        std::string sync = "INT_MAX";
-        for (int d : dists)
-            sync = "min(" + sync + ", s" + I2S(d) + (d ? " + " + I2S(d) + " * ii" : std::string()) + ")";
-        g.line("sync_min = " + sync + ";");
-    }
+    g.line("x.min_p = mnp; x.max_pl = mxp; x.min_o = mno; x.max_ol = mxo;");
+    for (int i = 0; i < lane_words; ++i) g.line("lm[" + I2S(i) + "] = lm" + I2S(i) + ";");
+    for (int i = 0; i < sync_words; ++i) g.line("sm[" + I2S(i) + "] = sm" + I2S(i) + ";");
+}
+
+// ring_warps > 0: the ring kernel (tfv_spec_ring) with that many consumer warps; else the
+// tiles kernel (tfv_spec_kernel) of `shape`. delta: the generated code is the mask form
+// (Spec::eval_masks), which every frame a DeltaTable describes by edges runs, with its bit
+// positions in lane_bit / sync_bit; otherwise the min form (Spec::eval), which only the
+// frame's own candidates run. One form per module: the straight-line code of both would
+// not fit the instruction cache together.
+std::string generate(const FrameInput& in, const int* issue, const int* lat, int body_rows, Shape shape,
+                     int ring_warps, int ring_slots, bool delta, std::vector<int>& lane_bit,
+                     std::vector<int>& sync_bit) {
+    const int N = in.N;
+    const int lane_words = mask_words(N), sync_words = mask_words(static_cast<int>(in.ea.size()));
+    Gen g;
+    if (delta) emit_mask_form(g, in, issue, lat, body_rows, lane_bit, sync_bit);
+    else emit_min_form(g, in, issue, lat, body_rows);
+    const std::string body = g.eval;
 
     std::string src;
     src += "// Generated by tfv_jit.cu for one frame.\n";
@@ -342,6 +419,10 @@ std::string generate(const FrameInput& in, const int* issue, const int* lat, int
     src += "    static constexpr int kSyncWords = " + I2S(sync_words) + ";\n";
     src += "    static constexpr int kSuper = " + I2S(shape.super) + ";\n";
     src += "    static constexpr int kPasses = " + I2S(shape.passes) + ";\n";
+    const std::string prelude =
+        "        const int16_t* P = reinterpret_cast<const int16_t*>(rp);\n"
+        "        const int16_t* O = reinterpret_cast<const int16_t*>(rp + " +
+        I2S(static_cast<long long>(N) * tfv::kTmaRowBytes) + ");\n        (void)O;\n";
     if (delta) {
         src += "    __device__ __forceinline__ static void eval(const char*, int, tfv::Extremes&, int&, int&) {}\n";
         src += "    __device__ __forceinline__ static void eval_masks(const char* rp, int ii, tfv::Extremes& x,\n";
@@ -352,13 +433,8 @@ std::string generate(const FrameInput& in, const int* issue, const int* lat, int
         src += "    __device__ __forceinline__ static void eval(const char* rp, int ii, tfv::Extremes& x, int& lane_min,\n";
         src += "                                                int& sync_min) {\n";
     }
-    src += "        const int16_t* P = reinterpret_cast<const int16_t*>(rp);\n";
-    src += "        const int16_t* O = reinterpret_cast<const int16_t*>(rp + " + I2S(static_cast<long long>(N) * tfv::kTmaRowBytes) + ");\n";
-    src += "        const volatile int16_t* VP = P;\n";
-    src += "        const volatile int16_t* VO = O;\n";
-    src += "        (void)O; (void)VP; (void)VO;\n";
-    src += g.eval;
-    src += "    }\n};\n";
+    src += prelude + body + "    }\n";
+    src += "};\n";
     // one warp: the base starts staged in shared memory, then every 32nd constant per thread
     src += "extern \"C\" __global__ void __launch_bounds__(32) tfv_spec_consts(const int* bp_in, const int* bo_in, int* c) {\n";
     src += "    __shared__ int bp[" + I2S(N) + "], bo[" + I2S(N) + "];\n";
@@ -373,8 +449,9 @@ std::string generate(const FrameInput& in, const int* issue, const int* lat, int
         src += "    tfv::DevProblem p, tfv::DevFrames fr, tfv::FrameTable ft, tfv::DevPeriodic b, tfv::DevResults out, int n_tiles,\n";
         src += "    const __grid_constant__ CUtensorMap map_p, const __grid_constant__ CUtensorMap map_o,\n";
         src += "    const int* spec_frame, tfv::DeltaTable dt, int slots, unsigned long long wait_ns) {\n";
-        src += "    tfv::tma_ring_body<" + I2S(body_rows) + ", Spec, " + I2S(ring_warps) +
-               ">(p, fr, ft, b, out, n_tiles, &map_p, &map_o, *spec_frame, dt, slots, wait_ns);\n";
+        src += "    (void)slots;  // the body's ring has " + I2S(ring_slots) + " slots, fixed at compile time\n";
+        src += "    tfv::tma_ring_body<" + I2S(body_rows) + ", Spec, " + I2S(ring_warps) + ", " + I2S(ring_slots) +
+               ">(p, fr, ft, b, out, n_tiles, &map_p, &map_o, *spec_frame, dt, wait_ns);\n";
         src += "}\n";
         return src;
     }
@@ -419,9 +496,16 @@ struct tfv_plan {
     cudaEvent_t fork = nullptr, join = nullptr;
     size_t smem = 0;
     int per_sm = 0;
+    int ring_warps = 0;  // consumer warps of the ring kernel
     std::string source;
+    // kernel timing (tfv_plan_set_timing): an event pair per recorded launch
+    bool timing = false;
+    std::vector<std::pair<cudaEvent_t, cudaEvent_t>> events;
+    size_t timed = 0;
     // the plan frame's signature on the device: [spec frame checked per call (int)] [lane_pos
-    // row N x u16, padded to 4 bytes] [sync program edges sig_len x 3 int]
+    // row N x u16, padded to 4 bytes] [sync program edges sig_len x 3 int] and, with delta
+    // verification, the generated code's mask bit of each lane edge [N int, by walk
+    // position] and sync program edge [sig_len int]
     void* sig = nullptr;
     int sig_len = 0;
 };
@@ -480,7 +564,8 @@ int tfv_plan_create_with(const tfv_problem* p, const tfv_frames* host_frames, in
                          const tfv_plan_options* options, tfv_plan** out) {
     if (!p || !out) return tfv_internal_fail(TFV_ERR_INVALID_ARGUMENT, "problem and out must not be NULL");
     const int want = options ? options->kernel : TFV_PLAN_AUTO;
-    const int ring_warps = options && options->ring_warps ? options->ring_warps : kRingWarpsDefault;
+    const bool fixed_warps = options && options->ring_warps;
+    int ring_warps = fixed_warps ? options->ring_warps : kRingWarpsDefault;
     if (want != TFV_PLAN_AUTO && want != TFV_PLAN_TILES && want != TFV_PLAN_RING)
         return tfv_internal_fail(TFV_ERR_INVALID_ARGUMENT, "unknown plan kernel");
     if (ring_warps < 1 || ring_warps > 31)
@@ -508,57 +593,6 @@ int tfv_plan_create_with(const tfv_problem* p, const tfv_frames* host_frames, in
             shape = candidate;
             break;
         }
-    // ring slots that fit beside the fixed part of the ring's shared memory
-    const size_t ring_fixed = tfv::ring_smem_bytes(d, 0, ring_warps);
-    const int slots = ring_fixed >= static_cast<size_t>(optin)
-                          ? 0
-                          : static_cast<int>(std::min<size_t>(tfv::kRingMaxSlots,
-                                                              (static_cast<size_t>(optin) - ring_fixed) /
-                                                                  tfv::ring_slot_bytes(d)));
-    if (want == TFV_PLAN_RING && slots < kRingMinSlots) {
-        delete plan;
-        return tfv_internal_fail(TFV_ERR_UNSUPPORTED, "the ring kernel needs three tile slots in shared memory");
-    }
-    plan->kernel = want == TFV_PLAN_TILES || slots < kRingMinSlots ? TFV_PLAN_TILES : TFV_PLAN_RING;
-    if (plan->kernel == TFV_PLAN_RING) {
-        plan->slots = slots;
-        plan->threads = 32 * (ring_warps + 1);
-    } else {
-        plan->super = shape.super;
-        plan->passes = shape.passes;
-        plan->threads = tfv::kTmaTile * shape.super / shape.passes;
-    }
-    plan->lane_words = mask_words(in.N);
-    plan->sync_words = mask_words(static_cast<int>(in.ea.size()));
-    plan->delta = !(options && options->no_delta) && plan->lane_words <= kDeltaMaxWords &&
-                  plan->sync_words <= kDeltaMaxWords;
-    plan->source = generate(in, tfv_internal_issue_host(p), tfv_internal_latency_host(p), body_rows, shape,
-                            plan->kernel == TFV_PLAN_RING ? ring_warps : 0, plan->delta);
-
-    const Nvrtc& nv = nvrtc();
-    void* prog = nullptr;
-    if (nv.create(&prog, plan->source.c_str(), "tfv_spec.cu", kJitHeaderCount, kJitHeaders, kJitHeaderNames) != 0) {
-        delete plan;
-        return tfv_internal_fail(TFV_ERR_UNSUPPORTED, "nvrtcCreateProgram failed");
-    }
-    const char* flags[] = {"--gpu-architecture=sm_100a", "-default-device", "--std=c++17", "-lineinfo"};
-    const int compiled = nv.compile(prog, 4, flags);
-    if (compiled != 0) {
-        size_t n = 0;
-        nv.log_size(prog, &n);
-        std::string log(n, '\0');
-        nv.log(prog, log.data());
-        nv.destroy(&prog);
-        delete plan;
-        std::fprintf(stderr, "tfv_plan_create: run-time compilation failed:\n%s\n", log.c_str());
-        return tfv_internal_fail(TFV_ERR_UNSUPPORTED, "run-time compilation of the frame-specialised kernel failed");
-    }
-    size_t bytes = 0;
-    nv.cubin_size(prog, &bytes);
-    std::vector<char> cubin(bytes);
-    nv.cubin(prog, cubin.data());
-    nv.destroy(&prog);
-
     const Driver& drv = driver();
     CurrentDevice current(plan->device);
     cudaError_t e = current.status();
@@ -568,15 +602,83 @@ int tfv_plan_create_with(const tfv_problem* p, const tfv_frames* host_frames, in
         return tfv_internal_cuda_fail(e, "tfv_plan_create");
     }
     size_t sym_bytes = 0;
-    if (drv.load(&plan->module, cubin.data()) != CUDA_SUCCESS ||
-        drv.function(&plan->function, plan->module,
-                     plan->kernel == TFV_PLAN_RING ? "tfv_spec_ring" : "tfv_spec_kernel") != CUDA_SUCCESS ||
-        drv.function(&plan->consts_kernel, plan->module, "tfv_spec_consts") != CUDA_SUCCESS ||
-        drv.global(&plan->consts_symbol, &sym_bytes, plan->module, "tfv_spec_c") != CUDA_SUCCESS) {
-        if (plan->module) drv.unload(plan->module);
-        delete plan;
-        return tfv_internal_fail(TFV_ERR_CUDA, "loading the frame-specialised module failed");
+    std::vector<int> lane_bit, sync_bit;
+    // the ring's consumer warps: the caller's count, else kRingWarpSteps until the compiled
+    // kernel keeps every value in registers (no local memory)
+    for (int attempt = 0;; ++attempt) {
+        // ring slots that fit beside the fixed part of the ring's shared memory
+        const size_t ring_fixed = tfv::ring_smem_bytes(d, 0, ring_warps);
+        const int slots = ring_fixed >= static_cast<size_t>(optin)
+                              ? 0
+                              : static_cast<int>(std::min<size_t>(tfv::kRingMaxSlots,
+                                                                  (static_cast<size_t>(optin) - ring_fixed) /
+                                                                      tfv::ring_slot_bytes(d)));
+        if (want == TFV_PLAN_RING && slots < kRingMinSlots) {
+            delete plan;
+            return tfv_internal_fail(TFV_ERR_UNSUPPORTED, "the ring kernel needs three tile slots in shared memory");
+        }
+        plan->kernel = want == TFV_PLAN_TILES || slots < kRingMinSlots ? TFV_PLAN_TILES : TFV_PLAN_RING;
+        if (plan->kernel == TFV_PLAN_RING) {
+            plan->slots = slots;
+            plan->threads = 32 * (ring_warps + 1);
+        } else {
+            plan->super = shape.super;
+            plan->passes = shape.passes;
+            plan->threads = tfv::kTmaTile * shape.super / shape.passes;
+        }
+        plan->lane_words = mask_words(in.N);
+        plan->sync_words = mask_words(static_cast<int>(in.ea.size()));
+        plan->delta = !(options && options->no_delta) && plan->lane_words <= kDeltaMaxWords &&
+                      plan->sync_words <= kDeltaMaxWords;
+        plan->source = generate(in, tfv_internal_issue_host(p), tfv_internal_latency_host(p), body_rows, shape,
+                                plan->kernel == TFV_PLAN_RING ? ring_warps : 0, plan->slots, plan->delta, lane_bit,
+                                sync_bit);
+
+        const Nvrtc& nv = nvrtc();
+        void* prog = nullptr;
+        if (nv.create(&prog, plan->source.c_str(), "tfv_spec.cu", kJitHeaderCount, kJitHeaders, kJitHeaderNames) != 0) {
+            delete plan;
+            return tfv_internal_fail(TFV_ERR_UNSUPPORTED, "nvrtcCreateProgram failed");
+        }
+        const char* flags[] = {"--gpu-architecture=sm_100a", "-default-device", "--std=c++17", "-lineinfo"};
+        const int compiled = nv.compile(prog, 4, flags);
+        if (compiled != 0) {
+            size_t n = 0;
+            nv.log_size(prog, &n);
+            std::string log(n, '\0');
+            nv.log(prog, log.data());
+            nv.destroy(&prog);
+            delete plan;
+            std::fprintf(stderr, "tfv_plan_create: run-time compilation failed:\n%s\n", log.c_str());
+            return tfv_internal_fail(TFV_ERR_UNSUPPORTED, "run-time compilation of the frame-specialised kernel failed");
+        }
+        size_t bytes = 0;
+        nv.cubin_size(prog, &bytes);
+        std::vector<char> cubin(bytes);
+        nv.cubin(prog, cubin.data());
+        nv.destroy(&prog);
+
+        if (drv.load(&plan->module, cubin.data()) != CUDA_SUCCESS ||
+            drv.function(&plan->function, plan->module,
+                         plan->kernel == TFV_PLAN_RING ? "tfv_spec_ring" : "tfv_spec_kernel") != CUDA_SUCCESS ||
+            drv.function(&plan->consts_kernel, plan->module, "tfv_spec_consts") != CUDA_SUCCESS ||
+            drv.global(&plan->consts_symbol, &sym_bytes, plan->module, "tfv_spec_c") != CUDA_SUCCESS) {
+            if (plan->module) drv.unload(plan->module);
+            delete plan;
+            return tfv_internal_fail(TFV_ERR_CUDA, "loading the frame-specialised module failed");
+        }
+        int local = 0;
+        const bool retry = plan->kernel == TFV_PLAN_RING && !fixed_warps &&
+                           attempt + 1 < static_cast<int>(sizeof(kRingWarpSteps) / sizeof(kRingWarpSteps[0])) &&
+                           drv.get_attribute &&
+                           drv.get_attribute(&local, CU_FUNC_ATTRIBUTE_LOCAL_SIZE_BYTES, plan->function) == CUDA_SUCCESS &&
+                           local > 0;
+        if (!retry) break;
+        drv.unload(plan->module);
+        plan->module = nullptr;
+        ring_warps = kRingWarpSteps[attempt + 1];
     }
+    plan->ring_warps = plan->kernel == TFV_PLAN_RING ? ring_warps : 0;
     plan->smem = plan->kernel == TFV_PLAN_RING ? tfv::ring_smem_bytes(d, plan->slots, ring_warps)
                                                : tfv::tma_body_smem_bytes(d, plan->super, plan->passes, true);
     if (drv.set_attribute(plan->function, CU_FUNC_ATTRIBUTE_MAX_DYNAMIC_SHARED_SIZE_BYTES,
@@ -602,11 +704,15 @@ int tfv_plan_create_with(const tfv_problem* p, const tfv_frames* host_frames, in
             for (int c = 0; c < 3; ++c) edges.push_back(host_frames->sync_edges[3 * e + c]);
         }
         plan->sig_len = static_cast<int>(in.ea.size());
+        lane_bit.resize(d.n_ops, -1);
+        sync_bit.resize(in.ea.size(), -1);
+        edges.insert(edges.end(), lane_bit.begin(), lane_bit.end());
+        edges.insert(edges.end(), sync_bit.begin(), sync_bit.end());
         const size_t bytes = sizeof(int) + lp_bytes + sizeof(int) * edges.size();
         std::vector<char> image(bytes, 0);
         std::memcpy(image.data() + sizeof(int), host_frames->lane_pos + static_cast<size_t>(frame) * d.n_ops,
                     sizeof(uint16_t) * d.n_ops);
-        if (!edges.empty()) std::memcpy(image.data() + sizeof(int) + lp_bytes, edges.data(), sizeof(int) * edges.size());
+        std::memcpy(image.data() + sizeof(int) + lp_bytes, edges.data(), sizeof(int) * edges.size());
         e = cudaMalloc(&plan->sig, bytes);
         if (e == cudaSuccess) e = cudaMemcpy(plan->sig, image.data(), bytes, cudaMemcpyHostToDevice);
         if (e != cudaSuccess) {
@@ -635,6 +741,10 @@ int tfv_plan_destroy(tfv_plan* plan) {
     if (plan->fork) cudaEventDestroy(plan->fork);
     if (plan->join) cudaEventDestroy(plan->join);
     if (plan->side) cudaStreamDestroy(plan->side);
+    for (auto& pair : plan->events) {
+        cudaEventDestroy(pair.first);
+        cudaEventDestroy(pair.second);
+    }
     if (plan->module) driver().unload(plan->module);
     delete plan;
     cudaGetLastError();  // a teardown call's error must not surface at a later launch check
@@ -648,6 +758,28 @@ int tfv_plan_source(const tfv_plan* plan, char* buffer, size_t size) {
 }
 
 int tfv_plan_delta(const tfv_plan* plan) { return plan ? (plan->delta ? 1 : 0) : -1; }
+
+int tfv_plan_ring_warps(const tfv_plan* plan) { return plan ? plan->ring_warps : -1; }
+
+int tfv_plan_set_timing(tfv_plan* plan, int enable) {
+    if (!plan) return tfv_internal_fail(TFV_ERR_INVALID_ARGUMENT, "plan must not be NULL");
+    plan->timing = enable != 0;
+    return TFV_OK;
+}
+
+int tfv_plan_kernel_times(tfv_plan* plan, float* ms, int capacity, int* count) {
+    if (!plan || !count || capacity < 0 || (capacity > 0 && !ms))
+        return tfv_internal_fail(TFV_ERR_INVALID_ARGUMENT, "invalid arguments");
+    CurrentDevice current(plan->device);
+    cudaError_t e = current.status();
+    const int n = static_cast<int>(plan->timed);
+    for (int i = 0; e == cudaSuccess && i < n && i < capacity; ++i)
+        e = cudaEventElapsedTime(&ms[i], plan->events[i].first, plan->events[i].second);
+    if (e != cudaSuccess) return tfv_internal_cuda_fail(e, "tfv_plan_kernel_times");
+    *count = n;
+    plan->timed = 0;
+    return TFV_OK;
+}
 
 int tfv_verify_periodic_planned(tfv_plan* plan, const tfv_frames* frames, void* table, size_t table_bytes,
                                 const tfv_periodic_batch* b, int spec_frame, const tfv_results* r, void* stream) {
@@ -719,8 +851,9 @@ int tfv_verify_periodic_planned(tfv_plan* plan, const tfv_frames* frames, void* 
             plan->delta_bytes = need;
         }
         dt = tfv::delta_table_view(plan->delta_buf, frames->n_frames, plan->lane_words, plan->sync_words);
-        e = tfv::launch_delta_frames(d, df, view, spec_dev, b->base_prologue, b->base_offset, dt,
-                                     tfv_internal_sm_count(p), s);
+        const int* lane_bit = sig_edges + 3 * plan->sig_len;
+        e = tfv::launch_delta_frames(d, df, view, spec_dev, b->base_prologue, b->base_offset, lane_bit,
+                                     lane_bit + d.n_ops, dt, tfv_internal_sm_count(p), s);
         if (e != cudaSuccess) return tfv_internal_cuda_fail(e, "tfv_verify_periodic_planned");
     }
     e = cudaStreamWaitEvent(s, plan->join, 0);  // the constants are in place
@@ -734,9 +867,29 @@ int tfv_verify_periodic_planned(tfv_plan* plan, const tfv_frames* frames, void* 
     tfv::DevProblem dp = d;
     unsigned long long wait_ns = tfv::device_wait_ns();
     void* args[] = {&dp, &df, &view, &db, &dr, &n_tiles, &map_p, &map_o, &spec_dev, &dt, &slots, &wait_ns};
+    const std::pair<cudaEvent_t, cudaEvent_t>* timed = nullptr;
+    if (plan->timing) {  // an event pair around the verification kernel alone
+        if (plan->timed == plan->events.size()) {
+            cudaEvent_t first = nullptr, second = nullptr;
+            e = cudaEventCreate(&first);
+            if (e == cudaSuccess) e = cudaEventCreate(&second);
+            if (e != cudaSuccess) {
+                if (first) cudaEventDestroy(first);
+                return tfv_internal_cuda_fail(e, "tfv_verify_periodic_planned");
+            }
+            plan->events.emplace_back(first, second);
+        }
+        timed = &plan->events[plan->timed++];
+        e = cudaEventRecord(timed->first, s);
+        if (e != cudaSuccess) return tfv_internal_cuda_fail(e, "tfv_verify_periodic_planned");
+    }
     cr = drv.launch(plan->function, grid, 1, 1, plan->threads, 1, 1, static_cast<unsigned>(plan->smem),
                     reinterpret_cast<CUstream>(s), args, nullptr);
     if (cr != CUDA_SUCCESS) return tfv_internal_fail(TFV_ERR_CUDA, "launching the frame-specialised kernel failed");
+    if (timed) {
+        e = cudaEventRecord(timed->second, s);
+        if (e != cudaSuccess) return tfv_internal_cuda_fail(e, "tfv_verify_periodic_planned");
+    }
     return TFV_OK;
 }
 

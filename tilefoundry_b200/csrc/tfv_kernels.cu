@@ -520,16 +520,21 @@ __global__ void __launch_bounds__(32) compile_sync_programs_kernel(DevProblem p,
 // triples of the two programs (edges before each set's first static failure); f's edges
 // absent from m's program are added as their set_prog entries. Frames with a structural
 // class need no lane or sync answer; frames with more than kDeltaMax added edges of a kind
-// are left to the frame-table path.
-// Bit k of `bits` (edge k of a mask word with n edges) moved to bit n - 1 - k: the
-// generated code shifts each edge's flag in from the bottom, so its first edge ends on top.
-__device__ __forceinline__ unsigned shifted_order(unsigned bits, int n) {
-    return n <= 0 ? 0u : __brev(bits) >> (32 - n);
+// are left to the frame-table path. The keep masks put each kept edge at the bit the plan's
+// generated code gives it: lane_bit[j] for the lane edge of walk position j (-1: none),
+// sync_bit[e] for program edge e, as word * 32 + bit.
+// The keep words of one warp's 32 edges: lane l keeps its edge at `bit` (or none), and
+// acc[w] collects the bits of word w.
+__device__ __forceinline__ void keep_bits(bool kept, int bit, int words, unsigned* acc) {
+#pragma unroll
+    for (int w = 0; w < kDeltaMaxWords; ++w)
+        if (w < words)
+            acc[w] |= __reduce_or_sync(kFull, kept && bit >= 0 && (bit >> 5) == w ? 1u << (bit & 31) : 0u);
 }
 
 __global__ void __launch_bounds__(128) delta_frames_kernel(DevProblem p, DevFrames fr, FrameTable ft, const int* m_ptr,
                                                            const int* base_prologue, const int* base_offset,
-                                                           DeltaTable dt) {
+                                                           const int* lane_bit, const int* sync_bit, DeltaTable dt) {
     const int N = p.n_ops, I = p.iterations;
     const int m = *m_ptr;  // the checked specialised frame, -1 when the caller's did not match
     const int lane = threadIdx.x & 31;
@@ -573,9 +578,10 @@ __global__ void __launch_bounds__(128) delta_frames_kernel(DevProblem p, DevFram
             if (lane == 0) dt.header[f] = make_int4(f == m ? kDeltaSame : kDeltaEdges, 0, 0, 0);
             continue;
         }
-        // lane edges, by m's walk position j of their source a (the generated code's bit order)
+        // lane edges, by m's walk position j of their source a
         int n_lane = 0;
-        for (int w = 0; w < dt.lane_words; ++w) {
+        unsigned acc[kDeltaMaxWords] = {0, 0, 0, 0};
+        for (int w = 0; w * 32 < N; ++w) {
             const int j = w * 32 + lane;
             const int a = j < N ? min(static_cast<int>(ft.order[static_cast<size_t>(j) * fr.n_frames + m]), N - 1) : 0;
             const int sf = j < N ? ft.succ[static_cast<size_t>(f) * N + a] : 0;
@@ -583,9 +589,8 @@ __global__ void __launch_bounds__(128) delta_frames_kernel(DevProblem p, DevFram
             const bool kept = j < N && sf == sm;
             const bool wrap = (sf & kWrap) != 0;
             const bool add = j < N && !kept && sf >= 0 && !(wrap && I < 2);
-            const unsigned kept_bits = __ballot_sync(kFull, kept);
             const unsigned add_bits = __ballot_sync(kFull, add);
-            if (lane == 0) keep[w] = shifted_order(kept_bits, min(32, N - w * 32));
+            keep_bits(kept, j < N ? lane_bit[j] : -1, dt.lane_words, acc);
             const int pos = n_lane + __popc(add_bits & ((1u << lane) - 1));
             if (add && pos < kDeltaMax) {
                 const int b = sf & kSuccMask;
@@ -603,6 +608,8 @@ __global__ void __launch_bounds__(128) delta_frames_kernel(DevProblem p, DevFram
             }
             n_lane += __popc(add_bits);
         }
+        if (lane == 0)
+            for (int w = 0; w < dt.lane_words; ++w) keep[w] = acc[w];
         // sync edges
         int n_sync = 0;
         const int s_f = fr.sync_set[f];
@@ -631,7 +638,14 @@ __global__ void __launch_bounds__(128) delta_frames_kernel(DevProblem p, DevFram
                 n_sync += __popc(bits);
             }
             __syncwarp();
-            for (int w = lane; w < dt.sync_words; w += 32) skeep[w] = shifted_order(kept_w[w], min(32, len_m - w * 32));
+            unsigned sacc[kDeltaMaxWords] = {0, 0, 0, 0};
+            for (int e0 = 0; e0 < len_m; e0 += 32) {
+                const int e = e0 + lane;
+                keep_bits(e < len_m && ((kept_w[e >> 5] >> (e & 31)) & 1u), e < len_m ? sync_bit[e] : -1,
+                          dt.sync_words, sacc);
+            }
+            if (lane == 0)
+                for (int w = 0; w < dt.sync_words; ++w) skeep[w] = sacc[w];
         }
         if (lane == 0)
             dt.header[f] = make_int4(n_lane > kDeltaMax || n_sync > kDeltaMax ? kDeltaGeneric : kDeltaEdges,
@@ -640,12 +654,13 @@ __global__ void __launch_bounds__(128) delta_frames_kernel(DevProblem p, DevFram
 }
 
 cudaError_t launch_delta_frames(const DevProblem& p, const DevFrames& f, FrameTable t, const int* spec_frame,
-                                const int* base_prologue, const int* base_offset, DeltaTable d, int sm_count,
-                                cudaStream_t stream) {
+                                const int* base_prologue, const int* base_offset, const int* lane_bit,
+                                const int* sync_bit, DeltaTable d, int sm_count, cudaStream_t stream) {
     if (f.n_frames <= 0) return cudaSuccess;
     const int grid = min((f.n_frames + 3) / 4, sm_count * 8);
     // four warps a block: the kernel keeps one row of kept_sync per warp
-    delta_frames_kernel<<<grid, 128, 0, stream>>>(p, f, t, spec_frame, base_prologue, base_offset, d);
+    delta_frames_kernel<<<grid, 128, 0, stream>>>(p, f, t, spec_frame, base_prologue, base_offset, lane_bit, sync_bit,
+                                                   d);
     return cudaGetLastError();
 }
 

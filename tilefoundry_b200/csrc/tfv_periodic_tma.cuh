@@ -256,9 +256,14 @@ __device__ __forceinline__ void column_verdict(const DevProblem& p, const DevFra
                     for (int w = 0; w < Spec::kSyncWords; ++w) sm[w] &= keep[Spec::kLaneWords + w];
                     const int4 h = dt.header[f];
                     const int4* added = dt.prog + static_cast<size_t>(f) * 2 * kDeltaMax;
-                    for (int j = 0; j < h.y; ++j) lane_min = min(lane_min, prog_slack(added[j], row_p, to_bytes, ii));
-                    for (int j = 0; j < h.z; ++j)
-                        sync_min = min(sync_min, prog_slack(added[kDeltaMax + j], row_p, to_bytes, ii));
+                    // the added lane edges, then the added sync edges, in one loop: a warp runs
+                    // as many rounds as its longest list of both
+                    for (int j = 0; j < h.y + h.z; ++j) {
+                        const bool is_lane = j < h.y;
+                        const int v = prog_slack(added[is_lane ? j : kDeltaMax + j - h.y], row_p, to_bytes, ii);
+                        if (is_lane) lane_min = min(lane_min, v);
+                        else sync_min = min(sync_min, v);
+                    }
                 }
                 unsigned any_lane = 0, any_sync = 0;
 #pragma unroll
@@ -569,6 +574,7 @@ __device__ __forceinline__ int select_bit(unsigned m, int r) {
 // CTA aborts.
 __device__ __forceinline__ bool ring_wait(uint64_t* bar, unsigned parity, const int* abort,
                                           unsigned long long wait_ns) {
+    if (mbar_try_wait_suspend(bar, parity, kRingSuspendNs)) return true;  // the usual case: no clock read
     const unsigned long long start = global_ns();
     for (long long spin = 0; spin < kWaitSpins; ++spin) {
         if (mbar_try_wait_suspend(bar, parity, kRingSuspendNs)) return true;
@@ -577,12 +583,14 @@ __device__ __forceinline__ bool ring_wait(uint64_t* bar, unsigned parity, const 
     return false;
 }
 
-template <int kBodyRows, class Spec, int kWarps>
+template <int kBodyRows, class Spec, int kWarps, int kSlots>
 __device__ __forceinline__ void tma_ring_body(const DevProblem& p, const DevFrames& fr, const FrameTable& ft,
                                               const DevPeriodic& b, const DevResults& out, int n_tiles,
                                               const CUtensorMap* map_p, const CUtensorMap* map_o, int spec_frame,
-                                              const DeltaTable& dt, int slots, unsigned long long wait_ns) {
+                                              const DeltaTable& dt, unsigned long long wait_ns) {
     static_assert(kWarps >= 1 && kWarps <= 31, "a producer warp and 1..31 consumer warps per CTA");
+    static_assert(kSlots >= 1 && kSlots <= kRingMaxSlots, "1..kRingMaxSlots tile slots");
+    constexpr int slots = kSlots;
     extern __shared__ __align__(128) unsigned char smem[];
     const int N = p.n_ops;
     const int t = threadIdx.x, warp = t >> 5, lane = t & 31;
@@ -677,7 +685,7 @@ __device__ __forceinline__ void tma_ring_body(const DevProblem& p, const DevFram
             // the slot must carry tile i before its `full` parity names that tile
             bool ok = false;
             if (lane == 0) {
-                const unsigned long long start = global_ns();
+                unsigned long long start = 0;  // read once the first look finds an older tile
                 for (long long spin = 0; spin < kWaitSpins; ++spin) {
                     const int tag = ld_acquire(&tags[slot]);
                     if (tag >= i) {  // never above i: tile i + slots needs this unit first
@@ -685,6 +693,7 @@ __device__ __forceinline__ void tma_ring_body(const DevProblem& p, const DevFram
                         break;
                     }
                     if (tag >= 0 && !ring_wait(&empty[slot], (tag / slots) & 1, abort, wait_ns)) break;  // tile tag's units
+                    if (start == 0) start = global_ns();
                     if (*reinterpret_cast<volatile int*>(abort) || global_ns() - start > wait_ns) break;
                     __nanosleep(128);  // the producer refills the slot next
                 }
@@ -703,6 +712,7 @@ __device__ __forceinline__ void tma_ring_body(const DevProblem& p, const DevFram
                 continue;
             }
             const int* fs = frames_s + slot * kTile;
+            const int left = static_cast<int>(min(b.n - first, static_cast<long long>(kTile)));  // live columns
             int col = q * 32 + lane;
             bool spec = false;
             if constexpr (Spec::kEnabled) {
@@ -715,9 +725,8 @@ __device__ __forceinline__ void tma_ring_body(const DevProblem& p, const DevFram
                 int total = 0;
 #pragma unroll
                 for (int w = 0; w < kRingUnits; ++w) {
-                    const long long c = first + w * 32 + lane;
-                    m[w] = __ballot_sync(0xFFFFFFFFu,
-                                         c < b.n && spec_candidate<Spec>(fs[w * 32 + lane], spec_frame, fr.n_frames, dt));
+                    m[w] = __ballot_sync(0xFFFFFFFFu, w * 32 + lane < left &&
+                                                          spec_candidate<Spec>(fs[w * 32 + lane], spec_frame, fr.n_frames, dt));
                     total += __popc(m[w]);
                 }
                 const int pos = q * 32 + lane;
@@ -738,7 +747,7 @@ __device__ __forceinline__ void tma_ring_body(const DevProblem& p, const DevFram
                 spec = q * 32 < (total & ~31);  // whole units run the generated code
             }
             const long long c = first + col;
-            const bool live = c < b.n;
+            const bool live = col < left;
             const int ii = live ? ii_s[slot * kTile + col] : 0;
             const int16_t* const mp = tile_p(slot) + col;
             int cls = 0, ms = 0;

@@ -63,18 +63,13 @@ def _objective(ii: np.ndarray, makespan: np.ndarray, iterations: int) -> np.ndar
     return lead * (1 << 32) + makespan.astype(np.int64)
 
 
-def _neighbours(packed, incumbent: Witness, n: int, rng: np.random.Generator, step: int):
-    """Seeded neighbours of the incumbent, as deltas against its own starts.
-
-    Kinds: (0) a tighter II with the same offsets; (1) a few operations pulled earlier in
-    the prologue and the body; (2) a tighter II with the body offsets of late operations
-    pulled earlier; (3) one operation moved to another lane position, times kept.
-    """
+def _lane_moves(packed, incumbent: Witness, rng: np.random.Generator, count: int = 16) -> FrameSet:
+    """The incumbent's frame (index 0) and ``count`` frames with one operation moved to a
+    random position of a random lane."""
     N = packed.n_ops
     frames = FrameSet(packed)
-    base = frames.add(incumbent.lanes, incumbent.sync)
-    moves = []
-    for _ in range(16):
+    frames.add(incumbent.lanes, incumbent.sync)
+    for _ in range(count):
         lanes = [list(lane) for lane in incumbent.lanes]
         op = packed.op_ids[int(rng.integers(N))]
         for lane in lanes:
@@ -82,35 +77,49 @@ def _neighbours(packed, incumbent: Witness, n: int, rng: np.random.Generator, st
                 lane.remove(op)
         target = lanes[int(rng.integers(len(lanes)))]
         target.insert(int(rng.integers(len(target) + 1)), op)
-        moves.append(frames.add(lanes, incumbent.sync))
-    kind = rng.integers(0, 4, size=n)
-    dp = np.zeros((N, n), dtype=np.int64)
-    dq = np.zeros((N, n), dtype=np.int64)
-    ii = np.full(n, incumbent.ii, dtype=np.int64)
-    frame = np.full(n, base, dtype=np.int32)
-    cut = rng.integers(1, max(2, step) + 1, size=n)
-    ii[(kind == 0) | (kind == 2)] -= cut[(kind == 0) | (kind == 2)]
-    for sel in (kind == 1, kind == 2):
-        cols = np.flatnonzero(sel)
-        for _ in range(3):
-            ops = rng.integers(0, N, size=cols.size)
-            pull = rng.integers(1, max(2, step) + 1, size=cols.size)
-            dp[ops, cols] -= np.where(rng.random(cols.size) < 0.5, pull, 0)
-            dq[ops, cols] -= pull
-    cols = np.flatnonzero(kind == 3)
-    frame[cols] = np.array(moves, dtype=np.int32)[rng.integers(0, len(moves), size=cols.size)]
-    # keep every materialised start representable and non-negative before the verifier sees it
-    dp = np.maximum(dp, -incumbent.prologue[:, None])
-    dq = np.maximum(dq, -(incumbent.offset[:, None] + np.maximum(ii, 1)[None, :]))
-    batch = PeriodicBatch(
-        base_prologue=incumbent.prologue.astype(np.int32),
-        base_offset=incumbent.offset.astype(np.int32),
-        prologue_delta=np.ascontiguousarray(np.clip(dp, -32768, 32767).astype(np.int16)),
-        offset_delta=np.ascontiguousarray(np.clip(dq, -32768, 32767).astype(np.int16)),
-        ii=np.maximum(ii, 1).astype(np.int32),
-        frame=frame,
-    )
-    return frames, batch
+        frames.add(lanes, incumbent.sync)
+    return frames
+
+
+def _device_neighbours(torch, incumbent: Witness, n: int, n_frames: int, gen, step: int, dev):
+    """Seeded neighbours of the incumbent drawn on the device, as a periodic batch of device
+    tensors with the incumbent's starts as base (nothing crosses the host link).
+
+    Kinds: (0) a tighter II with the same offsets; (1) up to three operations pulled earlier
+    in the body (and half the time in the prologue); (2) a tighter II with operations pulled
+    earlier; (3) one of the lane-move frames, times kept.
+    """
+    N = int(incumbent.prologue.shape[0])
+    i64 = dict(dtype=torch.int64, device=dev)
+    kind = torch.randint(0, 4, (n,), generator=gen, **i64)
+    cut = torch.randint(1, max(2, step) + 1, (n,), generator=gen, **i64)
+    tighter = (kind == 0) | (kind == 2)
+    ii = torch.full((n,), int(incumbent.ii), **i64) - torch.where(tighter, cut, 0)
+    dp = torch.zeros((N, n), **i64)
+    dq = torch.zeros((N, n), **i64)
+    pulled = (kind == 1) | (kind == 2)
+    cols = torch.arange(n, device=dev)
+    for _ in range(3):
+        ops = torch.randint(0, N, (n,), generator=gen, **i64)
+        pull = torch.randint(1, max(2, step) + 1, (n,), generator=gen, **i64) * pulled
+        half = torch.rand((n,), generator=gen, device=dev) < 0.5
+        dp.index_put_((ops, cols), -torch.where(half, pull, 0), accumulate=True)
+        dq.index_put_((ops, cols), -pull, accumulate=True)
+    frame = torch.where(kind == 3, torch.randint(1, max(2, n_frames), (n,), generator=gen, **i64), 0)
+    ii = ii.clamp(min=1)
+    # every materialised start stays representable and non-negative before the verifier sees it
+    base_p = torch.as_tensor(incumbent.prologue, **i64)
+    base_o = torch.as_tensor(incumbent.offset, **i64)
+    dp = torch.maximum(dp, -base_p[:, None]).clamp(-32768, 32767)
+    dq = torch.maximum(dq, -(base_o[:, None] + ii[None, :])).clamp(-32768, 32767)
+    return {
+        "base_prologue": base_p.to(torch.int32),
+        "base_offset": base_o.to(torch.int32),
+        "prologue_delta": dp.to(torch.int16).contiguous(),
+        "offset_delta": dq.to(torch.int16).contiguous(),
+        "ii": ii.to(torch.int32),
+        "frame": frame.to(torch.int32),
+    }
 
 
 def improve_periodic(
@@ -124,13 +133,20 @@ def improve_periodic(
 ) -> SearchResult:
     """Descend on (II, makespan) from a verified periodic incumbent.
 
-    Each round verifies ``batch`` neighbours on the GPU and moves to the best valid one
-    when it improves the objective; the step size adapts to the incumbent's II. The
+    Each round draws ``batch`` neighbours on the GPU, verifies them there with the exact
+    verifier, picks the best valid one by the solver's objective on the device, and moves
+    to it when it improves the incumbent; only the lane-move frames go to the device and
+    only the winner's starts come back. The step size adapts to the incumbent's II. The
     incumbent itself must verify.
     """
+    import torch
+
     verifier = _verifier_for(problem, device)
     packed = verifier.packed
     rng = np.random.default_rng(seed)
+    dev = torch.device("cuda", verifier.device)
+    gen = torch.Generator(device=dev)
+    gen.manual_seed(seed)
     frames = FrameSet(packed)
     f0 = frames.add(incumbent.lanes, incumbent.sync)
     start = PeriodicBatch.from_starts(incumbent.prologue[None, :], incumbent.offset[None, :],
@@ -140,29 +156,29 @@ def improve_periodic(
         raise ValueError(f"the incumbent does not verify (class {int(verdict[0])})")
     result = SearchResult(incumbent, int(incumbent.ii), int(makespan[0]))
     best_key = int(_objective(np.array([result.ii]), np.array([result.makespan]), packed.iterations)[0])
+    lead = 1 if packed.iterations >= 3 else 0
     for _ in range(rounds):
         step = max(1, result.ii // 16)
-        nframes, cand = _neighbours(packed, result.witness, batch, rng, step)
-        verdict, makespan, ii_out = verifier.verify_periodic(nframes, cand)
+        nframes = _lane_moves(packed, result.witness, rng)
+        dframes = verifier.frames_to_device(nframes)
+        table = verifier.analyze(dframes)
+        cand = _device_neighbours(torch, result.witness, batch, len(nframes), gen, step, dev)
+        verdict_d, makespan_d, _ii = verifier.verify_periodic_device(dframes, table, cand)
         result.evaluated += batch
-        valid = np.flatnonzero(verdict == 0)
-        if valid.size:
-            keys = _objective(cand.ii[valid], makespan[valid], packed.iterations)
-            j = int(valid[int(np.argmin(keys))])
-            key = int(keys.min())
-            if key < best_key:
-                best_key = key
-                lanes, sync = nframes.frames[int(cand.frame[j])]
-                result.witness = Witness(
-                    [list(lane) for lane in lanes],
-                    [tuple(edge) for edge in sync],
-                    cand.base_prologue.astype(np.int64) + cand.prologue_delta[:, j].astype(np.int64),
-                    cand.base_offset.astype(np.int64) + cand.offset_delta[:, j].astype(np.int64),
-                    int(cand.ii[j]),
-                )
-                result.ii = int(cand.ii[j])
-                result.makespan = int(makespan[j])
-                result.accepted += 1
+        keys = cand["ii"].to(torch.int64) * lead * (1 << 32) + makespan_d.to(torch.int64)
+        keys = torch.where(verdict_d == 0, keys, torch.iinfo(torch.int64).max)
+        j = int(torch.argmin(keys).item())
+        key = int(keys[j].item())
+        if key < best_key and int(verdict_d[j].item()) == 0:
+            best_key = key
+            lanes, sync = nframes.frames[int(cand["frame"][j].item())]
+            p = cand["base_prologue"].to(torch.int64) + cand["prologue_delta"][:, j].to(torch.int64)
+            o = cand["base_offset"].to(torch.int64) + cand["offset_delta"][:, j].to(torch.int64)
+            result.witness = Witness([list(lane) for lane in lanes], [tuple(edge) for edge in sync],
+                                     p.cpu().numpy(), o.cpu().numpy(), int(cand["ii"][j].item()))
+            result.ii = result.witness.ii
+            result.makespan = int(makespan_d[j].item())
+            result.accepted += 1
         result.history.append((result.ii, result.makespan))
     return result
 

@@ -140,6 +140,24 @@ class FramePlan:
         """Whether frames other than the plan's run its generated code (delta verification)."""
         return self._lib.tfv_plan_delta(self.handle) == 1
 
+    @property
+    def ring_warps(self) -> int:
+        """Consumer warps of the ring kernel (0 for the tiles kernel)."""
+        return int(self._lib.tfv_plan_ring_warps(self.handle))
+
+    def set_timing(self, enable: bool) -> None:
+        """Record CUDA events around the verification kernel of every later call (or stop)."""
+        _lib.check(self._lib.tfv_plan_set_timing(self.handle, 1 if enable else 0), "tfv_plan_set_timing")
+
+    def kernel_times(self, capacity: int = 4096) -> list[float]:
+        """Milliseconds of the verification kernels recorded since the last read (oldest
+        first); the launches must have completed. Clears the record."""
+        buf = (ctypes.c_float * capacity)()
+        count = ctypes.c_int(0)
+        _lib.check(self._lib.tfv_plan_kernel_times(self.handle, buf, capacity, ctypes.byref(count)),
+                   "tfv_plan_kernel_times")
+        return [float(buf[i]) for i in range(min(count.value, capacity))]
+
     def source(self) -> str:
         """The generated CUDA source."""
         buf = ctypes.create_string_buffer(1 << 22)

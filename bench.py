@@ -654,10 +654,11 @@ def run_ours(args) -> None:
             "cpu_baseline": cpu,
             "e2e": {"value": e2e_value, "unit": UNIT, "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h,
                     "steps": e2e_steps, "entry": e2e_entry, **link,
-                    # the copies bound the entry: one step needs h2d / h2d_gbs + d2h / d2h_gbs
-                    "link_bound": n * n_ii / (h2d / (link["h2d_gbs"] * 1e9) + d2h / (link["d2h_gbs"] * 1e9)),
-                    "frac_of_link_bound": e2e_value / (n * n_ii / (h2d / (link["h2d_gbs"] * 1e9) +
-                                                                   d2h / (link["d2h_gbs"] * 1e9)))},
+                    # the copies bound the entry: one step of a rank needs h2d / h2d_gbs + d2h /
+                    # d2h_gbs on its GPU's host link (rank 0's link measured, every rank has its own)
+                    "link_bound": world * n * n_ii / (h2d / (link["h2d_gbs"] * 1e9) + d2h / (link["d2h_gbs"] * 1e9)),
+                    "frac_of_link_bound": e2e_value / (world * n * n_ii / (h2d / (link["h2d_gbs"] * 1e9) +
+                                                                           d2h / (link["d2h_gbs"] * 1e9)))},
             # frame analysis, sync-program compile, verification (+ the plan's spec-frame check
             # and constants kernels and, with delta verification, its frame comparison)
             "gpu_launches": (3 + (0 if plan is None else 3 if plan.delta else 2)) * args.steps,

@@ -156,8 +156,9 @@ inline FrameTable frame_table_view(void* base, FrameTableShape s) {
 //   int4     header[F]                    {kind, added lane edges, added sync edges, 0}
 //   int4     record[F]                    {frame_class, class of the set's first static
 //                                          failure (set_meta.y), register crossing (0/1),
-//                                          first_unreached}: a candidate's frame facts in
-//                                          one load
+//                                          the first unreached relation as packed in the
+//                                          problem (a | b << 12 | d << 24) or -1}: a
+//                                          candidate's frame facts in one load
 //   uint32   keep[F][lane_words + sync_words]
 //   int4     prog[F][2 * kDeltaMax]       added lane edges, then added sync edges
 constexpr int kDeltaMax = 8;

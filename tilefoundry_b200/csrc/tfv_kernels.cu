@@ -566,8 +566,9 @@ __global__ void __launch_bounds__(128) delta_frames_kernel(DevProblem p, DevFram
         if (lane == 0) {  // the facts the verification reads per candidate
             const int set = fr.sync_set[f];
             const int tail = set >= 0 && set < fr.n_sync_sets ? ft.set_meta[set].y : TFV_CLASS_BAD_PACKING;
+            const int r = ft.first_unreached[f];
             dt.record[f] = make_int4(ft.frame_class[f], tail, (ft.frame_flags[f] & kFrameRegisterCross) ? 1 : 0,
-                                     ft.first_unreached[f]);
+                                     r >= 0 ? p.relation[r] : -1);
         }
         if (!m_ok) {
             if (lane == 0) dt.header[f] = make_int4(kDeltaGeneric, 0, 0, 0);

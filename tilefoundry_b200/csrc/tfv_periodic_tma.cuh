@@ -293,9 +293,14 @@ __device__ __forceinline__ void column_verdict(const DevProblem& p, const DevFra
         }
         // First relation without a lane/sync path: timing at instance 0 decides 17 vs 18.
         int rel_cls = 0;
-        const int r = from_record ? rec.w : ft.first_unreached[f];
-        if (r >= 0) {
-            const int packed = p.relation[r];
+        int packed = -1;  // the first unreached relation (a | b << 12 | d << 24), if any
+        if (from_record) {
+            packed = rec.w;
+        } else {
+            const int r = ft.first_unreached[f];
+            if (r >= 0) packed = p.relation[r];
+        }
+        if (packed >= 0) {
             const int a = packed & 0xFFF, bb = (packed >> 12) & 0xFFF, d = packed >> 24;
             const int ready = opc[a].z + mp[a * kTile] + opc[a].y;
             const int target = d == 0 ? opc[bb].z + mp[bb * kTile] : opc[bb].w + mo[bb * kTile] + ii;

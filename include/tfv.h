@@ -37,7 +37,7 @@
 extern "C" {
 #endif
 
-#define TFV_ABI_VERSION 4
+#define TFV_ABI_VERSION 5
 
 #if defined(__GNUC__)
 #define TFV_API __attribute__((visibility("default")))

@@ -29,7 +29,7 @@ def test_library_exports_every_declared_function():
     for name in names:
         assert hasattr(lib, name), name
     assert set(names) == set(_lib.EXPORTS)
-    assert lib.tfv_abi_version() == _lib.ABI_VERSION == 4
+    assert lib.tfv_abi_version() == _lib.ABI_VERSION == 5
 
 
 def test_invalid_arguments_are_rejected_before_cuda():

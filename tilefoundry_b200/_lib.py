@@ -26,7 +26,7 @@ TFV_MAX_LANES = 15
 TFV_MAX_OPS = 4095
 TFV_TIME_LIMIT = 1 << 30
 TFV_BASE_LIMIT = 1 << 28
-ABI_VERSION = 4
+ABI_VERSION = 5
 PLAN_AUTO = 0
 PLAN_TILES = 1
 PLAN_RING = 2

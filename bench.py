@@ -438,8 +438,14 @@ def run_ours(args) -> None:
     gathered = [[torch.empty(5 * m, dtype=torch.uint8, device=dev) for _ in range(world)] if rank == 0 else None
                 for _ in range(2)] if world > 1 and peer is None else None
     pending = [None, None]
-    table = verifier.analyze(dframes)
+    # Two frame tables: the analysis of step s + 1's frames runs on a side stream while step s
+    # verifies (its one-warp CTAs fit beside the ring kernel's on every SM), into the table
+    # step s - 1 used; each step's verification waits for its own table's analysis.
+    tables = [verifier.analyze(dframes), verifier.analyze(dframes)]
     stream = torch.cuda.current_stream(dev)
+    side = torch.cuda.Stream(dev)
+    analysed = [torch.cuda.Event() for _ in range(2)]
+    released = [None, None]  # per table: an event after the last call that read it
     # The batch's most frequent frame gets a kernel generated and compiled for it (before
     # any timing); its candidates run that code, the others the frame-table path.
     plan, spec_frame, plan_compile_ms = None, -1, None
@@ -458,26 +464,42 @@ def run_ours(args) -> None:
         if dist is not None:
             dist.barrier()
 
-    def step(s, events=None):
+    def analyse(s, events=None):
+        """Issue the frame analysis of step s into table s % 2 on the side stream."""
+        k = s % 2
+        if released[k] is not None:
+            side.wait_event(released[k])
+        if events is not None:
+            events[0].record(side)
+        verifier.analyze(dframes, table=tables[k], stream=side)
+        if events is not None:
+            events[1].record(side)
+        analysed[k].record(side)
+
+    def step(s, events=None, next_events=None):
+        """Verify step s (its analysis already issued); then issue step s + 1's analysis
+        unless next_events is False (the last step)."""
         buf = s % 2
         if peer is not None:
             peer.wait(buf, stream)  # the stream waits until that copy has read the buffer
         if pending[buf] is not None:
             pending[buf].wait()  # the stream waits until that gather has read the buffer
             pending[buf] = None
-        if events is not None:
-            events[0].record(stream)
-        verifier.analyze(dframes, table=table)
-        if events is not None:
-            events[1].record(stream)
-        out = (verdicts[buf], makespans[buf], iis[buf])
-        if ii_values is None:
-            verifier.verify_periodic_device(dframes, table, tensors, out=tuple(t[0] for t in out), plan=plan,
-                                            spec_frame=spec_frame)
-        else:
-            verifier.verify_periodic_sweep_device(dframes, table, tensors, ii_values, out=out)
+        stream.wait_event(analysed[s % 2])
         if events is not None:
             events[2].record(stream)
+        out = (verdicts[buf], makespans[buf], iis[buf])
+        if ii_values is None:
+            verifier.verify_periodic_device(dframes, tables[s % 2], tensors, out=tuple(t[0] for t in out),
+                                            plan=plan, spec_frame=spec_frame)
+        else:
+            verifier.verify_periodic_sweep_device(dframes, tables[s % 2], tensors, ii_values, out=out)
+        if events is not None:
+            events[3].record(stream)
+        released[s % 2] = torch.cuda.Event()
+        released[s % 2].record(stream)
+        if next_events is not False:
+            analyse(s + 1, next_events)
         if dist is not None:
             pack_results(verdicts[buf], makespans[buf], out=payload[buf])
             if peer is not None:
@@ -494,12 +516,13 @@ def run_ours(args) -> None:
                 pending[k].wait()
                 pending[k] = None
 
+    analyse(0)
     for s in range(args.warmup):
-        step(s)
+        step(s, next_events=None if s + 1 < args.warmup else False)
     drain()
     torch.cuda.synchronize(dev)
     barrier()
-    events = [[torch.cuda.Event(enable_timing=True) for _ in range(3)] for _ in range(args.steps)]
+    events = [[torch.cuda.Event(enable_timing=True) for _ in range(4)] for _ in range(args.steps)]
     begin = torch.cuda.Event(enable_timing=True)
     end = torch.cuda.Event(enable_timing=True)
     if plan is not None:  # CUDA events around the generated kernel alone, recorded by the plan
@@ -509,8 +532,10 @@ def run_ours(args) -> None:
         torch.cuda.synchronize(dev)
         barrier()
         begin.record(stream)
+        side.wait_stream(stream)  # the first analysis starts inside the timed region
+        analyse(0, events[0])
         for s in range(args.steps):
-            step(s, events[s])
+            step(s, events[s], events[s + 1] if s + 1 < args.steps else False)
         drain()
         end.record(stream)
         torch.cuda.synchronize(dev)
@@ -530,7 +555,7 @@ def run_ours(args) -> None:
             rows = peer.received(last_buf).to(torch.int64).sum(dim=1).tolist()
             assert rows == sums, "peer gather rows differ from the ranks' payloads"
     analyze_ms = [e[0].elapsed_time(e[1]) for e in events]
-    verify_ms = [e[1].elapsed_time(e[2]) for e in events]
+    verify_ms = [e[2].elapsed_time(e[3]) for e in events]
     if dist is not None:
         t = torch.tensor([elapsed_ms], device=dev)
         dist.all_reduce(t, op=dist.ReduceOp.MAX)

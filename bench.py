@@ -556,7 +556,16 @@ def run_ours(args) -> None:
             assert rows == sums, "peer gather rows differ from the ranks' payloads"
     analyze_ms = [e[0].elapsed_time(e[1]) for e in events]
     verify_ms = [e[2].elapsed_time(e[3]) for e in events]
+    per_rank = None
     if dist is not None:
+        # every rank's step time, generated-kernel time and call time (diagnostics), then the max
+        mine = torch.tensor([elapsed_ms / args.steps,
+                             statistics.mean(plan_kernel_ms) if plan_kernel_ms else float("nan"),
+                             statistics.mean(verify_ms)], device=dev, dtype=torch.float64)
+        every = [torch.empty_like(mine) for _ in range(world)]
+        dist.all_gather(every, mine)
+        per_rank = {key: [round(float(t[i].item()), 4) for t in every]
+                    for i, key in enumerate(("ms_per_step", "kernel_ms", "call_ms"))}
         t = torch.tensor([elapsed_ms], device=dev)
         dist.all_reduce(t, op=dist.ReduceOp.MAX)
         elapsed_ms = float(t.item())
@@ -687,6 +696,7 @@ def run_ours(args) -> None:
             # frame analysis, sync-program compile, verification (+ the plan's spec-frame check
             # and constants kernels and, with delta verification, its frame comparison)
             "gpu_launches": (3 + (0 if plan is None else 3 if plan.delta else 2)) * args.steps,
+            "ranks": per_rank,
             "clocks": clocks.summary(),
         }
         print(json.dumps(line), flush=True)

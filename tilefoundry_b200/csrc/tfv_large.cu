@@ -360,6 +360,11 @@ __global__ void __launch_bounds__(kLargeMaxThreads, 1)
                     }
                 }
                 const int r = frame_ok ? ft.first_unreached[f] : -1;
+                // An II sweep of three or more iterations defers the capacity check: every II's
+                // other classes first (the IIs that pass them marked pending in out.verdict),
+                // then per resource the prologue-start demands once and each pending II.
+                const bool defer = kSweep && kBodyRows >= 2 && p.n_resources > 0;
+                bool any_pending = false;
                 for (int k = 0; k < n_ii; ++k) {
                     const long long o = k * b.ii_stride + c;
                     const int ii = k == 0 ? ii0 : b.ii[o];
@@ -374,15 +379,47 @@ __global__ void __launch_bounds__(kLargeMaxThreads, 1)
                             cls = (s.rel_d == 0 ? s.rel_c < 0 : ii < -s.rel_c) ? TFV_CLASS_RELATION_TIMING
                                                                                : TFV_CLASS_RELATION_NO_PATH;
                         else if (s.carried_bad) cls = TFV_CLASS_CARRIED_SHARED_LIFETIME;
+                        else if (defer) cls = kResourcesPending;
                         else if (p.n_resources > 0)
                             cls = warp_resources_exceed(p, WordView{opc, cb}, ii, scratch, lane) ? TFV_CLASS_RESOURCE_CAPACITY
                                                                                                : TFV_CLASS_PASS;
                     }
+                    any_pending |= cls == kResourcesPending;
                     if (lane == 0) {
                         out.verdict[o] = cls;
                         out.makespan[o] = ms;
                         out.ii[o] = kBodyRows >= 2 ? ii : 0;
                     }
+                }
+                if (defer && any_pending) {  // lane 0 wrote and reads back the marks (program order)
+                    const WordView V{opc, cb};
+                    const WarpScratch ws(p, scratch);
+                    for (int q = 0; q < p.n_resources; ++q) {
+                        const int W = p.res_offsets[q + 1] - p.res_offsets[q];
+                        bool staged = false;  // the prologue-start demands of resource q
+                        for (int k = 0; k < n_ii; ++k) {
+                            const long long o = k * b.ii_stride + c;
+                            int v = 0;
+                            if (lane == 0) v = out.verdict[o];
+                            if (__shfl_sync(kAll, v, 0) != kResourcesPending) continue;
+                            const int ii = k == 0 ? ii0 : b.ii[o];  // > 0: class 10 passed
+                            const Divider div(ii);
+                            const ResourceSums rs = warp_stage_resource(p, V, q, ii, div, ws, lane);
+                            if (!staged) {  // P, P + D and a of the windows do not depend on the II
+                                warp_prologue_demands(ws.rec, W, lane, ws.pdem);
+                                staged = true;
+                            }
+                            const bool exceed =
+                                warp_periodic_exceed(ws.rec, ws.rec2, ws.Fv, W, lane, rs, p.capacity[q], ii, I, div, ws.pdem);
+                            if (__any_sync(kAll, exceed) && lane == 0) out.verdict[o] = TFV_CLASS_RESOURCE_CAPACITY;
+                            __syncwarp();  // every lane is done with this II's records
+                        }
+                    }
+                    if (lane == 0)  // passed every resource
+                        for (int k = 0; k < n_ii; ++k) {
+                            const long long o = k * b.ii_stride + c;
+                            if (out.verdict[o] == kResourcesPending) out.verdict[o] = TFV_CLASS_PASS;
+                        }
                 }
             }
             __syncwarp();

@@ -48,9 +48,10 @@ __host__ __device__ inline bool warp_resources_used(const DevProblem& p) {
     return p.n_resources > 0 && p.res_max_windows > kThreadWindowMax && p.res_max_windows <= kWarpWindowCap;
 }
 // int4 records of one warp's capacity-check scratch: two per window ({P, P + D, a, rs} and
-// {e, m, qs, S}) and each window's steady-state demand (one int per window).
+// {e, m, qs, S}), each window's steady-state demand and each window's prologue-start demand
+// (one int per window each).
 __host__ __device__ inline int warp_scratch_records(const DevProblem& p) {
-    return 2 * p.res_max_windows + (p.res_max_windows + 3) / 4;
+    return 2 * p.res_max_windows + 2 * ((p.res_max_windows + 3) / 4);
 }
 // Shared-memory bytes one warp needs for the warp path.
 __host__ __device__ inline size_t warp_resource_scratch_bytes(const DevProblem& p) {
@@ -273,11 +274,20 @@ __device__ __forceinline__ int staged_periodic_demand(const int4* rec, const int
     return F;
 }
 
+// Demand of the prologue copies at every window's prologue start (rec staged, every lane
+// calls it): no II changes it, so an II sweep computes it once per candidate and resource.
+__device__ inline void warp_prologue_demands(const int4* rec, int W, int lane, int* pdem) {
+    for (int v = lane; v < W; v += 32) pdem[v] = staged_prologue_demand(rec, W, rec[v].x);
+    __syncwarp();
+}
+
 // Warp driver for I >= 3 (see the file comment); lanes split the windows, every lane calls it.
-// Fv holds each window's F (or sumF when the steady state needs no check). Returns this
-// lane's finding; the caller combines the lanes.
+// Fv holds each window's F (or sumF when the steady state needs no check); pdem, when given,
+// each window's prologue-start demand (warp_prologue_demands). Returns this lane's finding;
+// the caller combines the lanes.
 __device__ inline bool warp_periodic_exceed(const int4* rec, const int4* rec2, int* Fv, int W, int lane,
-                                            const ResourceSums& s, int cap, int T, int I, const Divider& div) {
+                                            const ResourceSums& s, int cap, int T, int I, const Divider& div,
+                                            const int* pdem = nullptr) {
     const unsigned full = 0xFFFFFFFFu;
     const int n = I - 1;
     const StagedWindows src{rec, rec2};
@@ -299,7 +309,7 @@ __device__ inline bool warp_periodic_exceed(const int4* rec, const int4* rec2, i
     for (int v = lane; v < W; v += 32) {
         const int P = rec[v].x;
         if (P < s.Smin) {
-            if (s.sumA > cap) ex |= staged_prologue_demand(rec, W, P) > cap;
+            if (s.sumA > cap) ex |= (pdem ? pdem[v] : staged_prologue_demand(rec, W, P)) > cap;
         } else {
             const int qp = div.quot(P);
             ex |= clipped_demand(src, W, P, qp, P - qp * T, T, n) > cap;
@@ -329,6 +339,44 @@ __device__ inline bool warp_periodic_exceed(const int4* rec, const int4* rec2, i
     return ex;
 }
 
+// Scratch of the warp driver: the two window records, F and the prologue-start demands.
+struct WarpScratch {
+    int4* rec;
+    int4* rec2;
+    int* Fv;
+    int* pdem;
+    __device__ WarpScratch(const DevProblem& p, int4* scratch)
+        : rec(scratch),
+          rec2(scratch + p.res_max_windows),
+          Fv(reinterpret_cast<int*>(scratch + 2 * p.res_max_windows)),
+          pdem(reinterpret_cast<int*>(scratch + 2 * p.res_max_windows + (p.res_max_windows + 3) / 4)) {}
+};
+
+// Stages resource q's windows at II T into rec / rec2 and returns the sums (every lane).
+template <class Vals>
+__device__ ResourceSums warp_stage_resource(const DevProblem& p, const Vals& V, int q, int T, const Divider& div,
+                                            const WarpScratch& ws, int lane) {
+    const unsigned full = 0xFFFFFFFFu;
+    const int I = p.iterations;
+    const int w0 = p.res_offsets[q], W = p.res_offsets[q + 1] - w0;
+    const LiveWindows<Vals> live{p, V, div, w0, T, I};
+    ResourceSums s{INT_MIN, INT_MAX, INT_MIN, 0, 0, 0};
+    for (int w = lane; w < W; w += 32) {
+        const Win x = live(w);
+        ws.rec[w] = make_int4(x.P, x.P + x.D, x.a, x.rs);
+        ws.rec2[w] = make_int4(x.e, x.m, x.qs, x.S);
+        add_window(s, x, I - 1);
+    }
+    s.E = __reduce_max_sync(full, s.E);
+    s.Smin = __reduce_min_sync(full, s.Smin);
+    s.Lend = __reduce_max_sync(full, s.Lend);
+    s.sumA = __reduce_add_sync(full, s.sumA);
+    s.sumF = __reduce_add_sync(full, s.sumF);
+    s.C0 = __reduce_add_sync(full, s.C0);
+    __syncwarp();
+    return s;
+}
+
 // One warp per candidate: every lane passes the same V and T. Same requirements as the
 // thread driver, plus at most kWarpWindowCap windows per resource and scratch for
 // warp_scratch_records(p) int4 records private to the warp.
@@ -336,28 +384,14 @@ template <class Vals>
 __device__ bool warp_resources_exceed(const DevProblem& p, const Vals& V, int T, int4* scratch, int lane) {
     const unsigned full = 0xFFFFFFFFu;
     const int I = p.iterations;
-    int4* rec = scratch;
-    int4* rec2 = scratch + p.res_max_windows;
-    int* Fv = reinterpret_cast<int*>(scratch + 2 * p.res_max_windows);
+    const WarpScratch ws(p, scratch);
+    int4* rec = ws.rec;
+    int4* rec2 = ws.rec2;
     const Divider div(I >= 3 ? T : 1);
     for (int q = 0; q < p.n_resources; ++q) {
-        const int w0 = p.res_offsets[q], W = p.res_offsets[q + 1] - w0;
-        const LiveWindows<Vals> live{p, V, div, w0, T, I};
-        ResourceSums s{INT_MIN, INT_MAX, INT_MIN, 0, 0, 0};
-        for (int w = lane; w < W; w += 32) {
-            const Win x = live(w);
-            rec[w] = make_int4(x.P, x.P + x.D, x.a, x.rs);
-            rec2[w] = make_int4(x.e, x.m, x.qs, x.S);
-            add_window(s, x, I - 1);
-        }
-        s.E = __reduce_max_sync(full, s.E);
-        s.Smin = __reduce_min_sync(full, s.Smin);
-        s.Lend = __reduce_max_sync(full, s.Lend);
-        s.sumA = __reduce_add_sync(full, s.sumA);
-        s.sumF = __reduce_add_sync(full, s.sumF);
-        s.C0 = __reduce_add_sync(full, s.C0);
-        __syncwarp();
-        const bool exceed = I >= 3 ? warp_periodic_exceed(rec, rec2, Fv, W, lane, s, p.capacity[q], T, I, div)
+        const int W = p.res_offsets[q + 1] - p.res_offsets[q];
+        const ResourceSums s = warp_stage_resource(p, V, q, T, div, ws, lane);
+        const bool exceed = I >= 3 ? warp_periodic_exceed(rec, rec2, ws.Fv, W, lane, s, p.capacity[q], T, I, div)
                                    : starts_exceed(StagedWindows{rec, rec2}, W, lane, 32, s, p.capacity[q], T, I, div);
         if (__any_sync(full, exceed)) return true;
         __syncwarp();  // every lane is done with this resource's records

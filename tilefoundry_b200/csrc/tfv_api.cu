@@ -256,9 +256,24 @@ int tfv_problem_create(const tfv_problem_desc* d, int device, tfv_problem** out)
                 total[q] += static_cast<long long>(d->window_amount[w]) * I;
             }
         }
+        // Resources in order of their summed window amounts over the capacity, largest first: a
+        // candidate stops at the first exceeded resource, and the class (20) does not depend
+        // on which one it was, so the likeliest to be exceeded is checked first.
+        std::vector<int> order(Q);
+        std::vector<long long> amounts(Q, 0);
         for (int q = 0; q < Q; ++q) {
+            order[q] = q;
+            for (int w : by_res[q]) amounts[q] += d->window_amount[w];
+        }
+        std::stable_sort(order.begin(), order.end(), [&](int x, int y) {
+            return amounts[x] * capacity[y] > amounts[y] * capacity[x];  // amounts / capacity, descending
+        });
+        const std::vector<int> given = capacity;
+        for (int k = 0; k < Q; ++k) {
+            const int q = order[k];
             if (total[q] >= (1LL << 31)) return fail(TFV_ERR_RANGE, "resource %d total demand overflows int32", q);
-            res_offsets[q] = static_cast<int>(win_op.size());
+            capacity[k] = given[q];
+            res_offsets[k] = static_cast<int>(win_op.size());
             for (int w : by_res[q]) {
                 int a = 0;
                 while (!(d->window_offsets[a] <= w && w < d->window_offsets[a + 1])) ++a;

@@ -272,14 +272,15 @@ cudaError_t launch_verify_rows(const DevProblem& p, const DevFrames& f, FrameTab
                                const DevRows& b, DevResults r, int sm_count,
                                cudaStream_t stream);
 
-// Shared-memory footprint checks used by the host before launching.
-cudaError_t launch_delta_frames(const DevProblem& p, const DevFrames& f, FrameTable t, const int* spec_frame,
+// A plan's per-call preparation in one launch: writes spec to *spec_out when frame spec has
+// the lanes (sig_lane_pos [N]) and sync program (sig_edges [sig_len][3]) the plan was
+// generated for, else -1; compiles every sync set's program (TMA-row form); with d, fills the
+// DeltaTable of every frame relative to that frame (lane_bit [N] / sync_bit [sig_len]: the
+// generated code's mask bit of each lane edge and program edge).
+cudaError_t launch_prepare_plan(const DevProblem& p, const DevFrames& f, FrameTable t, int spec,
+                                const uint16_t* sig_lane_pos, const int* sig_edges, int sig_len, int* spec_out,
                                 const int* base_prologue, const int* base_offset, const int* lane_bit,
-                                const int* sync_bit, DeltaTable d, int sm_count, cudaStream_t stream);
-// Writes spec to *out when frame spec has the lanes (sig_lane_pos [N]) and sync program
-// (sig_edges [sig_len][3]) a plan was generated for, else -1.
-cudaError_t launch_check_spec_frame(const DevProblem& p, const DevFrames& f, int spec, const uint16_t* sig_lane_pos,
-                                    const int* sig_edges, int sig_len, int* out, cudaStream_t stream);
+                                const int* sync_bit, const DeltaTable* d, int sm_count, cudaStream_t stream);
 
 // Time after which a bounded wait of the ring and large-body kernels gives up (1 s unless a
 // caller changed it with tfv_set_device_wait_limit).

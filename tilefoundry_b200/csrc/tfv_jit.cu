@@ -11,7 +11,7 @@
 // kernel (a producer warp and consumer warps per SM) or the tiles kernel (CTAs in lock
 // step). With delta verification the generated code records one violation bit per lane and
 // sync edge instead of the smallest slack, and every frame that a per-call comparison
-// (delta_frames_kernel) describes by kept edges and a few added edges runs it as well; the
+// (prepare_plan_kernel) describes by kept edges and a few added edges runs it as well; the
 // body's tile permutation hands those candidates to whole warps and the rest take the
 // frame-table path. Verdicts are identical: the generated code computes the same extremes
 // and the same signs of every lane and sync slack.
@@ -828,17 +828,16 @@ int tfv_verify_periodic_planned(tfv_plan* plan, const tfv_frames* frames, void* 
                       sizeof(int) * static_cast<size_t>(plan->n_consts), reinterpret_cast<CUstream>(plan->side));
     if (cr != CUDA_SUCCESS) return tfv_internal_fail(TFV_ERR_CUDA, "launching the plan's constants kernel failed");
     e = cudaEventRecord(plan->join, plan->side);
-    if (e == cudaSuccess)
-        e = tfv::launch_compile_sync_programs(d, df, view, b->base_prologue, b->base_offset, tfv_internal_sm_count(p), s);
-    // the frame the generated code serves: spec_frame if it has the plan frame's lanes and
-    // sync program, else -1 (every candidate then takes the frame-table path)
+    if (e != cudaSuccess) return tfv_internal_cuda_fail(e, "tfv_verify_periodic_planned");
+    // One launch on the caller's stream: the frame the generated code serves (spec_frame if it
+    // has the plan frame's lanes and sync program, else -1: every candidate then takes the
+    // frame-table path), the sync programs and, with delta verification, every frame relative
+    // to spec_frame.
     int* spec_dev = static_cast<int*>(plan->sig);
     const size_t lp_bytes = (sizeof(uint16_t) * d.n_ops + 3) & ~static_cast<size_t>(3);
     const uint16_t* sig_lp = reinterpret_cast<const uint16_t*>(static_cast<char*>(plan->sig) + sizeof(int));
     const int* sig_edges = reinterpret_cast<const int*>(static_cast<char*>(plan->sig) + sizeof(int) + lp_bytes);
-    if (e == cudaSuccess) e = tfv::launch_check_spec_frame(d, df, spec_frame, sig_lp, sig_edges, plan->sig_len, spec_dev, s);
-    if (e != cudaSuccess) return tfv_internal_cuda_fail(e, "tfv_verify_periodic_planned");
-    // delta verification: every frame relative to spec_frame, after the sync programs
+    const int* lane_bit = sig_edges + 3 * plan->sig_len;
     tfv::DeltaTable dt{};
     if (plan->delta) {
         const size_t need = tfv::delta_table_bytes(frames->n_frames, plan->lane_words, plan->sync_words);
@@ -851,11 +850,11 @@ int tfv_verify_periodic_planned(tfv_plan* plan, const tfv_frames* frames, void* 
             plan->delta_bytes = need;
         }
         dt = tfv::delta_table_view(plan->delta_buf, frames->n_frames, plan->lane_words, plan->sync_words);
-        const int* lane_bit = sig_edges + 3 * plan->sig_len;
-        e = tfv::launch_delta_frames(d, df, view, spec_dev, b->base_prologue, b->base_offset, lane_bit,
-                                     lane_bit + d.n_ops, dt, tfv_internal_sm_count(p), s);
-        if (e != cudaSuccess) return tfv_internal_cuda_fail(e, "tfv_verify_periodic_planned");
     }
+    e = tfv::launch_prepare_plan(d, df, view, spec_frame, sig_lp, sig_edges, plan->sig_len, spec_dev, b->base_prologue,
+                                 b->base_offset, lane_bit, lane_bit + d.n_ops, plan->delta ? &dt : nullptr,
+                                 tfv_internal_sm_count(p), s);
+    if (e != cudaSuccess) return tfv_internal_cuda_fail(e, "tfv_verify_periodic_planned");
     e = cudaStreamWaitEvent(s, plan->join, 0);  // the constants are in place
     if (e != cudaSuccess) return tfv_internal_cuda_fail(e, "tfv_verify_periodic_planned");
     const long long tiles = (db.n + tfv::kTmaTile - 1) / tfv::kTmaTile;

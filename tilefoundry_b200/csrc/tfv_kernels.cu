@@ -456,56 +456,77 @@ cudaError_t launch_analyze_frames(const DevProblem& p, const DevFrames& f, Frame
 // address the TMA tile directly (see set_prog in tfv_device.cuh), for the TMA kernels
 // (N <= 256, iterations <= kMaxProgDistance), or name the operations (index_form), for the
 // large-body kernel.
+// The program of sync set s: its edges before the first statically failing one (unknown
+// operation, class 13, or no instance, class 14). Returns the end of that prefix (edge index)
+// and the set's tail class (that failure's class, BAD_PACKING for a malformed set, else 0) in
+// *tail. One warp; every lane gets the answer.
+__device__ int set_program_end(const DevProblem& p, const DevFrames& fr, int s, int* tail, int* first) {
+    const int N = p.n_ops, I = p.iterations;
+    const int lane = threadIdx.x & 31;
+    const int total = min(fr.sync_offsets[fr.n_sync_sets], fr.n_sync_edges);
+    int e0 = fr.sync_offsets[s], e1 = fr.sync_offsets[s + 1];
+    bool bad = e0 < 0 || e1 < e0 || e1 > total;
+    if (bad) e0 = e1 = 0;
+    int stop = e1;  // first statically failing edge
+    for (int k0 = e0; k0 < e1; k0 += 32) {
+        const int k = k0 + lane;
+        bool stat = false;
+        if (k < e1) {
+            const int a = fr.sync_edges[3 * k], b = fr.sync_edges[3 * k + 1], d = fr.sync_edges[3 * k + 2];
+            bad |= a < -1 || b < -1 || a >= N || b >= N || d < 0;
+            stat = a < 0 || b < 0 || d >= I;
+        }
+        const unsigned m = __ballot_sync(kFull, stat);
+        if (m) {
+            stop = k0 + __ffs(m) - 1;
+            break;
+        }
+    }
+    bad = __any_sync(kFull, bad);
+    *tail = 0;
+    if (bad) {
+        *tail = TFV_CLASS_BAD_PACKING;
+        stop = e0;
+    } else if (stop < e1) {
+        const int a = fr.sync_edges[3 * stop], b = fr.sync_edges[3 * stop + 1];
+        *tail = (a < 0 || b < 0) ? TFV_CLASS_SYNC_UNKNOWN_OP : TFV_CLASS_SYNC_NO_INSTANCE;
+    }
+    *first = e0;
+    return stop;
+}
+
+// set_prog entry of program edge k (inside a set's program: operations valid, d < I): the base
+// starts and a's latency folded into the weights, in the TMA-row form {a_row | b_row << 16,
+// x_row | d << 17, w0, w1} or the operation-index form {a | b << 16, d, w0, w1}.
+__device__ __forceinline__ int4 fold_sync_edge(const DevProblem& p, const DevFrames& fr, int k,
+                                               const int* base_prologue, const int* base_offset, bool index_form) {
+    const int N = p.n_ops, I = p.iterations;
+    const int a = fr.sync_edges[3 * k], b = fr.sync_edges[3 * k + 1], d = fr.sync_edges[3 * k + 2];
+    const int lat = p.latency[a];
+    const int w0 = (d == 0 ? base_prologue[b] : base_offset[b]) - base_prologue[a] - lat;
+    const int w1 = I - d >= 2 ? base_offset[b] - base_offset[a] - lat : kNoBodyWeight;
+    if (index_form) return make_int4(a | (b << 16), d, w0, w1);
+    const int a_row = a * kTmaRowBytes, b_row = b * kTmaRowBytes;
+    const int x_row = d == 0 ? b_row : N * kTmaRowBytes + b_row;  // the offset rows follow the N prologue rows
+    return make_int4(a_row | (b_row << 16), x_row | (min(d, kMaxProgDistance) << 17), w0, w1);
+}
+
+// One warp: set s's program into ft.set_prog and its length and tail class into ft.set_meta.
+__device__ void compile_set(const DevProblem& p, const DevFrames& fr, const FrameTable& ft, int s,
+                            const int* base_prologue, const int* base_offset, bool index_form) {
+    const int lane = threadIdx.x & 31;
+    int tail = 0, e0 = 0;
+    const int stop = set_program_end(p, fr, s, &tail, &e0);
+    for (int k = e0 + lane; k < stop; k += 32)
+        ft.set_prog[k] = fold_sync_edge(p, fr, k, base_prologue, base_offset, index_form);
+    if (lane == 0) ft.set_meta[s] = make_int2(stop - e0, tail);
+}
+
 __global__ void __launch_bounds__(32) compile_sync_programs_kernel(DevProblem p, DevFrames fr, FrameTable ft,
                                                                      const int* base_prologue, const int* base_offset,
                                                                      bool index_form) {
-    const int N = p.n_ops, I = p.iterations;
-    const int lane = threadIdx.x;
-    const int total = min(fr.sync_offsets[fr.n_sync_sets], fr.n_sync_edges);
-    for (int s = blockIdx.x; s < fr.n_sync_sets; s += gridDim.x) {
-        int e0 = fr.sync_offsets[s], e1 = fr.sync_offsets[s + 1];
-        bool bad = e0 < 0 || e1 < e0 || e1 > total;
-        if (bad) e0 = e1 = 0;
-        int stop = e1;  // first statically failing edge
-        for (int k0 = e0; k0 < e1; k0 += 32) {
-            const int k = k0 + lane;
-            bool stat = false;
-            if (k < e1) {
-                const int a = fr.sync_edges[3 * k], b = fr.sync_edges[3 * k + 1], d = fr.sync_edges[3 * k + 2];
-                bad |= a < -1 || b < -1 || a >= N || b >= N || d < 0;
-                stat = a < 0 || b < 0 || d >= I;
-            }
-            const unsigned m = __ballot_sync(kFull, stat);
-            if (m) {
-                stop = k0 + __ffs(m) - 1;
-                break;
-            }
-        }
-        bad = __any_sync(kFull, bad);
-        int tail = 0;
-        if (bad) {
-            tail = TFV_CLASS_BAD_PACKING;
-            stop = e0;
-        } else if (stop < e1) {
-            const int a = fr.sync_edges[3 * stop], b = fr.sync_edges[3 * stop + 1];
-            tail = (a < 0 || b < 0) ? TFV_CLASS_SYNC_UNKNOWN_OP : TFV_CLASS_SYNC_NO_INSTANCE;
-        }
-        const int to_rows = N * kTmaRowBytes;  // the offset rows follow the N prologue rows
-        for (int k = e0 + lane; k < stop; k += 32) {
-            const int a = fr.sync_edges[3 * k], b = fr.sync_edges[3 * k + 1], d = fr.sync_edges[3 * k + 2];
-            const int lat = p.latency[a];
-            const int w0 = (d == 0 ? base_prologue[b] : base_offset[b]) - base_prologue[a] - lat;
-            const int w1 = I - d >= 2 ? base_offset[b] - base_offset[a] - lat : kNoBodyWeight;
-            if (index_form) {
-                ft.set_prog[k] = make_int4(a | (b << 16), d, w0, w1);
-                continue;
-            }
-            const int a_row = a * kTmaRowBytes, b_row = b * kTmaRowBytes;
-            const int x_row = d == 0 ? b_row : to_rows + b_row;
-            ft.set_prog[k] = make_int4(a_row | (b_row << 16), x_row | (min(d, kMaxProgDistance) << 17), w0, w1);
-        }
-        if (lane == 0) ft.set_meta[s] = make_int2(stop - e0, tail);
-    }
+    for (int s = blockIdx.x; s < fr.n_sync_sets; s += gridDim.x)
+        compile_set(p, fr, ft, s, base_prologue, base_offset, index_form);
 }
 
 // ---------------------------------------------------------------------------------------
@@ -532,148 +553,124 @@ __device__ __forceinline__ void keep_bits(bool kept, int bit, int words, unsigne
             acc[w] |= __reduce_or_sync(kFull, kept && bit >= 0 && (bit >> 5) == w ? 1u << (bit & 31) : 0u);
 }
 
-__global__ void __launch_bounds__(128) delta_frames_kernel(DevProblem p, DevFrames fr, FrameTable ft, const int* m_ptr,
-                                                           const int* base_prologue, const int* base_offset,
-                                                           const int* lane_bit, const int* sync_bit, DeltaTable dt) {
+// Program edge k as an (a, b, d) key.
+__device__ __forceinline__ unsigned long long edge_key(int a, int b, int d) {
+    return static_cast<unsigned long long>(static_cast<unsigned>(a) & 0xFFFFu) |
+           static_cast<unsigned long long>(static_cast<unsigned>(b) & 0xFFFFu) << 16 |
+           static_cast<unsigned long long>(static_cast<unsigned>(d)) << 32;
+}
+
+// One warp: frame f's entries of the DeltaTable relative to the checked specialised frame m
+// (-1: none), whose program keys (len_m of them, at most 32 * kDeltaMaxWords) are staged in
+// mkeys; kept_w is the warp's row of kDeltaMaxWords words. Every program length, tail class
+// and added sync entry is derived from the frame set itself (set_program_end,
+// fold_sync_edge), so this needs no sync-program kernel before it.
+__device__ void delta_frame(const DevProblem& p, const DevFrames& fr, const FrameTable& ft, int f, int m, bool m_ok,
+                            const unsigned long long* mkeys, int len_m, unsigned* kept_w, const int* base_prologue,
+                            const int* base_offset, const int* lane_bit, const int* sync_bit, const DeltaTable& dt) {
     const int N = p.n_ops, I = p.iterations;
-    const int m = *m_ptr;  // the checked specialised frame, -1 when the caller's did not match
     const int lane = threadIdx.x & 31;
-    const int warps = blockDim.x >> 5;
     const int KW = dt.lane_words + dt.sync_words;
-    // m must be a well-formed frame whose edges fit the masks; otherwise every frame takes
-    // the frame-table path
-    const bool m_frame = m >= 0 && m < fr.n_frames;
-    const int s_m = m_frame ? fr.sync_set[m] : -1;
-    const bool m_ok = m_frame && dt.sync_words <= kDeltaMaxWords && dt.lane_words <= kDeltaMaxWords &&
-                      ft.frame_class[m] == 0 && s_m >= 0 && s_m < fr.n_sync_sets &&
-                      ft.set_meta[s_m].x <= 32 * dt.sync_words && N <= 32 * dt.lane_words;
-    const int len_m = m_ok ? ft.set_meta[s_m].x : 0;
-    const int off_m = m_ok ? fr.sync_offsets[s_m] : 0;
-    // m's program edges as (a, b, d) keys, staged once per block (at most 32 * sync_words)
-    __shared__ unsigned long long mkeys[32 * kDeltaMaxWords];
-    __shared__ unsigned kept_sync[4][kDeltaMaxWords];  // per warp: m's edges found in f's program
-    const auto key = [&](int k) {
-        return static_cast<unsigned long long>(static_cast<unsigned>(fr.sync_edges[3 * k]) & 0xFFFFu) |
-               static_cast<unsigned long long>(static_cast<unsigned>(fr.sync_edges[3 * k + 1]) & 0xFFFFu) << 16 |
-               static_cast<unsigned long long>(static_cast<unsigned>(fr.sync_edges[3 * k + 2])) << 32;
-    };
-    for (int e = threadIdx.x; e < len_m; e += blockDim.x) mkeys[e] = key(off_m + e);
-    __syncthreads();
-    unsigned* kept_w = kept_sync[threadIdx.x >> 5];
-    for (int f = blockIdx.x * warps + (threadIdx.x >> 5); f < fr.n_frames; f += gridDim.x * warps) {
-        unsigned* keep = dt.keep + static_cast<size_t>(f) * KW;
-        int4* prog = dt.prog + static_cast<size_t>(f) * 2 * kDeltaMax;
-        if (lane == 0) {  // the facts the verification reads per candidate
-            const int set = fr.sync_set[f];
-            const int tail = set >= 0 && set < fr.n_sync_sets ? ft.set_meta[set].y : TFV_CLASS_BAD_PACKING;
-            const int r = ft.first_unreached[f];
-            dt.record[f] = make_int4(ft.frame_class[f], tail, (ft.frame_flags[f] & kFrameRegisterCross) ? 1 : 0,
-                                     r >= 0 ? p.relation[r] : -1);
-        }
-        if (!m_ok) {
-            if (lane == 0) dt.header[f] = make_int4(kDeltaGeneric, 0, 0, 0);
-            continue;
-        }
-        if (f == m || ft.frame_class[f] != 0) {  // itself, or no lane/sync answer needed
-            for (int w = lane; w < KW; w += 32) keep[w] = 0xFFFFFFFFu;
-            if (lane == 0) dt.header[f] = make_int4(f == m ? kDeltaSame : kDeltaEdges, 0, 0, 0);
-            continue;
-        }
-        // lane edges, by m's walk position j of their source a
-        int n_lane = 0;
-        unsigned acc[kDeltaMaxWords] = {0, 0, 0, 0};
-        for (int w = 0; w * 32 < N; ++w) {
-            const int j = w * 32 + lane;
-            const int a = j < N ? min(static_cast<int>(ft.order[static_cast<size_t>(j) * fr.n_frames + m]), N - 1) : 0;
-            const int sf = j < N ? ft.succ[static_cast<size_t>(f) * N + a] : 0;
-            const int sm = j < N ? ft.succ[static_cast<size_t>(m) * N + a] : 0;
-            const bool kept = j < N && sf == sm;
-            const bool wrap = (sf & kWrap) != 0;
-            const bool add = j < N && !kept && sf >= 0 && !(wrap && I < 2);
-            const unsigned add_bits = __ballot_sync(kFull, add);
-            keep_bits(kept, j < N ? lane_bit[j] : -1, dt.lane_words, acc);
-            const int pos = n_lane + __popc(add_bits & ((1u << lane) - 1));
-            if (add && pos < kDeltaMax) {
-                const int b = sf & kSuccMask;
-                const int a_row = a * kTmaRowBytes, b_row = b * kTmaRowBytes;
-                const int issue = p.issue[a];
-                int4 e;
-                if (!wrap)
-                    e = make_int4(a_row | (b_row << 16), b_row, base_prologue[b] - base_prologue[a] - issue,
-                                  I >= 2 ? base_offset[b] - base_offset[a] - issue : kNoBodyWeight);
-                else
-                    e = make_int4(a_row | (b_row << 16), (N * kTmaRowBytes + b_row) | (1 << 17),
-                                  base_offset[b] - base_prologue[a] - issue,
-                                  I >= 3 ? base_offset[b] - base_offset[a] - issue : kNoBodyWeight);
-                prog[pos] = e;
-            }
-            n_lane += __popc(add_bits);
-        }
-        if (lane == 0)
-            for (int w = 0; w < dt.lane_words; ++w) keep[w] = acc[w];
-        // sync edges
-        int n_sync = 0;
-        const int s_f = fr.sync_set[f];
-        unsigned* skeep = keep + dt.lane_words;
-        if (s_f == s_m) {
-            for (int w = lane; w < dt.sync_words; w += 32) skeep[w] = 0xFFFFFFFFu;
-        } else {
-            const int len_f = ft.set_meta[s_f].x;
-            const int off_f = fr.sync_offsets[s_f];
-            if (lane < kDeltaMaxWords) kept_w[lane] = 0;
-            __syncwarp();
-            // each of f's program edges: the same edge of m's program is kept, none is added
-            for (int j0 = 0; j0 < len_f; j0 += 32) {
-                const int j = j0 + lane;
-                bool add = false;
-                if (j < len_f) {
-                    const unsigned long long kf = key(off_f + j);
-                    int e = 0;
-                    while (e < len_m && mkeys[e] != kf) ++e;
-                    if (e < len_m) atomicOr(&kept_w[e >> 5], 1u << (e & 31));
-                    add = e == len_m;
-                }
-                const unsigned bits = __ballot_sync(kFull, add);
-                const int pos = n_sync + __popc(bits & ((1u << lane) - 1));
-                if (add && pos < kDeltaMax) prog[kDeltaMax + pos] = ft.set_prog[off_f + j];
-                n_sync += __popc(bits);
-            }
-            __syncwarp();
-            unsigned sacc[kDeltaMaxWords] = {0, 0, 0, 0};
-            for (int e0 = 0; e0 < len_m; e0 += 32) {
-                const int e = e0 + lane;
-                keep_bits(e < len_m && ((kept_w[e >> 5] >> (e & 31)) & 1u), e < len_m ? sync_bit[e] : -1,
-                          dt.sync_words, sacc);
-            }
-            if (lane == 0)
-                for (int w = 0; w < dt.sync_words; ++w) skeep[w] = sacc[w];
-        }
-        if (lane == 0)
-            dt.header[f] = make_int4(n_lane > kDeltaMax || n_sync > kDeltaMax ? kDeltaGeneric : kDeltaEdges,
-                                     min(n_lane, kDeltaMax), min(n_sync, kDeltaMax), 0);
+    unsigned* keep = dt.keep + static_cast<size_t>(f) * KW;
+    int4* prog = dt.prog + static_cast<size_t>(f) * 2 * kDeltaMax;
+    const int s_f = fr.sync_set[f];
+    const bool set_ok = s_f >= 0 && s_f < fr.n_sync_sets;
+    int tail = TFV_CLASS_BAD_PACKING, off_f = 0, end_f = 0;
+    if (set_ok) end_f = set_program_end(p, fr, s_f, &tail, &off_f);
+    if (lane == 0) {  // the facts the verification reads per candidate
+        const int r = ft.first_unreached[f];
+        dt.record[f] = make_int4(ft.frame_class[f], tail, (ft.frame_flags[f] & kFrameRegisterCross) ? 1 : 0,
+                                 r >= 0 ? p.relation[r] : -1);
     }
+    if (!m_ok) {
+        if (lane == 0) dt.header[f] = make_int4(kDeltaGeneric, 0, 0, 0);
+        return;
+    }
+    if (f == m || ft.frame_class[f] != 0) {  // itself, or no lane/sync answer needed
+        for (int w = lane; w < KW; w += 32) keep[w] = 0xFFFFFFFFu;
+        if (lane == 0) dt.header[f] = make_int4(f == m ? kDeltaSame : kDeltaEdges, 0, 0, 0);
+        return;
+    }
+    // lane edges, by m's walk position j of their source a
+    int n_lane = 0;
+    unsigned acc[kDeltaMaxWords] = {0, 0, 0, 0};
+    for (int w = 0; w * 32 < N; ++w) {
+        const int j = w * 32 + lane;
+        const int a = j < N ? min(static_cast<int>(ft.order[static_cast<size_t>(j) * fr.n_frames + m]), N - 1) : 0;
+        const int sf = j < N ? ft.succ[static_cast<size_t>(f) * N + a] : 0;
+        const int sm = j < N ? ft.succ[static_cast<size_t>(m) * N + a] : 0;
+        const bool kept = j < N && sf == sm;
+        const bool wrap = (sf & kWrap) != 0;
+        const bool add = j < N && !kept && sf >= 0 && !(wrap && I < 2);
+        const unsigned add_bits = __ballot_sync(kFull, add);
+        keep_bits(kept, j < N ? lane_bit[j] : -1, dt.lane_words, acc);
+        const int pos = n_lane + __popc(add_bits & ((1u << lane) - 1));
+        if (add && pos < kDeltaMax) {
+            const int b = sf & kSuccMask;
+            const int a_row = a * kTmaRowBytes, b_row = b * kTmaRowBytes;
+            const int issue = p.issue[a];
+            int4 e;
+            if (!wrap)
+                e = make_int4(a_row | (b_row << 16), b_row, base_prologue[b] - base_prologue[a] - issue,
+                              I >= 2 ? base_offset[b] - base_offset[a] - issue : kNoBodyWeight);
+            else
+                e = make_int4(a_row | (b_row << 16), (N * kTmaRowBytes + b_row) | (1 << 17),
+                              base_offset[b] - base_prologue[a] - issue,
+                              I >= 3 ? base_offset[b] - base_offset[a] - issue : kNoBodyWeight);
+            prog[pos] = e;
+        }
+        n_lane += __popc(add_bits);
+    }
+    if (lane == 0)
+        for (int w = 0; w < dt.lane_words; ++w) keep[w] = acc[w];
+    // sync edges
+    int n_sync = 0;
+    unsigned* skeep = keep + dt.lane_words;
+    if (s_f == fr.sync_set[m]) {
+        for (int w = lane; w < dt.sync_words; w += 32) skeep[w] = 0xFFFFFFFFu;
+    } else {
+        const int len_f = end_f - off_f;
+        if (lane < kDeltaMaxWords) kept_w[lane] = 0;
+        __syncwarp();
+        // each of f's program edges: the same edge of m's program is kept, none is added
+        for (int j0 = 0; j0 < len_f; j0 += 32) {
+            const int j = j0 + lane;
+            bool add = false;
+            if (j < len_f) {
+                const int k = off_f + j;
+                const unsigned long long kf = edge_key(fr.sync_edges[3 * k], fr.sync_edges[3 * k + 1], fr.sync_edges[3 * k + 2]);
+                int e = 0;
+                while (e < len_m && mkeys[e] != kf) ++e;
+                if (e < len_m) atomicOr(&kept_w[e >> 5], 1u << (e & 31));
+                add = e == len_m;
+            }
+            const unsigned bits = __ballot_sync(kFull, add);
+            const int pos = n_sync + __popc(bits & ((1u << lane) - 1));
+            if (add && pos < kDeltaMax) prog[kDeltaMax + pos] = fold_sync_edge(p, fr, off_f + j, base_prologue, base_offset, false);
+            n_sync += __popc(bits);
+        }
+        __syncwarp();
+        unsigned sacc[kDeltaMaxWords] = {0, 0, 0, 0};
+        for (int e0 = 0; e0 < len_m; e0 += 32) {
+            const int e = e0 + lane;
+            keep_bits(e < len_m && ((kept_w[e >> 5] >> (e & 31)) & 1u), e < len_m ? sync_bit[e] : -1,
+                      dt.sync_words, sacc);
+        }
+        if (lane == 0)
+            for (int w = 0; w < dt.sync_words; ++w) skeep[w] = sacc[w];
+    }
+    if (lane == 0)
+        dt.header[f] = make_int4(n_lane > kDeltaMax || n_sync > kDeltaMax ? kDeltaGeneric : kDeltaEdges,
+                                 min(n_lane, kDeltaMax), min(n_sync, kDeltaMax), 0);
 }
 
-cudaError_t launch_delta_frames(const DevProblem& p, const DevFrames& f, FrameTable t, const int* spec_frame,
-                                const int* base_prologue, const int* base_offset, const int* lane_bit,
-                                const int* sync_bit, DeltaTable d, int sm_count, cudaStream_t stream) {
-    if (f.n_frames <= 0) return cudaSuccess;
-    const int grid = min((f.n_frames + 3) / 4, sm_count * 8);
-    // four warps a block: the kernel keeps one row of kept_sync per warp
-    delta_frames_kernel<<<grid, 128, 0, stream>>>(p, f, t, spec_frame, base_prologue, base_offset, lane_bit, sync_bit,
-                                                   d);
-    return cudaGetLastError();
-}
-
-// One warp: whether the caller's frame `spec` has the lanes and the sync program a plan's
-// code was generated for (sig_lane_pos [N]; sig_edges [sig_len][3], the set's edges before its
-// first static failure). Writes spec to *out when it has, else -1, so that a frame index that
-// names another frame makes every candidate take the frame-table path.
-__global__ void __launch_bounds__(32) check_spec_frame_kernel(DevProblem p, DevFrames fr, int spec,
-                                                               const uint16_t* sig_lane_pos, const int* sig_edges,
-                                                               int sig_len, int* out) {
+// One warp: whether the caller's frame `spec` has the lanes and the sync program a plan's code
+// was generated for (sig_lane_pos [N]; sig_edges [sig_len][3], the set's edges before its first
+// static failure). Every lane gets the answer.
+__device__ bool spec_frame_matches(const DevProblem& p, const DevFrames& fr, int spec, const uint16_t* sig_lane_pos,
+                                   const int* sig_edges, int sig_len) {
     const int N = p.n_ops, I = p.iterations;
-    const int lane = threadIdx.x;
+    const int lane = threadIdx.x & 31;
     bool ok = spec >= 0 && spec < fr.n_frames;
     int e0 = 0, e1 = 0;
     if (ok) {
@@ -685,26 +682,73 @@ __global__ void __launch_bounds__(32) check_spec_frame_kernel(DevProblem p, DevF
             ok = e0 >= 0 && e1 >= e0 && e1 <= fr.n_sync_edges && e1 - e0 >= sig_len;
         }
     }
-    if (ok) {
-        bool same = true;
-        for (int a = lane; a < N; a += 32) same &= fr.lane_pos[static_cast<size_t>(spec) * N + a] == sig_lane_pos[a];
-        for (int k = lane; k < sig_len; k += 32)
-            for (int c = 0; c < 3; ++c) same &= fr.sync_edges[3 * (e0 + k) + c] == sig_edges[3 * k + c];
-        if (lane == 0 && e0 + sig_len < e1) {  // the program must end where the signature's does
-            const int a = fr.sync_edges[3 * (e0 + sig_len)], b = fr.sync_edges[3 * (e0 + sig_len) + 1];
-            const int d = fr.sync_edges[3 * (e0 + sig_len) + 2];
-            same &= a < 0 || b < 0 || d >= I;
-        }
-        ok = __all_sync(kFull, same);
+    if (!ok) return false;
+    bool same = true;
+    for (int a = lane; a < N; a += 32) same &= fr.lane_pos[static_cast<size_t>(spec) * N + a] == sig_lane_pos[a];
+    for (int k = lane; k < sig_len; k += 32)
+        for (int c = 0; c < 3; ++c) same &= fr.sync_edges[3 * (e0 + k) + c] == sig_edges[3 * k + c];
+    if (lane == 0 && e0 + sig_len < e1) {  // the program must end where the signature's does
+        const int a = fr.sync_edges[3 * (e0 + sig_len)], b = fr.sync_edges[3 * (e0 + sig_len) + 1];
+        const int d = fr.sync_edges[3 * (e0 + sig_len) + 2];
+        same &= a < 0 || b < 0 || d >= I;
     }
-    if (lane == 0) *out = ok ? spec : -1;
+    return __all_sync(kFull, same);
 }
 
-cudaError_t launch_check_spec_frame(const DevProblem& p, const DevFrames& f, int spec, const uint16_t* sig_lane_pos,
-                                    const int* sig_edges, int sig_len, int* out, cudaStream_t stream) {
-    check_spec_frame_kernel<<<1, 32, 0, stream>>>(p, f, spec, sig_lane_pos, sig_edges, sig_len, out);
+// A plan's per-call preparation in one launch, four warps a block: the first warp of every block
+// checks the caller's spec frame against the plan's signature (block 0 writes the result, the
+// frame the generated code serves or -1, to *spec_out); then warp w compiles sync set w's
+// program (ft.set_prog / set_meta, read by the verification's frame-table path) and, with delta
+// verification, frame w's DeltaTable entries. The two roles share no data within the launch:
+// the frame entries take their program lengths and added sync entries from the frame set.
+__global__ void __launch_bounds__(128) prepare_plan_kernel(DevProblem p, DevFrames fr, FrameTable ft, int spec,
+                                                           const uint16_t* sig_lane_pos, const int* sig_edges,
+                                                           int sig_len, int* spec_out, const int* base_prologue,
+                                                           const int* base_offset, const int* lane_bit,
+                                                           const int* sync_bit, DeltaTable dt, int delta) {
+    __shared__ int m_s;
+    __shared__ unsigned long long mkeys[32 * kDeltaMaxWords];
+    __shared__ unsigned kept_sync[4][kDeltaMaxWords];  // per warp: m's edges found in f's program
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    if (warp == 0) {
+        const bool match = spec_frame_matches(p, fr, spec, sig_lane_pos, sig_edges, sig_len);
+        if (lane == 0) {
+            m_s = match ? spec : -1;
+            if (blockIdx.x == 0) *spec_out = m_s;
+        }
+    }
+    __syncthreads();
+    const int m = m_s;
+    // m must be a well-formed frame whose edges fit the masks; otherwise every frame takes the
+    // frame-table path. m's program is the signature's.
+    const bool m_ok = delta && m >= 0 && dt.sync_words <= kDeltaMaxWords && dt.lane_words <= kDeltaMaxWords &&
+                      ft.frame_class[m] == 0 && sig_len <= 32 * dt.sync_words && p.n_ops <= 32 * dt.lane_words;
+    const int len_m = m_ok ? sig_len : 0;
+    for (int e = threadIdx.x; e < len_m; e += blockDim.x)
+        mkeys[e] = edge_key(sig_edges[3 * e], sig_edges[3 * e + 1], sig_edges[3 * e + 2]);
+    __syncthreads();
+    const int roles = max(fr.n_sync_sets, delta ? fr.n_frames : 0);
+    for (int w = blockIdx.x * 4 + warp; w < roles; w += gridDim.x * 4) {
+        if (w < fr.n_sync_sets) compile_set(p, fr, ft, w, base_prologue, base_offset, false);
+        if (delta && w < fr.n_frames)
+            delta_frame(p, fr, ft, w, m, m_ok, mkeys, len_m, kept_sync[warp], base_prologue, base_offset, lane_bit,
+                        sync_bit, dt);
+    }
+}
+
+cudaError_t launch_prepare_plan(const DevProblem& p, const DevFrames& f, FrameTable t, int spec,
+                                const uint16_t* sig_lane_pos, const int* sig_edges, int sig_len, int* spec_out,
+                                const int* base_prologue, const int* base_offset, const int* lane_bit,
+                                const int* sync_bit, const DeltaTable* d, int sm_count, cudaStream_t stream) {
+    const int roles = max(f.n_sync_sets, d ? f.n_frames : 0);
+    const int grid = max(1, min((roles + 3) / 4, sm_count * 8));
+    prepare_plan_kernel<<<grid, 128, 0, stream>>>(p, f, t, spec, sig_lane_pos, sig_edges, sig_len, spec_out,
+                                                  base_prologue, base_offset, lane_bit, sync_bit,
+                                                  d ? *d : DeltaTable{}, d ? 1 : 0);
     return cudaGetLastError();
 }
+
+
 
 cudaError_t launch_compile_sync_programs(const DevProblem& p, const DevFrames& f, FrameTable t, const int* base_prologue,
                                          const int* base_offset, int sm_count, cudaStream_t stream, bool index_form) {

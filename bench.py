@@ -693,9 +693,10 @@ def run_ours(args) -> None:
                     "link_bound": world * n * n_ii / (h2d / (link["h2d_gbs"] * 1e9) + d2h / (link["d2h_gbs"] * 1e9)),
                     "frac_of_link_bound": e2e_value / (world * n * n_ii / (h2d / (link["h2d_gbs"] * 1e9) +
                                                                            d2h / (link["d2h_gbs"] * 1e9)))},
-            # frame analysis, sync-program compile, verification (+ the plan's spec-frame check
-            # and constants kernels and, with delta verification, its frame comparison)
-            "gpu_launches": (3 + (0 if plan is None else 3 if plan.delta else 2)) * args.steps,
+            # per step: the frame analysis, then either the sync-program compile and the
+            # verification kernel, or the plan's preparation (spec-frame check, sync programs,
+            # frame comparison in one launch), constants kernel and generated kernel
+            "gpu_launches": (3 if plan is None else 4) * args.steps,
             "ranks": per_rank,
             "clocks": clocks.summary(),
         }

@@ -73,7 +73,14 @@ struct Divider {
         while ((1u << l) < du) ++l;
 #endif
         shift = 30 + l;
-        m = ((1ull << shift) + du - 1) / du;
+        // m = ceil(2^shift / d) without a 64-bit integer division: the double quotient of the two
+        // exact operands lies within 1 of the true one (which is below 2^31 + 1), so truncating it
+        // and stepping once in either direction gives the exact ceiling.
+        const unsigned long long target = 1ull << shift;
+        unsigned long long q = static_cast<unsigned long long>(static_cast<double>(target) / static_cast<double>(du));
+        if (q * du < target) ++q;
+        if ((q - 1) * du >= target) --q;
+        m = q;
     }
     __host__ __device__ __forceinline__ int quot(int x) const {
         return static_cast<int>((static_cast<unsigned long long>(static_cast<unsigned>(x)) * m) >> shift);

@@ -5,15 +5,18 @@ Workload (default ``mla``): seeded neighbourhood perturbations of the MLA decode
 example's verified witness schedule (51 operations, 16 iterations, 3 warpgroups, 48
 sync edges, 120 required relations), in the compact periodic form (int16 deltas of
 the prologue and body-offset starts plus an II and a frame index per candidate). A
-step verifies every candidate of one rank's batch: frame analysis plus one
-verification launch, and for N > 1 the gather of all verdicts to rank 0.
+step verifies every candidate of one rank's batch: the frame analysis (issued on a side
+stream during the previous step's verification, into the second of two frame tables),
+the planned call (one preparation launch, the constants kernel and the kernel generated
+for the batch's most frequent frame), and for N > 1 the gather of all verdicts to rank 0.
 
 Reported:
   value     whole-job candidates/s with inputs resident in HBM (CUDA events, max over ranks)
   e2e       candidates/s through the C ABI host-buffer entry (tfv_verify_periodic_host):
             pinned host inputs copied in and host results copied out every step
   roofline  the verification kernel's algorithmic bytes per launch / its mean CUDA-event
-            duration inside the timed region, against the measured HBM copy bandwidth
+            duration inside the timed region (events the plan records around the generated
+            kernel alone), against the measured HBM copy bandwidth
   cpu_baseline  the oracle (a step-by-step restatement of the reference verifier) on
             all host cores, on a bounded sample of the same batch
 
